@@ -1,0 +1,889 @@
+// C ABI of libbgtq.so: object lifetimes, validation (before any state change, as the
+// reference's RangeError/Error checks are), host<->device staging and kernel launches.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "bgtq_internal.h"
+
+using namespace bgtq;
+
+namespace {
+
+thread_local std::string g_err;
+
+bgtq_status fail(bgtq_status s, const std::string &msg) {
+    g_err = msg;
+    return s;
+}
+bgtq_status cuda_fail(cudaError_t e, const char *where) {
+    g_err = std::string(where) + ": " + cudaGetErrorString(e);
+    return BGTQ_ECUDA;
+}
+#define CK(expr, where)                                   \
+    do {                                                  \
+        cudaError_t e_ = (expr);                          \
+        if (e_ != cudaSuccess) return cuda_fail(e_, where); \
+    } while (0)
+
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+uint32_t dim_template(uint32_t d) { return d <= 16 ? 16u : d <= 32 ? 32u : d <= 64 ? 64u : 128u; }
+uint32_t round_up(uint32_t x, uint32_t m) { return (x + m - 1) / m * m; }
+
+struct DevBuf {
+    void *p = nullptr;
+    size_t bytes = 0;
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    cudaError_t ensure(size_t n) {
+        if (n <= bytes) return cudaSuccess;
+        release();
+        cudaError_t e = cudaMalloc(&p, n);
+        if (e == cudaSuccess) bytes = n;
+        return e;
+    }
+};
+
+std::mutex g_status_mu;
+uint32_t *g_status[64] = {};
+
+}  // namespace
+
+namespace bgtq {
+uint32_t *device_status_word(int device) {
+    if (device < 0 || device >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(g_status_mu);
+    if (!g_status[device]) {
+        void *p = nullptr;
+        if (cudaMalloc(&p, sizeof(uint32_t)) != cudaSuccess) return nullptr;
+        cudaMemset(p, 0, sizeof(uint32_t));
+        g_status[device] = static_cast<uint32_t *>(p);
+    }
+    return g_status[device];
+}
+}  // namespace bgtq
+
+struct bgtq_tables {
+    int device = 0;
+    Layout L;
+    DeviceTables dt;
+};
+
+struct bgtq_keys {
+    bgtq_keys_kind kind;
+    int device = 0;
+    Layout L;          // packed/compressed only
+    DeviceTables dt;
+    uint32_t dim = 0, D = 0, capacity = 0, cap_alloc = 0, sequences = 0;
+    uint32_t row_stride = 0;    // bytes between device rows
+    uint32_t scale_stride = 0;  // halves between device scale rows
+    uint8_t *rows = nullptr;
+    uint16_t *scales = nullptr;
+    uint32_t *d_lengths = nullptr;
+    std::vector<uint32_t> lengths;
+    DevBuf row0, staging, materialized;
+    std::vector<bgtq_allocation> ledger;
+};
+
+struct bgtq_values {
+    bgtq_dtype dtype;
+    int device = 0;
+    uint32_t dim = 0, D = 0, capacity = 0, cap_alloc = 0, sequences = 0;
+    void *data = nullptr;
+    uint32_t *d_lengths = nullptr;
+    std::vector<uint32_t> lengths;
+    DevBuf row0, staging;
+};
+
+struct bgtq_attention {
+    uint32_t heads = 0, rows = 0, dim = 0, sequences = 0;
+    int device = 0;
+    std::vector<bgtq_keys *> keys;
+    std::vector<bgtq_values *> values;
+    float *part = nullptr;
+    uint32_t *counters = nullptr;
+    float *lse = nullptr;
+    DevBuf q_dev, pos_dev, out_dev, logits_dev, probs_dev;
+    uint32_t forced_splits = 0, last_splits = 0, last_launches = 0;
+};
+
+namespace {
+
+cudaError_t upload_tables(const Layout &L, DeviceTables &dt) {
+    const size_t n_rot = (size_t)L.d * L.d, n_cent = L.cent_compact.size();
+    auto a16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
+    size_t off = 0;
+    const size_t o_rot = off; off = a16(off + 4 * n_rot);
+    const size_t o_cent = off; off = a16(off + 4 * (n_cent ? n_cent : 1));
+    const size_t o_off = off; off = a16(off + 4 * L.d);
+    const size_t o_inv = off; off = a16(off + 4 * L.d);
+    const size_t o_lut = off; off = a16(off + L.lut.size());
+    const size_t o_perm = off; off = a16(off + L.d);
+    const size_t o_grp = off; off = a16(off + L.d);
+    const size_t o_cbi = off; off = a16(off + L.d);
+    const size_t o_cbb = off; off = a16(off + 2 * L.d);
+    std::vector<unsigned char> host(off, 0);
+    std::memcpy(host.data() + o_rot, L.rot.data(), 4 * n_rot);
+    if (n_cent) std::memcpy(host.data() + o_cent, L.cent_compact.data(), 4 * n_cent);
+    std::memcpy(host.data() + o_off, L.off.data(), 4 * L.d);
+    std::memcpy(host.data() + o_inv, L.inv.data(), 4 * L.d);
+    std::memcpy(host.data() + o_lut, L.lut.data(), L.lut.size());
+    std::memcpy(host.data() + o_perm, L.perm.data(), L.d);
+    std::memcpy(host.data() + o_grp, L.group_of.data(), L.d);
+    std::memcpy(host.data() + o_cbi, L.pos_to_cb.data(), L.d);
+    std::memcpy(host.data() + o_cbb, L.cb_base.data(), 2 * L.d);
+    void *blob = nullptr;
+    cudaError_t e = cudaMalloc(&blob, off);
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpy(blob, host.data(), off, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(blob);
+        return e;
+    }
+    unsigned char *b = static_cast<unsigned char *>(blob);
+    dt.blob = blob;
+    dt.bytes = off;
+    dt.rot = reinterpret_cast<const float *>(b + o_rot);
+    dt.cent = reinterpret_cast<const float *>(b + o_cent);
+    dt.off = reinterpret_cast<const float *>(b + o_off);
+    dt.inv = reinterpret_cast<const float *>(b + o_inv);
+    dt.lut = b + o_lut;
+    dt.perm = b + o_perm;
+    dt.group_of = b + o_grp;
+    dt.cbidx = b + o_cbi;
+    dt.cb_base = reinterpret_cast<const uint16_t *>(b + o_cbb);
+    return cudaSuccess;
+}
+
+bool host_finite(const void *src, bgtq_dtype dt, uint32_t dim, uint32_t count, uint64_t row_stride, uint32_t seq_count,
+                 uint64_t seq_stride) {
+    for (uint32_t s = 0; s < seq_count; ++s)
+        for (uint32_t r = 0; r < count; ++r) {
+            const uint64_t base = s * seq_stride + r * row_stride;
+            if (dt == BGTQ_F16) {
+                const uint16_t *p = static_cast<const uint16_t *>(src) + base;
+                for (uint32_t i = 0; i < dim; ++i)
+                    if ((p[i] & 0x7c00u) == 0x7c00u) return false;
+            } else {
+                const float *p = static_cast<const float *>(src) + base;
+                for (uint32_t i = 0; i < dim; ++i)
+                    if (!std::isfinite(p[i])) return false;
+            }
+        }
+    return true;
+}
+
+// Common validation + host staging of an append source.  On success `dsrc`,
+// `drow`, `dseq` describe a device-resident source.
+bgtq_status stage_source(const void *src, bgtq_dtype dtype, int host, uint32_t dim, uint32_t count, uint64_t row_stride,
+                         uint32_t seq_count, uint64_t seq_stride, DevBuf &staging, cudaStream_t stream,
+                         const void **dsrc, uint64_t *drow, uint64_t *dseq) {
+    const size_t es = dtype == BGTQ_F16 ? 2 : 4;
+    if (host) {
+        if (!host_finite(src, dtype, dim, count, row_stride, seq_count, seq_stride))
+            return fail(BGTQ_ENONFINITE, dtype == BGTQ_F16 ? "Finite FP16 K required" : "finite inputs required");
+        const size_t bytes = (size_t)seq_count * count * dim * es;
+        CK(staging.ensure(bytes), "staging allocation");
+        if (row_stride == dim && (seq_count == 1 || seq_stride == (uint64_t)count * dim)) {
+            CK(cudaMemcpyAsync(staging.p, src, bytes, cudaMemcpyHostToDevice, stream), "append upload");
+        } else {
+            for (uint32_t s = 0; s < seq_count; ++s)
+                CK(cudaMemcpy2DAsync(static_cast<unsigned char *>(staging.p) + (size_t)s * count * dim * es, dim * es,
+                                     static_cast<const unsigned char *>(src) + s * seq_stride * es, row_stride * es,
+                                     dim * es, count, cudaMemcpyHostToDevice, stream),
+                   "append upload");
+        }
+        *dsrc = staging.p;
+        *drow = dim;
+        *dseq = (uint64_t)count * dim;
+    } else {
+        *dsrc = src;
+        *drow = row_stride;
+        *dseq = seq_stride;
+    }
+    return BGTQ_OK;
+}
+
+// Start row of every target sequence: scalar when all equal, else a device vector.
+bgtq_status start_rows(const std::vector<uint32_t> &lengths, uint32_t seq_first, uint32_t seq_count, DevBuf &buf,
+                       cudaStream_t stream, const uint32_t **dev, uint32_t *scalar, std::vector<uint32_t> &tmp) {
+    bool uniform = true;
+    for (uint32_t s = 1; s < seq_count; ++s) uniform &= lengths[seq_first + s] == lengths[seq_first];
+    *scalar = lengths[seq_first];
+    *dev = nullptr;
+    if (!uniform) {
+        tmp.assign(lengths.begin() + seq_first, lengths.begin() + seq_first + seq_count);
+        CK(buf.ensure(sizeof(uint32_t) * seq_count), "row0 allocation");
+        CK(cudaMemcpyAsync(buf.p, tmp.data(), sizeof(uint32_t) * seq_count, cudaMemcpyHostToDevice, stream),
+           "row0 upload");
+        *dev = static_cast<const uint32_t *>(buf.p);
+    }
+    return BGTQ_OK;
+}
+
+bgtq_status check_append(uint32_t dim, uint32_t capacity, uint32_t sequences, const std::vector<uint32_t> &lengths,
+                         const void *src, bgtq_dtype dtype, uint32_t count, uint64_t row_stride, uint32_t seq_first,
+                         uint32_t seq_count, const char *what) {
+    if (!src || dtype < BGTQ_F16 || dtype > BGTQ_F32) return fail(BGTQ_EINVAL, std::string(what) + ": invalid source");
+    if (!count || !seq_count || row_stride < dim)
+        return fail(BGTQ_EINVAL, std::string(what) + " append must contain whole nonempty rows");
+    if ((uint64_t)seq_first + seq_count > sequences) return fail(BGTQ_EINVAL, std::string(what) + ": sequence range");
+    for (uint32_t s = 0; s < seq_count; ++s)
+        if ((uint64_t)lengths[seq_first + s] + count > capacity)
+            return fail(BGTQ_ECAPACITY, std::string(what) + " capacity exceeded");
+    return BGTQ_OK;
+}
+
+void fill_encode_head(const bgtq_keys *k, EncodeHead &h) {
+    std::memset(&h, 0, sizeof(h));
+    h.t = k->dt;
+    h.packed = k->rows;
+    h.scales = k->scales;
+    h.k_seq_stride = (uint64_t)k->cap_alloc * k->row_stride;
+    h.s_seq_stride = (uint64_t)k->cap_alloc * k->scale_stride;
+    h.row_stride = k->row_stride;
+    h.scale_stride = k->scale_stride;
+    h.ns = k->L.ns;
+    h.ng = k->L.ng;
+    h.n_cent = (uint32_t)k->L.cent_compact.size();
+    h.ncb = k->L.ncb;
+    for (int i = 0; i < 4; ++i) h.bound_mask[i] = k->L.bound_mask[i];
+    for (int g = 0; g <= kMaxGroups; ++g) h.group_off[g] = k->L.group_off[g];
+    h.lengths = k->d_lengths;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *bgtq_status_string(bgtq_status s) {
+    switch (s) {
+        case BGTQ_OK: return "ok";
+        case BGTQ_EINVAL: return "invalid argument";
+        case BGTQ_ECAPACITY: return "capacity exceeded";
+        case BGTQ_ENONFINITE: return "non-finite input";
+        case BGTQ_EBUSY: return "storage not ready";
+        case BGTQ_ELAYOUT: return "invalid layout";
+        case BGTQ_ETIMEOUT: return "device wait timed out";
+        case BGTQ_ECUDA: return "CUDA error";
+        case BGTQ_ENOMEM: return "out of memory";
+        default: return "unknown status";
+    }
+}
+const char *bgtq_last_error(void) { return g_err.c_str(); }
+const char *bgtq_version(void) { return "bgtq-b200 0.1 (sm_100a)"; }
+
+bgtq_status bgtq_layout_validate(const uint32_t *config, size_t n_config, const float *table, size_t n_table,
+                                 uint32_t *ranges_out, bgtq_layout_info *info) {
+    Layout L;
+    std::string err;
+    bgtq_status s = parse_layout(config, n_config, table, n_table, L, err);
+    if (s != BGTQ_OK) return fail(s, err);
+    if (ranges_out) std::copy(L.ranges.begin(), L.ranges.end(), ranges_out);
+    if (info) {
+        info->dim = L.d; info->groups = L.ng; info->row_bytes = L.row_bytes; info->norm_stride = L.norm_stride;
+        info->nibble_dims = L.ns; info->max_centroids = L.maxc; info->logical_row_bytes = L.logical_rb;
+        info->device_row_stride = L.dev_row_stride; info->device_scale_stride = L.dev_scale_stride;
+        info->codebooks = L.ncb;
+    }
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_tables_create(const uint32_t *config, size_t n_config, const float *table, size_t n_table, int device,
+                               bgtq_tables **out) {
+    if (!out) return fail(BGTQ_EINVAL, "null output");
+    auto *t = new bgtq_tables();
+    std::string err;
+    bgtq_status s = parse_layout(config, n_config, table, n_table, t->L, err);
+    if (s != BGTQ_OK) {
+        delete t;
+        return fail(s, err);
+    }
+    DeviceGuard g(device);
+    if (!g.ok) {
+        delete t;
+        return fail(BGTQ_ECUDA, "cannot select device");
+    }
+    t->device = device;
+    cudaError_t e = upload_tables(t->L, t->dt);
+    if (e != cudaSuccess) {
+        delete t;
+        return cuda_fail(e, "tables upload");
+    }
+    *out = t;
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_tables_info(const bgtq_tables *t, bgtq_layout_info *info) {
+    if (!t || !info) return fail(BGTQ_EINVAL, "null argument");
+    const Layout &L = t->L;
+    info->dim = L.d; info->groups = L.ng; info->row_bytes = L.row_bytes; info->norm_stride = L.norm_stride;
+    info->nibble_dims = L.ns; info->max_centroids = L.maxc; info->logical_row_bytes = L.logical_rb;
+    info->device_row_stride = L.dev_row_stride; info->device_scale_stride = L.dev_scale_stride;
+    info->codebooks = L.ncb;
+    return BGTQ_OK;
+}
+
+void bgtq_tables_destroy(bgtq_tables *t) {
+    if (!t) return;
+    DeviceGuard g(t->device);
+    if (t->dt.blob) cudaFree(t->dt.blob);
+    delete t;
+}
+
+bgtq_status bgtq_keys_create(bgtq_keys_kind kind, const bgtq_tables *tables, uint32_t dim, uint32_t capacity,
+                             uint32_t sequences, int device, bgtq_keys **out) {
+    if (!out) return fail(BGTQ_EINVAL, "null output");
+    if (kind != BGTQ_KEYS_PACKED && kind != BGTQ_KEYS_FP16 && kind != BGTQ_KEYS_COMPRESSED)
+        return fail(BGTQ_EINVAL, "Invalid K kind");
+    if (kind != BGTQ_KEYS_FP16 && !tables) return fail(BGTQ_ELAYOUT, "Block-GTQ keys need tables");
+    if (kind == BGTQ_KEYS_FP16 && (dim < 2 || dim % 2 || dim > 128)) return fail(BGTQ_EINVAL, "Invalid K dimensions");
+    if (capacity < 1 || capacity > (1u << 31) || sequences < 1) return fail(BGTQ_EINVAL, "Unsupported K capacity");
+    auto *k = new bgtq_keys();
+    k->kind = kind;
+    k->device = device;
+    k->capacity = capacity;
+    k->sequences = sequences;
+    k->cap_alloc = round_up(capacity, kTileRows);
+    DeviceGuard g(device);
+    if (!g.ok) {
+        delete k;
+        return fail(BGTQ_ECUDA, "cannot select device");
+    }
+    auto cleanup = [&](bgtq_status s, const std::string &m) {
+        if (k->rows) cudaFree(k->rows);
+        if (k->scales) cudaFree(k->scales);
+        if (k->d_lengths) cudaFree(k->d_lengths);
+        if (k->dt.blob) cudaFree(k->dt.blob);
+        delete k;
+        return fail(s, m);
+    };
+    if (kind == BGTQ_KEYS_FP16) {
+        k->dim = dim;
+        k->D = dim_template(dim);
+        k->row_stride = k->D * 2;
+    } else {
+        k->L = tables->L;
+        k->dim = k->L.d;
+        k->D = dim_template(k->dim);
+        k->row_stride = k->L.dev_row_stride;
+        k->scale_stride = k->L.dev_scale_stride;
+        cudaError_t e = upload_tables(k->L, k->dt);
+        if (e != cudaSuccess) return cleanup(BGTQ_ECUDA, std::string("tables upload: ") + cudaGetErrorString(e));
+        k->ledger.push_back({"K tables", "shared", (uint64_t)k->dt.bytes});
+    }
+    const size_t rows_bytes = (size_t)sequences * k->cap_alloc * k->row_stride;
+    if (cudaMalloc(&k->rows, rows_bytes) != cudaSuccess) return cleanup(BGTQ_ENOMEM, "K allocation failed");
+    cudaMemset(k->rows, 0, rows_bytes);
+    k->ledger.push_back({kind == BGTQ_KEYS_FP16 ? "FP16 K" : "K nibble/byte capacity", "persistent-k", rows_bytes});
+    if (kind != BGTQ_KEYS_FP16) {
+        const size_t sb = (size_t)sequences * k->cap_alloc * k->scale_stride * 2;
+        if (cudaMalloc(&k->scales, sb) != cudaSuccess) return cleanup(BGTQ_ENOMEM, "K scale allocation failed");
+        cudaMemset(k->scales, 0, sb);
+        k->ledger.push_back({"K FP16 scale capacity", "persistent-k", sb});
+    }
+    if (cudaMalloc(&k->d_lengths, sizeof(uint32_t) * sequences) != cudaSuccess)
+        return cleanup(BGTQ_ENOMEM, "length allocation failed");
+    cudaMemset(k->d_lengths, 0, sizeof(uint32_t) * sequences);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cleanup(BGTQ_ECUDA, std::string("K init: ") + cudaGetErrorString(e));
+    k->lengths.assign(sequences, 0);
+    *out = k;
+    return BGTQ_OK;
+}
+
+void bgtq_keys_destroy(bgtq_keys *k) {
+    if (!k) return;
+    DeviceGuard g(k->device);
+    cudaFree(k->rows);
+    if (k->scales) cudaFree(k->scales);
+    cudaFree(k->d_lengths);
+    if (k->dt.blob) cudaFree(k->dt.blob);
+    k->row0.release();
+    k->staging.release();
+    k->materialized.release();
+    delete k;
+}
+
+bgtq_status bgtq_keys_append(bgtq_keys *k, const void *src, bgtq_dtype dtype, int host, uint32_t count,
+                             uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
+                             void *stream_) {
+    if (!k) return fail(BGTQ_EINVAL, "null keys");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    bgtq_status s = check_append(k->dim, k->capacity, k->sequences, k->lengths, src, dtype, count, row_stride,
+                                 seq_first, seq_count, "K");
+    if (s != BGTQ_OK) return s;
+    const bool packed = k->kind != BGTQ_KEYS_FP16;
+    if (!host && packed) {
+        const size_t align = dtype == BGTQ_F16 ? 4 : 8;
+        if (reinterpret_cast<uintptr_t>(src) % align || row_stride % 2 || (seq_count > 1 && seq_stride % 2))
+            return fail(BGTQ_EINVAL, "device K source must be aligned with even strides");
+    }
+    DeviceGuard g(k->device);
+    if (!g.ok) return fail(BGTQ_ECUDA, "cannot select device");
+    const void *dsrc;
+    uint64_t drow, dseq;
+    s = stage_source(src, dtype, host, k->dim, count, row_stride, seq_count, seq_stride, k->staging, stream, &dsrc, &drow,
+                     &dseq);
+    if (s != BGTQ_OK) return s;
+    const uint32_t *row0 = nullptr;
+    uint32_t row0_scalar = 0;
+    std::vector<uint32_t> tmp;
+    s = start_rows(k->lengths, seq_first, seq_count, k->row0, stream, &row0, &row0_scalar, tmp);
+    if (s != BGTQ_OK) return s;
+    cudaError_t e;
+    if (packed) {
+        EncodeArgs a;
+        std::memset(&a, 0, sizeof(a));
+        fill_encode_head(k, a.head[0]);
+        a.src = dsrc;
+        a.row_stride = drow;
+        a.seq_stride = dseq;
+        a.row0 = row0;
+        a.row0_scalar = row0_scalar;
+        a.count = count;
+        a.seq_first = seq_first;
+        a.seq_count = seq_count;
+        a.heads = 1;
+        a.src_f32 = dtype == BGTQ_F32;
+        e = launch_encode(a, k->dim, (uint32_t)k->L.cent_compact.size() + 256u, k->L.ncb, stream);
+    } else {
+        e = launch_copy_rows(k->rows, (uint64_t)k->cap_alloc * k->D, k->D, 0, dsrc, drow, dseq, dtype == BGTQ_F32, row0,
+                             row0_scalar, count, seq_first, seq_count, k->d_lengths, k->dim, stream);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "K append launch");
+    if (host) {
+        e = cudaStreamSynchronize(stream);  // the staging buffer is reused by the next call
+        if (e != cudaSuccess) return cuda_fail(e, "K append");
+    }
+    for (uint32_t i = 0; i < seq_count; ++i) k->lengths[seq_first + i] += count;
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_keys_length(const bgtq_keys *k, uint32_t seq, uint32_t *out) {
+    if (!k || !out || seq >= k->sequences) return fail(BGTQ_EINVAL, "invalid argument");
+    *out = k->lengths[seq];
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_keys_info(const bgtq_keys *k, bgtq_keys_kind *kind, uint32_t *dim, uint32_t *capacity,
+                           uint32_t *sequences) {
+    if (!k) return fail(BGTQ_EINVAL, "null keys");
+    if (kind) *kind = k->kind;
+    if (dim) *dim = k->dim;
+    if (capacity) *capacity = k->capacity;
+    if (sequences) *sequences = k->sequences;
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_keys_read(const bgtq_keys *k, uint32_t seq, uint32_t row0, uint32_t count, uint8_t *packed_out,
+                           uint16_t *scales_out) {
+    if (!k || seq >= k->sequences || (uint64_t)row0 + count > k->cap_alloc) return fail(BGTQ_EINVAL, "invalid range");
+    DeviceGuard g(k->device);
+    CK(cudaDeviceSynchronize(), "K read");
+    if (k->kind == BGTQ_KEYS_FP16) {
+        if (packed_out && count)
+            CK(cudaMemcpy2D(packed_out, (size_t)k->dim * 2,
+                            k->rows + ((uint64_t)seq * k->cap_alloc + row0) * k->row_stride, k->row_stride,
+                            (size_t)k->dim * 2, count, cudaMemcpyDeviceToHost),
+               "K read");
+        return BGTQ_OK;
+    }
+    const uint32_t rb = k->L.row_bytes, w = std::min(rb, k->row_stride);
+    if (packed_out && count) {
+        std::memset(packed_out, 0, (size_t)rb * count);
+        CK(cudaMemcpy2D(packed_out, rb, k->rows + ((uint64_t)seq * k->cap_alloc + row0) * k->row_stride, k->row_stride, w,
+                        count, cudaMemcpyDeviceToHost),
+           "K read");
+    }
+    if (scales_out && count) {
+        const uint32_t ns = k->L.norm_stride, ws = std::min(ns, k->scale_stride);
+        std::memset(scales_out, 0, (size_t)ns * 2 * count);
+        CK(cudaMemcpy2D(scales_out, (size_t)ns * 2,
+                        k->scales + ((uint64_t)seq * k->cap_alloc + row0) * k->scale_stride, (size_t)k->scale_stride * 2,
+                        (size_t)ws * 2, count, cudaMemcpyDeviceToHost),
+           "K read");
+    }
+    return BGTQ_OK;
+}
+
+static bgtq_status reconstruct_into(const bgtq_keys *k, uint32_t seq, float *out, cudaStream_t stream) {
+    ReconArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.t = k->dt;
+    a.packed = k->rows + (uint64_t)seq * k->cap_alloc * k->row_stride;
+    a.scales = k->scales + (uint64_t)seq * k->cap_alloc * k->scale_stride;
+    a.row_stride = k->row_stride;
+    a.scale_stride = k->scale_stride;
+    a.ns = k->L.ns;
+    a.d = k->dim;
+    a.rows = k->lengths[seq];
+    a.out = out;
+    cudaError_t e = launch_reconstruct(a, (uint32_t)k->L.cent_compact.size(), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "reconstruct launch");
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_keys_reconstruct(const bgtq_keys *k, uint32_t seq, float *out, void *stream) {
+    if (!k || !out || seq >= k->sequences) return fail(BGTQ_EINVAL, "invalid argument");
+    if (k->kind == BGTQ_KEYS_FP16) return fail(BGTQ_EINVAL, "FP16 keys need no reconstruction");
+    DeviceGuard g(k->device);
+    return reconstruct_into(k, seq, out, static_cast<cudaStream_t>(stream));
+}
+
+bgtq_status bgtq_keys_allocations(const bgtq_keys *k, bgtq_allocation *out, uint32_t cap, uint32_t *n_out) {
+    if (!k) return fail(BGTQ_EINVAL, "null keys");
+    std::vector<bgtq_allocation> all = k->ledger;
+    if (k->materialized.bytes) all.push_back({"materialized FP32 K", "scratch", (uint64_t)k->materialized.bytes});
+    if (n_out) *n_out = (uint32_t)all.size();
+    for (uint32_t i = 0; out && i < cap && i < all.size(); ++i) out[i] = all[i];
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_values_create(bgtq_dtype dtype, uint32_t dim, uint32_t capacity, uint32_t sequences, int device,
+                               bgtq_values **out) {
+    if (!out) return fail(BGTQ_EINVAL, "null output");
+    if ((dtype != BGTQ_F16 && dtype != BGTQ_F32) || dim < 1 || dim > 128 || capacity < 1 || capacity > (1u << 31) ||
+        sequences < 1)
+        return fail(BGTQ_EINVAL, "Invalid V dimensions");
+    auto *v = new bgtq_values();
+    v->dtype = dtype;
+    v->device = device;
+    v->dim = dim;
+    v->D = dim_template(dim);
+    v->capacity = capacity;
+    v->cap_alloc = round_up(capacity, kTileRows);
+    v->sequences = sequences;
+    DeviceGuard g(device);
+    const size_t es = dtype == BGTQ_F16 ? 2 : 4;
+    const size_t bytes = (size_t)sequences * v->cap_alloc * v->D * es;
+    if (cudaMalloc(&v->data, bytes) != cudaSuccess) {
+        delete v;
+        return fail(BGTQ_ENOMEM, "V allocation failed");
+    }
+    if (cudaMalloc(&v->d_lengths, sizeof(uint32_t) * sequences) != cudaSuccess) {
+        cudaFree(v->data);
+        delete v;
+        return fail(BGTQ_ENOMEM, "V allocation failed");
+    }
+    cudaMemset(v->data, 0, bytes);
+    cudaMemset(v->d_lengths, 0, sizeof(uint32_t) * sequences);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(v->data);
+        cudaFree(v->d_lengths);
+        delete v;
+        return cuda_fail(e, "V init");
+    }
+    v->lengths.assign(sequences, 0);
+    *out = v;
+    return BGTQ_OK;
+}
+
+void bgtq_values_destroy(bgtq_values *v) {
+    if (!v) return;
+    DeviceGuard g(v->device);
+    cudaFree(v->data);
+    cudaFree(v->d_lengths);
+    v->row0.release();
+    v->staging.release();
+    delete v;
+}
+
+bgtq_status bgtq_values_append(bgtq_values *v, const void *src, bgtq_dtype dtype, int host, uint32_t count,
+                               uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
+                               void *stream_) {
+    if (!v) return fail(BGTQ_EINVAL, "null values");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    bgtq_status s = check_append(v->dim, v->capacity, v->sequences, v->lengths, src, dtype, count, row_stride, seq_first,
+                                 seq_count, "V");
+    if (s != BGTQ_OK) return s;
+    DeviceGuard g(v->device);
+    const void *dsrc;
+    uint64_t drow, dseq;
+    s = stage_source(src, dtype, host, v->dim, count, row_stride, seq_count, seq_stride, v->staging, stream, &dsrc, &drow,
+                     &dseq);
+    if (s != BGTQ_OK) return s;
+    const uint32_t *row0 = nullptr;
+    uint32_t row0_scalar = 0;
+    std::vector<uint32_t> tmp;
+    s = start_rows(v->lengths, seq_first, seq_count, v->row0, stream, &row0, &row0_scalar, tmp);
+    if (s != BGTQ_OK) return s;
+    cudaError_t e = launch_copy_rows(v->data, (uint64_t)v->cap_alloc * v->D, v->D, v->dtype == BGTQ_F32, dsrc, drow, dseq,
+                                     dtype == BGTQ_F32, row0, row0_scalar, count, seq_first, seq_count, v->d_lengths,
+                                     v->dim, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "V append launch");
+    if (host) {
+        e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return cuda_fail(e, "V append");
+    }
+    for (uint32_t i = 0; i < seq_count; ++i) v->lengths[seq_first + i] += count;
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_values_length(const bgtq_values *v, uint32_t seq, uint32_t *out) {
+    if (!v || !out || seq >= v->sequences) return fail(BGTQ_EINVAL, "invalid argument");
+    *out = v->lengths[seq];
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_attention_create(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, uint32_t rows,
+                                  bgtq_attention **out) {
+    if (!out || !keys || !values || heads < 1 || heads > (uint32_t)kMaxHeads)
+        return fail(BGTQ_EINVAL, "Incompatible attention storage");
+    if (rows < 1 || rows > (uint32_t)kMaxRows) return fail(BGTQ_EINVAL, "Incompatible attention storage");
+    for (uint32_t h = 0; h < heads; ++h) {
+        const bgtq_keys *k = keys[h];
+        const bgtq_values *v = values[h];
+        if (!k || !v || k->device != v->device || k->dim != v->dim || k->capacity != v->capacity ||
+            k->sequences != v->sequences || k->device != keys[0]->device || k->dim != keys[0]->dim ||
+            k->capacity != keys[0]->capacity || k->sequences != keys[0]->sequences || k->kind != keys[0]->kind ||
+            v->dtype != values[0]->dtype)
+            return fail(BGTQ_EINVAL, "Incompatible attention storage");
+    }
+    auto *a = new bgtq_attention();
+    a->heads = heads;
+    a->rows = rows;
+    a->dim = keys[0]->dim;
+    a->sequences = keys[0]->sequences;
+    a->device = keys[0]->device;
+    a->keys.assign(keys, keys + heads);
+    a->values.assign(values, values + heads);
+    DeviceGuard g(a->device);
+    const size_t pairs = (size_t)a->sequences * heads;
+    const size_t part_bytes = 64ull * pairs * rows * (a->dim + 2) * sizeof(float);
+    if (cudaMalloc(&a->part, part_bytes) != cudaSuccess || cudaMalloc(&a->counters, pairs * sizeof(uint32_t)) != cudaSuccess ||
+        cudaMalloc(&a->lse, pairs * rows * sizeof(float)) != cudaSuccess) {
+        if (a->part) cudaFree(a->part);
+        if (a->counters) cudaFree(a->counters);
+        delete a;
+        return fail(BGTQ_ENOMEM, "attention workspace allocation failed");
+    }
+    cudaMemset(a->counters, 0, pairs * sizeof(uint32_t));
+    if (!device_status_word(a->device)) {
+        bgtq_attention_destroy(a);
+        return fail(BGTQ_ENOMEM, "status word allocation failed");
+    }
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        bgtq_attention_destroy(a);
+        return cuda_fail(e, "attention init");
+    }
+    *out = a;
+    return BGTQ_OK;
+}
+
+void bgtq_attention_destroy(bgtq_attention *a) {
+    if (!a) return;
+    DeviceGuard g(a->device);
+    if (a->part) cudaFree(a->part);
+    if (a->counters) cudaFree(a->counters);
+    if (a->lse) cudaFree(a->lse);
+    a->q_dev.release();
+    a->pos_dev.release();
+    a->out_dev.release();
+    a->logits_dev.release();
+    a->probs_dev.release();
+    delete a;
+}
+
+bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *positions, int causal, uint32_t rows,
+                        uint32_t seq_first, uint32_t seq_count, float *out, float *logits, float *probs, int host,
+                        void *stream_) {
+    if (!at || !q || !out) return fail(BGTQ_EINVAL, "Invalid Q/K/V shape or positions");
+    if (rows < 1 || rows > at->rows || !seq_count || (uint64_t)seq_first + seq_count > at->sequences)
+        return fail(BGTQ_EINVAL, "Invalid Q/K/V shape or positions");
+    if (probs && !logits) return fail(BGTQ_EINVAL, "probabilities need logits");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    const uint32_t d = at->dim, H = at->heads;
+    // optimized.ts:29-31: ready storage, equal K/V lengths, positions inside the context
+    uint32_t max_len = 0, min_len = ~0u;
+    for (uint32_t s = 0; s < seq_count; ++s) {
+        const uint32_t seq = seq_first + s, L = at->keys[0]->lengths[seq];
+        for (uint32_t h = 0; h < H; ++h)
+            if (at->keys[h]->lengths[seq] != L || at->values[h]->lengths[seq] != L)
+                return fail(BGTQ_EBUSY, "K/V lengths must match and be nonzero");
+        if (!L) return fail(BGTQ_EBUSY, "K/V lengths must match and be nonzero");
+        max_len = std::max(max_len, L);
+        min_len = std::min(min_len, L);
+    }
+    if (logits && min_len != max_len) return fail(BGTQ_EINVAL, "logit capture needs equal lengths");
+    if (host) {
+        const size_t nq = (size_t)seq_count * H * rows * d;
+        for (size_t i = 0; i < nq; ++i)
+            if (!std::isfinite(q[i])) return fail(BGTQ_ENONFINITE, "Q: finite inputs required");
+        if (positions)
+            for (uint32_t s = 0; s < seq_count; ++s)
+                for (uint32_t r = 0; r < rows; ++r)
+                    if (positions[(size_t)s * rows + r] >= at->keys[0]->lengths[seq_first + s])
+                        return fail(BGTQ_EINVAL, "Invalid Q/K/V shape or positions");
+    }
+    DeviceGuard g(at->device);
+    if (!g.ok) return fail(BGTQ_ECUDA, "cannot select device");
+    uint32_t launches = 0;
+    const float *dq = q;
+    const uint32_t *dpos = positions;
+    float *dout = out, *dlogits = logits, *dprobs = probs;
+    const size_t nq = (size_t)seq_count * H * rows * d;
+    const size_t nl = (size_t)seq_count * H * rows * max_len;
+    if (host) {
+        CK(at->q_dev.ensure(nq * 4), "Q staging");
+        CK(at->out_dev.ensure(nq * 4), "output staging");
+        CK(cudaMemcpyAsync(at->q_dev.p, q, nq * 4, cudaMemcpyHostToDevice, stream), "Q upload");
+        dq = static_cast<const float *>(at->q_dev.p);
+        dout = static_cast<float *>(at->out_dev.p);
+        if (positions) {
+            CK(at->pos_dev.ensure((size_t)seq_count * rows * 4), "position staging");
+            CK(cudaMemcpyAsync(at->pos_dev.p, positions, (size_t)seq_count * rows * 4, cudaMemcpyHostToDevice, stream),
+               "position upload");
+            dpos = static_cast<const uint32_t *>(at->pos_dev.p);
+        }
+        if (logits) {
+            CK(at->logits_dev.ensure(nl * 4), "logit staging");
+            dlogits = static_cast<float *>(at->logits_dev.p);
+        }
+        if (probs) {
+            CK(at->probs_dev.ensure(nl * 4), "probability staging");
+            dprobs = static_cast<float *>(at->probs_dev.p);
+        }
+    }
+    // FP32 keys for the materialising (CompressedKeys) path: reconstruct, then dense attention
+    const bgtq_keys *k0 = at->keys[0];
+    KKind kk = k0->kind == BGTQ_KEYS_PACKED ? KKind::Packed : k0->kind == BGTQ_KEYS_FP16 ? KKind::F16 : KKind::F32;
+    AttnArgs a;
+    std::memset(&a, 0, sizeof(a));
+    uint32_t max_cent = 0;
+    for (uint32_t h = 0; h < H; ++h) {
+        bgtq_keys *k = at->keys[h];
+        const bgtq_values *v = at->values[h];
+        AttnHead &ah = a.head[h];
+        const size_t vsz = v->dtype == BGTQ_F32 ? 4 : 2;
+        ah.v = v->data;
+        ah.v_seq_stride = (uint64_t)v->cap_alloc * v->D * vsz;
+        if (kk == KKind::Packed) {
+            ah.k = k->rows;
+            ah.k_seq_stride = (uint64_t)k->cap_alloc * k->row_stride;
+            ah.row_stride = k->row_stride;
+            ah.scales = k->scales;
+            ah.s_seq_stride = (uint64_t)k->cap_alloc * k->scale_stride;
+            ah.scale_stride = k->scale_stride;
+            ah.rot = k->dt.rot;
+            ah.cent = k->dt.cent;
+            ah.perm = k->dt.perm;
+            ah.group_of = k->dt.group_of;
+            ah.ns = k->L.ns;
+            ah.ng = k->L.ng;
+            ah.n_cent = (uint32_t)k->L.cent_compact.size();
+            for (int i = 0; i < 4; ++i) ah.bound_mask[i] = k->L.bound_mask[i];
+            for (int gi = 0; gi <= kMaxGroups; ++gi) ah.group_off[gi] = k->L.group_off[gi];
+            for (uint32_t j = 0; j < (uint32_t)kMaxDim; ++j)
+                ah.cb_base[j] = j < k->dim ? k->L.cb_base[j] : (uint16_t)ah.n_cent;
+            max_cent = std::max(max_cent, ah.n_cent);
+        } else if (kk == KKind::F16) {
+            ah.k = k->rows;
+            ah.k_seq_stride = (uint64_t)k->cap_alloc * k->row_stride;
+            ah.row_stride = k->row_stride;
+            ah.scale_stride = 4;
+        } else {
+            // materialise every requested sequence: [sequences][cap_alloc][D] FP32
+            const size_t per_seq = (size_t)k->cap_alloc * k->D * 4;
+            CK(k->materialized.ensure(per_seq * k->sequences), "materialized K allocation");
+            if (k->D != k->dim) CK(cudaMemsetAsync(k->materialized.p, 0, per_seq * k->sequences, stream), "clear");
+            for (uint32_t s = 0; s < seq_count; ++s) {
+                const uint32_t seq = seq_first + s;
+                // reconstruct writes [length][dim]; the dense kernel reads rows of D floats
+                float *dst = reinterpret_cast<float *>(static_cast<unsigned char *>(k->materialized.p) + per_seq * seq);
+                if (k->D == k->dim) {
+                    bgtq_status st = reconstruct_into(k, seq, dst, stream);
+                    if (st != BGTQ_OK) return st;
+                    ++launches;
+                } else {
+                    return fail(BGTQ_ELAYOUT, "materialised attention needs dim 16, 32, 64 or 128");
+                }
+            }
+            ah.k = static_cast<const uint8_t *>(k->materialized.p);
+            ah.k_seq_stride = per_seq;
+            ah.row_stride = k->D * 4;
+            ah.scale_stride = 4;
+        }
+    }
+    a.q = dq;
+    a.positions = dpos;
+    a.lengths = k0->d_lengths;
+    a.out = dout;
+    a.logits = dlogits;
+    a.lse = (logits || probs) ? at->lse : nullptr;
+    a.part = at->part;
+    a.counters = at->counters + 0;
+    a.status = device_status_word(at->device);
+    a.seq_first = seq_first;
+    a.seq_count = seq_count;
+    a.heads = H;
+    a.rows = rows;
+    a.causal = causal ? 1u : 0u;
+    a.logit_stride = max_len;
+    uint32_t splits = 1;
+    cudaError_t e = launch_attention(a, kk, at->values[0]->dtype == BGTQ_F32, d, max_cent, max_len, at->forced_splits,
+                                     &splits, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+    ++launches;
+    if (probs) {
+        e = launch_probs(dlogits, at->lse, dprobs, (uint64_t)seq_count * H * rows, max_len, max_len, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "probabilities launch");
+        ++launches;
+    }
+    at->last_splits = splits;
+    at->last_launches = launches;
+    if (host) {
+        CK(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, stream), "output download");
+        if (logits) CK(cudaMemcpyAsync(logits, dlogits, nl * 4, cudaMemcpyDeviceToHost, stream), "logit download");
+        if (probs) CK(cudaMemcpyAsync(probs, dprobs, nl * 4, cudaMemcpyDeviceToHost, stream), "probability download");
+        CK(cudaStreamSynchronize(stream), "attend");
+    }
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_attention_last_splits(const bgtq_attention *a, uint32_t *out) {
+    if (!a || !out) return fail(BGTQ_EINVAL, "null argument");
+    *out = a->last_splits;
+    return BGTQ_OK;
+}
+bgtq_status bgtq_attention_set_splits(bgtq_attention *a, uint32_t splits) {
+    if (!a || splits > 64) return fail(BGTQ_EINVAL, "invalid split count");
+    a->forced_splits = splits;
+    return BGTQ_OK;
+}
+bgtq_status bgtq_attention_last_launches(const bgtq_attention *a, uint32_t *out) {
+    if (!a || !out) return fail(BGTQ_EINVAL, "null argument");
+    *out = a->last_launches;
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_device_status(int device, uint32_t *out) {
+    if (!out) return fail(BGTQ_EINVAL, "null argument");
+    DeviceGuard g(device);
+    uint32_t *w = device_status_word(device);
+    if (!w) return fail(BGTQ_ECUDA, "no status word");
+    CK(cudaMemcpy(out, w, sizeof(uint32_t), cudaMemcpyDeviceToHost), "status read");
+    return BGTQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,140 @@
+// Instantiation table and host launch logic for the attention kernels.
+#include <algorithm>
+
+#include "attention_impl.cuh"
+
+namespace bgtq {
+namespace {
+
+using attn::Plan;
+
+struct Entry {
+    cudaError_t (*run)(const AttnArgs &, const Plan &, uint32_t, dim3, cudaStream_t);
+    int (*occ)(const Plan &);
+    uint32_t qp;
+};
+
+template <int D, int QM, KKind KK, bool VF32>
+Entry entry() {
+    return Entry{&attn::run<D, QM, KK, VF32>, &attn::occupancy<D, QM, KK, VF32>, (uint32_t)attn::QPad<QM>::QP};
+}
+
+template <int D, KKind KK, bool VF32>
+Entry pick_qm(uint32_t rows) {
+    if constexpr (KK == KKind::Packed) {
+        if (rows <= 1) return entry<D, 1, KK, VF32>();
+        if (rows <= 2) return entry<D, 2, KK, VF32>();
+        if (rows <= 3) return entry<D, 3, KK, VF32>();
+        if (rows <= 4) return entry<D, 4, KK, VF32>();
+        return entry<D, 8, KK, VF32>();
+    } else {
+        if (rows <= 1) return entry<D, 1, KK, VF32>();
+        if (rows <= 4) return entry<D, 4, KK, VF32>();
+        return entry<D, 8, KK, VF32>();
+    }
+}
+
+template <int D>
+Entry pick(KKind kk, int v_f32, uint32_t rows) {
+    switch (kk) {
+        case KKind::Packed: return v_f32 ? pick_qm<D, KKind::Packed, true>(rows) : pick_qm<D, KKind::Packed, false>(rows);
+        case KKind::F16: return v_f32 ? pick_qm<D, KKind::F16, true>(rows) : pick_qm<D, KKind::F16, false>(rows);
+        default: return v_f32 ? pick_qm<D, KKind::F32, true>(rows) : pick_qm<D, KKind::F32, false>(rows);
+    }
+}
+
+Entry pick_entry(KKind kk, int v_f32, uint32_t D, uint32_t rows) {
+    switch (D) {
+        case 16: return pick<16>(kk, v_f32, rows);
+        case 32: return pick<32>(kk, v_f32, rows);
+        case 64: return pick<64>(kk, v_f32, rows);
+        default: return pick<128>(kk, v_f32, rows);
+    }
+}
+
+uint32_t dim_template(uint32_t d) { return d <= 16 ? 16u : d <= 32 ? 32u : d <= 64 ? 64u : 128u; }
+
+__global__ void probs_kernel(const float *logits, const float *lse, float *probs, uint64_t rows, uint32_t tokens,
+                             uint32_t stride) {
+    const uint64_t total = rows * tokens;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = i / tokens, t = i % tokens;
+        const float lg = logits[r * stride + t];
+        probs[r * stride + t] = lg == -INFINITY ? 0.0f : expf(lg - lse[r]);
+    }
+}
+
+}  // namespace
+
+uint32_t attention_tile_tokens(uint32_t d) { return (uint32_t)(dim_template(d) <= 64 ? 64 : 32); }
+
+size_t attention_smem_bytes(KKind kk, int v_f32, uint32_t d, uint32_t rows, uint32_t row_stride,
+                            uint32_t scale_stride, uint32_t max_cent) {
+    const uint32_t D = dim_template(d);
+    const Entry e = pick_entry(kk, v_f32, D, rows);
+    return attn::make_plan(kk, v_f32, D, e.qp, attention_tile_tokens(d), row_stride, scale_stride, max_cent).total;
+}
+
+cudaError_t launch_probs(const float *logits, const float *lse, float *probs, uint64_t rows, uint32_t tokens,
+                         uint32_t stride, cudaStream_t s) {
+    const uint64_t total = rows * tokens;
+    uint64_t blocks = (total + 255) / 256;
+    if (blocks > 148u * 8u) blocks = 148u * 8u;
+    if (blocks == 0) return cudaSuccess;
+    probs_kernel<<<(unsigned)blocks, 256, 0, s>>>(logits, lse, probs, rows, tokens, stride);
+    return cudaGetLastError();
+}
+
+// Split-KV factor: minimise (waves of CTAs) x (tokens per split), i.e. the quantised
+// critical path of a grid of pairs*splits equal CTAs over `slots` resident CTAs.
+static void choose_splits(uint32_t pairs, uint32_t max_len, uint32_t chunk, uint32_t slots, uint32_t forced,
+                          uint32_t *splits, uint32_t *tps) {
+    const uint32_t max_s = std::max(1u, std::min(64u, (max_len + chunk - 1) / chunk));
+    uint32_t best_s = 1;
+    uint64_t best_cost = ~0ull;
+    if (forced) {
+        best_s = std::min(forced, max_s);
+    } else {
+        for (uint32_t sp = 1; sp <= max_s; ++sp) {
+            const uint32_t t = ((max_len + sp - 1) / sp + chunk - 1) / chunk * chunk;
+            const uint64_t waves = ((uint64_t)pairs * sp + slots - 1) / slots;
+            const uint64_t cost = waves * t + (sp > 1 ? chunk / 4 : 0);
+            if (cost < best_cost) { best_cost = cost; best_s = sp; }
+        }
+    }
+    uint32_t t = ((max_len + best_s - 1) / best_s + chunk - 1) / chunk * chunk;
+    if (t == 0) t = chunk;
+    *tps = t;
+    *splits = std::max(1u, (max_len + t - 1) / t);
+}
+
+cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t d, uint32_t max_cent,
+                             uint32_t max_len, uint32_t forced_splits, uint32_t *splits_out, cudaStream_t s) {
+    AttnArgs a = a_in;
+    const uint32_t D = dim_template(d);
+    const Entry e = pick_entry(kk, v_f32, D, a.rows);
+    uint32_t row_stride = 0, scale_stride = 4;
+    for (uint32_t h = 0; h < a.heads; ++h) {
+        row_stride = std::max(row_stride, a.head[h].row_stride);
+        scale_stride = std::max(scale_stride, a.head[h].scale_stride);
+    }
+    const uint32_t TT = attention_tile_tokens(d);
+    const Plan pl = attn::make_plan(kk, v_f32, D, e.qp, TT, row_stride, scale_stride, max_cent);
+    int dev = 0, sms = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (pl.total > (uint32_t)optin) return cudaErrorInvalidConfiguration;
+    int per_sm = e.occ(pl);
+    if (per_sm < 1) per_sm = 1;
+    uint32_t splits = 1, tps = 0;
+    choose_splits(a.seq_count * a.heads, max_len, attn::kWarps * TT, (uint32_t)(sms * per_sm), forced_splits, &splits,
+                  &tps);
+    a.splits = splits;
+    a.tokens_per_split = tps;
+    if (splits_out) *splits_out = splits;
+    dim3 grid(splits, a.heads, a.seq_count);
+    return e.run(a, pl, d, grid, s);
+}
+
+}  // namespace bgtq

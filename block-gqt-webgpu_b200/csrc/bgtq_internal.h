@@ -1,0 +1,145 @@
+// Internal declarations shared by the C ABI (abi.cpp) and the kernels (*.cu).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/bgtq.h"
+
+namespace bgtq {
+
+constexpr int kMaxDim = 128;
+constexpr int kMaxGroups = 8;
+constexpr int kMaxHeads = 8;      // KV heads bound to one attention object / one launch
+constexpr int kMaxRows = 8;       // query rows per KV head
+constexpr uint32_t kTileRows = 64; // capacity is padded to a multiple of this
+
+// Device status word bits (bgtq_device_status).
+constexpr uint32_t kStatusWaitTimeout = 1u;   // an mbarrier wait hit its iteration bound
+constexpr uint32_t kStatusBadLength = 2u;     // a kernel saw a length beyond capacity
+
+// Host copy of one validated layout (src/webgpu/layout.ts:2-31) plus what the kernels
+// derive from it once: compact per-dimension codebooks and group boundaries.
+struct Layout {
+    uint32_t d = 0, ng = 0, row_bytes = 0, norm_stride = 0, ns = 0, maxc = 0, ncb = 0;
+    uint32_t logical_rb = 0, dev_row_stride = 0, dev_scale_stride = 0;
+    std::vector<uint8_t> perm, group_of, pos_to_cb, lut;   // lut: ncb*256 codes
+    std::vector<float> rot, cent, off, inv;                // rot d*d, cent d*maxc
+    uint32_t group_off[kMaxGroups + 1] = {};               // group g = dims [off[g], off[g+1])
+    uint32_t bound_mask[4] = {};                           // bit j: a group starts at dim j (j > 0)
+    std::vector<uint16_t> cb_base;                         // compact centroid base per dim
+    std::vector<float> cent_compact;                       // per-dim codebooks, 2^w entries each
+    std::vector<uint32_t> ranges;                          // [2d] PackedKeys group ranges
+};
+
+// Parse + validate the flattened tables.  Returns BGTQ_OK or an error with message.
+bgtq_status parse_layout(const uint32_t *config, size_t n_config, const float *table, size_t n_table, Layout &out,
+                         std::string &err);
+
+// Device copy of one head's tables (one allocation, 16-byte aligned sections).
+struct DeviceTables {
+    void *blob = nullptr;
+    size_t bytes = 0;
+    const float *rot = nullptr;        // [d][d] row j = output j
+    const float *cent = nullptr;       // compact codebooks
+    const float *off = nullptr, *inv = nullptr;
+    const uint8_t *lut = nullptr;      // [ncb][256]
+    const uint8_t *perm = nullptr, *group_of = nullptr, *cbidx = nullptr;
+    const uint16_t *cb_base = nullptr;
+};
+
+// Per-head constants of the encode kernel.
+struct EncodeHead {
+    DeviceTables t;
+    uint8_t *packed;           // base of sequence 0 row 0
+    uint16_t *scales;
+    uint64_t k_seq_stride;     // bytes between sequences
+    uint64_t s_seq_stride;     // halves between sequences
+    uint32_t row_stride;       // bytes between packed rows (multiple of 16)
+    uint32_t scale_stride;     // halves between scale rows (4 or 8)
+    uint32_t ns, ng, n_cent, ncb;
+    uint32_t bound_mask[4];
+    uint32_t group_off[kMaxGroups + 1];
+    uint64_t src_head_offset;  // elements added to the source address for this head
+    uint32_t *lengths;         // device per-sequence lengths (updated by the launch)
+};
+
+struct EncodeArgs {
+    EncodeHead head[kMaxHeads];
+    const void *src;
+    uint64_t row_stride, seq_stride;  // source elements
+    const uint32_t *row0;             // device start row per sequence (nullable -> row0_scalar)
+    uint32_t row0_scalar;
+    uint32_t count, seq_first, seq_count, heads;
+    int src_f32;
+};
+
+// Per-head constants of the attention kernels.
+struct AttnHead {
+    const uint8_t *k;          // packed rows | FP16 K rows | FP32 K rows, sequence 0 row 0
+    const uint16_t *scales;
+    const void *v;
+    const float *rot;          // dense rotation (packed path)
+    const float *cent;         // compact codebooks (packed path)
+    const uint8_t *perm, *group_of;
+    uint64_t k_seq_stride;     // bytes
+    uint64_t s_seq_stride;     // halves
+    uint64_t v_seq_stride;     // bytes
+    uint32_t row_stride;       // bytes between K rows
+    uint32_t scale_stride;     // halves
+    uint32_t ns, ng, n_cent;
+    uint32_t bound_mask[4];
+    uint32_t group_off[kMaxGroups + 1];
+    uint16_t cb_base[kMaxDim];
+};
+
+struct AttnArgs {
+    AttnHead head[kMaxHeads];
+    const float *q;            // [S][H][R][D]
+    const uint32_t *positions; // [S][R] or null
+    const uint32_t *lengths;   // [sequences] key lengths (device), indexed seq_first + s
+    float *out;                // [S][H][R][D]
+    float *logits;             // optional [S][H][R][logit_stride]
+    float *lse;                // optional [S][H][R]
+    float *part;               // [splits][S][H][R][D + 2]
+    uint32_t *counters;        // [S][H], zero between launches
+    uint32_t *status;
+    uint32_t seq_first, seq_count, heads, rows, splits, tokens_per_split, causal, logit_stride;
+};
+
+struct ReconArgs {
+    DeviceTables t;
+    const uint8_t *packed;
+    const uint16_t *scales;
+    uint32_t row_stride, scale_stride, ns, d, rows;
+    float *out;
+};
+
+// Kernel launchers (return cudaError_t of the launch).
+cudaError_t launch_encode(const EncodeArgs &a, uint32_t d, uint32_t smem_cent_floats, uint32_t max_ncb,
+                          cudaStream_t s);
+cudaError_t launch_copy_rows(void *dst, uint64_t dst_seq_stride, uint32_t dst_row_elems, int dst_f32,
+                             const void *src, uint64_t src_row_stride, uint64_t src_seq_stride, int src_f32,
+                             const uint32_t *row0, uint32_t row0_scalar, uint32_t count, uint32_t seq_first,
+                             uint32_t seq_count, uint32_t *lengths, uint32_t d, cudaStream_t s);
+cudaError_t launch_reconstruct(const ReconArgs &a, uint32_t n_cent, cudaStream_t s);
+
+enum class KKind { Packed, F16, F32 };
+// Attention over a.seq_count sequences x a.heads KV heads; picks the split-KV factor
+// (forced_splits = 0: automatic) and writes it to *splits_out.
+cudaError_t launch_attention(const AttnArgs &a, KKind kk, int v_f32, uint32_t d, uint32_t max_cent,
+                             uint32_t max_len, uint32_t forced_splits, uint32_t *splits_out, cudaStream_t s);
+cudaError_t launch_probs(const float *logits, const float *lse, float *probs, uint64_t rows, uint32_t tokens,
+                         uint32_t stride, cudaStream_t s);
+// Shared-memory bytes the attention kernel needs for a launch; 0 if unsupported.
+size_t attention_smem_bytes(KKind kk, int v_f32, uint32_t d, uint32_t rows_bound, uint32_t row_stride,
+                            uint32_t scale_stride, uint32_t max_cent);
+uint32_t attention_tile_tokens(uint32_t d);
+
+uint32_t *device_status_word(int device);  // lazily allocated per device
+
+}  // namespace bgtq

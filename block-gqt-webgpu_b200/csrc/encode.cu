@@ -1,0 +1,256 @@
+// Block-GTQ K encode for sm_100a (replaces src/webgpu/mixed.wgsl:15-41 and
+// src/model/codec.wgsl:11-33; arithmetic of src/reference/production_math.py:4-24,
+// packing of src/reference/mixed_layout.py:21-27, FP16 rounding of src/webgpu/half.wgsl:2-12).
+//
+// One thread encodes one key; a persistent CTA of 128 threads walks tiles of 128 keys so
+// the rotation, codebooks and code LUT are staged in shared memory once per CTA.
+// Per key, in the canonical order the CPU oracle shares bit for bit:
+//   x_i   = FP16 key element perm[i]              (exact promotion)
+//   n_g   = sqrt(sum_{i in g} x_i^2 + 1e-30)      (sequential FMA, ascending i)
+//   xn_i  = x_i / (n_g > 1e-10 ? n_g : 1)         (IEEE division)
+//   y_j   = sum_i xn_i R[j][i]                    (sequential FMA over the group of j)
+//   bin_j = trunc(clamp((y_j - off_j) * inv_j, 0, 255)); code_j = LUT[cb_j][bin_j]
+//   s_g   = n_g / max(sqrt(sum_{j in g} cent[j][code_j]^2), 1e-10) -> FP16 (RNE)
+// This file is compiled with -fmad=false so no separate multiply/add pair is contracted;
+// every fused multiply-add above is an explicit fmaf.
+#include <cuda_fp16.h>
+
+#include "bgtq_internal.h"
+
+namespace bgtq {
+namespace {
+
+constexpr int kThreads = 128;
+
+__device__ __forceinline__ bool bit_set(const uint32_t (&m)[4], int j) { return (m[j >> 5] >> (j & 31)) & 1u; }
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant__ EncodeArgs a, uint32_t d,
+                                                          uint32_t cent_alloc, uint32_t lut_bytes, uint32_t total) {
+    const EncodeHead &h = a.head[blockIdx.y];
+    constexpr int SW = D / 2 + 1;  // staged input words per key (odd: conflict-free gathers)
+    const uint32_t row_words = h.row_stride / 4, ow = row_words + 1;
+    const uint32_t sc_words = h.scale_stride / 2, sw = sc_words + 1;
+
+    extern __shared__ __align__(16) unsigned char smem[];
+    float *rot_s = reinterpret_cast<float *>(smem);           // [D][D]
+    float *cent_s = rot_s + D * D;                            // [cent_alloc]
+    float *off_s = cent_s + cent_alloc;                       // [D]
+    float *inv_s = off_s + D;                                 // [D]
+    float *norm_s = inv_s + D;                                // [kMaxGroups][kThreads]
+    uint32_t *stage_s = reinterpret_cast<uint32_t *>(norm_s + kMaxGroups * kThreads);  // [kThreads][SW]
+    uint32_t *out_s = stage_s + kThreads * SW;                // [kThreads][ow]
+    uint32_t *sc_s = out_s + kThreads * ow;                   // [kThreads][sw]
+    uint16_t *cbbase_s = reinterpret_cast<uint16_t *>(sc_s + kThreads * sw);  // [D]
+    uint8_t *lut_s = reinterpret_cast<uint8_t *>(cbbase_s + D);               // [lut_bytes]
+    uint8_t *perm_s = lut_s + lut_bytes;                      // [D]
+    uint8_t *cbidx_s = perm_s + D;                            // [D]
+    uint8_t *glo_s = cbidx_s + D;                             // [D] group start of dim j
+    uint8_t *ghi_s = glo_s + D;                               // [D] group end (exclusive); 128 fits
+
+    const int tid = threadIdx.x;
+    // ---- stage the tables once per CTA ----
+    for (uint32_t i = tid; i < (uint32_t)(D * D); i += kThreads) {
+        const uint32_t j = i / D, c = i % D;
+        rot_s[i] = (j < d && c < d) ? h.t.rot[j * d + c] : 0.0f;
+    }
+    for (uint32_t i = tid; i < cent_alloc; i += kThreads) cent_s[i] = i < h.n_cent ? h.t.cent[i] : 0.0f;
+    for (uint32_t i = tid; i < (uint32_t)D; i += kThreads) {
+        const bool live = i < d;
+        off_s[i] = live ? h.t.off[i] : 0.0f;
+        inv_s[i] = live ? h.t.inv[i] : 0.0f;
+        perm_s[i] = live ? h.t.perm[i] : (uint8_t)i;
+        cbidx_s[i] = live ? h.t.cbidx[i] : 0;
+        cbbase_s[i] = live ? h.t.cb_base[i] : 0;
+        const uint32_t g = live ? h.t.group_of[i] : 0;
+        glo_s[i] = live ? (uint8_t)h.group_off[g] : 0;
+        ghi_s[i] = live ? (uint8_t)h.group_off[g + 1] : 0;
+    }
+    for (uint32_t i = tid; i < lut_bytes; i += kThreads) lut_s[i] = i < h.ncb * 256u ? h.t.lut[i] : 0;
+    uint32_t bm[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) bm[w] = h.bound_mask[w];
+    const uint32_t ns = h.ns, ng = h.ng, count = a.count;
+    __syncthreads();
+
+    const uint32_t n_tiles = (total + kThreads - 1) / kThreads;
+    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const uint32_t first = tile * kThreads;
+        const uint32_t nrows = min((uint32_t)kThreads, total - first);
+        // ---- stage the input rows as FP16 words (coalesced) ----
+        const uint32_t in_words = d / 2;
+        for (uint32_t w = tid; w < nrows * (uint32_t)(D / 2); w += kThreads) {
+            const uint32_t r = w / (D / 2), c = w % (D / 2);
+            uint32_t word = 0;
+            if (c < in_words) {
+                const uint32_t q = first + r, s = q / count, rr = q % count;
+                const uint64_t e = (uint64_t)s * a.seq_stride + (uint64_t)rr * a.row_stride + h.src_head_offset + 2u * c;
+                if (a.src_f32) {
+                    const float2 f = *reinterpret_cast<const float2 *>(static_cast<const float *>(a.src) + e);
+                    word = (uint32_t)__half_as_ushort(__float2half_rn(f.x)) |
+                           ((uint32_t)__half_as_ushort(__float2half_rn(f.y)) << 16);
+                } else {
+                    word = *reinterpret_cast<const uint32_t *>(static_cast<const uint16_t *>(a.src) + e);
+                }
+            }
+            stage_s[r * SW + c] = word;
+        }
+        __syncthreads();
+
+        if ((uint32_t)tid < nrows) {
+            const uint16_t *st = reinterpret_cast<const uint16_t *>(stage_s + tid * SW);
+            float x[D];
+#pragma unroll
+            for (int i = 0; i < D; ++i) x[i] = __half2float(__ushort_as_half(st[perm_s[i]]));
+            // group sums of squares, ascending dimension order
+            {
+                uint32_t g = 0;
+                float acc = 0.0f;
+#pragma unroll
+                for (int i = 0; i < D; ++i) {
+                    acc = fmaf(x[i], x[i], acc);
+                    if (i + 1 < D && bit_set(bm, i + 1)) {
+                        norm_s[g * kThreads + tid] = sqrtf(acc + 1e-30f);
+                        ++g;
+                        acc = 0.0f;
+                    }
+                }
+                norm_s[g * kThreads + tid] = sqrtf(acc + 1e-30f);
+            }
+            // normalise each group by its own norm
+            {
+                uint32_t g = 0;
+                float n = norm_s[tid];
+#pragma unroll
+                for (int i = 0; i < D; ++i) {
+                    if (i > 0 && bit_set(bm, i)) {
+                        ++g;
+                        n = norm_s[g * kThreads + tid];
+                    }
+                    x[i] = x[i] / (n > 1e-10f ? n : 1.0f);
+                }
+            }
+            uint32_t *orow = out_s + tid * ow;
+            uint16_t *srow = reinterpret_cast<uint16_t *>(sc_s + tid * sw);
+            for (uint32_t w = 0; w < ow; ++w) orow[w] = 0;
+            for (uint32_t w = 0; w < sw; ++w) sc_s[tid * sw + w] = 0;
+            uint8_t *ob = reinterpret_cast<uint8_t *>(orow);
+            uint32_t g = 0, pend = 0;
+            float n = norm_s[tid], cl = 0.0f;
+            for (uint32_t j = 0; j < d; ++j) {
+                const int lo = glo_s[j], hi = ghi_s[j];
+                const float *rj = rot_s + j * D;
+                float y = 0.0f;
+#pragma unroll
+                for (int c = 0; c < D / 8; ++c) {
+                    if (c * 8 < hi && c * 8 + 8 > lo) {
+                        const float4 r0 = *reinterpret_cast<const float4 *>(rj + c * 8);
+                        const float4 r1 = *reinterpret_cast<const float4 *>(rj + c * 8 + 4);
+                        y = fmaf(x[c * 8 + 0], r0.x, y);
+                        y = fmaf(x[c * 8 + 1], r0.y, y);
+                        y = fmaf(x[c * 8 + 2], r0.z, y);
+                        y = fmaf(x[c * 8 + 3], r0.w, y);
+                        y = fmaf(x[c * 8 + 4], r1.x, y);
+                        y = fmaf(x[c * 8 + 5], r1.y, y);
+                        y = fmaf(x[c * 8 + 6], r1.z, y);
+                        y = fmaf(x[c * 8 + 7], r1.w, y);
+                    }
+                }
+                float t = (y - off_s[j]) * inv_s[j];
+                t = fminf(fmaxf(t, 0.0f), 255.0f);
+                const uint32_t bin = (uint32_t)t;
+                const uint32_t code = lut_s[(uint32_t)cbidx_s[j] * 256u + bin];
+                const float cv = cent_s[cbbase_s[j] + code];
+                cl = fmaf(cv, cv, cl);
+                if (j < ns) {
+                    if (j & 1u) ob[j >> 1] = (uint8_t)(pend | (code << 4));
+                    else pend = code;
+                } else {
+                    ob[(ns >> 1) + (j - ns)] = (uint8_t)code;
+                }
+                const uint32_t jn = j + 1;
+                if (jn == d || ((bm[jn >> 5] >> (jn & 31)) & 1u)) {
+                    const float s = n / fmaxf(sqrtf(cl), 1e-10f);
+                    srow[g] = __half_as_ushort(__float2half_rn(s));
+                    ++g;
+                    cl = 0.0f;
+                    if (g < ng) n = norm_s[g * kThreads + tid];
+                }
+            }
+        }
+        __syncthreads();
+        // ---- write packed rows and scales (coalesced words) ----
+        for (uint32_t w = tid; w < nrows * row_words; w += kThreads) {
+            const uint32_t r = w / row_words, c = w % row_words;
+            const uint32_t q = first + r, s = q / count, rr = q % count;
+            const uint32_t dst_row = (a.row0 ? a.row0[s] : a.row0_scalar) + rr;
+            uint32_t *dst = reinterpret_cast<uint32_t *>(h.packed + (uint64_t)(a.seq_first + s) * h.k_seq_stride +
+                                                         (uint64_t)dst_row * h.row_stride);
+            dst[c] = out_s[r * ow + c];
+        }
+        for (uint32_t w = tid; w < nrows * sc_words; w += kThreads) {
+            const uint32_t r = w / sc_words, c = w % sc_words;
+            const uint32_t q = first + r, s = q / count, rr = q % count;
+            const uint32_t dst_row = (a.row0 ? a.row0[s] : a.row0_scalar) + rr;
+            uint32_t *dst = reinterpret_cast<uint32_t *>(h.scales + (uint64_t)(a.seq_first + s) * h.s_seq_stride +
+                                                         (uint64_t)dst_row * h.scale_stride);
+            dst[c] = sc_s[r * sw + c];
+        }
+        __syncthreads();
+    }
+    // ---- publish the new lengths ----
+    if (blockIdx.x == 0 && h.lengths) {
+        for (uint32_t s = tid; s < a.seq_count; s += kThreads)
+            h.lengths[a.seq_first + s] = (a.row0 ? a.row0[s] : a.row0_scalar) + count;
+    }
+}
+
+template <int D>
+size_t encode_smem(uint32_t cent_alloc, uint32_t lut_bytes, uint32_t row_stride, uint32_t scale_stride) {
+    const size_t ow = row_stride / 4 + 1, sw = scale_stride / 2 + 1;
+    size_t b = sizeof(float) * ((size_t)D * D + cent_alloc + 2 * D + kMaxGroups * kThreads);
+    b += sizeof(uint32_t) * (size_t)kThreads * ((D / 2 + 1) + ow + sw);
+    b += sizeof(uint16_t) * D + lut_bytes + 4 * D;
+    return (b + 15) & ~(size_t)15;
+}
+
+template <int D>
+cudaError_t run_encode(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uint32_t max_ncb, cudaStream_t s) {
+    uint32_t row_stride = 0, scale_stride = 0;
+    for (uint32_t h = 0; h < a.heads; ++h) {
+        row_stride = row_stride > a.head[h].row_stride ? row_stride : a.head[h].row_stride;
+        scale_stride = scale_stride > a.head[h].scale_stride ? scale_stride : a.head[h].scale_stride;
+    }
+    const uint32_t lut_bytes = (max_ncb * 256u + 15u) & ~15u;
+    const size_t smem = encode_smem<D>(cent_alloc, lut_bytes, row_stride, scale_stride);
+    int dev = 0, sms = 0, max_optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (smem > (size_t)max_optin) return cudaErrorInvalidConfiguration;
+    cudaError_t e = cudaFuncSetAttribute(encode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, encode_kernel<D>, kThreads, smem);
+    if (per_sm < 1) per_sm = 1;
+    const uint32_t total = a.count * a.seq_count;
+    const uint32_t tiles = (total + kThreads - 1) / kThreads;
+    uint32_t grid_x = (uint32_t)(sms * per_sm) / (a.heads ? a.heads : 1);
+    if (grid_x < 1) grid_x = 1;
+    if (grid_x > tiles) grid_x = tiles;
+    dim3 grid(grid_x, a.heads);
+    encode_kernel<D><<<grid, kThreads, smem, s>>>(a, d, cent_alloc, lut_bytes, total);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_encode(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uint32_t max_ncb, cudaStream_t s) {
+    if (a.count == 0 || a.seq_count == 0) return cudaSuccess;
+    if (d <= 16) return run_encode<16>(a, d, cent_alloc, max_ncb, s);
+    if (d <= 32) return run_encode<32>(a, d, cent_alloc, max_ncb, s);
+    if (d <= 64) return run_encode<64>(a, d, cent_alloc, max_ncb, s);
+    return run_encode<128>(a, d, cent_alloc, max_ncb, s);
+}
+
+}  // namespace bgtq

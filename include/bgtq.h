@@ -1,0 +1,205 @@
+/*
+ * bgtq.h - C ABI of the B200 Block-GTQ key-cache library (libbgtq.so).
+ *
+ * Two hot paths, each a hand-written sm_100a CUDA kernel:
+ *   1. K encode: permute -> per-group norm -> block-diagonal rotation -> LUT
+ *      quantisation -> nibble/byte packing + FP16 corrected scales.
+ *   2. Compressed-K GQA attention: flash-decoding over packed K rows and an FP16 or
+ *      FP32 V cache; each key is dequantised in registers against a query rotated
+ *      into the code domain, never materialised.
+ *
+ * The objects mirror the reference's TypeScript surface (reference paths are inside
+ * the amw720386/block-gqt-webgpu repository):
+ *   bgtq_tables      <- BlockGTQParameters + tables()/validateLayout()  src/webgpu/layout.ts:2-31
+ *   bgtq_keys        <- PackedKeys      src/runtime/packed-keys.ts:7-52
+ *                       FP16Keys        src/runtime/keys.ts:16-27
+ *                       CompressedKeys  src/runtime/compressed-keys.ts:5-59
+ *   bgtq_values      <- Values          src/runtime/values.ts:3-16 (FP32) and the
+ *                       model's FP16 V cache  src/model/decoder.ts:20-21, append.wgsl:6-10
+ *   bgtq_attention   <- OptimizedAttention  src/attention/optimized.ts:5-45 and
+ *                       AttentionSession    src/attention/attention.ts:19-70
+ * A WebGPU buffer per object becomes device memory owned by the object; the
+ * reference's single sequence per store generalises to `sequences` independent
+ * sequences so that one object covers one (layer, KV head) of a whole batch.
+ *
+ * Conventions
+ *   - Every function returns a bgtq_status.  Status codes map onto the reference's
+ *     synchronous errors: RangeError -> BGTQ_EINVAL / BGTQ_ECAPACITY / BGTQ_ENONFINITE /
+ *     BGTQ_ELAYOUT, Error -> BGTQ_EBUSY / BGTQ_ELAYOUT.  Validation happens before any
+ *     state changes, so a rejected call leaves the object untouched
+ *     (tests/webgpu/runtime-contracts.ts:24-25).  bgtq_last_error() gives the message.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).  Work
+ *     is stream-ordered; objects are not thread-safe.
+ *   - Pointers flagged `host` are ordinary (ideally pinned) host memory; otherwise they
+ *     are device pointers on the object's device.
+ *   - No C++ exception crosses this boundary; no call allocates on the hot path.
+ */
+#ifndef BGTQ_H
+#define BGTQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t bgtq_status;
+enum {
+    BGTQ_OK = 0,
+    BGTQ_EINVAL = 1,      /* RangeError: shapes, counts, positions  (keys.ts:12, optimized.ts:30) */
+    BGTQ_ECAPACITY = 2,   /* RangeError: capacity exceeded          (keys.ts:14, values.ts:12) */
+    BGTQ_ENONFINITE = 3,  /* RangeError: non-finite input           (keys.ts:13, buffers.ts:19-21) */
+    BGTQ_EBUSY = 4,       /* Error: storage not ready / K,V mismatch (packed-keys.ts:50, optimized.ts:34) */
+    BGTQ_ELAYOUT = 5,     /* RangeError/Error: layout or tables     (layout.ts:8-23, packed-keys.ts:15-23) */
+    BGTQ_ETIMEOUT = 6,    /* a bounded device wait expired; the device status word says where */
+    BGTQ_ECUDA = 7,       /* CUDA runtime error */
+    BGTQ_ENOMEM = 8       /* device or host allocation failed */
+};
+
+typedef enum { BGTQ_F16 = 1, BGTQ_F32 = 2 } bgtq_dtype;
+typedef enum { BGTQ_KEYS_PACKED = 1, BGTQ_KEYS_FP16 = 2, BGTQ_KEYS_COMPRESSED = 3 } bgtq_keys_kind;
+
+typedef struct bgtq_tables bgtq_tables;
+typedef struct bgtq_keys bgtq_keys;
+typedef struct bgtq_values bgtq_values;
+typedef struct bgtq_attention bgtq_attention;
+
+/* Shape of a validated layout.  row_bytes / norm_stride are the reference's strides
+ * (config[2], config[3]); the device strides pad them to 16 B / 8 B for aligned loads. */
+typedef struct bgtq_layout_info {
+    uint32_t dim, groups, row_bytes, norm_stride, nibble_dims, max_centroids;
+    uint32_t logical_row_bytes;   /* nibble_dims/2 + dim - nibble_dims */
+    uint32_t device_row_stride;   /* bytes between packed rows in device memory */
+    uint32_t device_scale_stride; /* FP16 scales between rows in device memory */
+    uint32_t codebooks;           /* code LUT rows (config payload / 256) */
+} bgtq_layout_info;
+
+/* One device allocation owned by an object, with the reference's ledger roles
+ * ("persistent-k", "persistent-v", "shared", "scratch"; src/webgpu/buffers.ts:1). */
+typedef struct bgtq_allocation {
+    const char *name;
+    const char *role;
+    uint64_t bytes;
+} bgtq_allocation;
+
+/* ---- errors ------------------------------------------------------------------ */
+const char *bgtq_status_string(bgtq_status s);
+/* Message of the last failing call on this thread ("" if none). */
+const char *bgtq_last_error(void);
+/* Library version string. */
+const char *bgtq_version(void);
+
+/* ---- host-only helpers (no GPU needed) ----------------------------------------- */
+
+/* Greedy bit allocation: widths minimising sum s_i*4^-b_i with sum b_i = budget,
+ * min_bits <= b_i <= max_bits; first index wins ties; priorities in FP64 of FP32 scores.
+ * Replaces src/reference/allocator.py:4-17 (upstream vendor/blockgtq/allocator.py:20-55). */
+bgtq_status bgtq_allocate_bits(const float *scores, uint32_t n, int64_t budget, int32_t min_bits,
+                               int32_t max_bits, int64_t *widths_out);
+
+/* validateLayout() plus the PackedKeys inverse-group check, on host memory only.
+ * config/table are the flattened tables() output (src/webgpu/layout.ts:24-31).
+ * ranges_out (nullable, 2*dim entries) receives the [start,end) group bounds of each
+ * dimension exactly as PackedKeys builds them (src/runtime/packed-keys.ts:15-23). */
+bgtq_status bgtq_layout_validate(const uint32_t *config, size_t n_config, const float *table, size_t n_table,
+                                 uint32_t *ranges_out, bgtq_layout_info *info_out);
+
+/* ---- tables ------------------------------------------------------------------------ */
+
+/* Validate and upload one head's tables to `device`.  Replaces tables() + the upload of
+ * the K integer/float tables and `ranges` (packed-keys.ts:24-27). */
+bgtq_status bgtq_tables_create(const uint32_t *config, size_t n_config, const float *table, size_t n_table,
+                               int device, bgtq_tables **out);
+bgtq_status bgtq_tables_info(const bgtq_tables *t, bgtq_layout_info *info_out);
+void bgtq_tables_destroy(bgtq_tables *t);
+
+/* ---- key stores ------------------------------------------------------------------- */
+
+/* kind PACKED/COMPRESSED need tables (dim is taken from them); FP16 needs dim only.
+ * capacity <= 2^31 rows per sequence (the reference caps at the WebGPU dispatch limit,
+ * packed-keys.ts:13).  Device memory is zero-filled, as WebGPU buffers are. */
+bgtq_status bgtq_keys_create(bgtq_keys_kind kind, const bgtq_tables *tables, uint32_t dim, uint32_t capacity,
+                             uint32_t sequences, int device, bgtq_keys **out);
+void bgtq_keys_destroy(bgtq_keys *k);
+
+/* Append `count` rows to each of `seq_count` sequences starting at `seq_first`.
+ * src element (s, r, i) is at src[s*seq_stride + r*row_stride + i] (elements of dtype).
+ * F16 sources are FP16 bits (PackedKeys.append(Uint16Array), keys.ts:11-15); F32 sources
+ * are rounded to FP16 first (model path, src/model/codec.wgsl:14).  Host sources are
+ * checked for whole non-empty rows and finite values before anything is written; device
+ * sources are trusted like the reference's GPU-resident model path.  Packed/compressed
+ * stores run the encode kernel; FP16 stores copy (converting F32). */
+bgtq_status bgtq_keys_append(bgtq_keys *k, const void *src, bgtq_dtype dtype, int host, uint32_t count,
+                             uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
+                             void *stream);
+bgtq_status bgtq_keys_length(const bgtq_keys *k, uint32_t seq, uint32_t *length_out);
+bgtq_status bgtq_keys_info(const bgtq_keys *k, bgtq_keys_kind *kind, uint32_t *dim, uint32_t *capacity,
+                           uint32_t *sequences);
+
+/* Copy rows [row0, row0+count) of sequence `seq` to host memory in the reference's
+ * strides: packed rows of config rowBytes bytes, scales of config normStride FP16 bits
+ * (zero padded), as the reference's packed/norms GPU buffers hold them.  FP16 stores
+ * return FP16 K rows in `packed_out` (2*dim bytes each) and ignore scales_out.
+ * Synchronous (inspection / tests only). */
+bgtq_status bgtq_keys_read(const bgtq_keys *k, uint32_t seq, uint32_t row0, uint32_t count, uint8_t *packed_out,
+                           uint16_t *scales_out);
+
+/* CompressedKeys.prepare(): materialise FP32 K of sequence `seq` (all `length` rows) into
+ * device memory `out` [length][dim] (mixed.wgsl:decode).  Test/debug path. */
+bgtq_status bgtq_keys_reconstruct(const bgtq_keys *k, uint32_t seq, float *out, void *stream);
+
+bgtq_status bgtq_keys_allocations(const bgtq_keys *k, bgtq_allocation *out, uint32_t capacity_n, uint32_t *n_out);
+
+/* ---- value stores ----------------------------------------------------------------- */
+
+/* dtype F32 mirrors the synthetic Values (values.ts:7); F16 mirrors the model V cache. */
+bgtq_status bgtq_values_create(bgtq_dtype dtype, uint32_t dim, uint32_t capacity, uint32_t sequences, int device,
+                               bgtq_values **out);
+void bgtq_values_destroy(bgtq_values *v);
+/* Same addressing and validation as bgtq_keys_append (values.ts:9-14). */
+bgtq_status bgtq_values_append(bgtq_values *v, const void *src, bgtq_dtype dtype, int host, uint32_t count,
+                               uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
+                               void *stream);
+bgtq_status bgtq_values_length(const bgtq_values *v, uint32_t seq, uint32_t *length_out);
+
+/* ---- attention ------------------------------------------------------------------- */
+
+/* Bind `heads` KV heads (keys[h], values[h]) that share dim, capacity and sequence
+ * count; each head serves up to `rows` query rows (GQA group size x query positions;
+ * the reference's maxQueries, optimized.ts:20).  rows <= 8.  Mirrors
+ * OptimizedAttention.create (optimized.ts:20-28) / AttentionEngine.session. */
+bgtq_status bgtq_attention_create(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, uint32_t rows,
+                                  bgtq_attention **out);
+void bgtq_attention_destroy(bgtq_attention *a);
+
+/* One attention pass for sequences [seq_first, seq_first+seq_count) with `rows` query
+ * rows per head (<= the bound rows).
+ *   q        [seq_count][heads][rows][dim] FP32 (GQA: query head h*rows+r uses KV head h)
+ *   positions [seq_count][rows] u32 context positions, or NULL for "last token"
+ *   causal   mask tokens t > position (attention.wgsl:15); non-causal attends all keys
+ *   out      [seq_count][heads][rows][dim] FP32
+ *   logits   optional [seq_count][heads][rows][length] FP32 (inspect(): raw q.k/sqrt(d),
+ *            -inf where masked); needs equal lengths across the sequences
+ *   probs    optional, same shape as logits (requires logits)
+ * host=1: q/positions/out/logits/probs are host memory, copied inside the call.
+ * Errors (optimized.ts:29-35): empty or mismatched K/V lengths, rows out of range,
+ * positions >= length, non-finite host Q.  Mirrors setQueries()+attend(). */
+bgtq_status bgtq_attend(bgtq_attention *a, const float *q, const uint32_t *positions, int causal, uint32_t rows,
+                        uint32_t seq_first, uint32_t seq_count, float *out, float *logits, float *probs, int host,
+                        void *stream);
+
+/* Split-KV factor the last bgtq_attend used (diagnostics / benches). */
+bgtq_status bgtq_attention_last_splits(const bgtq_attention *a, uint32_t *splits_out);
+/* Force a split-KV factor (0 = automatic). */
+bgtq_status bgtq_attention_set_splits(bgtq_attention *a, uint32_t splits);
+/* Number of kernel launches issued by the last bgtq_attend (benches count launches). */
+bgtq_status bgtq_attention_last_launches(const bgtq_attention *a, uint32_t *launches_out);
+
+/* Device status word written by kernels (0 = fine); reading it synchronises. */
+bgtq_status bgtq_device_status(int device, uint32_t *status_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BGTQ_H */

@@ -1,0 +1,176 @@
+"""K encode on the GPU through the C ABI versus the CPU oracle (bit-exact) and the
+reference's golden vectors.
+
+Contracts follow the reference's GPU codec tests: codes and packed bytes exact, FP16
+scales within one half-ulp of the reference encoder (tests/webgpu/phase2/phase2-test.ts:
+53-59), appends split at an odd row boundary (tests/webgpu/attention-test.ts:33-39),
+rejections leave state unchanged (tests/webgpu/runtime-contracts.ts:24-25), and the
+model-path encoder fed from FP32 RoPE output equals the FP16 path
+(tests/webgpu/model-codec-test.ts:7-26).
+"""
+import numpy as np
+import pytest
+
+import oracle
+from bgtq import PackedKeys, _lib, device_status, synthetic
+from conftest import GOLDEN, load_config, load_mixed, mixed_cases, params_tables
+
+pytestmark = pytest.mark.gpu
+
+
+def encode_gpu(cfg, tab, k_bits, capacity=None, chunks=None):
+    n = k_bits.shape[0]
+    keys = PackedKeys((cfg, tab), capacity or n)
+    if chunks:
+        start = 0
+        for c in chunks:
+            keys.append(k_bits[start:start + c])
+            start += c
+    else:
+        keys.append(k_bits)
+    packed, norms = keys.read()
+    return keys, packed, norms
+
+
+@pytest.mark.parametrize("name", mixed_cases())
+def test_reference_fixtures_bit_exact(cuda, name):
+    z = load_mixed(name)
+    p, cfg, tab = params_tables(z)
+    kb = z["original"].astype(np.float16).view(np.uint16)
+    keys, packed, norms = encode_gpu(cfg, tab, kb, capacity=int(z["capacity"]), chunks=[3, 2])
+    np.testing.assert_array_equal(packed, z["packed"])
+    np.testing.assert_array_equal(oracle.unpack(packed, p.dim, p.nibble_dims), z["codes"])
+    np.testing.assert_array_equal(norms, z["norm_bits"])
+    # reserved capacity stays zero (test_mixed.py:81-90 / phase2 cache_packed)
+    full, fnorms = keys.read(0, 0, int(z["capacity"]))
+    np.testing.assert_array_equal(full, z["cache_packed"])
+    np.testing.assert_array_equal(fnorms, z["cache_norm_bits"])
+    assert device_status(0) == 0
+
+
+@pytest.mark.parametrize("name,seed", [("config1", 0), ("config4", 4)])
+def test_config_workloads_bit_exact_vs_oracle_and_reference(cuda, name, seed):
+    z = load_config(name)
+    p, cfg, tab = params_tables(z)
+    k, q, v = synthetic.decode_workload(seed, int(z["tokens"]), p.dim)
+    kb = k.view(np.uint16)
+    _, packed, norms = encode_gpu(cfg, tab, kb)
+    ref = oracle.encode(cfg, tab, kb, threads=4)
+    np.testing.assert_array_equal(packed, ref["packed"])
+    np.testing.assert_array_equal(norms, ref["scales"])
+    n = int(z["sample"])
+    np.testing.assert_array_equal(oracle.unpack(packed[:n], p.dim, p.nibble_dims), z["codes"])
+    assert np.abs(norms[:n, :p.groups].astype(int) - z["norm_bits"][:, :p.groups].astype(int)).max() <= 1
+
+
+def _edge_keys(rng, n, d):
+    k = (rng.standard_normal((n, d)) * np.exp(rng.uniform(-6, 6, (n, 1)))).astype(np.float32)
+    k[0] = 0.0                       # all-zero key: norm below 1e-10, scale rounds to 0
+    k[1] = 65504.0                   # largest finite FP16
+    k[2, ::3] = -1e-7                # subnormal FP16 inputs
+    k[3] = np.where(np.arange(d) % 2, 1.0, -1.0)
+    return np.clip(k, -65504, 65504).astype(np.float16).view(np.uint16)
+
+
+def test_calibrated_heads_random_and_edge_keys(cuda):
+    z = np.load(GOLDEN / "smollm2_heads.npz")
+    rng = np.random.default_rng(7)
+    for i in range(int(z["heads"])):
+        cfg, tab = z[f"h{i}_config"], z[f"h{i}_table"]
+        kb = _edge_keys(rng, 777, 64)
+        _, packed, norms = encode_gpu(cfg, tab, kb, chunks=[1, 128, 300, 348])
+        ref = oracle.encode(cfg, tab, kb)
+        np.testing.assert_array_equal(packed, ref["packed"])
+        np.testing.assert_array_equal(norms, ref["scales"])
+
+
+def test_append_validation_leaves_state_unchanged(cuda):
+    z = load_mixed("mixed_d64")
+    p, cfg, tab = params_tables(z)
+    kb = z["original"].astype(np.float16).view(np.uint16)
+    keys = PackedKeys((cfg, tab), 6)
+    keys.append(kb[:5])
+    before = keys.read(0, 0, 6)
+    with pytest.raises(_lib.RangeError, match="capacity"):
+        keys.append(kb[:2])
+    bad = kb[:1].copy()
+    bad[0, 5] = 0x7c00  # +inf
+    with pytest.raises(_lib.RangeError, match="Finite"):
+        keys.append(bad)
+    with pytest.raises(_lib.RangeError):
+        keys.append(np.zeros(p.dim + 1, np.uint16))
+    with pytest.raises(_lib.RangeError):
+        keys.append(np.zeros(0, np.uint16))
+    assert keys.length == 5
+    after = keys.read(0, 0, 6)
+    np.testing.assert_array_equal(before[0], after[0])
+    np.testing.assert_array_equal(before[1], after[1])
+    keys.append(kb[:1])
+    assert keys.length == 6
+
+
+def test_device_fp16_and_fp32_model_path_sources(cuda):
+    import torch
+    z = load_config("config4")
+    p, cfg, tab = params_tables(z)
+    rng = np.random.default_rng(11)
+    rows, kvh = 333, 3
+    act = synthetic.profiled(rng, rows * kvh, 64).reshape(rows, kvh, 64)
+    dev = torch.from_numpy(act).to(cuda)
+    for head in range(kvh):
+        keys = PackedKeys((cfg, tab), rows + 7)
+        keys.append(dev[:, head, :])            # FP32 strided source (codec.wgsl:14)
+        packed, norms = keys.read()
+        rp, rs = oracle.encode_f32(cfg, tab, act.reshape(-1), kvh * 64, head * 64, rows)
+        np.testing.assert_array_equal(packed, rp)
+        np.testing.assert_array_equal(norms, rs)
+        # FP16 device source gives the same bytes as the FP16 host source
+        k16 = torch.from_numpy(act[:, head, :].astype(np.float16)).to(cuda)
+        keys2 = PackedKeys((cfg, tab), rows)
+        keys2.append(k16)
+        np.testing.assert_array_equal(keys2.read()[0], packed)
+
+
+def test_multi_sequence_ragged_appends(cuda):
+    z = load_config("config4")
+    p, cfg, tab = params_tables(z)
+    rng = np.random.default_rng(5)
+    S = 4
+    keys = PackedKeys((cfg, tab), 64, sequences=S)
+    first = _edge_keys(rng, 5, 64)
+    keys.append(first, seq_first=1)                       # only sequence 1
+    batch = _edge_keys(rng, S * 3, 64).reshape(S, 3, 64)  # then 3 rows to every sequence
+    keys.append(batch, seq_first=0)
+    assert [keys.lengths(s) for s in range(S)] == [3, 8, 3, 3]
+    for s in range(S):
+        rows = batch[s] if s != 1 else np.concatenate([first, batch[1]])
+        ref = oracle.encode(cfg, tab, rows)
+        packed, norms = keys.read(s)
+        np.testing.assert_array_equal(packed, ref["packed"])
+        np.testing.assert_array_equal(norms, ref["scales"])
+
+
+def test_large_batch_sampled_bit_exact_and_deterministic(cuda):
+    """Two million keys encoded on the GPU; random rows checked against the oracle,
+    and a second encode of the same input gives identical bytes."""
+    import torch
+    z = load_config("config4")
+    p, cfg, tab = params_tables(z)
+    n = 1 << 21
+    g = torch.Generator(device=cuda).manual_seed(3)
+    sig = torch.from_numpy(synthetic.pair_sigma(32).astype(np.float32)).to(cuda)
+    blocks = torch.randn((n, 32, 2), device=cuda, generator=g) * sig[None, :, None]
+    k = torch.cat([blocks[..., 0], blocks[..., 1]], dim=-1).half()
+    a = PackedKeys((cfg, tab), n)
+    b = PackedKeys((cfg, tab), n)
+    a.append(k)
+    b.append(k)
+    pa, na = a.read()
+    pb, nb = b.read()
+    np.testing.assert_array_equal(pa, pb)
+    np.testing.assert_array_equal(na, nb)
+    rows = np.sort(np.random.default_rng(0).choice(n, 4096, replace=False))
+    kh = k[torch.from_numpy(rows).to(cuda)].cpu().numpy().view(np.uint16)
+    ref = oracle.encode(cfg, tab, kh, threads=4)
+    np.testing.assert_array_equal(pa[rows], ref["packed"])
+    np.testing.assert_array_equal(na[rows], ref["scales"])
