@@ -1,0 +1,387 @@
+"""Benchmark: batched compressed-K GQA decode on B200.
+
+Workload per GPU (weak scaling: every rank holds its own batch):
+  SmolLM2-135M attention geometry - 30 layers, 3 KV heads, 9 query heads (GQA 3),
+  head_dim 64 - batch 256 sequences x 32768 cached tokens, Block-GTQ packed K
+  (config-4 tables: allocator widths for the synthetic pair-energy profile at budget 128,
+  built by the reference's table code) + FP16 V, synthetic data drawn on the device.
+One step = one decode step of the whole batch through all 30 layers' attention: per
+layer, append the new token's K (encode kernel) and V for every sequence and KV head,
+then compressed-K GQA attention over the cache.  Metric: decoded tokens/s (whole job).
+
+  value  inputs resident in HBM, device-timed with CUDA events (max over ranks)
+  e2e    the same step through the C ABI with host buffers: Q / new K / new V copied
+         from pinned host memory and attention outputs copied back, inside the timed region
+  roofline  attention launch (query rotation + attention kernel) timed with CUDA events
+         inside the timed region, algorithmic bytes = tokens x KV heads x (row bytes +
+         2 x groups + 2 x head_dim) at logical row size, against MEASURED_PEAKS.json HBM
+  k_encode  bulk encode of the 32768-token prefix per (layer, head), Mkeys/s
+  cpu_baseline  the CPU oracle port (tests' checker) on a bounded sample, all host cores
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT / "block-gqt-webgpu_b200")]
+
+LAYERS, KV_HEADS, Q_HEADS, HEAD_DIM = 30, 3, 9, 64
+GQA = Q_HEADS // KV_HEADS
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=256, help="sequences per GPU")
+    ap.add_argument("--context", type=int, default=32768)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def tables():
+    import bgtq
+    z = np.load(ROOT / "tests" / "golden" / "config4.npz")
+    p = bgtq.BlockGTQParameters.from_arrays(z)
+    return p, *bgtq.tables(p)
+
+
+def peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        m = json.loads(f.read_text())
+        return float(m["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def bytes_per_token_head(p):
+    logical = p.nibble_dims // 2 + p.dim - p.nibble_dims
+    return logical + 2 * p.groups + 2 * p.dim
+
+
+def encode_flops_per_key(p):
+    sizes = np.bincount(np.asarray(p.group_of, np.int64))
+    return int(2 * (sizes ** 2).sum())
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.path = index, None, None
+
+    def start(self):
+        try:
+            out_dir = ROOT / "gpurun_out"
+            out_dir.mkdir(exist_ok=True)
+            self.path = out_dir / f"clocks_gpu{self.index}.csv"
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 8:
+                try:
+                    rows.append((float(parts[0]), float(parts[1]), parts[4:8]))
+                except ValueError:
+                    pass
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags) if f.lower() == "active"})
+        loaded = [r[0] for r in rows if r[0] > 0.5 * r[1]] or [r[0] for r in rows]
+        return {"sm_mhz": float(np.median(loaded)), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_baseline(p, cfg, tab, context, batch, layers, budget_s, threads):
+    """Time the CPU oracle (reconstruct + attention, plus the new-token encode) on a bounded
+    sample of (sequence, KV head) pairs at the full context; extrapolate to tokens/s of
+    the whole workload (batch sequences x layers x KV heads per decoded token)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    from bgtq import synthetic
+    rng = np.random.default_rng(123)
+    k = synthetic.profiled(rng, context, HEAD_DIM).astype(np.float16).view(np.uint16)
+    v = rng.standard_normal((context, HEAD_DIM)).astype(np.float32)
+    enc = oracle.encode(cfg, tab, k, threads=threads)
+    q = synthetic.profiled(rng, GQA, HEAD_DIM)
+    pairs, t0 = 0, time.perf_counter()
+    while True:
+        oracle.encode(cfg, tab, k[:1], threads=1)                      # the new token's key
+        kh = oracle.reconstruct(cfg, tab, enc["packed"], enc["scales"], threads=threads)
+        oracle.attention(q, kh, v, threads=threads)
+        pairs += 1
+        if time.perf_counter() - t0 > budget_s or pairs >= 64:
+            break
+    per_pair = (time.perf_counter() - t0) / pairs
+    step_s = per_pair * batch * layers * KV_HEADS
+    return {"value": batch / step_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{pairs} (sequence, KV head) pairs at context {context}: encode 1 key + reconstruct "
+                      f"{context} keys + attention for {GQA} query heads, {per_pair * 1e3:.1f} ms each; "
+                      f"extrapolated to {batch} seqs x {layers} layers x {KV_HEADS} KV heads per token"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    import bgtq  # noqa: F401  (tables only)
+    p, cfg, tab = tables()
+    threads = os.cpu_count() or 1
+    warm = cpu_baseline(p, cfg, tab, args.context, args.batch, args.layers, 0.5, threads)
+    vals = []
+    for _ in range(max(1, args.steps)):
+        vals.append(cpu_baseline(p, cfg, tab, args.context, args.batch, args.layers, 2.0, threads)["value"])
+    value = float(np.median(vals))
+    step_ms = args.batch / value * 1e3
+    cb = dict(warm, value=value)
+    print(json.dumps({"impl": "reference", "metric": "compressed-K decode attention tokens/s", "value": value,
+                      "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                      "dtype": "f32", "data": "synthetic",
+                      "config": {"workload": "config4: SmolLM2 attention geometry, 30 layers x 3 KV / 9 Q heads, "
+                                             "head_dim 64, batch 256 x context 32768, Block-GTQ K + FP16 V",
+                                 "global_batch": args.batch, "seq_len": args.context, "parallelism": "cpu"},
+                      "cpu_baseline": cb,
+                      "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+          flush=True)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import bgtq
+    from bgtq import synthetic
+    dist = None
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    p, cfg, tab = tables()
+    B, T, L, H, R, d = args.batch, args.context, args.layers, KV_HEADS, GQA, HEAD_DIM
+    steps, warmup = args.steps, args.warmup
+    e2e_steps = 0 if args.no_e2e else max(2, steps // 2)
+    capacity = T + warmup + steps + 2 * e2e_steps + 8
+    sig = torch.from_numpy(synthetic.pair_sigma(d // 2).astype(np.float32)).to(dev)
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+
+    def profiled_keys(n0, n1):
+        out = torch.empty((n0, n1, d), dtype=torch.float16, device=dev)
+        chunk = max(1, (1 << 26) // (n1 * d))
+        for i in range(0, n0, chunk):
+            blocks = torch.randn((min(chunk, n0 - i), n1, d // 2, 2), device=dev, generator=gen) * sig[None, None, :, None]
+            out[i:i + chunk] = torch.cat([blocks[..., 0], blocks[..., 1]], -1).half()
+        return out
+
+    # ---- build the caches: T tokens for B sequences in every (layer, KV head) ----
+    keys, values, atts, enc_ms = [], [], [], []
+    t_setup = time.perf_counter()
+    for layer in range(L):
+        lk, lv = [], []
+        for h in range(H):
+            k = bgtq.PackedKeys((cfg, tab), capacity, sequences=B, device=local_rank)
+            v = bgtq.Values(d, capacity, "f16", sequences=B, device=local_rank)
+            kk = profiled_keys(B, T)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            k.append(kk)
+            e1.record()
+            del kk
+            v.append(torch.randn((B, T, d), device=dev, generator=gen).half())
+            torch.cuda.synchronize()
+            enc_ms.append(e0.elapsed_time(e1))
+            lk.append(k)
+            lv.append(v)
+        keys.append(lk)
+        values.append(lv)
+        atts.append(bgtq.GroupedAttention(lk, lv, R))
+    setup_s = time.perf_counter() - t_setup
+    q = [torch.randn((B, H, R, d), device=dev, generator=gen) for _ in range(L)]
+    knew = [profiled_keys(B, H) for _ in range(L)]                 # [B, H, d] new token keys
+    vnew = [torch.randn((B, H, d), device=dev, generator=gen).half() for _ in range(L)]
+    outs = [torch.empty((B, H, R, d), device=dev) for _ in range(L)]
+    stream = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+
+    def step(record=False):
+        for layer in range(L):
+            for h in range(H):
+                keys[layer][h].append(knew[layer][:, h:h + 1, :])
+                values[layer][h].append(vnew[layer][:, h:h + 1, :])
+            if record:
+                ev[layer][0].record(stream)
+            atts[layer].attend(q[layer], out=outs[layer])
+            if record:
+                ev[layer][1].record(stream)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(warmup):
+        step()
+    barrier()
+    clocks = Clocks(local_rank)
+    clocks.start()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    attn_ms = []
+    t_start.record(stream)
+    for _ in range(steps):
+        step(record=True)
+        # per-layer attention durations are read after the region (events are async)
+        attn_ms.append(ev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+    t_end.record(stream)
+    barrier()
+    clk = clocks.stop()
+    elapsed = t_start.elapsed_time(t_end) / 1e3
+    launch_ms = [a.elapsed_time(b) for evs in attn_ms for a, b in evs]
+    launches = steps * L * (2 * H + 2)  # per layer: H encodes + H V appends + query rotation + attention
+
+    # ---- e2e through the C ABI with host buffers ----
+    e2e = None
+    if e2e_steps:
+        qh = [t.cpu().pin_memory() for t in q]
+        kh = [t.cpu().pin_memory() for t in knew]
+        vh = [t.cpu().pin_memory() for t in vnew]
+        oh = [torch.empty((B, H, R, d), pin_memory=True) for _ in range(L)]
+        qn = [t.numpy() for t in qh]
+        kn = [t.view(torch.int16).numpy().view(np.uint16) for t in kh]
+        vn = [t.view(torch.int16).numpy().view(np.uint16) for t in vh]
+        on = [t.numpy() for t in oh]
+
+        def step_host():
+            for layer in range(L):
+                for h in range(H):
+                    keys[layer][h].append(kn[layer][:, h:h + 1, :])
+                    values[layer][h].append(vn[layer][:, h:h + 1, :])
+                atts[layer].attend(qn[layer], out=on[layer])
+
+        step_host()
+        barrier()
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h0.record(stream)
+        for _ in range(e2e_steps):
+            step_host()
+        h1.record(stream)
+        barrier()
+        e2e_s = h0.elapsed_time(h1) / 1e3
+        e2e = (e2e_s, e2e_steps)
+
+    # ---- max over ranks, verification gather ----
+    stats = torch.tensor([elapsed, e2e[0] if e2e else 0.0], device=dev, dtype=torch.float64)
+    if dist:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+        sums = torch.stack([o.double().sum() for o in outs]).sum().reshape(1)
+        gathered = [torch.zeros_like(sums) for _ in range(world)]
+        dist.all_gather(gathered, sums)
+        finite = all(bool(torch.isfinite(g).all()) for g in gathered)
+    else:
+        finite = all(bool(torch.isfinite(o).all()) for o in outs)
+    elapsed_max, e2e_max = float(stats[0]), float(stats[1])
+    status = bgtq.device_status(local_rank)
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        ctx_mean = T + warmup + (steps + 1) / 2.0
+        bpt = bytes_per_token_head(p)
+        alg_bytes = B * ctx_mean * H * bpt
+        mean_launch_s = float(np.mean(launch_ms)) / 1e3
+        achieved = alg_bytes / mean_launch_s / 1e9
+        traffic = None
+        tf = ROOT / "profiles" / "attention_traffic.json"
+        if tf.exists():
+            per_token_head = json.loads(tf.read_text())["dram_bytes_per_token_head"]
+            traffic = per_token_head * B * ctx_mean * H
+        enc_keys = B * T
+        enc_ms_med = float(np.median(enc_ms))
+        enc_rate = enc_keys / (enc_ms_med / 1e3)
+        enc_bytes = 2 * d + (p.nibble_dims // 2 + d - p.nibble_dims) + 2 * p.groups
+        cpu = cpu_baseline(p, cfg, tab, T, B, L, args.cpu_seconds, os.cpu_count() or 1)
+        value = B * world * steps / elapsed_max
+        line = {
+            "metric": "compressed-K decode attention tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": elapsed_max / steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (device-drawn K with the pair-energy profile, N(0,1) V and Q)",
+            "config": {"workload": "config4: SmolLM2 attention geometry, 30 layers x 3 KV / 9 Q heads (GQA 3), "
+                                   "head_dim 64, batch 256 x context 32768 per GPU, Block-GTQ K (config-4 tables) "
+                                   "+ FP16 V; step = append new K/V + attention for every layer",
+                       "layers": L, "kv_heads": H, "q_heads": H * R, "head_dim": d, "global_batch": B * world,
+                       "seq_len": T, "parallelism": f"sequence-sharded x{world} (independent batches, no collective)",
+                       "l2": "inputs larger than L2: ~139 GB cache resident per GPU, no flush needed"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6650 GB/s", "traffic": traffic,
+                         "kernel": "query rotation + attn_kernel<64,3,packed,f16> per layer (CUDA events)",
+                         "algorithmic_bytes_per_launch": alg_bytes,
+                         "bytes_per_token_head": bpt, "mean_launch_ms": mean_launch_s * 1e3},
+            "k_encode": {"value": enc_rate / 1e6, "unit": "Mkeys/s", "keys_per_launch": enc_keys,
+                         "ms_per_launch": enc_ms_med, "hbm_frac": enc_rate * enc_bytes / 1e9 / hbm,
+                         "fp32_tflops": enc_rate * encode_flops_per_key(p) / 1e12,
+                         "bytes_per_key": enc_bytes, "flops_per_key": encode_flops_per_key(p)},
+            "cpu_baseline": cpu,
+            "gpu_launches": launches,
+            "clocks": clk,
+            "checks": {"outputs_finite": finite, "device_status": status, "setup_s": setup_s},
+        }
+        if e2e:
+            h2d = L * (q[0].numel() * 4 + knew[0].numel() * 2 + vnew[0].numel() * 2)
+            line["e2e"] = {"value": B * world * e2e[1] / e2e_max, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                           "d2h_bytes_per_step": L * outs[0].numel() * 4,
+                           "path": "bgtq C ABI (PackedKeys/Values.append + GroupedAttention.attend) on pinned host "
+                                   "NumPy buffers"}
+        print(json.dumps(line), flush=True)
+    for a in atts:
+        a.destroy()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -121,8 +121,9 @@ struct bgtq_attention {
     float *part = nullptr;
     uint32_t *counters = nullptr;
     float *lse = nullptr;
+    float *qt = nullptr;
     DevBuf q_dev, pos_dev, out_dev, logits_dev, probs_dev;
-    uint32_t forced_splits = 0, last_splits = 0, last_launches = 0;
+    uint32_t forced_splits = 0, last_splits = 0, last_launches = 0, max_splits = 64;
 };
 
 namespace {
@@ -669,11 +670,16 @@ bgtq_status bgtq_attention_create(uint32_t heads, bgtq_keys *const *keys, bgtq_v
     a->values.assign(values, values + heads);
     DeviceGuard g(a->device);
     const size_t pairs = (size_t)a->sequences * heads;
-    const size_t part_bytes = 64ull * pairs * rows * (a->dim + 2) * sizeof(float);
+    // split-KV partials: up to 64 splits, capped at 16 MiB of workspace
+    const size_t per_split = pairs * rows * (a->dim + 2) * sizeof(float);
+    a->max_splits = (uint32_t)std::max<size_t>(1, std::min<size_t>(64, (16u << 20) / per_split));
+    const size_t part_bytes = a->max_splits * per_split;
     if (cudaMalloc(&a->part, part_bytes) != cudaSuccess || cudaMalloc(&a->counters, pairs * sizeof(uint32_t)) != cudaSuccess ||
-        cudaMalloc(&a->lse, pairs * rows * sizeof(float)) != cudaSuccess) {
+        cudaMalloc(&a->lse, pairs * rows * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&a->qt, pairs * kMaxDim * kMaxRows * sizeof(float)) != cudaSuccess) {
         if (a->part) cudaFree(a->part);
         if (a->counters) cudaFree(a->counters);
+        if (a->lse) cudaFree(a->lse);
         delete a;
         return fail(BGTQ_ENOMEM, "attention workspace allocation failed");
     }
@@ -697,6 +703,7 @@ void bgtq_attention_destroy(bgtq_attention *a) {
     if (a->part) cudaFree(a->part);
     if (a->counters) cudaFree(a->counters);
     if (a->lse) cudaFree(a->lse);
+    if (a->qt) cudaFree(a->qt);
     a->q_dev.release();
     a->pos_dev.release();
     a->out_dev.release();
@@ -826,6 +833,7 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
         }
     }
     a.q = dq;
+    a.qt = at->qt;
     a.positions = dpos;
     a.lengths = k0->d_lengths;
     a.out = dout;
@@ -842,9 +850,9 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
     a.logit_stride = max_len;
     uint32_t splits = 1;
     cudaError_t e = launch_attention(a, kk, at->values[0]->dtype == BGTQ_F32, d, max_cent, max_len, at->forced_splits,
-                                     &splits, stream);
+                                     at->max_splits, &splits, stream);
     if (e != cudaSuccess) return cuda_fail(e, "attention launch");
-    ++launches;
+    launches += 2;  // query rotation + attention
     if (probs) {
         e = launch_probs(dlogits, at->lse, dprobs, (uint64_t)seq_count * H * rows, max_len, max_len, stream);
         if (e != cudaSuccess) return cuda_fail(e, "probabilities launch");

@@ -88,8 +88,8 @@ cudaError_t launch_probs(const float *logits, const float *lse, float *probs, ui
 // Split-KV factor: minimise (waves of CTAs) x (tokens per split), i.e. the quantised
 // critical path of a grid of pairs*splits equal CTAs over `slots` resident CTAs.
 static void choose_splits(uint32_t pairs, uint32_t max_len, uint32_t chunk, uint32_t slots, uint32_t forced,
-                          uint32_t *splits, uint32_t *tps) {
-    const uint32_t max_s = std::max(1u, std::min(64u, (max_len + chunk - 1) / chunk));
+                          uint32_t cap, uint32_t *splits, uint32_t *tps) {
+    const uint32_t max_s = std::max(1u, std::min(cap, (max_len + chunk - 1) / chunk));
     uint32_t best_s = 1;
     uint64_t best_cost = ~0ull;
     if (forced) {
@@ -98,7 +98,9 @@ static void choose_splits(uint32_t pairs, uint32_t max_len, uint32_t chunk, uint
         for (uint32_t sp = 1; sp <= max_s; ++sp) {
             const uint32_t t = ((max_len + sp - 1) / sp + chunk - 1) / chunk * chunk;
             const uint64_t waves = ((uint64_t)pairs * sp + slots - 1) / slots;
-            const uint64_t cost = waves * t + (sp > 1 ? chunk / 4 : 0);
+            // each CTA also pays a fixed start-up (tables, first tile latency, merge)
+            // worth about one tile round of its warps
+            const uint64_t cost = waves * (t + chunk);
             if (cost < best_cost) { best_cost = cost; best_s = sp; }
         }
     }
@@ -109,7 +111,8 @@ static void choose_splits(uint32_t pairs, uint32_t max_len, uint32_t chunk, uint
 }
 
 cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t d, uint32_t max_cent,
-                             uint32_t max_len, uint32_t forced_splits, uint32_t *splits_out, cudaStream_t s) {
+                             uint32_t max_len, uint32_t forced_splits, uint32_t max_splits, uint32_t *splits_out,
+                             cudaStream_t s) {
     AttnArgs a = a_in;
     const uint32_t D = dim_template(d);
     const Entry e = pick_entry(kk, v_f32, D, a.rows);
@@ -119,21 +122,24 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
         scale_stride = std::max(scale_stride, a.head[h].scale_stride);
     }
     const uint32_t TT = attention_tile_tokens(d);
-    const Plan pl = attn::make_plan(kk, v_f32, D, e.qp, TT, row_stride, scale_stride, max_cent);
     int dev = 0, sms = 0, optin = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    const Plan pl = attn::make_plan(kk, v_f32, D, e.qp, TT, row_stride, scale_stride, max_cent, (uint32_t)optin - 64u);
     if (pl.total > (uint32_t)optin) return cudaErrorInvalidConfiguration;
     int per_sm = e.occ(pl);
     if (per_sm < 1) per_sm = 1;
     uint32_t splits = 1, tps = 0;
-    choose_splits(a.seq_count * a.heads, max_len, attn::kWarps * TT, (uint32_t)(sms * per_sm), forced_splits, &splits,
-                  &tps);
+    choose_splits(a.seq_count * a.heads, max_len, attn::kWarps * TT, (uint32_t)(sms * per_sm), forced_splits,
+                  std::max(1u, max_splits), &splits, &tps);
     a.splits = splits;
     a.tokens_per_split = tps;
     if (splits_out) *splits_out = splits;
     dim3 grid(splits, a.heads, a.seq_count);
+    attn::qrot_kernel<<<dim3(a.heads, a.seq_count), 128, 0, s>>>(a, d, D, e.qp, kk == KKind::Packed ? 1 : 0);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
     return e.run(a, pl, d, grid, s);
 }
 

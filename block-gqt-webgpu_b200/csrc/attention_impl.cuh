@@ -48,13 +48,16 @@ struct QPad {
 struct Plan {
     uint32_t cent, qrec, stage, pbuf, bars, total;
     uint32_t kbytes, sbytes, vbytes, stage_bytes, cent_alloc;
+    uint32_t stages;  // 2: prefetch the next tile while computing; 1 when two do not fit
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
 
 inline Plan make_plan(KKind kk, int v_f32, uint32_t D, uint32_t QP, uint32_t TT, uint32_t row_stride,
-                      uint32_t scale_stride, uint32_t n_cent) {
+                      uint32_t scale_stride, uint32_t n_cent, uint32_t smem_limit = 227u * 1024u,
+                      uint32_t stages = 2) {
     Plan p{};
+    p.stages = stages;
     uint32_t off = 0;
     p.cent = off;
     p.cent_alloc = kk == KKind::Packed ? n_cent + 256u : 0u;
@@ -67,12 +70,14 @@ inline Plan make_plan(KKind kk, int v_f32, uint32_t D, uint32_t QP, uint32_t TT,
     p.stage_bytes = align16(p.kbytes) + align16(p.sbytes) + align16(p.vbytes);
     off = (off + 127u) & ~127u;
     p.stage = off;
-    off += kWarps * 2u * p.stage_bytes;
+    off += kWarps * stages * p.stage_bytes;
     p.pbuf = off;
     off = align16(off + kWarps * TT * QP * 4u);
     p.bars = off;
     off += kWarps * 2u * 8u;
     p.total = align16(off);
+    if (p.total > smem_limit && stages == 2)
+        return make_plan(kk, v_f32, D, QP, TT, row_stride, scale_stride, n_cent, smem_limit, 1);
     return p;
 }
 
@@ -141,18 +146,20 @@ __device__ __forceinline__ void load_q(const float *p, float (&q)[QP]) {
     }
 }
 
-// Dequantise + QK for the TPL tokens of this lane: packed rows in registers, codes
-// extracted at compile-time bit positions (nibble region) or after a runtime byte
-// realignment (byte region), per-group partial sums scaled once per group.
+// Dequantise + QK for the TPL tokens of this lane.  The packed rows sit in registers.
+// Pass 1 walks the nibble region two dimensions (one byte) at a time at compile-time bit
+// positions; the row is then realigned in place by ns/2 bytes so that pass 2 finds the
+// byte-region code of dimension j at byte j, again at a compile-time position.  Both
+// passes keep per-group partial sums and scale them once per group (groups are whole
+// pairs and the nibble/byte split is a group boundary, as parse_layout enforces).
 template <int D, int QM, int QP>
 __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char *kb, const uint16_t *sb,
                                           const float *cent_s, const float *qrec_s, const uint32_t (&bm)[4],
                                           int lane, float (&acc)[Geo<D>::TPL][QM]) {
     constexpr int TPL = Geo<D>::TPL, RW = Geo<D>::RW;
     const uint32_t row_stride = h.row_stride, ns = h.ns;
-    uint32_t W[TPL][RW], S[TPL][RW], sw[TPL][4];
+    uint32_t W[TPL][RW], sw[TPL][4];
     float part[TPL][QM];
-    const uint32_t sbytes = ns >> 1, aw = sbytes >> 2, c8 = (sbytes & 3u) * 8u;
 #pragma unroll
     for (int tt = 0; tt < TPL; ++tt) {
         const int tl = tt * 32 + lane;
@@ -163,20 +170,6 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
             if ((uint32_t)q4 * 16u < row_stride) v = rp[q4];
             W[tt][4 * q4 + 0] = v.x; W[tt][4 * q4 + 1] = v.y; W[tt][4 * q4 + 2] = v.z; W[tt][4 * q4 + 3] = v.w;
         }
-        // S = row shifted by ns/2 bytes towards higher addresses: byte-region code of
-        // dimension j (>= ns) then sits at byte j of S.
-        uint32_t T[RW];
-#pragma unroll
-        for (int k = 0; k < RW; ++k) T[k] = W[tt][k];
-#pragma unroll
-        for (int b = 1; b < RW; b <<= 1) {
-            if (aw & (uint32_t)b) {
-#pragma unroll
-                for (int k = RW - 1; k >= 0; --k) T[k] = k >= b ? T[k - b] : 0u;
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < RW; ++k) S[tt][k] = __funnelshift_l(k > 0 ? T[k - 1] : 0u, T[k], c8);
         if (h.scale_stride == 4) {
             const uint2 v = *reinterpret_cast<const uint2 *>(sb + (size_t)tl * 4);
             sw[tt][0] = v.x; sw[tt][1] = v.y; sw[tt][2] = 0u; sw[tt][3] = 0u;
@@ -187,30 +180,68 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
 #pragma unroll
         for (int r = 0; r < QM; ++r) { acc[tt][r] = 0.0f; part[tt][r] = 0.0f; }
     }
-#pragma unroll
-    for (int j = 0; j < D; ++j) {
-        float qv[QP];
-        load_q<QP>(qrec_s + j * QP, qv);
-        const float *cb = cent_s + h.cb_base[j];
-        const bool nib = (uint32_t)j < ns;
+    auto flush = [&]() {
 #pragma unroll
         for (int tt = 0; tt < TPL; ++tt) {
-            const uint32_t code = nib ? (W[tt][j >> 3] >> ((j & 7) * 4)) & 15u : (S[tt][j >> 2] >> ((j & 3) * 8)) & 255u;
-            const float c = cb[code];
+            const float sc = half_lo(sw[tt][0]);
 #pragma unroll
-            for (int r = 0; r < QM; ++r) part[tt][r] = fmaf(qv[r], c, part[tt][r]);
+            for (int r = 0; r < QM; ++r) { acc[tt][r] = fmaf(sc, part[tt][r], acc[tt][r]); part[tt][r] = 0.0f; }
+            sw[tt][0] = __funnelshift_r(sw[tt][0], sw[tt][1], 16);
+            sw[tt][1] = __funnelshift_r(sw[tt][1], sw[tt][2], 16);
+            sw[tt][2] = __funnelshift_r(sw[tt][2], sw[tt][3], 16);
+            sw[tt][3] >>= 16;
         }
-        if (j + 1 < D && ((bm[(j + 1) >> 5] >> ((j + 1) & 31)) & 1u)) {
+    };
+    // ---- pass 1: nibble region, dimensions (j, j+1) share byte j/2 ----
+#pragma unroll
+    for (int j = 0; j < D; j += 2) {
+        if ((uint32_t)j < ns) {
+            float q0[QP], q1[QP];
+            load_q<QP>(qrec_s + j * QP, q0);
+            load_q<QP>(qrec_s + (j + 1) * QP, q1);
+            const float *cb0 = cent_s + h.cb_base[j], *cb1 = cent_s + h.cb_base[j + 1];
 #pragma unroll
             for (int tt = 0; tt < TPL; ++tt) {
-                const float sc = half_lo(sw[tt][0]);
+                const uint32_t byte = W[tt][j >> 3] >> (((j >> 1) & 3) * 8);
+                const float c0 = cb0[byte & 15u], c1 = cb1[(byte >> 4) & 15u];
 #pragma unroll
-                for (int r = 0; r < QM; ++r) { acc[tt][r] = fmaf(sc, part[tt][r], acc[tt][r]); part[tt][r] = 0.0f; }
-                sw[tt][0] = __funnelshift_r(sw[tt][0], sw[tt][1], 16);
-                sw[tt][1] = __funnelshift_r(sw[tt][1], sw[tt][2], 16);
-                sw[tt][2] = __funnelshift_r(sw[tt][2], sw[tt][3], 16);
-                sw[tt][3] >>= 16;
+                for (int r = 0; r < QM; ++r) part[tt][r] = fmaf(q1[r], c1, fmaf(q0[r], c0, part[tt][r]));
             }
+            if (j + 2 < D && ((bm[(j + 2) >> 5] >> ((j + 2) & 31)) & 1u)) flush();
+        }
+    }
+    // ---- realign: byte-region code of dimension j (>= ns) moves to byte j ----
+    if (ns < (uint32_t)D) {
+        const uint32_t sbytes = ns >> 1, aw = sbytes >> 2, c8 = (sbytes & 3u) * 8u;
+#pragma unroll
+        for (int tt = 0; tt < TPL; ++tt) {
+#pragma unroll
+            for (int b = 1; b < RW; b <<= 1) {
+                if (aw & (uint32_t)b) {
+#pragma unroll
+                    for (int k = RW - 1; k >= 0; --k) W[tt][k] = k >= b ? W[tt][k - b] : 0u;
+                }
+            }
+#pragma unroll
+            for (int k = RW - 1; k >= 0; --k) W[tt][k] = __funnelshift_l(k > 0 ? W[tt][k - 1] : 0u, W[tt][k], c8);
+        }
+    }
+    // ---- pass 2: byte region ----
+#pragma unroll
+    for (int j = 0; j < D; j += 2) {
+        if ((uint32_t)j >= ns) {
+            float q0[QP], q1[QP];
+            load_q<QP>(qrec_s + j * QP, q0);
+            load_q<QP>(qrec_s + (j + 1) * QP, q1);
+            const float *cb0 = cent_s + h.cb_base[j], *cb1 = cent_s + h.cb_base[j + 1];
+#pragma unroll
+            for (int tt = 0; tt < TPL; ++tt) {
+                const float c0 = cb0[(W[tt][j >> 2] >> ((j & 3) * 8)) & 255u];
+                const float c1 = cb1[(W[tt][(j + 1) >> 2] >> (((j + 1) & 3) * 8)) & 255u];
+#pragma unroll
+                for (int r = 0; r < QM; ++r) part[tt][r] = fmaf(q1[r], c1, fmaf(q0[r], c0, part[tt][r]));
+            }
+            if (j + 2 < D && ((bm[(j + 2) >> 5] >> ((j + 2) & 31)) & 1u)) flush();
         }
     }
 #pragma unroll
@@ -263,21 +294,11 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
     if constexpr (KK == KKind::Packed) {
         for (uint32_t i = tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < h.n_cent ? h.cent[i] : 0.0f;
     }
-    const float *qg = a.q + ((uint64_t)s * a.heads + hd) * (uint64_t)R * d;
-    const float inv_sqrt_d = 1.0f / sqrtf((float)d);
-    for (uint32_t idx = tid; idx < (uint32_t)(D * QP); idx += kThreads) {
-        const uint32_t j = idx / QP, r = idx % QP;
-        float v = 0.0f;
-        if (r < R && r < (uint32_t)QM && j < d) {
-            if constexpr (KK == KKind::Packed) {
-                const uint32_t g = h.group_of[j], lo = h.group_off[g], hi = h.group_off[g + 1];
-                for (uint32_t i = lo; i < hi; ++i) v = fmaf(h.rot[j * d + i], qg[r * d + h.perm[i]], v);
-            } else {
-                v = qg[r * d + j];
-            }
-            v *= inv_sqrt_d;
-        }
-        qrec_s[idx] = v;
+    // query records (rotated into code order and scaled by 1/sqrt(d) by qrot_kernel)
+    {
+        const float4 *src = reinterpret_cast<const float4 *>(a.qt + ((uint64_t)s * a.heads + hd) * (uint64_t)(D * QP));
+        float4 *dst = reinterpret_cast<float4 *>(qrec_s);
+        for (uint32_t i = tid; i < (uint32_t)(D * QP / 4); i += kThreads) dst[i] = __ldg(src + i);
     }
     if (tid < kWarps * 2) mbar_init(smem_u32(smem + pl.bars) + tid * 8u, 1u);
     fence_barrier_init();
@@ -304,7 +325,8 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
     }
     const uint32_t ntok = t1 > t0 ? t1 - t0 : 0u;
     const uint32_t ntiles = (ntok + TT - 1) / TT;
-    unsigned char *stage0 = smem + pl.stage + (size_t)w * 2u * pl.stage_bytes;
+    unsigned char *stage0 = smem + pl.stage + (size_t)w * pl.stages * pl.stage_bytes;
+    const bool two = pl.stages == 2;
     const unsigned char *kbase = h.k + (uint64_t)seq * h.k_seq_stride;
     const unsigned char *sbase =
         KK == KKind::Packed ? reinterpret_cast<const unsigned char *>(h.scales + (uint64_t)seq * h.s_seq_stride) : nullptr;
@@ -332,8 +354,8 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
     if ((uint32_t)w < ntiles) issue(w, 0);
     int it = 0;
     for (uint32_t k = w; k < ntiles; k += kWarps, ++it) {
-        const int st = it & 1;
-        if (k + kWarps < ntiles) issue(k + kWarps, st ^ 1);
+        const int st = two ? (it & 1) : 0;
+        if (two && k + kWarps < ntiles) issue(k + kWarps, st ^ 1);
         if (!mbar_wait_bounded(bar0 + (uint32_t)st * 8u, (phase >> st) & 1u)) {
             ok = false;
             break;
@@ -462,6 +484,7 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
             }
         }
         __syncwarp();
+        if (!two && k + kWarps < ntiles) issue(k + kWarps, 0);
     }
     if (!ok) atomicOr(a.status, kStatusWaitTimeout);
 
@@ -541,6 +564,40 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
             }
             if (tid == 0) a.counters[s * a.heads + hd] = 0u;
         }
+    }
+}
+
+// Query records for one (sequence, KV head): qt[j][r] = sum_{i in group(j)} R[j][i] *
+// q_r[perm[i]] / sqrt(d) for packed keys (the query rotated into the code domain), or
+// q_r[j] / sqrt(d) for dense keys; zero for j >= d and r >= rows.  One CTA per
+// (head, sequence), computed once instead of once per split.
+__global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant__ AttnArgs a, uint32_t d, uint32_t D,
+                                                   uint32_t QP, int packed) {
+    __shared__ float qraw[kMaxRows * kMaxDim];
+    const uint32_t hd = blockIdx.x, s = blockIdx.y, R = a.rows;
+    const AttnHead &h = a.head[hd];
+    const float *qg = a.q + ((uint64_t)s * a.heads + hd) * (uint64_t)R * d;
+    for (uint32_t idx = threadIdx.x; idx < R * d; idx += blockDim.x) {
+        const uint32_t r = idx / d, i = idx % d;
+        qraw[idx] = packed ? qg[r * d + h.perm[i]] : qg[r * d + i];
+    }
+    __syncthreads();
+    const float inv_sqrt_d = 1.0f / sqrtf((float)d);
+    float *out = a.qt + ((uint64_t)s * a.heads + hd) * (uint64_t)(D * QP);
+    for (uint32_t idx = threadIdx.x; idx < D * QP; idx += blockDim.x) {
+        const uint32_t j = idx / QP, r = idx % QP;
+        float v = 0.0f;
+        if (r < R && j < d) {
+            if (packed) {
+                const uint32_t g = h.group_of[j], lo = h.group_off[g], hi = h.group_off[g + 1];
+                const float *rj = h.rot + (uint64_t)j * d;
+                for (uint32_t i = lo; i < hi; ++i) v = fmaf(rj[i], qraw[r * d + i], v);
+            } else {
+                v = qraw[r * d + j];
+            }
+            v *= inv_sqrt_d;
+        }
+        out[idx] = v;
     }
 }
 

@@ -99,7 +99,8 @@ struct AttnHead {
 
 struct AttnArgs {
     AttnHead head[kMaxHeads];
-    const float *q;            // [S][H][R][D]
+    const float *q;            // [S][H][R][d]
+    float *qt;                 // [S][H][D][QP] query records (written by qrot_kernel)
     const uint32_t *positions; // [S][R] or null
     const uint32_t *lengths;   // [sequences] key lengths (device), indexed seq_first + s
     float *out;                // [S][H][R][D]
@@ -132,7 +133,8 @@ enum class KKind { Packed, F16, F32 };
 // Attention over a.seq_count sequences x a.heads KV heads; picks the split-KV factor
 // (forced_splits = 0: automatic) and writes it to *splits_out.
 cudaError_t launch_attention(const AttnArgs &a, KKind kk, int v_f32, uint32_t d, uint32_t max_cent,
-                             uint32_t max_len, uint32_t forced_splits, uint32_t *splits_out, cudaStream_t s);
+                             uint32_t max_len, uint32_t forced_splits, uint32_t max_splits, uint32_t *splits_out,
+                             cudaStream_t s);
 cudaError_t launch_probs(const float *logits, const float *lse, float *probs, uint64_t rows, uint32_t tokens,
                          uint32_t stride, cudaStream_t s);
 // Shared-memory bytes the attention kernel needs for a launch; 0 if unsupported.

@@ -137,44 +137,56 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant_
             uint8_t *ob = reinterpret_cast<uint8_t *>(orow);
             uint32_t g = 0, pend = 0;
             float n = norm_s[tid], cl = 0.0f;
-            for (uint32_t j = 0; j < d; ++j) {
-                const int lo = glo_s[j], hi = ghi_s[j];
-                const float *rj = rot_s + j * D;
-                float y = 0.0f;
+            // Four outputs per pass: four independent FMA chains, each still summed in
+            // ascending i.  The pass covers the union of the four rows' group ranges; a
+            // row's entries outside its own group are exact zeros and change nothing.
+            for (uint32_t j0 = 0; j0 < d; j0 += 4) {
+                const uint32_t jl = min(j0 + 3u, d - 1u);
+                const int lo = glo_s[j0], hi = ghi_s[jl];
+                const float *rj = rot_s + j0 * D;
+                float y[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
                 for (int c = 0; c < D / 8; ++c) {
                     if (c * 8 < hi && c * 8 + 8 > lo) {
-                        const float4 r0 = *reinterpret_cast<const float4 *>(rj + c * 8);
-                        const float4 r1 = *reinterpret_cast<const float4 *>(rj + c * 8 + 4);
-                        y = fmaf(x[c * 8 + 0], r0.x, y);
-                        y = fmaf(x[c * 8 + 1], r0.y, y);
-                        y = fmaf(x[c * 8 + 2], r0.z, y);
-                        y = fmaf(x[c * 8 + 3], r0.w, y);
-                        y = fmaf(x[c * 8 + 4], r1.x, y);
-                        y = fmaf(x[c * 8 + 5], r1.y, y);
-                        y = fmaf(x[c * 8 + 6], r1.z, y);
-                        y = fmaf(x[c * 8 + 7], r1.w, y);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const float4 r0 = *reinterpret_cast<const float4 *>(rj + q * D + c * 8);
+                            const float4 r1 = *reinterpret_cast<const float4 *>(rj + q * D + c * 8 + 4);
+                            y[q] = fmaf(x[c * 8 + 0], r0.x, y[q]);
+                            y[q] = fmaf(x[c * 8 + 1], r0.y, y[q]);
+                            y[q] = fmaf(x[c * 8 + 2], r0.z, y[q]);
+                            y[q] = fmaf(x[c * 8 + 3], r0.w, y[q]);
+                            y[q] = fmaf(x[c * 8 + 4], r1.x, y[q]);
+                            y[q] = fmaf(x[c * 8 + 5], r1.y, y[q]);
+                            y[q] = fmaf(x[c * 8 + 6], r1.z, y[q]);
+                            y[q] = fmaf(x[c * 8 + 7], r1.w, y[q]);
+                        }
                     }
                 }
-                float t = (y - off_s[j]) * inv_s[j];
-                t = fminf(fmaxf(t, 0.0f), 255.0f);
-                const uint32_t bin = (uint32_t)t;
-                const uint32_t code = lut_s[(uint32_t)cbidx_s[j] * 256u + bin];
-                const float cv = cent_s[cbbase_s[j] + code];
-                cl = fmaf(cv, cv, cl);
-                if (j < ns) {
-                    if (j & 1u) ob[j >> 1] = (uint8_t)(pend | (code << 4));
-                    else pend = code;
-                } else {
-                    ob[(ns >> 1) + (j - ns)] = (uint8_t)code;
-                }
-                const uint32_t jn = j + 1;
-                if (jn == d || ((bm[jn >> 5] >> (jn & 31)) & 1u)) {
-                    const float s = n / fmaxf(sqrtf(cl), 1e-10f);
-                    srow[g] = __half_as_ushort(__float2half_rn(s));
-                    ++g;
-                    cl = 0.0f;
-                    if (g < ng) n = norm_s[g * kThreads + tid];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t j = j0 + q;
+                    if (j >= d) break;
+                    float t = (y[q] - off_s[j]) * inv_s[j];
+                    t = fminf(fmaxf(t, 0.0f), 255.0f);
+                    const uint32_t bin = (uint32_t)t;
+                    const uint32_t code = lut_s[(uint32_t)cbidx_s[j] * 256u + bin];
+                    const float cv = cent_s[cbbase_s[j] + code];
+                    cl = fmaf(cv, cv, cl);
+                    if (j < ns) {
+                        if (j & 1u) ob[j >> 1] = (uint8_t)(pend | (code << 4));
+                        else pend = code;
+                    } else {
+                        ob[(ns >> 1) + (j - ns)] = (uint8_t)code;
+                    }
+                    const uint32_t jn = j + 1;
+                    if (jn == d || ((bm[jn >> 5] >> (jn & 31)) & 1u)) {
+                        const float s = n / fmaxf(sqrtf(cl), 1e-10f);
+                        srow[g] = __half_as_ushort(__float2half_rn(s));
+                        ++g;
+                        cl = 0.0f;
+                        if (g < ng) n = norm_s[g * kThreads + tid];
+                    }
                 }
             }
         }

@@ -103,6 +103,14 @@ bgtq_status parse_layout(const uint32_t *config, size_t n_config, const float *t
         const uint32_t j = L.group_off[g];
         L.bound_mask[j >> 5] |= 1u << (j & 31);
     }
+    // kernel requirement: groups hold whole RoPE pairs and the nibble/byte split falls
+    // on a group boundary (groups are width classes, so every reference table does)
+    bool ns_on_boundary = ns == 0 || ns == d;
+    for (uint32_t g = 0; g <= ng; ++g) {
+        if (L.group_off[g] % 2) return fail(err, BGTQ_ELAYOUT, "Groups must hold whole dimension pairs");
+        ns_on_boundary |= L.group_off[g] == ns;
+    }
+    if (!ns_on_boundary) return fail(err, BGTQ_ELAYOUT, "Nibble/byte split must fall on a group boundary");
     // compact per-dimension codebooks (entries 0..max reachable code)
     L.cb_base.resize(d);
     uint32_t total = 0;
