@@ -7,7 +7,7 @@
 #include <string>
 #include <vector>
 
-#include "bgtq_internal.h"
+#include "objects.h"
 
 using namespace bgtq;
 
@@ -45,29 +45,20 @@ struct DeviceGuard {
 uint32_t dim_template(uint32_t d) { return d <= 16 ? 16u : d <= 32 ? 32u : d <= 64 ? 64u : 128u; }
 uint32_t round_up(uint32_t x, uint32_t m) { return (x + m - 1) / m * m; }
 
-struct DevBuf {
-    void *p = nullptr;
-    size_t bytes = 0;
-    void release() {
-        if (p) cudaFree(p);
-        p = nullptr;
-        bytes = 0;
-    }
-    cudaError_t ensure(size_t n) {
-        if (n <= bytes) return cudaSuccess;
-        release();
-        cudaError_t e = cudaMalloc(&p, n);
-        if (e == cudaSuccess) bytes = n;
-        return e;
-    }
-};
-
 std::mutex g_status_mu;
 uint32_t *g_status[64] = {};
 
 }  // namespace
 
 namespace bgtq {
+void set_last_error(const std::string &message) { g_err = message; }
+
+uint32_t *device_status_word_if_present(int device) {
+    if (device < 0 || device >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(g_status_mu);
+    return g_status[device];
+}
+
 uint32_t *device_status_word(int device) {
     if (device < 0 || device >= 64) return nullptr;
     std::lock_guard<std::mutex> lock(g_status_mu);
@@ -80,51 +71,6 @@ uint32_t *device_status_word(int device) {
     return g_status[device];
 }
 }  // namespace bgtq
-
-struct bgtq_tables {
-    int device = 0;
-    Layout L;
-    DeviceTables dt;
-};
-
-struct bgtq_keys {
-    bgtq_keys_kind kind;
-    int device = 0;
-    Layout L;          // packed/compressed only
-    DeviceTables dt;
-    uint32_t dim = 0, D = 0, capacity = 0, cap_alloc = 0, sequences = 0;
-    uint32_t row_stride = 0;    // bytes between device rows
-    uint32_t scale_stride = 0;  // halves between device scale rows
-    uint8_t *rows = nullptr;
-    uint16_t *scales = nullptr;
-    uint32_t *d_lengths = nullptr;
-    std::vector<uint32_t> lengths;
-    DevBuf row0, staging, materialized;
-    std::vector<bgtq_allocation> ledger;
-};
-
-struct bgtq_values {
-    bgtq_dtype dtype;
-    int device = 0;
-    uint32_t dim = 0, D = 0, capacity = 0, cap_alloc = 0, sequences = 0;
-    void *data = nullptr;
-    uint32_t *d_lengths = nullptr;
-    std::vector<uint32_t> lengths;
-    DevBuf row0, staging;
-};
-
-struct bgtq_attention {
-    uint32_t heads = 0, rows = 0, dim = 0, sequences = 0;
-    int device = 0;
-    std::vector<bgtq_keys *> keys;
-    std::vector<bgtq_values *> values;
-    float *part = nullptr;
-    uint32_t *counters = nullptr;
-    float *lse = nullptr;
-    float *qt = nullptr;
-    DevBuf q_dev, pos_dev, out_dev, logits_dev, probs_dev;
-    uint32_t forced_splits = 0, last_splits = 0, last_launches = 0, max_splits = 64;
-};
 
 namespace {
 

@@ -143,5 +143,7 @@ size_t attention_smem_bytes(KKind kk, int v_f32, uint32_t d, uint32_t rows_bound
 uint32_t attention_tile_tokens(uint32_t d);
 
 uint32_t *device_status_word(int device);  // lazily allocated per device
+uint32_t *device_status_word_if_present(int device);  // never allocates; null if absent
+void set_last_error(const std::string &message);     // message of bgtq_last_error()
 
 }  // namespace bgtq

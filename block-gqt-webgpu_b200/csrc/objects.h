@@ -1,0 +1,73 @@
+// Definitions of the opaque C ABI objects, shared by the ABI translation units.
+#pragma once
+
+#include <vector>
+
+#include "bgtq_internal.h"
+
+namespace bgtq {
+
+// Device buffer that grows on demand (staging and workspace of the ABI objects).
+struct DevBuf {
+    void *p = nullptr;
+    size_t bytes = 0;
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    cudaError_t ensure(size_t n) {
+        if (n <= bytes) return cudaSuccess;
+        release();
+        cudaError_t e = cudaMalloc(&p, n);
+        if (e == cudaSuccess) bytes = n;
+        return e;
+    }
+};
+
+}  // namespace bgtq
+
+struct bgtq_tables {
+    int device = 0;
+    bgtq::Layout L;
+    bgtq::DeviceTables dt;
+};
+
+struct bgtq_keys {
+    bgtq_keys_kind kind;
+    int device = 0;
+    bgtq::Layout L;          // packed/compressed only
+    bgtq::DeviceTables dt;
+    uint32_t dim = 0, D = 0, capacity = 0, cap_alloc = 0, sequences = 0;
+    uint32_t row_stride = 0;    // bytes between device rows
+    uint32_t scale_stride = 0;  // halves between device scale rows
+    uint8_t *rows = nullptr;
+    uint16_t *scales = nullptr;
+    uint32_t *d_lengths = nullptr;
+    std::vector<uint32_t> lengths;
+    bgtq::DevBuf row0, staging, materialized;
+    std::vector<bgtq_allocation> ledger;
+};
+
+struct bgtq_values {
+    bgtq_dtype dtype;
+    int device = 0;
+    uint32_t dim = 0, D = 0, capacity = 0, cap_alloc = 0, sequences = 0;
+    void *data = nullptr;
+    uint32_t *d_lengths = nullptr;
+    std::vector<uint32_t> lengths;
+    bgtq::DevBuf row0, staging;
+};
+
+struct bgtq_attention {
+    uint32_t heads = 0, rows = 0, dim = 0, sequences = 0;
+    int device = 0;
+    std::vector<bgtq_keys *> keys;
+    std::vector<bgtq_values *> values;
+    float *part = nullptr;
+    uint32_t *counters = nullptr;
+    float *lse = nullptr;
+    float *qt = nullptr;
+    bgtq::DevBuf q_dev, pos_dev, out_dev, logits_dev, probs_dev;
+    uint32_t forced_splits = 0, last_splits = 0, last_launches = 0, max_splits = 64;
+};

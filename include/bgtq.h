@@ -196,6 +196,25 @@ bgtq_status bgtq_attention_set_splits(bgtq_attention *a, uint32_t splits);
 /* Number of kernel launches issued by the last bgtq_attend (benches count launches). */
 bgtq_status bgtq_attention_last_launches(const bgtq_attention *a, uint32_t *launches_out);
 
+/* Attention without any device allocation (no counterpart in the reference, which has
+ * no such constraint).  For callers that must not allocate device memory when they run
+ * attention: a server whose memory pool has taken all free device memory once the
+ * caches exist, a plugin inside a framework that owns every device allocation, or work
+ * recorded while a stream is being captured, where cudaMalloc is not allowed.  It needs
+ * no bgtq_attention object: `heads` packed key stores and their value stores (same
+ * rules as bgtq_attention_create) are attended directly, with device pointers only
+ * (q/positions/out as in bgtq_attend; no logit capture).  Scratch comes from one fixed
+ * 4 MiB array inside the library on every GPU that loads it, kept until the process
+ * exits: at most 262,144 floats of query records (sequences x heads x padded dim x padded
+ * rows; padded dim is 16/32/64/128, padded rows 1/2/4/8) - larger requests fail with
+ * BGTQ_EINVAL - and the split-KV factor is limited to what 3 MiB of partials hold.  All
+ * calls share that array: calls whose kernels may overlap on the GPU race, so serialise
+ * them (one stream per device).  The first call on a device looks up the array's address
+ * (cudaGetSymbolAddress) and should be made before any stream capture starts. */
+bgtq_status bgtq_attend_static(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, const float *q,
+                               const uint32_t *positions, int causal, uint32_t rows, uint32_t seq_first,
+                               uint32_t seq_count, float *out, void *stream);
+
 /* Device status word written by kernels (0 = fine); reading it synchronises. */
 bgtq_status bgtq_device_status(int device, uint32_t *status_out);
 
