@@ -414,7 +414,7 @@ bgtq_status bgtq_keys_append(bgtq_keys *k, const void *src, bgtq_dtype dtype, in
         e = launch_encode(a, k->dim, (uint32_t)k->L.cent_compact.size() + 256u, k->L.ncb, stream);
     } else {
         e = launch_copy_rows(k->rows, (uint64_t)k->cap_alloc * k->D, k->D, 0, dsrc, drow, dseq, dtype == BGTQ_F32, row0,
-                             row0_scalar, count, seq_first, seq_count, k->d_lengths, k->dim, stream);
+                             row0_scalar, count, seq_first, seq_count, k->d_lengths, k->dim, 0, stream);
     }
     if (e != cudaSuccess) return cuda_fail(e, "K append launch");
     if (host) {
@@ -576,7 +576,7 @@ bgtq_status bgtq_values_append(bgtq_values *v, const void *src, bgtq_dtype dtype
     if (s != BGTQ_OK) return s;
     cudaError_t e = launch_copy_rows(v->data, (uint64_t)v->cap_alloc * v->D, v->D, v->dtype == BGTQ_F32, dsrc, drow, dseq,
                                      dtype == BGTQ_F32, row0, row0_scalar, count, seq_first, seq_count, v->d_lengths,
-                                     v->dim, stream);
+                                     v->dim, values_swizzled(v->dtype == BGTQ_F32, v->D) ? 1 : 0, stream);
     if (e != cudaSuccess) return cuda_fail(e, "V append launch");
     if (host) {
         e = cudaStreamSynchronize(stream);

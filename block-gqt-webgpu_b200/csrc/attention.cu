@@ -11,12 +11,13 @@ using attn::Plan;
 struct Entry {
     cudaError_t (*run)(const AttnArgs &, const Plan &, uint32_t, dim3, cudaStream_t);
     int (*occ)(const Plan &);
-    uint32_t qp;
+    uint32_t qp, qm;
 };
 
 template <int D, int QM, KKind KK, bool VF32>
 Entry entry() {
-    return Entry{&attn::run<D, QM, KK, VF32>, &attn::occupancy<D, QM, KK, VF32>, (uint32_t)attn::QPad<QM>::QP};
+    return Entry{&attn::run<D, QM, KK, VF32>, &attn::occupancy<D, QM, KK, VF32>, (uint32_t)attn::QPad<QM>::QP,
+                 (uint32_t)QM};
 }
 
 template <int D, KKind KK, bool VF32>
@@ -72,7 +73,8 @@ size_t attention_smem_bytes(KKind kk, int v_f32, uint32_t d, uint32_t rows, uint
                             uint32_t scale_stride, uint32_t max_cent) {
     const uint32_t D = dim_template(d);
     const Entry e = pick_entry(kk, v_f32, D, rows);
-    return attn::make_plan(kk, v_f32, D, e.qp, attention_tile_tokens(d), row_stride, scale_stride, max_cent).total;
+    return attn::make_plan(kk, v_f32, D, e.qp, attention_tile_tokens(d), row_stride, scale_stride, max_cent,
+                           227u * 1024u, 2, e.qm).total;
 }
 
 cudaError_t launch_probs(const float *logits, const float *lse, float *probs, uint64_t rows, uint32_t tokens,
@@ -126,7 +128,8 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    const Plan pl = attn::make_plan(kk, v_f32, D, e.qp, TT, row_stride, scale_stride, max_cent, (uint32_t)optin - 64u);
+    const Plan pl =
+        attn::make_plan(kk, v_f32, D, e.qp, TT, row_stride, scale_stride, max_cent, (uint32_t)optin - 64u, 2, e.qm);
     if (pl.total > (uint32_t)optin) return cudaErrorInvalidConfiguration;
     int per_sm = e.occ(pl);
     if (per_sm < 1) per_sm = 1;

@@ -4,22 +4,37 @@
 // (src/attention/fused-dot.wgsl:15-37), parallel softmax and weighted sum
 // (src/attention/parallel-tail.wgsl:10-33), the model's compressed_dot / softmax /
 // weighted kernels (src/model/compressed-dot.wgsl:14-31, src/model/attention.wgsl:13-39)
-// and the baseline FP16/FP32-K passes (src/attention/attention.wgsl:17-43) - with one
-// kernel per (split, KV head, sequence) plus a last-CTA split combine.  Semantics follow
-// src/reference/attention.py:5-22: logits = q.k/sqrt(d), positions t > pos masked when
-// causal, softmax, P.V, all accumulated in FP32.
+// and the baseline FP16/FP32-K passes (src/attention/attention.wgsl:17-43) - with a query
+// rotation kernel plus one attention kernel per (split, KV head, sequence) with a last-CTA
+// split combine.  Semantics follow src/reference/attention.py:5-22: logits = q.k/sqrt(d),
+// positions t > pos masked when causal, softmax, P.V, FP32 accumulation.
 //
 // Packed keys are never reconstructed.  The query is rotated once into the code domain,
 //   qt_i = sum_{j in group(i)} R[i][j] q[perm[j]] / sqrt(d),
 // so that q.k = sum_g s_g sum_{i in g} qt_i cent[i][code_i] (k = reconstruct(codes) of
 // src/reference/production_math.py:27-31, R block-diagonal as PackedKeys enforces).
 //
-// Data movement: each warp owns a two-stage ring of shared-memory tiles (packed rows,
-// FP16 scales, V rows) filled by cp.async.bulk (TMA bulk copies, no multicast) that
-// complete on an mbarrier; every mbarrier wait is bounded and reports a timeout through
-// the device status word instead of spinning forever.
-// Compute layout: lane = token for dequantisation + QK (codes in registers, codebooks in
-// shared memory, query records broadcast), lane = 16-byte slice of V for P.V.
+// Data movement: each warp owns a ring of shared-memory tiles (packed rows, FP16 scales,
+// V rows) filled by cp.async.bulk (TMA bulk copies, no multicast) that complete on an
+// mbarrier; every mbarrier wait is bounded and reports a timeout through the device status
+// word instead of spinning forever.  Tiles are always copied whole: capacity is padded to
+// 64 rows and zero-filled, and tokens past the end of a split get probability 0.
+//
+// Compute:
+//   dequant + QK   lane = token.  Packed rows sit in shared memory at an odd word stride,
+//                  so the 32 lanes reading word w of their rows hit 32 banks.  The nibble
+//                  region is walked in runs of 4 dimension pairs (one 32-bit code word),
+//                  the byte region in runs of 4 pairs (two words), group by group, with the
+//                  group's FP16 scale applied once at its end; per-pair query records and
+//                  codebook offsets come from small shared tables built per (sequence,
+//                  head).
+//   softmax        online, warp-wide max/sum per tile.
+//   P.V            tensor cores (mma.sync m16n8k16, FP16 in, FP32 accumulate) for FP16 V of
+//                  64/128 dims: P is scaled by 2^12 and split into high and low FP16 parts
+//                  (about 22 significant bits) that occupy fragment rows 0-7 and 8-15 of
+//                  one MMA; V tiles arrive chunk-swizzled from the value
+//                  store so ldmatrix reads them without bank conflicts.  FP32 V and small
+//                  head dims use FP32 FMAs with lane = 16-byte slice of V.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -33,16 +48,32 @@ constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr float kPScale = 4096.0f, kPUnscale = 1.0f / 4096.0f;
 
 template <int D>
 struct Geo {
     static constexpr int TPL = D <= 64 ? 2 : 1;  // tokens per lane in the lane=token phase
     static constexpr int TT = 32 * TPL;          // tokens per warp tile
-    static constexpr int RW = D / 4;             // max 32-bit words of a packed row
 };
 template <int QM>
 struct QPad {
     static constexpr int QP = QM <= 1 ? 1 : QM <= 2 ? 2 : QM <= 4 ? 4 : 8;
+};
+// Shared tables of the packed path: one record per dimension pair, laid out group by group,
+// each group padded with zero records to a whole number of 4-pair blocks.  A record holds,
+// for each query row r, the pair's rotated query values (q_2b,r, q_2b+1,r) as a float2, then
+// the absolute shared-memory byte offsets of the two dimensions' codebooks; RP words,
+// padded to 16 bytes.
+template <int D, int QM>
+struct RecGeo {
+    static constexpr int RP = (2 * QM + 2 + 3) & ~3;         // words per pair record
+    static constexpr int NP = D / 2 + 3 * kMaxGroups;        // pair records incl. padding
+    static constexpr int BYTES = (NP * RP * 4 + 15) & ~15;
+};
+
+template <int D, bool VF32>
+struct UseMma {
+    static constexpr bool value = !VF32 && (D == 64 || D == 128);
 };
 
 struct Plan {
@@ -55,19 +86,21 @@ __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15
 
 inline Plan make_plan(KKind kk, int v_f32, uint32_t D, uint32_t QP, uint32_t TT, uint32_t row_stride,
                       uint32_t scale_stride, uint32_t n_cent, uint32_t smem_limit = 227u * 1024u,
-                      uint32_t stages = 2) {
+                      uint32_t stages = 2, uint32_t QM = 0) {
     Plan p{};
     p.stages = stages;
     uint32_t off = 0;
     p.cent = off;
     p.cent_alloc = kk == KKind::Packed ? n_cent + 256u : 0u;
     off = align16(off + 4u * p.cent_alloc);
-    p.qrec = off;
-    off = align16(off + 4u * D * QP);
+    p.qrec = off;  // dense: [D][QP] query records; packed: RecGeo tables
+    const uint32_t rp = (2u * (QM ? QM : QP) + 2u + 3u) & ~3u;
+    const uint32_t rec_bytes = kk == KKind::Packed ? align16((D / 2u + 3u * kMaxGroups) * rp * 4u) : 4u * D * QP;
+    off = align16(off + rec_bytes);
     p.kbytes = TT * row_stride;
     p.sbytes = kk == KKind::Packed ? TT * scale_stride * 2u : 0u;
     p.vbytes = TT * D * (v_f32 ? 4u : 2u);
-    p.stage_bytes = align16(p.kbytes) + align16(p.sbytes) + align16(p.vbytes);
+    p.stage_bytes = align16(p.kbytes) + 16u + align16(p.sbytes) + align16(p.vbytes);
     off = (off + 127u) & ~127u;
     p.stage = off;
     off += kWarps * stages * p.stage_bytes;
@@ -77,11 +110,11 @@ inline Plan make_plan(KKind kk, int v_f32, uint32_t D, uint32_t QP, uint32_t TT,
     off += kWarps * 2u * 8u;
     p.total = align16(off);
     if (p.total > smem_limit && stages == 2)
-        return make_plan(kk, v_f32, D, QP, TT, row_stride, scale_stride, n_cent, smem_limit, 1);
+        return make_plan(kk, v_f32, D, QP, TT, row_stride, scale_stride, n_cent, smem_limit, 1, QM);
     return p;
 }
 
-// ---- PTX helpers: mbarrier + bulk async copies (sm_90+, no multicast) ----
+// ---- PTX helpers: mbarrier + bulk async copies (sm_90+, no multicast), tensor cores ----
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -117,6 +150,29 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
+// Loads at 32-bit byte offsets into the kernel's dynamic shared memory (plain C++ loads,
+// so the compiler keeps them ordered after barrier waits but may schedule them freely).
+__device__ __forceinline__ uint32_t lds_u32(const unsigned char *sm, uint32_t off) {
+    return *reinterpret_cast<const uint32_t *>(sm + off);
+}
+__device__ __forceinline__ float lds_f32(const unsigned char *sm, uint32_t off) {
+    return *reinterpret_cast<const float *>(sm + off);
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+// C (16x8, f32) += A (16x16, f16) * B (16x8, f16); fragments as in the PTX ISA for
+// mma.m16n8k16 (row g = lane/4, column pair 2*(lane%4)).
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -129,6 +185,7 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 __device__ __forceinline__ float half_lo(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w & 0xffffu))); }
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 
 template <int QP>
 __device__ __forceinline__ void load_q(const float *p, float (&q)[QP]) {
@@ -146,30 +203,59 @@ __device__ __forceinline__ void load_q(const float *p, float (&q)[QP]) {
     }
 }
 
-// Dequantise + QK for the TPL tokens of this lane.  The packed rows sit in registers.
-// Pass 1 walks the nibble region two dimensions (one byte) at a time at compile-time bit
-// positions; the row is then realigned in place by ns/2 bytes so that pass 2 finds the
-// byte-region code of dimension j at byte j, again at a compile-time position.  Both
-// passes keep per-group partial sums and scale them once per group (groups are whole
-// pairs and the nibble/byte split is a group boundary, as parse_layout enforces).
+// Build the packed-path pair records for one (sequence, head) from the query records qt
+// [D][QP] and the head's codebook offsets: group g's pairs [off_g/2, off_{g+1}/2) padded
+// to 4*ceil(pairs/4) records; padding records carry zero query values (their codebook
+// offsets stay in range, so whatever code bytes they meet contribute exactly 0).
 template <int D, int QM, int QP>
-__device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char *kb, const uint16_t *sb,
-                                          const float *cent_s, const float *qrec_s, const uint32_t (&bm)[4],
-                                          int lane, float (&acc)[Geo<D>::TPL][QM]) {
-    constexpr int TPL = Geo<D>::TPL, RW = Geo<D>::RW;
-    const uint32_t row_stride = h.row_stride, ns = h.ns;
-    uint32_t W[TPL][RW], sw[TPL][4];
-    float part[TPL][QM];
+__device__ __forceinline__ void build_tables(const AttnHead &h, const float *qt, unsigned char *rec, uint32_t d,
+                                             uint32_t cent_off, int tid) {
+    using G = RecGeo<D, QM>;
+    uint32_t *recs = reinterpret_cast<uint32_t *>(rec);
+    uint32_t base = 0;
+    for (uint32_t g = 0; g < h.ng; ++g) {
+        const uint32_t p0 = h.group_off[g] / 2, p1 = h.group_off[g + 1] / 2;
+        const uint32_t n = ((p1 - p0 + 3) / 4) * 4;
+        for (uint32_t i = tid; i < n; i += kThreads) {
+            uint32_t *rp = recs + (base + i) * G::RP;
+            const uint32_t pr = p0 + i, j0 = 2 * pr;
+            const bool live = pr < p1;
+            for (int r = 0; r < QM; ++r) {
+                rp[2 * r] = __float_as_uint(live ? __ldg(qt + j0 * QP + r) : 0.0f);
+                rp[2 * r + 1] = __float_as_uint(live ? __ldg(qt + (j0 + 1) * QP + r) : 0.0f);
+            }
+            const uint32_t ja = min(j0, 127u), jb = min(j0 + 1, 127u);
+            rp[2 * QM] = cent_off + 4u * h.cb_base[ja];
+            rp[2 * QM + 1] = cent_off + 4u * h.cb_base[jb];
+            for (int x = 2 * QM + 2; x < G::RP; ++x) rp[x] = 0u;
+        }
+        base += n;
+    }
+    (void)d;
+}
+
+// Dequantise + QK for the TPL tokens of this lane (see the file comment).  Groups are
+// walked in order; inside a group, straight-line blocks of 4 dimension pairs (no branches)
+// accumulate each pair into a float2 (even, odd dims) with one packed FMA per query row,
+// and the group's FP16 scale is applied once at the group's end.  A lookup is one byte
+// extract of an index word pre-scaled by 4, one add of the record's codebook offset and one
+// shared load.  Code bytes are read as (unaligned) words: a nibble block needs 4 bytes, a
+// byte block 8.
+template <int D, int QM>
+__device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char *sm, uint32_t kb_s,
+                                          const uint16_t *sb, const unsigned char *rec, uint32_t d, int lane,
+                                          float (&acc)[Geo<D>::TPL][QM]) {
+    using G = RecGeo<D, QM>;
+    constexpr int TPL = Geo<D>::TPL, RP = G::RP;
+    const uint32_t *recs = reinterpret_cast<const uint32_t *>(rec);
+    const uint32_t krow = h.row_stride, ns = h.ns;
+    uint32_t row[TPL];
+    uint32_t sw[TPL][4];
+    float2 part[TPL][QM];
 #pragma unroll
     for (int tt = 0; tt < TPL; ++tt) {
         const int tl = tt * 32 + lane;
-        const uint4 *rp = reinterpret_cast<const uint4 *>(kb + (size_t)tl * row_stride);
-#pragma unroll
-        for (int q4 = 0; q4 < RW / 4; ++q4) {
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if ((uint32_t)q4 * 16u < row_stride) v = rp[q4];
-            W[tt][4 * q4 + 0] = v.x; W[tt][4 * q4 + 1] = v.y; W[tt][4 * q4 + 2] = v.z; W[tt][4 * q4 + 3] = v.w;
-        }
+        row[tt] = kb_s + (uint32_t)tl * krow;
         if (h.scale_stride == 4) {
             const uint2 v = *reinterpret_cast<const uint2 *>(sb + (size_t)tl * 4);
             sw[tt][0] = v.x; sw[tt][1] = v.y; sw[tt][2] = 0u; sw[tt][3] = 0u;
@@ -178,87 +264,123 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
             sw[tt][0] = v.x; sw[tt][1] = v.y; sw[tt][2] = v.z; sw[tt][3] = v.w;
         }
 #pragma unroll
-        for (int r = 0; r < QM; ++r) { acc[tt][r] = 0.0f; part[tt][r] = 0.0f; }
+        for (int r = 0; r < QM; ++r) { acc[tt][r] = 0.0f; part[tt][r] = make_float2(0.0f, 0.0f); }
     }
-    auto flush = [&]() {
+    // one dimension pair: record + the two pre-scaled indices of each token
+    auto pair = [&](const uint32_t *rp, const uint32_t (&ia)[TPL], const uint32_t (&ib)[TPL]) {
+        uint32_t v[RP];
+#pragma unroll
+        for (int x = 0; x < RP; x += 4) {
+            const uint4 t = *reinterpret_cast<const uint4 *>(rp + x);
+            v[x] = t.x; v[x + 1] = t.y; v[x + 2] = t.z; v[x + 3] = t.w;
+        }
+        const uint32_t ba = v[2 * QM], bb = v[2 * QM + 1];
+#pragma unroll
+        for (int tt = 0; tt < TPL; ++tt) {
+            const float2 c = make_float2(lds_f32(sm, ba + ia[tt]), lds_f32(sm, bb + ib[tt]));
+#pragma unroll
+            for (int r = 0; r < QM; ++r)
+                part[tt][r] = __ffma2_rn(make_float2(__uint_as_float(v[2 * r]), __uint_as_float(v[2 * r + 1])), c,
+                                         part[tt][r]);
+        }
+    };
+    // a run of cnt <= 4 pairs starting at pair record rp0 whose codes start at byte a of the
+    // row (nibble run: pair b = byte b; byte run: pair b = bytes 2b, 2b+1)
+    auto nib_run = [&](uint32_t a, const uint32_t *rp0, uint32_t cnt) {
+        const uint32_t al = a & ~3u, sh = (a & 3u) * 8u;
+        uint32_t lo4[TPL], hi4[TPL];
+#pragma unroll
+        for (int tt = 0; tt < TPL; ++tt) {
+            const uint32_t word = __funnelshift_r(lds_u32(sm, row[tt] + al), lds_u32(sm, row[tt] + al + 4), sh);
+            lo4[tt] = (word << 2) & 0x3c3c3c3cu;   // even dims: low nibble x 4 per byte
+            hi4[tt] = (word >> 2) & 0x3c3c3c3cu;   // odd dims: high nibble x 4 per byte
+        }
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            if ((uint32_t)p < cnt) {
+                uint32_t ia[TPL], ib[TPL];
+#pragma unroll
+                for (int tt = 0; tt < TPL; ++tt) {
+                    ia[tt] = __byte_perm(lo4[tt], 0u, 0x4440u | p);
+                    ib[tt] = __byte_perm(hi4[tt], 0u, 0x4440u | p);
+                }
+                pair(rp0 + p * RP, ia, ib);
+            }
+        }
+    };
+    auto byte_run = [&](uint32_t a, const uint32_t *rp0, uint32_t cnt) {
+        const uint32_t al = a & ~3u, sh = (a & 3u) * 8u;
+        uint32_t x4[TPL][4];
+#pragma unroll
+        for (int tt = 0; tt < TPL; ++tt) {
+            const uint32_t w0 = lds_u32(sm, row[tt] + al), w1 = lds_u32(sm, row[tt] + al + 4),
+                           w2 = lds_u32(sm, row[tt] + al + 8);
+            const uint32_t x = __funnelshift_r(w0, w1, sh), y = __funnelshift_r(w1, w2, sh);
+            x4[tt][0] = (x << 2) & 0x03fc03fcu;   // bytes 0, 2 of x (x 4)
+            x4[tt][1] = (x >> 6) & 0x03fc03fcu;   // bytes 1, 3 of x
+            x4[tt][2] = (y << 2) & 0x03fc03fcu;
+            x4[tt][3] = (y >> 6) & 0x03fc03fcu;
+        }
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            if ((uint32_t)p < cnt) {
+                uint32_t ia[TPL], ib[TPL];
+#pragma unroll
+                for (int tt = 0; tt < TPL; ++tt) {
+                    const uint32_t e = x4[tt][(p >> 1) * 2], o = x4[tt][(p >> 1) * 2 + 1];
+                    ia[tt] = (p & 1) ? e >> 16 : e & 0xffffu;
+                    ib[tt] = (p & 1) ? o >> 16 : o & 0xffffu;
+                }
+                pair(rp0 + p * RP, ia, ib);
+            }
+        }
+    };
+    uint32_t rix = 0;  // first record of the current group
+#pragma unroll 1
+    for (uint32_t g = 0; g < h.ng; ++g) {
+        const uint32_t go = h.group_off[g], p0 = go / 2, np = h.group_off[g + 1] / 2 - p0;
+        const uint32_t nfull = np / 4, rem = np & 3u;
+        const uint32_t *rg = recs + rix * RP;
+        if (go < ns) {
+#pragma unroll 1
+            for (uint32_t k = 0; k < nfull; ++k) nib_run(p0 + 4 * k, rg + 4 * k * RP, 4);
+            if (rem) nib_run(p0 + 4 * nfull, rg + 4 * nfull * RP, rem);
+        } else {
+            // byte group: dim 2*p0 sits at byte ns/2 + (2*p0 - ns)
+            const uint32_t ob = 2 * p0 - ns / 2;
+#pragma unroll 1
+            for (uint32_t k = 0; k < nfull; ++k) byte_run(ob + 8 * k, rg + 4 * k * RP, 4);
+            if (rem) byte_run(ob + 8 * nfull, rg + 4 * nfull * RP, rem);
+        }
+        const uint32_t nblk = nfull + (rem ? 1u : 0u);
+        rix += 4 * nblk;
+        // group end: apply this group's FP16 scale, move to the next scale
 #pragma unroll
         for (int tt = 0; tt < TPL; ++tt) {
             const float sc = half_lo(sw[tt][0]);
 #pragma unroll
-            for (int r = 0; r < QM; ++r) { acc[tt][r] = fmaf(sc, part[tt][r], acc[tt][r]); part[tt][r] = 0.0f; }
+            for (int r = 0; r < QM; ++r) {
+                acc[tt][r] = fmaf(sc, part[tt][r].x + part[tt][r].y, acc[tt][r]);
+                part[tt][r] = make_float2(0.0f, 0.0f);
+            }
             sw[tt][0] = __funnelshift_r(sw[tt][0], sw[tt][1], 16);
             sw[tt][1] = __funnelshift_r(sw[tt][1], sw[tt][2], 16);
             sw[tt][2] = __funnelshift_r(sw[tt][2], sw[tt][3], 16);
             sw[tt][3] >>= 16;
         }
-    };
-    // ---- pass 1: nibble region, dimensions (j, j+1) share byte j/2 ----
-#pragma unroll
-    for (int j = 0; j < D; j += 2) {
-        if ((uint32_t)j < ns) {
-            float q0[QP], q1[QP];
-            load_q<QP>(qrec_s + j * QP, q0);
-            load_q<QP>(qrec_s + (j + 1) * QP, q1);
-            const float *cb0 = cent_s + h.cb_base[j], *cb1 = cent_s + h.cb_base[j + 1];
-#pragma unroll
-            for (int tt = 0; tt < TPL; ++tt) {
-                const uint32_t byte = W[tt][j >> 3] >> (((j >> 1) & 3) * 8);
-                const float c0 = cb0[byte & 15u], c1 = cb1[(byte >> 4) & 15u];
-#pragma unroll
-                for (int r = 0; r < QM; ++r) part[tt][r] = fmaf(q1[r], c1, fmaf(q0[r], c0, part[tt][r]));
-            }
-            if (j + 2 < D && ((bm[(j + 2) >> 5] >> ((j + 2) & 31)) & 1u)) flush();
-        }
     }
-    // ---- realign: byte-region code of dimension j (>= ns) moves to byte j ----
-    if (ns < (uint32_t)D) {
-        const uint32_t sbytes = ns >> 1, aw = sbytes >> 2, c8 = (sbytes & 3u) * 8u;
-#pragma unroll
-        for (int tt = 0; tt < TPL; ++tt) {
-#pragma unroll
-            for (int b = 1; b < RW; b <<= 1) {
-                if (aw & (uint32_t)b) {
-#pragma unroll
-                    for (int k = RW - 1; k >= 0; --k) W[tt][k] = k >= b ? W[tt][k - b] : 0u;
-                }
-            }
-#pragma unroll
-            for (int k = RW - 1; k >= 0; --k) W[tt][k] = __funnelshift_l(k > 0 ? W[tt][k - 1] : 0u, W[tt][k], c8);
-        }
-    }
-    // ---- pass 2: byte region ----
-#pragma unroll
-    for (int j = 0; j < D; j += 2) {
-        if ((uint32_t)j >= ns) {
-            float q0[QP], q1[QP];
-            load_q<QP>(qrec_s + j * QP, q0);
-            load_q<QP>(qrec_s + (j + 1) * QP, q1);
-            const float *cb0 = cent_s + h.cb_base[j], *cb1 = cent_s + h.cb_base[j + 1];
-#pragma unroll
-            for (int tt = 0; tt < TPL; ++tt) {
-                const float c0 = cb0[(W[tt][j >> 2] >> ((j & 3) * 8)) & 255u];
-                const float c1 = cb1[(W[tt][(j + 1) >> 2] >> (((j + 1) & 3) * 8)) & 255u];
-#pragma unroll
-                for (int r = 0; r < QM; ++r) part[tt][r] = fmaf(q1[r], c1, fmaf(q0[r], c0, part[tt][r]));
-            }
-            if (j + 2 < D && ((bm[(j + 2) >> 5] >> ((j + 2) & 31)) & 1u)) flush();
-        }
-    }
-#pragma unroll
-    for (int tt = 0; tt < TPL; ++tt) {
-        const float sc = half_lo(sw[tt][0]);
-#pragma unroll
-        for (int r = 0; r < QM; ++r) acc[tt][r] = fmaf(sc, part[tt][r], acc[tt][r]);
-    }
+    (void)d;
 }
 
 template <int D, int QM, KKind KK, bool VF32>
 __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ AttnArgs a, const Plan pl, uint32_t d) {
     constexpr int TPL = Geo<D>::TPL, TT = Geo<D>::TT, QP = QPad<QM>::QP;
+    constexpr bool MMA = UseMma<D, VF32>::value;
     constexpr int VSZ = VF32 ? 4 : 2, VEC = 16 / VSZ, LPT = D / VEC, TPS = 32 / LPT;
     static_assert(LPT >= 1 && LPT <= 32, "V slice layout");
     constexpr int KSZ = KK == KKind::F32 ? 4 : 2, KVEC = 16 / KSZ, LPTK = D / KVEC, TPSK = 32 / LPTK;
     static_assert(KK == KKind::Packed || (LPTK >= 1 && LPTK <= 32), "K slice layout");
+    constexpr int NT = D / 8;  // MMA n-tiles (8 dims each)
 
     const uint32_t split = blockIdx.x, hd = blockIdx.y, s = blockIdx.z;
     const AttnHead &h = a.head[hd];
@@ -269,8 +391,9 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
 
     extern __shared__ __align__(128) unsigned char smem[];
     float *cent_s = reinterpret_cast<float *>(smem + pl.cent);
-    float *qrec_s = reinterpret_cast<float *>(smem + pl.qrec);
-    float *pbuf = reinterpret_cast<float *>(smem + pl.pbuf) + w * TT * QP;
+    unsigned char *rec = smem + pl.qrec;
+    float *qrec_s = reinterpret_cast<float *>(rec);
+    float *pbuf = reinterpret_cast<float *>(smem + pl.pbuf) + w * TT * QP;  // [QP][TT]
     const uint32_t bar0 = smem_u32(smem + pl.bars) + (uint32_t)w * 16u;
     __shared__ uint32_t s_last;
 
@@ -290,31 +413,28 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
     const uint32_t t0 = split * a.tokens_per_split;
     const uint32_t t1 = min(t0 + a.tokens_per_split, tend);
 
-    // ---- prologue: codebooks, query records, barriers ----
+    // ---- prologue: codebooks, query tables, barriers ----
+    const float *qt = a.qt + ((uint64_t)s * a.heads + hd) * (uint64_t)(D * QP);
     if constexpr (KK == KKind::Packed) {
         for (uint32_t i = tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < h.n_cent ? h.cent[i] : 0.0f;
-    }
-    // query records (rotated into code order and scaled by 1/sqrt(d) by qrot_kernel)
-    {
-        const float4 *src = reinterpret_cast<const float4 *>(a.qt + ((uint64_t)s * a.heads + hd) * (uint64_t)(D * QP));
+        build_tables<D, QM, QP>(h, qt, rec, d, pl.cent, tid);
+    } else {
+        const float4 *src = reinterpret_cast<const float4 *>(qt);
         float4 *dst = reinterpret_cast<float4 *>(qrec_s);
         for (uint32_t i = tid; i < (uint32_t)(D * QP / 4); i += kThreads) dst[i] = __ldg(src + i);
     }
     if (tid < kWarps * 2) mbar_init(smem_u32(smem + pl.bars) + tid * 8u, 1u);
     fence_barrier_init();
-    uint32_t bm[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) bm[i] = h.bound_mask[i];
     __syncthreads();
 
     // ---- per-warp flash-decoding over this split ----
-    float m[QM], l[QM], O[QM][VEC];
+    float m[QM], l[QM];
 #pragma unroll
-    for (int r = 0; r < QM; ++r) {
-        m[r] = -INFINITY; l[r] = 0.0f;
+    for (int r = 0; r < QM; ++r) { m[r] = -INFINITY; l[r] = 0.0f; }
+    constexpr int OS = MMA ? NT * 4 : QM * VEC;  // output accumulators per lane
+    float O[OS];
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) O[r][e] = 0.0f;
-    }
+    for (int i = 0; i < OS; ++i) O[i] = 0.0f;
     float qreg[QM][KVEC];
     if constexpr (KK != KKind::Packed) {
         const int dl = (lane % LPTK) * KVEC;
@@ -332,20 +452,19 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
         KK == KKind::Packed ? reinterpret_cast<const unsigned char *>(h.scales + (uint64_t)seq * h.s_seq_stride) : nullptr;
     const unsigned char *vbase = static_cast<const unsigned char *>(h.v) + (uint64_t)seq * h.v_seq_stride;
     const uint32_t krow = h.row_stride, vrow = D * VSZ, srow = h.scale_stride * 2u;
+    const uint32_t soff = align16(pl.kbytes) + 16u, voff = soff + align16(pl.sbytes);
 
+    // whole tiles: rows past the sequence end exist (capacity padded to 64, zero filled)
     auto issue = [&](uint32_t k, int st) {
         if (lane == 0) {
-            const uint32_t at = t0 + k * TT, n = min((uint32_t)TT, t1 - at);
+            const uint32_t at = t0 + k * TT;
             unsigned char *buf = stage0 + (size_t)st * pl.stage_bytes;
-            const uint32_t kb = n * krow, vb = n * vrow;
-            const uint32_t sb = KK == KKind::Packed ? ((n + 1u) & ~1u) * srow : 0u;
             const uint32_t bar = bar0 + (uint32_t)st * 8u;
             fence_proxy_async();
-            mbar_expect_tx(bar, kb + sb + vb);
-            bulk_g2s(smem_u32(buf), kbase + (uint64_t)at * krow, kb, bar);
-            if (KK == KKind::Packed)
-                bulk_g2s(smem_u32(buf + align16(pl.kbytes)), sbase + (uint64_t)at * srow, sb, bar);
-            bulk_g2s(smem_u32(buf + align16(pl.kbytes) + align16(pl.sbytes)), vbase + (uint64_t)at * vrow, vb, bar);
+            mbar_expect_tx(bar, pl.kbytes + pl.sbytes + pl.vbytes);
+            bulk_g2s(smem_u32(buf), kbase + (uint64_t)at * krow, pl.kbytes, bar);
+            if (KK == KKind::Packed) bulk_g2s(smem_u32(buf + soff), sbase + (uint64_t)at * srow, pl.sbytes, bar);
+            bulk_g2s(smem_u32(buf + voff), vbase + (uint64_t)at * vrow, pl.vbytes, bar);
         }
     };
 
@@ -363,13 +482,13 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
         phase ^= 1u << st;
         const uint32_t at = t0 + k * TT, n = min((uint32_t)TT, t1 - at);
         const unsigned char *kb = stage0 + (size_t)st * pl.stage_bytes;
-        const uint16_t *sb = reinterpret_cast<const uint16_t *>(kb + align16(pl.kbytes));
-        const unsigned char *vb = kb + align16(pl.kbytes) + align16(pl.sbytes);
+        const uint16_t *sb = reinterpret_cast<const uint16_t *>(kb + soff);
+        const unsigned char *vb = kb + voff;
 
         // ---- logits for this lane's TPL tokens ----
         float acc[TPL][QM];
         if constexpr (KK == KKind::Packed) {
-            packed_qk<D, QM, QP>(h, kb, sb, cent_s, qrec_s, bm, lane, acc);
+            packed_qk<D, QM>(h, smem, (uint32_t)(kb - smem), sb, rec, d, lane, acc);
         } else {
             const uint32_t steps = (n + TPSK - 1) / TPSK;
             for (uint32_t st2 = 0; st2 < steps; ++st2) {
@@ -399,7 +518,7 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
                     for (int e = 0; e < KVEC; ++e) sum = fmaf(qreg[r][e], kv[e], sum);
 #pragma unroll
                     for (int o = 1; o < LPTK; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-                    if ((lane % LPTK) == 0 && tl < n) pbuf[tl * QP + r] = sum;
+                    if ((lane % LPTK) == 0 && tl < n) pbuf[r * TT + tl] = sum;
                 }
             }
             __syncwarp();
@@ -407,7 +526,7 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
             for (int tt = 0; tt < TPL; ++tt) {
                 const uint32_t tl = tt * 32 + lane;
 #pragma unroll
-                for (int r = 0; r < QM; ++r) acc[tt][r] = tl < n ? pbuf[tl * QP + r] : 0.0f;
+                for (int r = 0; r < QM; ++r) acc[tt][r] = tl < n ? pbuf[r * TT + tl] : 0.0f;
             }
             __syncwarp();
         }
@@ -434,7 +553,7 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
 #pragma unroll
             for (int tt = 0; tt < TPL; ++tt) {
                 const float p = lg[tt] == -INFINITY ? 0.0f : exp2f((lg[tt] - mnew) * kLog2e);
-                pbuf[(tt * 32 + lane) * QP + r] = p;
+                pbuf[r * TT + tt * 32 + lane] = p;
                 ps += p;
             }
             ps = warp_sum(ps);
@@ -445,16 +564,54 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
 #pragma unroll
             for (int tt = 0; tt < TPL; ++tt)
 #pragma unroll
-                for (int r = QM; r < QP; ++r) pbuf[(tt * 32 + lane) * QP + r] = 0.0f;
+                for (int r = QM; r < QP; ++r) pbuf[r * TT + tt * 32 + lane] = 0.0f;
         }
-#pragma unroll
-        for (int r = 0; r < QM; ++r)
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) O[r][e] *= alpha[r];
         __syncwarp();
 
-        // ---- P.V: lane = 16-byte slice of a V row ----
-        {
+        // ---- P.V ----
+        if constexpr (MMA) {
+            // fragment row g = query (high part of P), row g + 8 = the same query (low part);
+            // column pair 2c/2c+1 (+8) = token (A) or dim (C)
+            const int g = lane >> 2, c = lane & 3;
+            float ag = 1.0f;
+#pragma unroll
+            for (int r = 0; r < QM; ++r) ag = g == r ? alpha[r] : ag;
+#pragma unroll
+            for (int i = 0; i < NT * 4; ++i) O[i] *= ag;
+            const uint32_t vb_s = smem_u32(vb);
+            const int mi = lane >> 3, ri = lane & 7;
+#pragma unroll
+            for (int kb16 = 0; kb16 < TT / 16; ++kb16) {
+                float2 pa = make_float2(0.0f, 0.0f), pb = make_float2(0.0f, 0.0f);
+                if (g < QP) {
+                    pa = *reinterpret_cast<const float2 *>(pbuf + g * TT + kb16 * 16 + 2 * c);
+                    pb = *reinterpret_cast<const float2 *>(pbuf + g * TT + kb16 * 16 + 2 * c + 8);
+                }
+                pa.x *= kPScale; pa.y *= kPScale; pb.x *= kPScale; pb.y *= kPScale;
+                const __half2 ha = __floats2half2_rn(pa.x, pa.y), hb = __floats2half2_rn(pb.x, pb.y);
+                const float2 fa = __half22float2(ha), fb = __half22float2(hb);
+                const __half2 la = __floats2half2_rn(pa.x - fa.x, pa.y - fa.y);
+                const __half2 lb = __floats2half2_rn(pb.x - fb.x, pb.y - fb.y);
+                const uint32_t ahi0 = h2_bits(ha), ahi2 = h2_bits(hb), alo0 = h2_bits(la), alo2 = h2_bits(lb);
+                // ldmatrix row address of this lane: matrix mi (tokens +8*(mi&1), chunk +(mi>>1)), row ri
+                const uint32_t tok = (uint32_t)(kb16 * 16 + (mi & 1) * 8 + ri);
+#pragma unroll
+                for (int np = 0; np < NT / 2; ++np) {
+                    const uint32_t chunk = (uint32_t)(2 * np + (mi >> 1));
+                    const uint32_t pos_c = (chunk & ~7u) | ((chunk ^ tok) & 7u);
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_trans(vb_s + tok * (D * 2) + pos_c * 16, b0, b1, b2, b3);
+                    float(&c0)[4] = *reinterpret_cast<float(*)[4]>(&O[(2 * np) * 4]);
+                    float(&c1)[4] = *reinterpret_cast<float(*)[4]>(&O[(2 * np + 1) * 4]);
+                    mma_16816(c0, ahi0, alo0, ahi2, alo2, b0, b1);
+                    mma_16816(c1, ahi0, alo0, ahi2, alo2, b2, b3);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < QM; ++r)
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) O[r * VEC + e] *= alpha[r];
             const int slot = lane / LPT, dl = (lane % LPT) * VEC;
             const uint32_t steps = (n + TPS - 1) / TPS;
 #pragma unroll 4
@@ -474,12 +631,12 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
                         vv[0] = __uint_as_float(raw.x); vv[1] = __uint_as_float(raw.y);
                         vv[2] = __uint_as_float(raw.z); vv[3] = __uint_as_float(raw.w);
                     }
-                    float p[QP];
-                    load_q<QP>(pbuf + tl * QP, p);
 #pragma unroll
-                    for (int r = 0; r < QM; ++r)
+                    for (int r = 0; r < QM; ++r) {
+                        const float p = pbuf[r * TT + tl];
 #pragma unroll
-                        for (int e = 0; e < VEC; ++e) O[r][e] = fmaf(p[r], vv[e], O[r][e]);
+                        for (int e = 0; e < VEC; ++e) O[r * VEC + e] = fmaf(p, vv[e], O[r * VEC + e]);
+                    }
                 }
             }
         }
@@ -488,24 +645,33 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
     }
     if (!ok) atomicOr(a.status, kStatusWaitTimeout);
 
-    // ---- reduce P.V partial sums across token slots of the warp ----
-#pragma unroll
-    for (int r = 0; r < QM; ++r)
-#pragma unroll
-        for (int e = 0; e < VEC; ++e)
-#pragma unroll
-            for (int o = LPT; o < 32; o <<= 1) O[r][e] += __shfl_xor_sync(0xffffffffu, O[r][e], o);
-
     // ---- merge the warps of this CTA ----
+    if constexpr (!MMA) {
+#pragma unroll
+        for (int i = 0; i < OS; ++i)
+#pragma unroll
+            for (int o = LPT; o < 32; o <<= 1) O[i] += __shfl_xor_sync(0xffffffffu, O[i], o);
+    }
     __syncthreads();
     float *mO = reinterpret_cast<float *>(smem + pl.stage);  // [kWarps][QP][D]
     float *mm = mO + kWarps * QP * D;                        // [kWarps][QP]
     float *ml = mm + kWarps * QP;
-    if (lane < LPT) {
+    if constexpr (MMA) {
+        const int g = lane >> 2, c = lane & 3;
+        if (g < QM) {
 #pragma unroll
-        for (int r = 0; r < QM; ++r)
+            for (int nt = 0; nt < NT; ++nt) {
+                mO[(w * QP + g) * D + nt * 8 + 2 * c] = (O[nt * 4 + 0] + O[nt * 4 + 2]) * kPUnscale;
+                mO[(w * QP + g) * D + nt * 8 + 2 * c + 1] = (O[nt * 4 + 1] + O[nt * 4 + 3]) * kPUnscale;
+            }
+        }
+    } else {
+        if (lane < LPT) {
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) mO[(w * QP + r) * D + (lane % LPT) * VEC + e] = O[r][e];
+            for (int r = 0; r < QM; ++r)
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) mO[(w * QP + r) * D + (lane % LPT) * VEC + e] = O[r * VEC + e];
+        }
     }
     if (lane == 0) {
 #pragma unroll

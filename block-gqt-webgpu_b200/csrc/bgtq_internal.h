@@ -126,7 +126,9 @@ cudaError_t launch_encode(const EncodeArgs &a, uint32_t d, uint32_t smem_cent_fl
 cudaError_t launch_copy_rows(void *dst, uint64_t dst_seq_stride, uint32_t dst_row_elems, int dst_f32,
                              const void *src, uint64_t src_row_stride, uint64_t src_seq_stride, int src_f32,
                              const uint32_t *row0, uint32_t row0_scalar, uint32_t count, uint32_t seq_first,
-                             uint32_t seq_count, uint32_t *lengths, uint32_t d, cudaStream_t s);
+                             uint32_t seq_count, uint32_t *lengths, uint32_t d, int swizzle, cudaStream_t s);
+// FP16 value rows of 64 or 128 halves are stored chunk-swizzled (see copy_rows_kernel).
+inline bool values_swizzled(int f32, uint32_t D) { return !f32 && (D == 64 || D == 128); }
 cudaError_t launch_reconstruct(const ReconArgs &a, uint32_t n_cent, cudaStream_t s);
 
 enum class KKind { Packed, F16, F32 };

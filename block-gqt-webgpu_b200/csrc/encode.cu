@@ -29,7 +29,7 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant_
                                                           uint32_t cent_alloc, uint32_t lut_bytes, uint32_t total) {
     const EncodeHead &h = a.head[blockIdx.y];
     constexpr int SW = D / 2 + 1;  // staged input words per key (odd: conflict-free gathers)
-    const uint32_t row_words = h.row_stride / 4, ow = row_words + 1;
+    const uint32_t row_words = h.row_stride / 4, ow = row_words | 1u;  // odd: conflict-free row stores
     const uint32_t sc_words = h.scale_stride / 2, sw = sc_words + 1;
 
     extern __shared__ __align__(16) unsigned char smem[];
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant_
 
 template <int D>
 size_t encode_smem(uint32_t cent_alloc, uint32_t lut_bytes, uint32_t row_stride, uint32_t scale_stride) {
-    const size_t ow = row_stride / 4 + 1, sw = scale_stride / 2 + 1;
+    const size_t ow = (row_stride / 4) | 1u, sw = scale_stride / 2 + 1;
     size_t b = sizeof(float) * ((size_t)D * D + cent_alloc + 2 * D + kMaxGroups * kThreads);
     b += sizeof(uint32_t) * (size_t)kThreads * ((D / 2 + 1) + ow + sw);
     b += sizeof(uint16_t) * D + lut_bytes + 4 * D;

@@ -38,7 +38,9 @@ bgtq_status parse_layout(const uint32_t *config, size_t n_config, const float *t
     L.d = d; L.ng = ng; L.row_bytes = rb; L.norm_stride = nstride; L.ns = ns; L.maxc = maxc;
     L.ncb = (uint32_t)(lut_len / 256);
     L.logical_rb = ns / 2 + d - ns;
-    L.dev_row_stride = (L.logical_rb + 15u) & ~15u;
+    // an odd number of 32-bit words: lanes reading word k of 32 consecutive rows in shared
+    // memory hit 32 different banks
+    L.dev_row_stride = 4u * (((L.logical_rb + 3u) / 4u) | 1u);
     L.dev_scale_stride = ng <= 4 ? 4u : 8u;
     L.perm.resize(d); L.group_of.resize(d); L.pos_to_cb.resize(d);
     std::set<uint32_t> seen;

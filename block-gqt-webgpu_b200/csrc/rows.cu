@@ -14,10 +14,13 @@
 namespace bgtq {
 namespace {
 
+// swizzle: FP16 rows of 64 or 128 halves store 16-byte chunk c of row t at chunk
+// (c & ~7) | ((c ^ t) & 7), so that a tile of rows copied verbatim into shared memory can
+// be read column-wise (ldmatrix) without bank conflicts.
 __global__ void copy_rows_kernel(void *dst, uint64_t dst_seq_stride, uint32_t dst_row_elems, int dst_f32,
                                  const void *src, uint64_t src_row_stride, uint64_t src_seq_stride, int src_f32,
                                  const uint32_t *row0, uint32_t row0_scalar, uint32_t count, uint32_t seq_first,
-                                 uint32_t seq_count, uint32_t d, uint32_t *lengths) {
+                                 uint32_t seq_count, uint32_t d, uint32_t *lengths, int swizzle) {
     const uint64_t total = (uint64_t)seq_count * count * d;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
         const uint32_t e = (uint32_t)(i % d);
@@ -25,7 +28,12 @@ __global__ void copy_rows_kernel(void *dst, uint64_t dst_seq_stride, uint32_t ds
         const uint32_t r = (uint32_t)(rowi % count), s = (uint32_t)(rowi / count);
         const uint64_t si = (uint64_t)s * src_seq_stride + (uint64_t)r * src_row_stride + e;
         const uint32_t drow = (row0 ? row0[s] : row0_scalar) + r;
-        const uint64_t di = (uint64_t)(seq_first + s) * dst_seq_stride + (uint64_t)drow * dst_row_elems + e;
+        uint32_t de = e;
+        if (swizzle) {
+            const uint32_t c = e >> 3;
+            de = (((c & ~7u) | ((c ^ drow) & 7u)) << 3) | (e & 7u);
+        }
+        const uint64_t di = (uint64_t)(seq_first + s) * dst_seq_stride + (uint64_t)drow * dst_row_elems + de;
         if (dst_f32) {
             const float v = src_f32 ? static_cast<const float *>(src)[si]
                                     : __half2float(__ushort_as_half(static_cast<const uint16_t *>(src)[si]));
@@ -100,14 +108,14 @@ cudaError_t run_reconstruct(const ReconArgs &a, uint32_t n_cent, cudaStream_t s)
 cudaError_t launch_copy_rows(void *dst, uint64_t dst_seq_stride, uint32_t dst_row_elems, int dst_f32, const void *src,
                              uint64_t src_row_stride, uint64_t src_seq_stride, int src_f32, const uint32_t *row0,
                              uint32_t row0_scalar, uint32_t count, uint32_t seq_first, uint32_t seq_count,
-                             uint32_t *lengths, uint32_t d, cudaStream_t s) {
+                             uint32_t *lengths, uint32_t d, int swizzle, cudaStream_t s) {
     if (count == 0 || seq_count == 0) return cudaSuccess;
     const uint64_t total = (uint64_t)seq_count * count * d;
     uint64_t blocks = (total + 255) / 256;
     if (blocks > 148u * 16u) blocks = 148u * 16u;
     copy_rows_kernel<<<(unsigned)blocks, 256, 0, s>>>(dst, dst_seq_stride, dst_row_elems, dst_f32, src, src_row_stride,
                                                        src_seq_stride, src_f32, row0, row0_scalar, count, seq_first,
-                                                       seq_count, d, lengths);
+                                                       seq_count, d, lengths, swizzle);
     return cudaGetLastError();
 }
 

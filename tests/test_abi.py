@@ -40,7 +40,9 @@ def test_validate_accepts_reference_tables_and_derives_ranges(name):
     info, ranges = validate_layout(cfg, tab)
     assert (info.dim, info.groups, info.nibble_dims, info.row_bytes) == (p.dim, p.groups, p.nibble_dims, p.row_bytes)
     assert info.logical_row_bytes == int(z["logical_row_bytes"])
-    assert info.device_row_stride % 16 == 0 and info.device_row_stride >= info.logical_row_bytes
+    # odd number of 32-bit words (conflict-free shared-memory row reads), covering the row
+    assert info.device_row_stride % 4 == 0 and (info.device_row_stride // 4) % 2 == 1
+    assert info.logical_row_bytes <= info.device_row_stride < info.logical_row_bytes + 8
     np.testing.assert_array_equal(ranges, oracle.group_ranges(p.group_of, p.rotation, p.dim))
 
 
