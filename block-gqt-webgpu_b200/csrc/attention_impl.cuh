@@ -14,11 +14,14 @@
 // so that q.k = sum_g s_g sum_{i in g} qt_i cent[i][code_i] (k = reconstruct(codes) of
 // src/reference/production_math.py:27-31, R block-diagonal as PackedKeys enforces).
 //
-// Data movement: each warp owns a ring of shared-memory tiles (packed rows, FP16 scales,
-// V rows) filled by cp.async.bulk (TMA bulk copies, no multicast) that complete on an
-// mbarrier; every mbarrier wait is bounded and reports a timeout through the device status
-// word instead of spinning forever.  Tiles are always copied whole: capacity is padded to
-// 64 rows and zero-filled, and tokens past the end of a split get probability 0.
+// Data movement: each warp owns two shared-memory K tiles (packed rows + FP16 scales) and
+// one V tile, filled by cp.async.bulk (TMA bulk copies, no multicast) that complete on
+// mbarriers.  The next K tile is fetched while the current one is computed; the next V tile
+// is fetched right after the current P.V and lands during the next dequant + QK, so one V
+// buffer suffices and three CTAs fit on an SM.  Every mbarrier wait is bounded and reports
+// a timeout through the device status word instead of spinning forever.  Tiles are always
+// copied whole: capacity is padded to 64 rows and zero-filled, and tokens past the end of
+// a split get probability 0.
 //
 // Compute:
 //   dequant + QK   lane = token.  Packed rows sit in shared memory at an odd word stride,
@@ -76,13 +79,18 @@ struct UseMma {
     static constexpr bool value = !VF32 && (D == 64 || D == 128);
 };
 
+// Shared-memory plan of one CTA.  Each warp owns a V tile buffer and a ring of `stages`
+// K tile buffers (packed rows + FP16 scales, or dense rows): the next tile's keys are
+// fetched while the current tile is computed, and the next tile's values are fetched as
+// soon as the current P.V is done, behind the next tile's dequant + QK.
 struct Plan {
     uint32_t cent, qrec, stage, pbuf, bars, total;
-    uint32_t kbytes, sbytes, vbytes, stage_bytes, cent_alloc;
-    uint32_t stages;  // 2: prefetch the next tile while computing; 1 when two do not fit
+    uint32_t kbytes, sbytes, vbytes, kstage_bytes, warp_bytes, cent_alloc;
+    uint32_t stages;  // K buffers per warp: 2, or 1 when two do not fit
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
+__host__ __device__ inline uint32_t align128(uint32_t x) { return (x + 127u) & ~127u; }
 
 inline Plan make_plan(KKind kk, int v_f32, uint32_t D, uint32_t QP, uint32_t TT, uint32_t row_stride,
                       uint32_t scale_stride, uint32_t n_cent, uint32_t smem_limit = 227u * 1024u,
@@ -100,14 +108,16 @@ inline Plan make_plan(KKind kk, int v_f32, uint32_t D, uint32_t QP, uint32_t TT,
     p.kbytes = TT * row_stride;
     p.sbytes = kk == KKind::Packed ? TT * scale_stride * 2u : 0u;
     p.vbytes = TT * D * (v_f32 ? 4u : 2u);
-    p.stage_bytes = align16(p.kbytes) + 16u + align16(p.sbytes) + align16(p.vbytes);
-    off = (off + 127u) & ~127u;
+    // 16 spare bytes after the K rows: the code-word reads of the last row run past its end
+    p.kstage_bytes = align128(align16(p.kbytes) + 16u + align16(p.sbytes));
+    p.warp_bytes = align128(p.vbytes) + stages * p.kstage_bytes;
+    off = align128(off);
     p.stage = off;
-    off += kWarps * stages * p.stage_bytes;
+    off += kWarps * p.warp_bytes;
     p.pbuf = off;
     off = align16(off + kWarps * TT * QP * 4u);
     p.bars = off;
-    off += kWarps * 2u * 8u;
+    off += kWarps * 4u * 8u;  // per warp: K barriers 0, 1 and the V barrier
     p.total = align16(off);
     if (p.total > smem_limit && stages == 2)
         return make_plan(kk, v_f32, D, QP, TT, row_stride, scale_stride, n_cent, smem_limit, 1, QM);
@@ -394,7 +404,7 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
     unsigned char *rec = smem + pl.qrec;
     float *qrec_s = reinterpret_cast<float *>(rec);
     float *pbuf = reinterpret_cast<float *>(smem + pl.pbuf) + w * TT * QP;  // [QP][TT]
-    const uint32_t bar0 = smem_u32(smem + pl.bars) + (uint32_t)w * 16u;
+    const uint32_t bar0 = smem_u32(smem + pl.bars) + (uint32_t)w * 32u, vbar = bar0 + 16u;
     __shared__ uint32_t s_last;
 
     uint32_t pos[QM];
@@ -423,7 +433,7 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
         float4 *dst = reinterpret_cast<float4 *>(qrec_s);
         for (uint32_t i = tid; i < (uint32_t)(D * QP / 4); i += kThreads) dst[i] = __ldg(src + i);
     }
-    if (tid < kWarps * 2) mbar_init(smem_u32(smem + pl.bars) + tid * 8u, 1u);
+    if (tid < kWarps * 4) mbar_init(smem_u32(smem + pl.bars) + tid * 8u, 1u);
     fence_barrier_init();
     __syncthreads();
 
@@ -445,45 +455,60 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
     }
     const uint32_t ntok = t1 > t0 ? t1 - t0 : 0u;
     const uint32_t ntiles = (ntok + TT - 1) / TT;
-    unsigned char *stage0 = smem + pl.stage + (size_t)w * pl.stages * pl.stage_bytes;
+    unsigned char *vbuf = smem + pl.stage + (size_t)w * pl.warp_bytes;
+    unsigned char *kstage0 = vbuf + align128(pl.vbytes);
     const bool two = pl.stages == 2;
     const unsigned char *kbase = h.k + (uint64_t)seq * h.k_seq_stride;
     const unsigned char *sbase =
         KK == KKind::Packed ? reinterpret_cast<const unsigned char *>(h.scales + (uint64_t)seq * h.s_seq_stride) : nullptr;
     const unsigned char *vbase = static_cast<const unsigned char *>(h.v) + (uint64_t)seq * h.v_seq_stride;
     const uint32_t krow = h.row_stride, vrow = D * VSZ, srow = h.scale_stride * 2u;
-    const uint32_t soff = align16(pl.kbytes) + 16u, voff = soff + align16(pl.sbytes);
+    const uint32_t soff = align16(pl.kbytes) + 16u;
 
     // whole tiles: rows past the sequence end exist (capacity padded to 64, zero filled)
-    auto issue = [&](uint32_t k, int st) {
+    uint32_t pending = 0;  // bit st: K buffer st has a copy in flight; bit 2: the V buffer
+    auto issue_k = [&](uint32_t k, int st) {
         if (lane == 0) {
             const uint32_t at = t0 + k * TT;
-            unsigned char *buf = stage0 + (size_t)st * pl.stage_bytes;
+            unsigned char *buf = kstage0 + (size_t)st * pl.kstage_bytes;
             const uint32_t bar = bar0 + (uint32_t)st * 8u;
             fence_proxy_async();
-            mbar_expect_tx(bar, pl.kbytes + pl.sbytes + pl.vbytes);
+            mbar_expect_tx(bar, pl.kbytes + pl.sbytes);
             bulk_g2s(smem_u32(buf), kbase + (uint64_t)at * krow, pl.kbytes, bar);
             if (KK == KKind::Packed) bulk_g2s(smem_u32(buf + soff), sbase + (uint64_t)at * srow, pl.sbytes, bar);
-            bulk_g2s(smem_u32(buf + voff), vbase + (uint64_t)at * vrow, pl.vbytes, bar);
         }
+        pending |= 1u << st;
+    };
+    auto issue_v = [&](uint32_t k) {
+        if (lane == 0) {
+            fence_proxy_async();
+            mbar_expect_tx(vbar, pl.vbytes);
+            bulk_g2s(smem_u32(vbuf), vbase + (uint64_t)(t0 + k * TT) * vrow, pl.vbytes, vbar);
+        }
+        pending |= 4u;
     };
 
     bool ok = true;
-    uint32_t phase = 0;
-    if ((uint32_t)w < ntiles) issue(w, 0);
+    uint32_t phase = 0;  // bit st: parity of K buffer st; bit 2: parity of the V buffer
+    if ((uint32_t)w < ntiles) {
+        issue_k(w, 0);
+        issue_v(w);
+    }
     int it = 0;
     for (uint32_t k = w; k < ntiles; k += kWarps, ++it) {
         const int st = two ? (it & 1) : 0;
-        if (two && k + kWarps < ntiles) issue(k + kWarps, st ^ 1);
+        const bool more = k + kWarps < ntiles;
+        if (two && more) issue_k(k + kWarps, st ^ 1);
         if (!mbar_wait_bounded(bar0 + (uint32_t)st * 8u, (phase >> st) & 1u)) {
             ok = false;
             break;
         }
         phase ^= 1u << st;
+        pending &= ~(1u << st);
         const uint32_t at = t0 + k * TT, n = min((uint32_t)TT, t1 - at);
-        const unsigned char *kb = stage0 + (size_t)st * pl.stage_bytes;
+        const unsigned char *kb = kstage0 + (size_t)st * pl.kstage_bytes;
         const uint16_t *sb = reinterpret_cast<const uint16_t *>(kb + soff);
-        const unsigned char *vb = kb + voff;
+        const unsigned char *vb = vbuf;
 
         // ---- logits for this lane's TPL tokens ----
         float acc[TPL][QM];
@@ -567,6 +592,13 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
                 for (int r = QM; r < QP; ++r) pbuf[r * TT + tt * 32 + lane] = 0.0f;
         }
         __syncwarp();
+        if (!two && more) issue_k(k + kWarps, 0);
+        if (!mbar_wait_bounded(vbar, (phase >> 2) & 1u)) {
+            ok = false;
+            break;
+        }
+        phase ^= 4u;
+        pending &= ~4u;
 
         // ---- P.V ----
         if constexpr (MMA) {
@@ -641,9 +673,15 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
             }
         }
         __syncwarp();
-        if (!two && k + kWarps < ntiles) issue(k + kWarps, 0);
+        if (more) issue_v(k + kWarps);
     }
-    if (!ok) atomicOr(a.status, kStatusWaitTimeout);
+    if (!ok) {
+        // report the timeout, then give the copies still in flight a bounded chance to land
+        // before this shared memory is reused or released
+        if (lane == 0) atomicOr(a.status, kStatusWaitTimeout);
+        for (int b = 0; b < 3; ++b)
+            if (pending & (1u << b)) mbar_wait_bounded(bar0 + (b == 2 ? 16u : 8u * b), (phase >> b) & 1u);
+    }
 
     // ---- merge the warps of this CTA ----
     if constexpr (!MMA) {
