@@ -59,7 +59,7 @@ struct EncodeHead {
     uint16_t *scales;
     uint64_t k_seq_stride;     // bytes between sequences
     uint64_t s_seq_stride;     // halves between sequences
-    uint32_t row_stride;       // bytes between packed rows (multiple of 16)
+    uint32_t row_stride;       // bytes between packed rows (an odd number of 32-bit words)
     uint32_t scale_stride;     // halves between scale rows (4 or 8)
     uint32_t ns, ng, n_cent, ncb;
     uint32_t bound_mask[4];

@@ -2,8 +2,10 @@
 // src/model/codec.wgsl:11-33; arithmetic of src/reference/production_math.py:4-24,
 // packing of src/reference/mixed_layout.py:21-27, FP16 rounding of src/webgpu/half.wgsl:2-12).
 //
-// One thread encodes one key; a persistent CTA of 128 threads walks tiles of 128 keys so
-// the rotation, codebooks and code LUT are staged in shared memory once per CTA.
+// Bulk (a prefix of many tokens): one thread encodes one key; a persistent CTA of 128
+// threads walks tiles of 128 keys so the rotation, codebooks and code LUT are staged in
+// shared memory once per CTA.  Few keys (decode steps): one warp per key, tables read
+// through the L1 cache (encode_warp_kernel).
 // Per key, in the canonical order the CPU oracle shares bit for bit:
 //   x_i   = FP16 key element perm[i]              (exact promotion)
 //   n_g   = sqrt(sum_{i in g} x_i^2 + 1e-30)      (sequential FMA, ascending i)
@@ -21,6 +23,8 @@ namespace bgtq {
 namespace {
 
 constexpr int kThreads = 128;
+// Launches of at most this many keys per head use the warp-per-key kernel.
+constexpr uint32_t kWarpKeysMax = 4096;
 
 __device__ __forceinline__ bool bit_set(const uint32_t (&m)[4], int j) { return (m[j >> 5] >> (j & 31)) & 1u; }
 
@@ -217,6 +221,90 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant_
     }
 }
 
+// Few keys (a decode step appends one token per sequence): one warp per key, lanes over
+// dimensions, so a launch of a few hundred keys spreads over many SMs instead of a couple
+// of threads-per-key CTAs.  Same arithmetic and order as encode_kernel, bit for bit: group
+// sums and scales are still sequential per group (one lane per group), every y_j is still
+// one lane's sequential FMA chain over its group, ascending.
+__global__ void __launch_bounds__(kThreads) encode_warp_kernel(const __grid_constant__ EncodeArgs a, uint32_t d,
+                                                               uint32_t total) {
+    constexpr int W = kThreads / 32;
+    const EncodeHead &h = a.head[blockIdx.y];
+    __shared__ float xs[W][kMaxDim];            // permuted key, then normalised
+    __shared__ float nrm[W][kMaxGroups];
+    __shared__ uint8_t codes[W][kMaxDim];
+    __shared__ uint32_t orow[W][kMaxDim / 4 + 1];
+    __shared__ uint16_t srow[W][8];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t ns = h.ns, ng = h.ng, count = a.count;
+    const uint32_t row_words = h.row_stride / 4, sc_words = h.scale_stride / 2;
+    uint8_t *ob = reinterpret_cast<uint8_t *>(orow[w]);
+    for (uint32_t q = blockIdx.x * W + w; q < total; q += gridDim.x * W) {
+        const uint32_t s = q / count, rr = q % count;
+        const uint64_t e0 = (uint64_t)s * a.seq_stride + (uint64_t)rr * a.row_stride + h.src_head_offset;
+        for (uint32_t i = lane; i < d; i += 32) {
+            const uint64_t e = e0 + h.t.perm[i];
+            const __half x = a.src_f32 ? __float2half_rn(static_cast<const float *>(a.src)[e])
+                                       : __ushort_as_half(static_cast<const uint16_t *>(a.src)[e]);
+            xs[w][i] = __half2float(x);
+        }
+        __syncwarp();
+        if ((uint32_t)lane < ng) {
+            float acc = 0.0f;
+            for (uint32_t i = h.group_off[lane]; i < h.group_off[lane + 1]; ++i) acc = fmaf(xs[w][i], xs[w][i], acc);
+            nrm[w][lane] = sqrtf(acc + 1e-30f);
+        }
+        __syncwarp();
+        for (uint32_t i = lane; i < d; i += 32) {
+            const float n = nrm[w][h.t.group_of[i]];
+            xs[w][i] = xs[w][i] / (n > 1e-10f ? n : 1.0f);
+        }
+        __syncwarp();
+        for (uint32_t j = lane; j < d; j += 32) {
+            const uint32_t g = h.t.group_of[j];
+            const float *rj = h.t.rot + (uint64_t)j * d;
+            float y = 0.0f;
+#pragma unroll 4
+            for (uint32_t i = h.group_off[g]; i < h.group_off[g + 1]; ++i) y = fmaf(xs[w][i], __ldg(rj + i), y);
+            float t = (y - h.t.off[j]) * h.t.inv[j];
+            t = fminf(fmaxf(t, 0.0f), 255.0f);
+            codes[w][j] = h.t.lut[(uint32_t)h.t.cbidx[j] * 256u + (uint32_t)t];
+        }
+        __syncwarp();
+        if ((uint32_t)lane < ng) {
+            float cl = 0.0f;
+            for (uint32_t j = h.group_off[lane]; j < h.group_off[lane + 1]; ++j) {
+                const float cv = h.t.cent[h.t.cb_base[j] + codes[w][j]];
+                cl = fmaf(cv, cv, cl);
+            }
+            srow[w][lane] = __half_as_ushort(__float2half_rn(nrm[w][lane] / fmaxf(sqrtf(cl), 1e-10f)));
+        } else if ((uint32_t)lane < 8) {
+            srow[w][lane] = 0;
+        }
+        for (uint32_t b = lane; b < row_words * 4; b += 32) {
+            uint32_t v = 0;
+            if (b < ns / 2) v = (uint32_t)codes[w][2 * b] | ((uint32_t)codes[w][2 * b + 1] << 4);
+            else if (b < ns / 2 + (d - ns)) v = codes[w][ns + (b - ns / 2)];
+            ob[b] = (uint8_t)v;
+        }
+        __syncwarp();
+        const uint32_t dst_row = (a.row0 ? a.row0[s] : a.row0_scalar) + rr;
+        uint32_t *dst = reinterpret_cast<uint32_t *>(h.packed + (uint64_t)(a.seq_first + s) * h.k_seq_stride +
+                                                     (uint64_t)dst_row * h.row_stride);
+        for (uint32_t c = lane; c < row_words; c += 32) dst[c] = orow[w][c];
+        if ((uint32_t)lane < sc_words) {
+            uint32_t *sdst = reinterpret_cast<uint32_t *>(h.scales + (uint64_t)(a.seq_first + s) * h.s_seq_stride +
+                                                          (uint64_t)dst_row * h.scale_stride);
+            sdst[lane] = (uint32_t)srow[w][2 * lane] | ((uint32_t)srow[w][2 * lane + 1] << 16);
+        }
+        __syncwarp();
+    }
+    if (blockIdx.x == 0 && h.lengths) {
+        for (uint32_t s = threadIdx.x; s < a.seq_count; s += kThreads)
+            h.lengths[a.seq_first + s] = (a.row0 ? a.row0[s] : a.row0_scalar) + count;
+    }
+}
+
 template <int D>
 size_t encode_smem(uint32_t cent_alloc, uint32_t lut_bytes, uint32_t row_stride, uint32_t scale_stride) {
     const size_t ow = (row_stride / 4) | 1u, sw = scale_stride / 2 + 1;
@@ -259,6 +347,14 @@ cudaError_t run_encode(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uin
 
 cudaError_t launch_encode(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uint32_t max_ncb, cudaStream_t s) {
     if (a.count == 0 || a.seq_count == 0) return cudaSuccess;
+    const uint32_t total = a.count * a.seq_count;
+    if (total <= kWarpKeysMax) {
+        // a warp per key: at most 4 keys per CTA, so even one sequence's token uses a CTA
+        // and a decode step of a few hundred sequences spreads over the SMs
+        const uint32_t blocks = (total + kThreads / 32 - 1) / (kThreads / 32);
+        encode_warp_kernel<<<dim3(blocks, a.heads), kThreads, 0, s>>>(a, d, total);
+        return cudaGetLastError();
+    }
     if (d <= 16) return run_encode<16>(a, d, cent_alloc, max_ncb, s);
     if (d <= 32) return run_encode<32>(a, d, cent_alloc, max_ncb, s);
     if (d <= 64) return run_encode<64>(a, d, cent_alloc, max_ncb, s);

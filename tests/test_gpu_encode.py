@@ -174,3 +174,21 @@ def test_large_batch_sampled_bit_exact_and_deterministic(cuda):
     ref = oracle.encode(cfg, tab, kh, threads=4)
     np.testing.assert_array_equal(pa[rows], ref["packed"])
     np.testing.assert_array_equal(na[rows], ref["scales"])
+
+
+@pytest.mark.parametrize("name", mixed_cases() + ["config4"])
+def test_warp_and_bulk_encoders_agree(cuda, name):
+    """Appends of up to 4096 keys per head run one warp per key, larger ones one thread
+    per key; both give the oracle's bytes for every table shape (head dims 16 to 128,
+    nibble-only, byte-only and mixed rows)."""
+    z = load_config(name) if name.startswith("config") else load_mixed(name)
+    p, cfg, tab = params_tables(z)
+    kb = _edge_keys(np.random.default_rng(17), 5000, p.dim)
+    _, bulk_p, bulk_n = encode_gpu(cfg, tab, kb)                              # one 5000-key launch
+    _, warp_p, warp_n = encode_gpu(cfg, tab, kb, chunks=[1, 999, 4000])      # three small launches
+    ref = oracle.encode(cfg, tab, kb, threads=4)
+    np.testing.assert_array_equal(bulk_p, ref["packed"])
+    np.testing.assert_array_equal(bulk_n, ref["scales"])
+    np.testing.assert_array_equal(warp_p, ref["packed"])
+    np.testing.assert_array_equal(warp_n, ref["scales"])
+    assert device_status(0) == 0
