@@ -181,14 +181,10 @@ def run_reference(args, rank):
 def run_ours(args, rank, world, local_rank):
     import torch
     import bgtq
-    from bgtq import synthetic
-    dist = None
+    from bgtq import sharding, synthetic
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    dist = sharding.init_from_env("nccl", timeout_s=300.0, device=dev)
     p, cfg, tab = tables()
     B, T, L, H, R, d = args.batch, args.context, args.layers, KV_HEADS, GQA, HEAD_DIM
     steps, warmup = args.steps, args.warmup
@@ -247,10 +243,7 @@ def run_ours(args, rank, world, local_rank):
                 ev[layer][1].record(stream)
 
     def barrier():
-        torch.cuda.synchronize()
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
+        sharding.barrier(dist, torch.cuda.synchronize)
 
     for _ in range(warmup):
         step()
@@ -303,16 +296,9 @@ def run_ours(args, rank, world, local_rank):
         e2e = (e2e_s, e2e_steps)
 
     # ---- max over ranks, verification gather ----
-    stats = torch.tensor([elapsed, e2e[0] if e2e else 0.0], device=dev, dtype=torch.float64)
-    if dist:
-        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-        sums = torch.stack([o.double().sum() for o in outs]).sum().reshape(1)
-        gathered = [torch.zeros_like(sums) for _ in range(world)]
-        dist.all_gather(gathered, sums)
-        finite = all(bool(torch.isfinite(g).all()) for g in gathered)
-    else:
-        finite = all(bool(torch.isfinite(o).all()) for o in outs)
-    elapsed_max, e2e_max = float(stats[0]), float(stats[1])
+    elapsed_max, e2e_max = sharding.max_over_ranks([elapsed, e2e[0] if e2e else 0.0], dist, dev)
+    checksums = sharding.gather_checksums(outs, dist, dev)
+    finite = all(np.isfinite(c) for c in checksums)
     status = bgtq.device_status(local_rank)
     if rank == 0:
         hbm, peak_kind = peaks()
@@ -356,7 +342,9 @@ def run_ours(args, rank, world, local_rank):
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             "clocks": clk,
-            "checks": {"outputs_finite": finite, "device_status": status, "setup_s": setup_s},
+            "checks": {"outputs_finite": finite, "device_status": status, "setup_s": setup_s,
+                       "output_checksums": checksums,
+                       "sequences": [sharding.sequence_range(B, r)[0] for r in range(world)]},
         }
         if e2e:
             h2d = L * (q[0].numel() * 4 + knew[0].numel() * 2 + vnew[0].numel() * 2)

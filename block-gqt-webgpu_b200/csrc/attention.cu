@@ -67,7 +67,19 @@ __global__ void probs_kernel(const float *logits, const float *lse, float *probs
 
 }  // namespace
 
-uint32_t attention_tile_tokens(uint32_t d) { return (uint32_t)(dim_template(d) <= 64 ? 64 : 32); }
+// The kernel's own tile size (Geo<D>::TT): split boundaries and shared-memory plans use it,
+// and whole-tile copies stay inside the capacity because it divides the row padding.
+uint32_t attention_tile_tokens(uint32_t d) {
+    static_assert(kTileRows % attn::Geo<16>::TT == 0 && kTileRows % attn::Geo<32>::TT == 0 &&
+                      kTileRows % attn::Geo<64>::TT == 0 && kTileRows % attn::Geo<128>::TT == 0,
+                  "tiles must divide the capacity padding");
+    switch (dim_template(d)) {
+        case 16: return attn::Geo<16>::TT;
+        case 32: return attn::Geo<32>::TT;
+        case 64: return attn::Geo<64>::TT;
+        default: return attn::Geo<128>::TT;
+    }
+}
 
 size_t attention_smem_bytes(KKind kk, int v_f32, uint32_t d, uint32_t rows, uint32_t row_stride,
                             uint32_t scale_stride, uint32_t max_cent) {
