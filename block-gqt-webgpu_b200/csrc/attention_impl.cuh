@@ -31,7 +31,9 @@
 //                  group's FP16 scale applied once at its end; per-pair query records and
 //                  codebook offsets come from small shared tables built per (sequence,
 //                  head).
-//   softmax        online, warp-wide max/sum per tile.
+//   softmax        online, in log2 units, with per-lane running sums (reduced once at the
+//                  end) and a lazily moved maximum: a warp vote skips the warp-wide max and
+//                  the rescale of O unless a score exceeds the running maximum by 2^3.
 //   P.V            tensor cores (mma.sync m16n8k16, FP16 in, FP32 accumulate) for FP16 V of
 //                  64/128 dims: P is scaled by 2^12 and split into high and low FP16 parts
 //                  (about 22 significant bits) that occupy fragment rows 0-7 and 8-15 of
@@ -49,9 +51,16 @@ namespace attn {
 
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
 constexpr uint32_t kWaitLimit = 1u << 22;
-constexpr float kPScale = 4096.0f, kPUnscale = 1.0f / 4096.0f;
+// Scores are kept in log2 units (the query records carry log2(e)/sqrt(d)), and
+// probabilities are scaled by 2^kPShift so that their FP16 high/low split for the P.V MMA
+// keeps about 22 significant bits; the running sums carry the same factor, which cancels
+// in O / l and is taken out of the log-sum-exp.
+constexpr float kPShift = 12.0f;
+// Lazy rescaling: the running maximum moves only when a score exceeds it by more than
+// kLazy (log2 units), so probabilities stay below 2^(kPShift + kLazy) = 32768, inside FP16.
+constexpr float kLazy = 3.0f;
 
 template <int D>
 struct Geo {
@@ -115,7 +124,7 @@ inline Plan make_plan(KKind kk, int v_f32, uint32_t D, uint32_t QP, uint32_t TT,
     p.stage = off;
     off += kWarps * p.warp_bytes;
     p.pbuf = off;
-    off = align16(off + kWarps * TT * QP * 4u);
+    off = align16(off + kWarps * TT * (QM ? QM : QP) * 4u);
     p.bars = off;
     off += kWarps * 4u * 8u;  // per warp: K barriers 0, 1 and the V barrier
     p.total = align16(off);
@@ -261,7 +270,7 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
     const uint32_t krow = h.row_stride, ns = h.ns;
     uint32_t row[TPL];
     uint32_t sw[TPL][4];
-    float2 part[TPL][QM];
+    float2 part[TPL][QM], acc2[TPL][QM];
 #pragma unroll
     for (int tt = 0; tt < TPL; ++tt) {
         const int tl = tt * 32 + lane;
@@ -274,7 +283,7 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
             sw[tt][0] = v.x; sw[tt][1] = v.y; sw[tt][2] = v.z; sw[tt][3] = v.w;
         }
 #pragma unroll
-        for (int r = 0; r < QM; ++r) { acc[tt][r] = 0.0f; part[tt][r] = make_float2(0.0f, 0.0f); }
+        for (int r = 0; r < QM; ++r) { acc2[tt][r] = make_float2(0.0f, 0.0f); part[tt][r] = make_float2(0.0f, 0.0f); }
     }
     // one dimension pair: record + the two pre-scaled indices of each token
     auto pair = [&](const uint32_t *rp, const uint32_t (&ia)[TPL], const uint32_t (&ib)[TPL]) {
@@ -364,26 +373,38 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
         }
         const uint32_t nblk = nfull + (rem ? 1u : 0u);
         rix += 4 * nblk;
-        // group end: apply this group's FP16 scale, move to the next scale
+        // group end.  part holds the running (unscaled) sum over all groups so far, C_g;
+        // sum_g s_g (C_g - C_{g-1}) = sum_g (s_g - s_{g+1}) C_g with s past the last group
+        // = 0 (the scale rows are zero-padded), so no per-group reset is needed.
 #pragma unroll
         for (int tt = 0; tt < TPL; ++tt) {
-            const float sc = half_lo(sw[tt][0]);
+            const float ds = half_lo(sw[tt][0]) - half_lo(sw[tt][0] >> 16);
+            const float2 ds2 = make_float2(ds, ds);
 #pragma unroll
-            for (int r = 0; r < QM; ++r) {
-                acc[tt][r] = fmaf(sc, part[tt][r].x + part[tt][r].y, acc[tt][r]);
-                part[tt][r] = make_float2(0.0f, 0.0f);
-            }
+            for (int r = 0; r < QM; ++r) acc2[tt][r] = __ffma2_rn(ds2, part[tt][r], acc2[tt][r]);
             sw[tt][0] = __funnelshift_r(sw[tt][0], sw[tt][1], 16);
             sw[tt][1] = __funnelshift_r(sw[tt][1], sw[tt][2], 16);
             sw[tt][2] = __funnelshift_r(sw[tt][2], sw[tt][3], 16);
             sw[tt][3] >>= 16;
         }
     }
+#pragma unroll
+    for (int tt = 0; tt < TPL; ++tt)
+#pragma unroll
+        for (int r = 0; r < QM; ++r) acc[tt][r] = acc2[tt][r].x + acc2[tt][r].y;
     (void)d;
 }
 
+// Minimum resident CTAs per SM the register allocation must allow: the packed kernels of
+// head dims up to 64 fit three CTAs in shared memory, and giving the compiler the
+// registers of exactly three (up to 168 per thread) schedules the lookup loads deeper.
+template <int D, int QM, KKind KK>
+struct MinBlocks {
+    static constexpr int value = (KK == KKind::Packed && D <= 64 && QM <= 4) ? 3 : 1;
+};
+
 template <int D, int QM, KKind KK, bool VF32>
-__global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ AttnArgs a, const Plan pl, uint32_t d) {
+__global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_kernel(const __grid_constant__ AttnArgs a, const Plan pl, uint32_t d) {
     constexpr int TPL = Geo<D>::TPL, TT = Geo<D>::TT, QP = QPad<QM>::QP;
     constexpr bool MMA = UseMma<D, VF32>::value;
     constexpr int VSZ = VF32 ? 4 : 2, VEC = 16 / VSZ, LPT = D / VEC, TPS = 32 / LPT;
@@ -403,7 +424,7 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
     float *cent_s = reinterpret_cast<float *>(smem + pl.cent);
     unsigned char *rec = smem + pl.qrec;
     float *qrec_s = reinterpret_cast<float *>(rec);
-    float *pbuf = reinterpret_cast<float *>(smem + pl.pbuf) + w * TT * QP;  // [QP][TT]
+    float *pbuf = reinterpret_cast<float *>(smem + pl.pbuf) + w * TT * QM;  // [QM][TT]
     const uint32_t bar0 = smem_u32(smem + pl.bars) + (uint32_t)w * 32u, vbar = bar0 + 16u;
     __shared__ uint32_t s_last;
 
@@ -420,6 +441,10 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
         }
     }
     if (a.logits) tend = len;
+    uint32_t pmin = 0xffffffffu;
+#pragma unroll
+    for (int r = 0; r < QM; ++r)
+        if ((uint32_t)r < R) pmin = min(pmin, pos[r]);
     const uint32_t t0 = split * a.tokens_per_split;
     const uint32_t t1 = min(t0 + a.tokens_per_split, tend);
 
@@ -557,39 +582,49 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
         }
 
         // ---- masking, optional raw-logit capture, online softmax ----
+        // A tile wholly inside the split and, when causal, at or before every row's position
+        // needs no per-token mask.
+        const bool full = n == (uint32_t)TT && (!a.causal || at + (uint32_t)TT - 1u <= pmin);
         float alpha[QM];
+        bool rescale = false;
 #pragma unroll
         for (int r = 0; r < QM; ++r) {
+            const bool live = (uint32_t)r < R;
             float lg[TPL];
-            float tm = -INFINITY;
+            bool up = false;
 #pragma unroll
             for (int tt = 0; tt < TPL; ++tt) {
                 const uint32_t tl = tt * 32 + lane, tok = at + tl;
-                const bool valid = tl < n && (uint32_t)r < R && (!a.causal || tok <= pos[r]);
+                const bool valid = live && (full || (tl < n && (!a.causal || tok <= pos[r])));
                 lg[tt] = valid ? acc[tt][r] : -INFINITY;
-                if (a.logits && tl < n && (uint32_t)r < R)
-                    a.logits[(((uint64_t)s * a.heads + hd) * R + r) * a.logit_stride + tok] = lg[tt];
-                tm = fmaxf(tm, lg[tt]);
+                up |= lg[tt] > m[r] + kLazy;
             }
-            tm = warp_max(tm);
-            const float mnew = fmaxf(m[r], tm);
-            alpha[r] = mnew == -INFINITY ? 1.0f : exp2f((m[r] - mnew) * kLog2e);
+            if (a.logits && live) {
+#pragma unroll
+                for (int tt = 0; tt < TPL; ++tt) {
+                    const uint32_t tl = tt * 32 + lane, tok = at + tl;
+                    if (tl < n) a.logits[(((uint64_t)s * a.heads + hd) * R + r) * a.logit_stride + tok] = lg[tt] * kLn2;
+                }
+            }
+            alpha[r] = 1.0f;
+            if (__any_sync(0xffffffffu, up)) {
+                float tm = lg[0];
+#pragma unroll
+                for (int tt = 1; tt < TPL; ++tt) tm = fmaxf(tm, lg[tt]);
+                const float mnew = fmaxf(m[r], warp_max(tm));
+                alpha[r] = exp2f(m[r] - mnew);  // 0 on the first live tile: l and O are still 0
+                m[r] = mnew;
+                rescale = true;
+            }
+            const float mref = m[r] - kPShift;
             float ps = 0.0f;
 #pragma unroll
             for (int tt = 0; tt < TPL; ++tt) {
-                const float p = lg[tt] == -INFINITY ? 0.0f : exp2f((lg[tt] - mnew) * kLog2e);
+                const float p = lg[tt] == -INFINITY ? 0.0f : exp2f(lg[tt] - mref);
                 pbuf[r * TT + tt * 32 + lane] = p;
                 ps += p;
             }
-            ps = warp_sum(ps);
-            l[r] = l[r] * alpha[r] + ps;
-            m[r] = mnew;
-        }
-        if constexpr (QP > QM) {
-#pragma unroll
-            for (int tt = 0; tt < TPL; ++tt)
-#pragma unroll
-                for (int r = QM; r < QP; ++r) pbuf[r * TT + tt * 32 + lane] = 0.0f;
+            l[r] = fmaf(l[r], alpha[r], ps);  // this lane's share; summed over lanes at the end
         }
         __syncwarp();
         if (!two && more) issue_k(k + kWarps, 0);
@@ -605,21 +640,22 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
             // fragment row g = query (high part of P), row g + 8 = the same query (low part);
             // column pair 2c/2c+1 (+8) = token (A) or dim (C)
             const int g = lane >> 2, c = lane & 3;
-            float ag = 1.0f;
+            if (rescale) {
+                float ag = 1.0f;
 #pragma unroll
-            for (int r = 0; r < QM; ++r) ag = g == r ? alpha[r] : ag;
+                for (int r = 0; r < QM; ++r) ag = g == r ? alpha[r] : ag;
 #pragma unroll
-            for (int i = 0; i < NT * 4; ++i) O[i] *= ag;
+                for (int i = 0; i < NT * 4; ++i) O[i] *= ag;
+            }
             const uint32_t vb_s = smem_u32(vb);
             const int mi = lane >> 3, ri = lane & 7;
 #pragma unroll
             for (int kb16 = 0; kb16 < TT / 16; ++kb16) {
                 float2 pa = make_float2(0.0f, 0.0f), pb = make_float2(0.0f, 0.0f);
-                if (g < QP) {
+                if (g < QM) {
                     pa = *reinterpret_cast<const float2 *>(pbuf + g * TT + kb16 * 16 + 2 * c);
                     pb = *reinterpret_cast<const float2 *>(pbuf + g * TT + kb16 * 16 + 2 * c + 8);
                 }
-                pa.x *= kPScale; pa.y *= kPScale; pb.x *= kPScale; pb.y *= kPScale;
                 const __half2 ha = __floats2half2_rn(pa.x, pa.y), hb = __floats2half2_rn(pb.x, pb.y);
                 const float2 fa = __half22float2(ha), fb = __half22float2(hb);
                 const __half2 la = __floats2half2_rn(pa.x - fa.x, pa.y - fa.y);
@@ -640,10 +676,12 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
                 }
             }
         } else {
+            if (rescale) {
 #pragma unroll
-            for (int r = 0; r < QM; ++r)
+                for (int r = 0; r < QM; ++r)
 #pragma unroll
-                for (int e = 0; e < VEC; ++e) O[r * VEC + e] *= alpha[r];
+                    for (int e = 0; e < VEC; ++e) O[r * VEC + e] *= alpha[r];
+            }
             const int slot = lane / LPT, dl = (lane % LPT) * VEC;
             const uint32_t steps = (n + TPS - 1) / TPS;
 #pragma unroll 4
@@ -684,6 +722,8 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
     }
 
     // ---- merge the warps of this CTA ----
+#pragma unroll
+    for (int r = 0; r < QM; ++r) l[r] = warp_sum(l[r]);
     if constexpr (!MMA) {
 #pragma unroll
         for (int i = 0; i < OS; ++i)
@@ -699,8 +739,8 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
         if (g < QM) {
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                mO[(w * QP + g) * D + nt * 8 + 2 * c] = (O[nt * 4 + 0] + O[nt * 4 + 2]) * kPUnscale;
-                mO[(w * QP + g) * D + nt * 8 + 2 * c + 1] = (O[nt * 4 + 1] + O[nt * 4 + 3]) * kPUnscale;
+                mO[(w * QP + g) * D + nt * 8 + 2 * c] = O[nt * 4 + 0] + O[nt * 4 + 2];
+                mO[(w * QP + g) * D + nt * 8 + 2 * c + 1] = O[nt * 4 + 1] + O[nt * 4 + 3];
             }
         }
     } else {
@@ -727,13 +767,13 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
 #pragma unroll
         for (int ww = 0; ww < kWarps; ++ww) {
             const float mw = mm[ww * QP + r];
-            const float f = mw == -INFINITY ? 0.0f : exp2f((mw - M) * kLog2e);
+            const float f = mw == -INFINITY ? 0.0f : exp2f(mw - M);
             L = fmaf(ml[ww * QP + r], f, L);
             Ov = fmaf(mO[(ww * QP + r) * D + dd], f, Ov);
         }
         if (a.splits == 1) {
             a.out[(obase + r) * d + dd] = Ov / L;
-            if (dd == 0 && a.lse) a.lse[obase + r] = M + logf(L);
+            if (dd == 0 && a.lse) a.lse[obase + r] = (M + log2f(L) - kPShift) * kLn2;
         } else {
             float *pp = a.part + ((((uint64_t)split * a.seq_count + s) * a.heads + hd) * R + r) * (uint64_t)(d + 2);
             pp[dd] = Ov;
@@ -759,12 +799,12 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __grid_constant__ 
                 float L = 0.0f, Ov = 0.0f;
                 for (uint32_t sp = 0; sp < a.splits; ++sp) {
                     const float ms = __ldcg(pp + sp * sstride + d);
-                    const float f = ms == -INFINITY ? 0.0f : exp2f((ms - M) * kLog2e);
+                    const float f = ms == -INFINITY ? 0.0f : exp2f(ms - M);
                     L = fmaf(__ldcg(pp + sp * sstride + d + 1), f, L);
                     Ov = fmaf(__ldcg(pp + sp * sstride + dd), f, Ov);
                 }
                 a.out[(obase + r) * d + dd] = Ov / L;
-                if (dd == 0 && a.lse) a.lse[obase + r] = M + logf(L);
+                if (dd == 0 && a.lse) a.lse[obase + r] = (M + log2f(L) - kPShift) * kLn2;
             }
             if (tid == 0) a.counters[s * a.heads + hd] = 0u;
         }
@@ -786,7 +826,7 @@ __global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant__ AttnA
         qraw[idx] = packed ? qg[r * d + h.perm[i]] : qg[r * d + i];
     }
     __syncthreads();
-    const float inv_sqrt_d = 1.0f / sqrtf((float)d);
+    const float qscale = kLog2e / sqrtf((float)d);  // scores in log2 units
     float *out = a.qt + ((uint64_t)s * a.heads + hd) * (uint64_t)(D * QP);
     for (uint32_t idx = threadIdx.x; idx < D * QP; idx += blockDim.x) {
         const uint32_t j = idx / QP, r = idx % QP;
@@ -799,7 +839,7 @@ __global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant__ AttnA
             } else {
                 v = qraw[r * d + j];
             }
-            v *= inv_sqrt_d;
+            v *= qscale;
         }
         out[idx] = v;
     }
