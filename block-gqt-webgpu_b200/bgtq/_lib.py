@@ -85,6 +85,7 @@ SIGNATURES = {
     "bgtq_attention_last_launches": (I32, [P, C.POINTER(U32)]),
     "bgtq_device_status": (I32, [C.c_int, C.POINTER(U32)]),
     "bgtq_attend_static": (I32, [U32, P, P, P, P, C.c_int, U32, U32, U32, P, P]),
+    "bgtq_attend_prefill": (I32, [P, P, U32, U32, U32, U32, U32, P, C.c_int, P]),
 }
 
 _lib = None

@@ -65,6 +65,29 @@ class GroupedAttention:
                   None if probs is None else C.c_void_p(probs.data_ptr()), 0, C.c_void_p(int(st)))
         return o
 
+    def prefill(self, q, pos_first: int = 0, seq_first: int = 0, out=None, stream=None):
+        """Causal prefill (bgtq_attend_prefill): q [seq_count, n, heads * gqa, dim] holds the
+        queries at positions pos_first .. pos_first + n - 1 of sequences seq_first ..;
+        query head h * gqa + r uses KV head h and sees keys 0 .. its position.  NumPy in ->
+        NumPy out (synchronous); a CUDA tensor in -> a CUDA tensor out (stream-ordered)."""
+        if q.ndim != 4 or q.shape[2] % self.heads or q.shape[3] != self.dim:
+            raise _lib.RangeError(_lib.EINVAL, "Invalid Q/K/V shape or positions")
+        seq_count, n, gqa = int(q.shape[0]), int(q.shape[1]), q.shape[2] // self.heads
+        if isinstance(q, np.ndarray) or not hasattr(q, "data_ptr"):
+            qa = np.ascontiguousarray(np.asarray(q, dtype=np.float32))
+            o = np.zeros(qa.shape, np.float32) if out is None else out
+            _lib.call("bgtq_attend_prefill", self._handle, qa.ctypes.data, pos_first, n, gqa, seq_first, seq_count,
+                      o.ctypes.data, 1, None)
+            return o
+        import torch
+        if not q.is_contiguous() or q.dtype != torch.float32:
+            raise _lib.RangeError(_lib.EINVAL, "Invalid Q/K/V shape or positions")
+        o = torch.empty_like(q) if out is None else out
+        st = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
+        _lib.call("bgtq_attend_prefill", self._handle, C.c_void_p(q.data_ptr()), pos_first, n, gqa, seq_first,
+                  seq_count, C.c_void_p(o.data_ptr()), 0, C.c_void_p(int(st)))
+        return o
+
     @property
     def last_splits(self) -> int:
         n = C.c_uint32()

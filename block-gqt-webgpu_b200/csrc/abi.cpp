@@ -658,6 +658,35 @@ void bgtq_attention_destroy(bgtq_attention *a) {
     delete a;
 }
 
+}  // extern "C"
+
+namespace {
+// Kernel arguments of one packed-key head with its value store.
+void fill_packed_head(AttnHead &ah, const bgtq_keys *k, const bgtq_values *v) {
+    const size_t vsz = v->dtype == BGTQ_F32 ? 4 : 2;
+    ah.v = v->data;
+    ah.v_seq_stride = (uint64_t)v->cap_alloc * v->D * vsz;
+    ah.k = k->rows;
+    ah.k_seq_stride = (uint64_t)k->cap_alloc * k->row_stride;
+    ah.row_stride = k->row_stride;
+    ah.scales = k->scales;
+    ah.s_seq_stride = (uint64_t)k->cap_alloc * k->scale_stride;
+    ah.scale_stride = k->scale_stride;
+    ah.rot = k->dt.rot;
+    ah.cent = k->dt.cent;
+    ah.perm = k->dt.perm;
+    ah.group_of = k->dt.group_of;
+    ah.ns = k->L.ns;
+    ah.ng = k->L.ng;
+    ah.n_cent = (uint32_t)k->L.cent_compact.size();
+    for (int i = 0; i < 4; ++i) ah.bound_mask[i] = k->L.bound_mask[i];
+    for (int gi = 0; gi <= kMaxGroups; ++gi) ah.group_off[gi] = k->L.group_off[gi];
+    for (uint32_t j = 0; j < (uint32_t)kMaxDim; ++j) ah.cb_base[j] = j < k->dim ? k->L.cb_base[j] : (uint16_t)ah.n_cent;
+}
+}  // namespace
+
+extern "C" {
+
 bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *positions, int causal, uint32_t rows,
                         uint32_t seq_first, uint32_t seq_count, float *out, float *logits, float *probs, int host,
                         void *stream_) {
@@ -732,23 +761,7 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
         ah.v = v->data;
         ah.v_seq_stride = (uint64_t)v->cap_alloc * v->D * vsz;
         if (kk == KKind::Packed) {
-            ah.k = k->rows;
-            ah.k_seq_stride = (uint64_t)k->cap_alloc * k->row_stride;
-            ah.row_stride = k->row_stride;
-            ah.scales = k->scales;
-            ah.s_seq_stride = (uint64_t)k->cap_alloc * k->scale_stride;
-            ah.scale_stride = k->scale_stride;
-            ah.rot = k->dt.rot;
-            ah.cent = k->dt.cent;
-            ah.perm = k->dt.perm;
-            ah.group_of = k->dt.group_of;
-            ah.ns = k->L.ns;
-            ah.ng = k->L.ng;
-            ah.n_cent = (uint32_t)k->L.cent_compact.size();
-            for (int i = 0; i < 4; ++i) ah.bound_mask[i] = k->L.bound_mask[i];
-            for (int gi = 0; gi <= kMaxGroups; ++gi) ah.group_off[gi] = k->L.group_off[gi];
-            for (uint32_t j = 0; j < (uint32_t)kMaxDim; ++j)
-                ah.cb_base[j] = j < k->dim ? k->L.cb_base[j] : (uint16_t)ah.n_cent;
+            fill_packed_head(ah, k, v);
             max_cent = std::max(max_cent, ah.n_cent);
         } else if (kk == KKind::F16) {
             ah.k = k->rows;
@@ -811,6 +824,72 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
         if (logits) CK(cudaMemcpyAsync(logits, dlogits, nl * 4, cudaMemcpyDeviceToHost, stream), "logit download");
         if (probs) CK(cudaMemcpyAsync(probs, dprobs, nl * 4, cudaMemcpyDeviceToHost, stream), "probability download");
         CK(cudaStreamSynchronize(stream), "attend");
+    }
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_attend_prefill(bgtq_attention *at, const float *q, uint32_t pos_first, uint32_t n, uint32_t gqa,
+                                uint32_t seq_first, uint32_t seq_count, float *out, int host, void *stream_) {
+    if (!at || !q || !out) return fail(BGTQ_EINVAL, "Invalid Q/K/V shape or positions");
+    if (!n || !seq_count || gqa < 1 || gqa > (uint32_t)kMaxRows || (uint64_t)seq_first + seq_count > at->sequences ||
+        (uint64_t)pos_first + n > 0xffffffffull)
+        return fail(BGTQ_EINVAL, "Invalid Q/K/V shape or positions");
+    const uint32_t d = at->dim, H = at->heads;
+    if (d > 64) return fail(BGTQ_EINVAL, "prefill needs head dim <= 64");
+    for (uint32_t h = 0; h < H; ++h)
+        if (at->keys[h]->kind != BGTQ_KEYS_PACKED || at->values[h]->dtype != BGTQ_F16)
+            return fail(BGTQ_EINVAL, "prefill needs packed keys and FP16 values");
+    // every query position must have its key appended: lengths >= pos_first + n
+    for (uint32_t s = 0; s < seq_count; ++s) {
+        const uint32_t seq = seq_first + s, L = at->keys[0]->lengths[seq];
+        for (uint32_t h = 0; h < H; ++h)
+            if (at->keys[h]->lengths[seq] != L || at->values[h]->lengths[seq] != L)
+                return fail(BGTQ_EBUSY, "K/V lengths must match and be nonzero");
+        if ((uint64_t)pos_first + n > L) return fail(BGTQ_EINVAL, "Invalid Q/K/V shape or positions");
+    }
+    const size_t nq = (size_t)seq_count * n * H * gqa * d;
+    if (host)
+        for (size_t i = 0; i < nq; ++i)
+            if (!std::isfinite(q[i])) return fail(BGTQ_ENONFINITE, "Q: finite inputs required");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+    DeviceGuard g(at->device);
+    if (!g.ok) return fail(BGTQ_ECUDA, "cannot select device");
+    const float *dq = q;
+    float *dout = out;
+    if (host) {
+        CK(at->q_dev.ensure(nq * 4), "Q staging");
+        CK(at->out_dev.ensure(nq * 4), "output staging");
+        CK(cudaMemcpyAsync(at->q_dev.p, q, nq * 4, cudaMemcpyHostToDevice, stream), "Q upload");
+        dq = static_cast<const float *>(at->q_dev.p);
+        dout = static_cast<float *>(at->out_dev.p);
+    }
+    CK(at->prefill_qt.ensure((size_t)seq_count * n * H * gqa * 64 * 4), "query record allocation");
+    PrefillArgs a;
+    std::memset(&a, 0, sizeof(a));
+    uint32_t max_cent = 0;
+    for (uint32_t h = 0; h < H; ++h) {
+        fill_packed_head(a.head[h], at->keys[h], at->values[h]);
+        max_cent = std::max(max_cent, a.head[h].n_cent);
+    }
+    a.q = dq;
+    a.qt = static_cast<float *>(at->prefill_qt.p);
+    a.out = dout;
+    a.lengths = at->keys[0]->d_lengths;
+    a.status = device_status_word(at->device);
+    a.seq_first = seq_first;
+    a.seq_count = seq_count;
+    a.heads = H;
+    a.gqa = gqa;
+    a.n = n;
+    a.pos_first = pos_first;
+    a.d = d;
+    cudaError_t e = launch_prefill(a, max_cent, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+    at->last_splits = 1;
+    at->last_launches = 2;  // query rotation + prefill attention
+    if (host) {
+        CK(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, stream), "output download");
+        CK(cudaStreamSynchronize(stream), "prefill");
     }
     return BGTQ_OK;
 }

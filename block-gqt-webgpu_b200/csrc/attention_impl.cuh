@@ -492,15 +492,17 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
 
     // whole tiles: rows past the sequence end exist (capacity padded to 64, zero filled)
     uint32_t pending = 0;  // bit st: K buffer st has a copy in flight; bit 2: the V buffer
+    // this head's tile sizes: the plan's buffers fit the widest head of the launch
+    const uint32_t kb_h = (uint32_t)TT * krow, sb_h = KK == KKind::Packed ? (uint32_t)TT * srow : 0u;
     auto issue_k = [&](uint32_t k, int st) {
         if (lane == 0) {
             const uint32_t at = t0 + k * TT;
             unsigned char *buf = kstage0 + (size_t)st * pl.kstage_bytes;
             const uint32_t bar = bar0 + (uint32_t)st * 8u;
             fence_proxy_async();
-            mbar_expect_tx(bar, pl.kbytes + pl.sbytes);
-            bulk_g2s(smem_u32(buf), kbase + (uint64_t)at * krow, pl.kbytes, bar);
-            if (KK == KKind::Packed) bulk_g2s(smem_u32(buf + soff), sbase + (uint64_t)at * srow, pl.sbytes, bar);
+            mbar_expect_tx(bar, kb_h + sb_h);
+            bulk_g2s(smem_u32(buf), kbase + (uint64_t)at * krow, kb_h, bar);
+            if (KK == KKind::Packed) bulk_g2s(smem_u32(buf + soff), sbase + (uint64_t)at * srow, sb_h, bar);
         }
         pending |= 1u << st;
     };
@@ -815,7 +817,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
 // q_r[perm[i]] / sqrt(d) for packed keys (the query rotated into the code domain), or
 // q_r[j] / sqrt(d) for dense keys; zero for j >= d and r >= rows.  One CTA per
 // (head, sequence), computed once instead of once per split.
-__global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant__ AttnArgs a, uint32_t d, uint32_t D,
+static __global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant__ AttnArgs a, uint32_t d, uint32_t D,
                                                    uint32_t QP, int packed) {
     __shared__ float qraw[kMaxRows * kMaxDim];
     const uint32_t hd = blockIdx.x, s = blockIdx.y, R = a.rows;

@@ -112,6 +112,17 @@ struct AttnArgs {
     uint32_t seq_first, seq_count, heads, rows, splits, tokens_per_split, causal, logit_stride;
 };
 
+// Prefill: n query positions per sequence, all gqa query heads of each KV head.
+struct PrefillArgs {
+    AttnHead head[kMaxHeads];
+    const float *q;            // [S][n][heads*gqa][d]
+    float *qt;                 // [S][n][heads*gqa][64] code-domain queries (rotation kernel)
+    float *out;                // [S][n][heads*gqa][d]
+    const uint32_t *lengths;   // [sequences] key lengths (device), indexed seq_first + s
+    uint32_t *status;
+    uint32_t seq_first, seq_count, heads, gqa, n, pos_first, d;
+};
+
 struct ReconArgs {
     DeviceTables t;
     const uint8_t *packed;
@@ -137,6 +148,8 @@ enum class KKind { Packed, F16, F32 };
 cudaError_t launch_attention(const AttnArgs &a, KKind kk, int v_f32, uint32_t d, uint32_t max_cent,
                              uint32_t max_len, uint32_t forced_splits, uint32_t max_splits, uint32_t *splits_out,
                              cudaStream_t s);
+// Causal prefill attention (packed keys, FP16 values, head dim <= 64).
+cudaError_t launch_prefill(const PrefillArgs &a, uint32_t max_cent, cudaStream_t s);
 cudaError_t launch_probs(const float *logits, const float *lse, float *probs, uint64_t rows, uint32_t tokens,
                          uint32_t stride, cudaStream_t s);
 // Shared-memory bytes the attention kernel needs for a launch; 0 if unsupported.

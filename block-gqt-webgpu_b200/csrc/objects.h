@@ -68,6 +68,6 @@ struct bgtq_attention {
     uint32_t *counters = nullptr;
     float *lse = nullptr;
     float *qt = nullptr;
-    bgtq::DevBuf q_dev, pos_dev, out_dev, logits_dev, probs_dev;
+    bgtq::DevBuf q_dev, pos_dev, out_dev, logits_dev, probs_dev, prefill_qt;
     uint32_t forced_splits = 0, last_splits = 0, last_launches = 0, max_splits = 64;
 };

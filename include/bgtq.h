@@ -189,6 +189,19 @@ bgtq_status bgtq_attend(bgtq_attention *a, const float *q, const uint32_t *posit
                         uint32_t seq_first, uint32_t seq_count, float *out, float *logits, float *probs, int host,
                         void *stream);
 
+/* Causal prefill over packed keys: the model path's chunked prefill (src/model/decoder.ts:
+ * 30-81; compressed_dot / softmax / weighted, src/model/compressed-dot.wgsl:14-31 and
+ * src/model/attention.wgsl:13-39) for n query positions pos_first .. pos_first+n-1 of
+ * sequences [seq_first, seq_first+seq_count), all gqa query heads of each of the object's
+ * KV heads (query head h*gqa + r uses KV head h).  q and out: [seq_count][n][heads*gqa][dim]
+ * FP32, token-major like a model's activations; a row at position p sees keys 0..p.
+ * Requires packed keys, FP16 values, dim <= 64, gqa 1..8, and keys/values appended up to
+ * pos_first+n on every sequence (equal K/V lengths).  host != 0: q/out are host memory
+ * (staged, call synchronises).  Errors: BGTQ_EINVAL (shape, kind, positions), BGTQ_EBUSY
+ * (K/V lengths), BGTQ_ENONFINITE (host Q). */
+bgtq_status bgtq_attend_prefill(bgtq_attention *a, const float *q, uint32_t pos_first, uint32_t n, uint32_t gqa,
+                                uint32_t seq_first, uint32_t seq_count, float *out, int host, void *stream);
+
 /* Split-KV factor the last bgtq_attend used (diagnostics / benches). */
 bgtq_status bgtq_attention_last_splits(const bgtq_attention *a, uint32_t *splits_out);
 /* Force a split-KV factor (0 = automatic). */
