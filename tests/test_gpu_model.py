@@ -1,0 +1,121 @@
+"""Model-path decoder (bgtq.model.Decoder) against a plain PyTorch FP32 decoder whose
+attention is the oracle on the library's own codes.
+
+The reference decoder below restates src/model/decoder.ts:31-81 in torch (embedding,
+RMSNorm, projections, split-half RoPE, SiLU-gated MLP, tied lm_head); its keys are the
+oracle's reconstruction of the packed cache the Decoder wrote, its values the FP16-rounded
+projections, and its attention is oracle.attention in double precision.  Both run the same
+torch GEMMs on the same device, so the only difference is the attention kernels: logits
+must agree to 1e-4 abs + 1e-3 rel through a prefill chunk and decode steps, for a
+SmolLM2-like (GQA 3, no bias) and a Qwen-like (GQA 3 x 2 KV heads, QKV bias) geometry.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from bgtq import device_status
+from bgtq.model import Decoder, ModelGeometry, random_weights
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+GEOMS = {
+    "smollm2-like": ModelGeometry("smollm2", 2, 192, 256, 3, 1, 1e5, 1e-5, 500, False),
+    "qwen-like": ModelGeometry("qwen2", 2, 384, 512, 6, 2, 1e6, 1e-6, 700, True),
+}
+
+
+def _tables(g):
+    zh = np.load(GOLDEN / "smollm2_heads.npz")
+    return [(zh[f"h{i % 6}_config"], zh[f"h{i % 6}_table"]) for i in range(g.layers * g.kv_heads)]
+
+
+def _reference_forward(dec, w, g, tokens, start, tables):
+    """One forward of the restated decoder; K from the Decoder's packed cache."""
+    import torch
+    B, n = tokens.shape
+    h = w["model.embed_tokens.weight"][tokens].float()
+
+    def norm(x, wt):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + g.rms_eps) * wt.float()
+
+    pairs = g.head_dim // 2
+    inv = torch.pow(torch.tensor(float(g.rope_theta), device=h.device),
+                    -torch.arange(pairs, device=h.device, dtype=torch.float32) / pairs)
+    pos = torch.arange(start, start + n, device=h.device, dtype=torch.float32)
+    ang = pos[:, None] * inv[None, :]
+    c, s = torch.cos(ang)[None, :, None, :], torch.sin(ang)[None, :, None, :]
+
+    def rope(x):
+        a, b = x[..., :pairs], x[..., pairs:]
+        return torch.cat([a * c - b * s, b * c + a * s], -1)
+
+    for layer in range(g.layers):
+        p = f"model.layers.{layer}."
+        x = norm(h, w[p + "input_layernorm.weight"])
+        lin = lambda t, nm, b=None: t @ w[nm].float().t() + (w[b].float() if b else 0)
+        bias = (lambda nm: p + f"self_attn.{nm}.bias") if g.qkv_bias else (lambda nm: None)
+        q = rope(lin(x, p + "self_attn.q_proj.weight", bias("q_proj")).view(B, n, g.q_heads, 64))
+        v = lin(x, p + "self_attn.v_proj.weight", bias("v_proj")).view(B, n, g.kv_heads, 64)
+        ref_v = dec._ref_v.setdefault(layer, [[None] * g.kv_heads for _ in range(B)])
+        out = np.zeros((B, n, g.q_heads, 64), np.float32)
+        qn = q.cpu().numpy()
+        for b in range(B):
+            for hd in range(g.kv_heads):
+                vh = v[b, :, hd].half().float().cpu().numpy()
+                ref_v[b][hd] = vh if ref_v[b][hd] is None else np.concatenate([ref_v[b][hd], vh])
+                cfg, tab = tables[layer * g.kv_heads + hd]
+                packed, scales = dec.keys[layer][hd].read(b, 0, start + n)
+                kh = oracle.reconstruct(cfg, tab, packed, scales, threads=8)
+                rows = qn[b, :, hd * g.gqa:(hd + 1) * g.gqa].reshape(n * g.gqa, 64)
+                ps = np.repeat(np.arange(start, start + n, dtype=np.uint32), g.gqa)
+                _, _, o = oracle.attention(rows, kh, ref_v[b][hd], ps, True, threads=8)
+                out[b, :, hd * g.gqa:(hd + 1) * g.gqa] = o.reshape(n, g.gqa, 64)
+        att = torch.from_numpy(out).to(h.device).reshape(B, n, g.hidden)
+        h = h + lin(att, p + "self_attn.o_proj.weight")
+        x = norm(h, w[p + "post_attention_layernorm.weight"])
+        up = lin(x, p + "mlp.up_proj.weight")
+        h = h + lin(torch.nn.functional.silu(lin(x, p + "mlp.gate_proj.weight")) * up, p + "mlp.down_proj.weight")
+    last = norm(h[:, -1], w["model.norm.weight"])
+    return last @ w["model.embed_tokens.weight"].float().t()
+
+
+@pytest.mark.parametrize("name", sorted(GEOMS))
+def test_decoder_matches_reference_decoder(cuda, name):
+    import torch
+    g = GEOMS[name]
+    tables = _tables(g)
+    w = random_weights(g, seed=3, device=cuda, std=0.08)
+    B, prompt, steps = 2, 150, 3
+    dec = Decoder(w, g, 256, tables, batch=B)
+    dec._ref_v = {}
+    rng = np.random.default_rng(1)
+    toks = torch.from_numpy(rng.integers(0, g.vocab, (B, prompt))).to(cuda)
+    got = dec.prefill(toks, chunk=100)       # two chunks: 100 + 50 positions
+    # the reference consumes the same chunks (its V cache grows with them)
+    _reference_forward(dec, w, g, toks[:, :100], 0, tables)
+    ref = _reference_forward(dec, w, g, toks[:, 100:], 100, tables)
+    np.testing.assert_allclose(got.cpu().numpy(), ref.cpu().numpy(), atol=1e-4, rtol=1e-3)
+    start = prompt
+    for _ in range(steps):
+        nxt = torch.from_numpy(rng.integers(0, g.vocab, (B, 1))).to(cuda)
+        got = dec.decode(nxt)
+        ref = _reference_forward(dec, w, g, nxt, start, tables)
+        np.testing.assert_allclose(got.cpu().numpy(), ref.cpu().numpy(), atol=1e-4, rtol=1e-3)
+        start += 1
+    assert dec.length == prompt + steps
+    assert device_status(0) == 0
+    dec.destroy()
+
+
+def test_decoder_rejects_bad_requests(cuda):
+    g = GEOMS["smollm2-like"]
+    with pytest.raises(ValueError, match="geometry"):
+        ModelGeometry("smollm2", 2, 200, 256, 3, 1, 1e5, 1e-5, 500, False)
+    with pytest.raises(ValueError, match="Calibration"):
+        Decoder(random_weights(g, device=cuda), g, 64, _tables(g)[:1] * 0, batch=1)
+    dec = Decoder(random_weights(g, device=cuda), g, 8, _tables(g), batch=1)
+    with pytest.raises(ValueError, match="tokens"):
+        dec.prefill(np.zeros((1, 9), np.int64))
+    with pytest.raises(ValueError, match="tokens"):
+        dec.decode(np.array([[g.vocab]]))
+    dec.destroy()
