@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", choices=["decode", "model-smollm2", "model-qwen", "prefill"], default="decode",
+                    help="decode: config 4 (the headline); model-*: configs 2/3; prefill: config 5")
     return ap.parse_args()
 
 
@@ -360,6 +362,177 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def _event_ms(fn, steps, warmup):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        fn()
+    t1.record()
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) / steps
+
+
+def run_model(args, rank, world, local_rank):
+    """Configs 2/3: whole-model decode, batch 1 per GPU (replicas), random-init FP16
+    weights computed in FP32 like the reference's shaders, 4096-token random-id prefix,
+    then timed decode steps through bgtq.model.Decoder."""
+    import torch
+    import bgtq
+    from bgtq import sharding
+    from bgtq.model import QWEN25_05B, SMOLLM2_135M, Decoder, random_weights
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = sharding.init_from_env("nccl", timeout_s=300.0, device=dev)
+    g = SMOLLM2_135M if args.workload == "model-smollm2" else QWEN25_05B
+    prefix, steps, warmup = 4096, args.steps, max(3, args.warmup)
+    z = np.load(ROOT / "tests" / "golden" / "smollm2_heads.npz")
+    tables = [(z[f"h{i % 6}_config"], z[f"h{i % 6}_table"]) for i in range(g.layers * g.kv_heads)]
+    dec = Decoder(random_weights(g, seed=7 + rank, device=dev), g, prefix + warmup + steps + 4, tables, batch=1)
+    rng = np.random.default_rng(rank)
+    t_pre = time.perf_counter()
+    dec.prefill(torch.from_numpy(rng.integers(0, g.vocab, (1, prefix))).to(dev), chunk=1024)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t_pre
+    toks = [torch.from_numpy(rng.integers(0, g.vocab, (1, 1))).to(dev) for _ in range(warmup + steps)]
+    it = iter(toks)
+    logits = []
+
+    def step():
+        logits.append(dec.decode(next(it)))
+
+    def barrier():
+        sharding.barrier(dist, torch.cuda.synchronize)
+
+    for _ in range(warmup):
+        step()
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    barrier()
+    (ms,) = sharding.max_over_ranks([t0.elapsed_time(t1) / steps], dist, dev)
+    finite = all(bool(torch.isfinite(x).all()) for x in logits)
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"{g.family} whole-model decode tokens/s (batch 1 per GPU, 4096-token prefix)",
+            "value": world * 1e3 / ms, "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (random-init FP16 weights N(0,0.02), uniform random token ids)",
+            "config": {"workload": f"config {2 if g.family == 'smollm2' else 3}: {g.family} geometry, {g.layers} layers, "
+                                   f"{g.q_heads}/{g.kv_heads} heads, head_dim 64, Block-GTQ K + FP16 V",
+                       "model": g.family, "global_batch": world, "seq_len": prefix, "parallelism": f"replicas x{world}"},
+            "prefill_s": prefill_s, "reference_webgpu_ms_per_token": 375.6 if g.family == "smollm2" else 348.4,
+            "checks": {"logits_finite": finite, "device_status": bgtq.device_status(local_rank)}}), flush=True)
+    dec.destroy()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_prefill(args, rank, world, local_rank):
+    """Config 5: compressed prefill, Qwen2.5-0.5B attention geometry (24 layers, 14 / 2
+    heads, head_dim 64), 16 sequences x 8192 tokens per GPU.  Per layer: Q/K/V projections
+    of N(0,1) BF16 activations (random-init BF16 weights, FP32 out), split-half RoPE, bulk K
+    encode into the packed cache, FP16 V append, causal prefill attention on the tensor
+    cores.  roofline: attention FLOPs / attention launch time against the measured dense
+    BF16 tensor peak."""
+    import torch
+    import bgtq
+    from bgtq import sharding
+    from bgtq.model import QWEN25_05B
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = sharding.init_from_env("nccl", timeout_s=300.0, device=dev)
+    g = QWEN25_05B
+    S, T, L, H, G, d = 16, 8192, args.layers if args.layers != LAYERS else g.layers, g.kv_heads, g.gqa, 64
+    z = np.load(ROOT / "tests" / "golden" / "smollm2_heads.npz")
+    gen = torch.Generator(device=dev).manual_seed(11 + rank)
+    x = torch.randn((S * T, g.hidden), device=dev, generator=gen, dtype=torch.bfloat16)
+    wqkv = [(torch.randn((g.hidden, (g.q_heads + 2 * H) * d), device=dev, generator=gen) * 0.05).bfloat16()
+            for _ in range(L)]
+    pairs = d // 2
+    inv = torch.pow(torch.tensor(float(g.rope_theta), device=dev), -torch.arange(pairs, device=dev) / pairs)
+    ang = torch.arange(T, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
+    cos, sin = torch.cos(ang)[None, :, None, :], torch.sin(ang)[None, :, None, :]
+
+    def rope(t):
+        a, b = t[..., :pairs], t[..., pairs:]
+        return torch.cat([a * cos - b * sin, b * cos + a * sin], -1)
+
+    steps, warmup = args.steps, max(3, args.warmup)
+    stores = []
+    for layer in range(L):
+        ks = [bgtq.PackedKeys((z[f"h{(layer * H + h) % 6}_config"], z[f"h{(layer * H + h) % 6}_table"]), T,
+                              sequences=S, device=local_rank) for h in range(H)]
+        vs = [bgtq.Values(d, T, "f16", sequences=S, device=local_rank) for _ in range(H)]
+        stores.append((ks, vs, bgtq.GroupedAttention(ks, vs, G)))
+    ev = []
+
+    def step(record=False):
+        for layer in range(L):
+            ks, vs, att = stores[layer]
+            for o in ks + vs:
+                o.reset()
+            qkv = (x @ wqkv[layer]).float().view(S, T, g.q_heads + 2 * H, d)
+            q = rope(qkv[:, :, :g.q_heads]).contiguous()
+            k = rope(qkv[:, :, g.q_heads:g.q_heads + H])
+            for h in range(H):
+                ks[h].append(k[:, :, h, :])
+                vs[h].append(qkv[:, :, g.q_heads + H + h, :])
+            if record:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+            att.prefill(q)
+            if record:
+                e1.record()
+                ev.append((e0, e1))
+
+    for _ in range(warmup):
+        step()
+    sharding.barrier(dist, torch.cuda.synchronize)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step(record=True)
+    t1.record()
+    sharding.barrier(dist, torch.cuda.synchronize)
+    (ms,) = sharding.max_over_ranks([t0.elapsed_time(t1) / steps], dist, dev)
+    attn_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+    flops = S * g.q_heads * 2 * (2 * d * T * (T + 1) / 2)
+    peak = 0.0
+    mp = ROOT / "MEASURED_PEAKS.json"
+    if mp.exists():
+        peak = float(json.loads(mp.read_text())["bf16_tflops"])
+    if rank == 0:
+        achieved = flops / attn_ms / 1e9
+        print(json.dumps({
+            "metric": "compressed prefill tokens/s (config 5)", "value": world * S * T / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16x2 split (FP32-accurate) on tensor cores",
+            "data": "synthetic (N(0,1) BF16 activations, random-init BF16 projections)",
+            "config": {"workload": f"config 5: Qwen2.5-0.5B attention geometry, {L} layers, 14/2 heads, head_dim 64, "
+                                   f"{S} sequences x {T} tokens, causal", "global_batch": S * world, "seq_len": T,
+                       "parallelism": f"sequence-sharded x{world}"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak or None, "unit": "TFLOP/s",
+                         "frac": achieved / peak if peak else None,
+                         "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)",
+                         "flops_per_layer": flops, "mean_attention_ms": attn_ms,
+                         "note": "real attention FLOPs; the FP16 high/low split issues 3 QK and 2 PV tensor-core "
+                                 "products per real one"},
+            "checks": {"device_status": bgtq.device_status(local_rank)}}), flush=True)
+    for ks, vs, att in stores:
+        att.destroy()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -368,7 +541,12 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
-    run_ours(args, rank, world, local_rank)
+    if args.workload == "decode":
+        run_ours(args, rank, world, local_rank)
+    elif args.workload == "prefill":
+        run_prefill(args, rank, world, local_rank)
+    else:
+        run_model(args, rank, world, local_rank)
 
 
 if __name__ == "__main__":

@@ -86,6 +86,8 @@ SIGNATURES = {
     "bgtq_device_status": (I32, [C.c_int, C.POINTER(U32)]),
     "bgtq_attend_static": (I32, [U32, P, P, P, P, C.c_int, U32, U32, U32, P, P]),
     "bgtq_attend_prefill": (I32, [P, P, U32, U32, U32, U32, U32, P, C.c_int, P]),
+    "bgtq_keys_reset": (I32, [P, P]),
+    "bgtq_values_reset": (I32, [P, P]),
 }
 
 _lib = None

@@ -130,6 +130,10 @@ class _Keys(_Store):
         _lib.call("bgtq_keys_length", self._handle, seq, C.byref(n))
         return n.value
 
+    def reset(self, stream=None) -> None:
+        """Start every sequence over (lengths 0), keeping the capacity (bgtq_keys_reset)."""
+        _lib.call("bgtq_keys_reset", self._handle, _stream_ptr(stream))
+
     @property
     def length(self) -> int:
         return self.lengths(0)
@@ -228,6 +232,10 @@ class Values(_Store):
         n = C.c_uint32()
         _lib.call("bgtq_values_length", self._handle, seq, C.byref(n))
         return n.value
+
+    def reset(self, stream=None) -> None:
+        """Start every sequence over (lengths 0), keeping the capacity (bgtq_values_reset)."""
+        _lib.call("bgtq_values_reset", self._handle, _stream_ptr(stream))
 
     @property
     def length(self) -> int:

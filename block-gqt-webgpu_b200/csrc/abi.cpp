@@ -431,6 +431,15 @@ bgtq_status bgtq_keys_length(const bgtq_keys *k, uint32_t seq, uint32_t *out) {
     return BGTQ_OK;
 }
 
+bgtq_status bgtq_keys_reset(bgtq_keys *k, void *stream) {
+    if (!k) return fail(BGTQ_EINVAL, "null keys");
+    DeviceGuard g(k->device);
+    if (!g.ok) return fail(BGTQ_ECUDA, "cannot select device");
+    CK(cudaMemsetAsync(k->d_lengths, 0, (size_t)k->sequences * 4, static_cast<cudaStream_t>(stream)), "reset");
+    std::fill(k->lengths.begin(), k->lengths.end(), 0u);
+    return BGTQ_OK;
+}
+
 bgtq_status bgtq_keys_info(const bgtq_keys *k, bgtq_keys_kind *kind, uint32_t *dim, uint32_t *capacity,
                            uint32_t *sequences) {
     if (!k) return fail(BGTQ_EINVAL, "null keys");
@@ -589,6 +598,15 @@ bgtq_status bgtq_values_append(bgtq_values *v, const void *src, bgtq_dtype dtype
 bgtq_status bgtq_values_length(const bgtq_values *v, uint32_t seq, uint32_t *out) {
     if (!v || !out || seq >= v->sequences) return fail(BGTQ_EINVAL, "invalid argument");
     *out = v->lengths[seq];
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_values_reset(bgtq_values *v, void *stream) {
+    if (!v) return fail(BGTQ_EINVAL, "null values");
+    DeviceGuard g(v->device);
+    if (!g.ok) return fail(BGTQ_ECUDA, "cannot select device");
+    CK(cudaMemsetAsync(v->d_lengths, 0, (size_t)v->sequences * 4, static_cast<cudaStream_t>(stream)), "reset");
+    std::fill(v->lengths.begin(), v->lengths.end(), 0u);
     return BGTQ_OK;
 }
 

@@ -134,6 +134,11 @@ bgtq_status bgtq_keys_append(bgtq_keys *k, const void *src, bgtq_dtype dtype, in
                              uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
                              void *stream);
 bgtq_status bgtq_keys_length(const bgtq_keys *k, uint32_t seq, uint32_t *length_out);
+/* Start every sequence of the store over (lengths 0), keeping its capacity: a new request
+ * reusing the cache.  Rows past a length are never attended, so their old contents stay
+ * until appends overwrite them.  No counterpart in the reference (its stores only grow);
+ * stream-ordered like appends. */
+bgtq_status bgtq_keys_reset(bgtq_keys *k, void *stream);
 bgtq_status bgtq_keys_info(const bgtq_keys *k, bgtq_keys_kind *kind, uint32_t *dim, uint32_t *capacity,
                            uint32_t *sequences);
 
@@ -162,6 +167,8 @@ bgtq_status bgtq_values_append(bgtq_values *v, const void *src, bgtq_dtype dtype
                                uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
                                void *stream);
 bgtq_status bgtq_values_length(const bgtq_values *v, uint32_t seq, uint32_t *length_out);
+/* As bgtq_keys_reset, for a value store. */
+bgtq_status bgtq_values_reset(bgtq_values *v, void *stream);
 
 /* ---- attention ------------------------------------------------------------------- */
 

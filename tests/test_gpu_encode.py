@@ -192,3 +192,29 @@ def test_warp_and_bulk_encoders_agree(cuda, name):
     np.testing.assert_array_equal(warp_p, ref["packed"])
     np.testing.assert_array_equal(warp_n, ref["scales"])
     assert device_status(0) == 0
+
+
+def test_reset_starts_every_sequence_over(cuda):
+    """bgtq_keys_reset / bgtq_values_reset: lengths back to 0, the next appends write from
+    row 0 and attention sees only them."""
+    from bgtq import GroupedAttention, Values
+    z = load_config("config4")
+    p, cfg, tab = params_tables(z)
+    rng = np.random.default_rng(21)
+    a, b = _edge_keys(rng, 300, 64), _edge_keys(rng, 120, 64)
+    keys, vals = PackedKeys((cfg, tab), 320, sequences=2), Values(64, 320, "f16", sequences=2)
+    keys.append(np.stack([a, a])), vals.append(np.zeros((2, 300, 64), np.float16).view(np.uint16))
+    keys.reset(), vals.reset()
+    assert keys.lengths(0) == keys.lengths(1) == vals.lengths(1) == 0
+    vb = rng.standard_normal((2, 120, 64)).astype(np.float16)
+    keys.append(np.stack([b, b])), vals.append(vb.view(np.uint16))
+    fresh = PackedKeys((cfg, tab), 320, sequences=2)
+    fresh.append(np.stack([b, b]))
+    for s in range(2):
+        np.testing.assert_array_equal(keys.read(s)[0], fresh.read(s)[0])
+        np.testing.assert_array_equal(keys.read(s)[1], fresh.read(s)[1])
+    q = rng.standard_normal((2, 1, 3, 64)).astype(np.float32)
+    att = GroupedAttention([keys], [vals], 3)
+    kh = oracle.reconstruct(cfg, tab, *keys.read(0))
+    _, _, ref = oracle.attention(q[0, 0], kh, vb[0].astype(np.float32))
+    np.testing.assert_allclose(att.attend(q)[0, 0], ref, atol=1e-5, rtol=1e-4)
