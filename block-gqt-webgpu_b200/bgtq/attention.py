@@ -88,6 +88,10 @@ class GroupedAttention:
                   seq_count, C.c_void_p(o.data_ptr()), 0, C.c_void_p(int(st)))
         return o
 
+    def set_prefill_kernel(self, kernel: str) -> None:
+        """"umma" (tcgen05 with TMEM accumulators, the default) or "mma" (mma.sync)."""
+        _lib.call("bgtq_attention_set_prefill_kernel", self._handle, {"umma": 0, "mma": 1}[kernel])
+
     @property
     def last_splits(self) -> int:
         n = C.c_uint32()

@@ -901,7 +901,7 @@ bgtq_status bgtq_attend_prefill(bgtq_attention *at, const float *q, uint32_t pos
     a.n = n;
     a.pos_first = pos_first;
     a.d = d;
-    cudaError_t e = launch_prefill(a, max_cent, stream);
+    cudaError_t e = launch_prefill(a, max_cent, at->prefill_kernel == 0 ? 1 : 0, stream);
     if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
     at->last_splits = 1;
     at->last_launches = 2;  // query rotation + prefill attention
@@ -920,6 +920,11 @@ bgtq_status bgtq_attention_last_splits(const bgtq_attention *a, uint32_t *out) {
 bgtq_status bgtq_attention_set_splits(bgtq_attention *a, uint32_t splits) {
     if (!a || splits > 64) return fail(BGTQ_EINVAL, "invalid split count");
     a->forced_splits = splits;
+    return BGTQ_OK;
+}
+bgtq_status bgtq_attention_set_prefill_kernel(bgtq_attention *a, uint32_t kernel) {
+    if (!a || kernel > 1) return fail(BGTQ_EINVAL, "invalid prefill kernel");
+    a->prefill_kernel = kernel;
     return BGTQ_OK;
 }
 bgtq_status bgtq_attention_last_launches(const bgtq_attention *a, uint32_t *out) {

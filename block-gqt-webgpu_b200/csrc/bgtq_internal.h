@@ -148,8 +148,10 @@ enum class KKind { Packed, F16, F32 };
 cudaError_t launch_attention(const AttnArgs &a, KKind kk, int v_f32, uint32_t d, uint32_t max_cent,
                              uint32_t max_len, uint32_t forced_splits, uint32_t max_splits, uint32_t *splits_out,
                              cudaStream_t s);
-// Causal prefill attention (packed keys, FP16 values, head dim <= 64).
-cudaError_t launch_prefill(const PrefillArgs &a, uint32_t max_cent, cudaStream_t s);
+// Causal prefill attention (packed keys, FP16 values, head dim <= 64): the query rotation,
+// then the tcgen05/TMEM kernel (umma != 0) or the mma.sync kernel.
+cudaError_t launch_prefill(const PrefillArgs &a, uint32_t max_cent, int umma, cudaStream_t s);
+cudaError_t launch_prefill_tc(const PrefillArgs &a, uint32_t max_cent, cudaStream_t s);
 cudaError_t launch_probs(const float *logits, const float *lse, float *probs, uint64_t rows, uint32_t tokens,
                          uint32_t stride, cudaStream_t s);
 // Shared-memory bytes the attention kernel needs for a launch; 0 if unsupported.

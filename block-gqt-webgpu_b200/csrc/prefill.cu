@@ -432,7 +432,7 @@ cudaError_t run(const PrefillArgs &a, const Plan &pl, cudaStream_t s) {
 
 }  // namespace pre
 
-cudaError_t launch_prefill(const PrefillArgs &a, uint32_t max_cent, cudaStream_t s) {
+cudaError_t launch_prefill(const PrefillArgs &a, uint32_t max_cent, int umma, cudaStream_t s) {
     if (!a.n || !a.seq_count) return cudaSuccess;
     uint32_t row_stride = 0, scale_stride = 0;
     for (uint32_t h = 0; h < a.heads; ++h) {
@@ -444,6 +444,7 @@ cudaError_t launch_prefill(const PrefillArgs &a, uint32_t max_cent, cudaStream_t
     pre::prefill_qrot_kernel<<<dim3(a.n, a.heads, a.seq_count), 128, 0, s>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    if (umma) return launch_prefill_tc(a, max_cent, s);
     switch (a.gqa) {
         case 1: return pre::run<1>(a, pl, s);
         case 2: return pre::run<2>(a, pl, s);

@@ -213,6 +213,10 @@ bgtq_status bgtq_attend_prefill(bgtq_attention *a, const float *q, uint32_t pos_
 bgtq_status bgtq_attention_last_splits(const bgtq_attention *a, uint32_t *splits_out);
 /* Force a split-KV factor (0 = automatic). */
 bgtq_status bgtq_attention_set_splits(bgtq_attention *a, uint32_t splits);
+/* Which tensor-core kernel bgtq_attend_prefill runs: 0 = tcgen05 UMMA with TMEM
+ * accumulators (default), 1 = mma.sync (diagnostics, A/B comparisons).  Both compute the
+ * same causal attention to the same tolerance. */
+bgtq_status bgtq_attention_set_prefill_kernel(bgtq_attention *a, uint32_t kernel);
 /* Number of kernel launches issued by the last bgtq_attend (benches count launches). */
 bgtq_status bgtq_attention_last_launches(const bgtq_attention *a, uint32_t *launches_out);
 

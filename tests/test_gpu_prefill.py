@@ -51,12 +51,14 @@ def _check(att, keys, kv, q, pos_first, heads, G):
     return out
 
 
+@pytest.mark.parametrize("kernel", ["umma", "mma"])
 @pytest.mark.parametrize("heads,G", [(3, 3), (2, 7), (1, 1), (2, 4)])
-def test_prefill_matches_oracle(cuda, heads, G):
+def test_prefill_matches_oracle(cuda, heads, G, kernel):
     rng = np.random.default_rng(100 + G)
     S, lengths = 2, [700, 1203]
     keys, vals, kv = _stores(rng, heads, S, lengths, 1280)
     att = GroupedAttention(keys, vals, min(G, 8))
+    att.set_prefill_kernel(kernel)
     # whole prefix of the shorter sequence, then a chunk in the middle
     q = synthetic.profiled(rng, S * 700 * heads * G, 64).reshape(S, 700, heads * G, 64)
     _check(att, keys, kv, q, 0, heads, G)
