@@ -87,7 +87,9 @@ SIGNATURES = {
     "bgtq_attend_static": (I32, [U32, P, P, P, P, C.c_int, U32, U32, U32, P, P]),
     "bgtq_attend_prefill": (I32, [P, P, U32, U32, U32, U32, U32, P, C.c_int, P]),
     "bgtq_keys_reset": (I32, [P, P]),
+    "bgtq_append_kv_rope": (I32, [U32, P, P, P, C.c_uint64, C.c_uint64, U32, U32, U32, U32, U32, P, P]),
     "bgtq_attention_set_prefill_kernel": (I32, [P, U32]),
+    "bgtq_attention_set_rope": (I32, [P, P, U32]),
     "bgtq_values_reset": (I32, [P, P]),
 }
 

@@ -94,11 +94,19 @@ class Decoder:
     each a (config u32, table f32) pair in the reference's flattened format.
     compute: torch dtype of the activations and GEMMs (float32 mirrors the reference's FP32
     shaders; float16 runs the GEMMs on FP16 tensor cores with FP32 accumulation).
+
+    Per layer: RMSNorm, one fused Q/K/V GEMM, one library call that applies RoPE to the new
+    keys, encodes them into the packed stores and appends the FP16 values
+    (bgtq_append_kv_rope), attention on the raw query projection with RoPE applied inside
+    the query rotation (bgtq_attention_set_rope), the output projection fused with the
+    residual add, RMSNorm, one fused gate/up GEMM, SiLU gating and the down projection fused
+    with the residual add.
     """
 
     def __init__(self, weights, geometry: ModelGeometry, capacity: int, tables, batch: int = 1,
                  compute=None, device: int = 0):
         import torch
+        from . import _lib
         g = geometry
         if capacity < 1 or batch < 1:
             raise ValueError("Unsupported capacity/batch")
@@ -107,82 +115,82 @@ class Decoder:
         self.g, self.capacity, self.batch, self.length = g, int(capacity), int(batch), 0
         self.compute = compute or torch.float32
         self.dev = torch.device("cuda", device)
-        self.w = {k: v.to(self.dev, self.compute) for k, v in weights.items()}
+        w = {k: v.to(self.dev, self.compute) for k, v in weights.items()}
+        self.emb, self.final_norm = w["model.embed_tokens.weight"], w["model.norm.weight"]
+        self.layers = []
+        for layer in range(g.layers):
+            p = f"model.layers.{layer}."
+            qkv = torch.cat([w[p + f"self_attn.{n}.weight"] for n in ("q_proj", "k_proj", "v_proj")]).contiguous()
+            bias = (torch.cat([w[p + f"self_attn.{n}.bias"] for n in ("q_proj", "k_proj", "v_proj")]).contiguous()
+                    if g.qkv_bias else None)
+            gate_up = torch.cat([w[p + "mlp.gate_proj.weight"], w[p + "mlp.up_proj.weight"]]).contiguous()
+            self.layers.append(dict(ln1=w[p + "input_layernorm.weight"], ln2=w[p + "post_attention_layernorm.weight"],
+                                    qkv=qkv, qkv_b=bias, o=w[p + "self_attn.o_proj.weight"], gate_up=gate_up,
+                                    down=w[p + "mlp.down_proj.weight"]))
+        del w
+        pairs = g.head_dim // 2
+        # inv_freq as the reference's rope kernel raises theta (kernels.wgsl:52), FP32
+        self.inv_freq = torch.pow(torch.tensor(float(g.rope_theta), dtype=torch.float32),
+                                  -torch.arange(pairs, dtype=torch.float32) / pairs).numpy()
         self.keys, self.values, self.attn = [], [], []
         for layer in range(g.layers):
             ks = [PackedKeys(tables[layer * g.kv_heads + h], capacity, sequences=batch, device=device)
                   for h in range(g.kv_heads)]
             vs = [Values(g.head_dim, capacity, "f16", sequences=batch, device=device) for _ in range(g.kv_heads)]
+            att = GroupedAttention(ks, vs, g.gqa)
+            _lib.call("bgtq_attention_set_rope", att._handle, self.inv_freq.ctypes.data, pairs)
             self.keys.append(ks)
             self.values.append(vs)
-            self.attn.append(GroupedAttention(ks, vs, g.gqa))
-        pairs = g.head_dim // 2
-        self.inv_freq = torch.pow(torch.tensor(float(g.rope_theta), device=self.dev),
-                                  -torch.arange(pairs, device=self.dev, dtype=torch.float32) / pairs)
+            self.attn.append(att)
+        self._kv_ptrs = []
+        import ctypes as C
+        for layer in range(g.layers):
+            kp = (C.c_void_p * g.kv_heads)(*[k._handle for k in self.keys[layer]])
+            vp = (C.c_void_p * g.kv_heads)(*[v._handle for v in self.values[layer]])
+            self._kv_ptrs.append((kp, vp))
 
-    # ---- kernels.wgsl equivalents ----
     def _norm(self, x, w):
         import torch
-        xf = x.float()
-        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.g.rms_eps)
-        return (y * w.float()).to(self.compute)
-
-    def _lin(self, x, name, bias=None):
-        import torch
-        y = x @ self.w[name].t()
-        if bias is not None:
-            y = y + self.w[bias]
-        return y
-
-    def _rope(self, x, start):
-        """Split-half RoPE (kernels.wgsl:49-54): pair p of head h rotates dims p and p + d/2
-        by (start + row) * theta^(-p / (d/2))."""
-        import torch
-        n = x.shape[1]
-        pos = torch.arange(start, start + n, device=self.dev, dtype=torch.float32)
-        ang = pos[:, None] * self.inv_freq[None, :]                     # [n, d/2]
-        c, s = torch.cos(ang)[None, :, None, :], torch.sin(ang)[None, :, None, :]
-        xf = x.float()
-        a, b = xf[..., : self.g.head_dim // 2], xf[..., self.g.head_dim // 2:]
-        return torch.cat([a * c - b * s, b * c + a * s], dim=-1)
+        return torch.nn.functional.rms_norm(x, (self.g.hidden,), w, self.g.rms_eps)
 
     def forward(self, tokens):
         """decoder.ts:31-81 for a [batch, n] chunk: returns the last position's logits
         [batch, vocab] (FP32)."""
+        import ctypes as C
         import torch
+        import torch.nn.functional as F
+        from . import _lib
         g = self.g
         tokens = torch.as_tensor(tokens, device=self.dev).reshape(self.batch, -1).long()
         B, n = tokens.shape
         if n < 1 or self.length + n > self.capacity or int(tokens.max()) >= g.vocab or int(tokens.min()) < 0:
             raise ValueError("Invalid tokens/capacity")  # decoder.ts:33
         start = self.length
-        h = self.w["model.embed_tokens.weight"][tokens]                  # [B, n, hidden]
-        for layer in range(g.layers):
-            p = f"model.layers.{layer}."
-            x = self._norm(h, self.w[p + "input_layernorm.weight"])
-            bias = (lambda name: p + f"self_attn.{name}.bias") if g.qkv_bias else (lambda name: None)
-            q = self._lin(x, p + "self_attn.q_proj.weight", bias("q_proj")).view(B, n, g.q_heads, g.head_dim)
-            k = self._lin(x, p + "self_attn.k_proj.weight", bias("k_proj")).view(B, n, g.kv_heads, g.head_dim)
-            v = self._lin(x, p + "self_attn.v_proj.weight", bias("v_proj")).view(B, n, g.kv_heads, g.head_dim)
-            qr = self._rope(q, start)                                    # FP32 [B, n, Hq, d]
-            kr = self._rope(k, start)
-            vf = v.float()
-            for hd in range(g.kv_heads):
-                self.keys[layer][hd].append(kr[:, :, hd, :], seq_first=0)     # encode from FP32
-                self.values[layer][hd].append(vf[:, :, hd, :], seq_first=0)   # FP32 -> FP16
+        st = torch.cuda.current_stream(self.dev).cuda_stream
+        qw, kvw = g.q_heads * g.head_dim, g.kv_heads * g.head_dim
+        row = qw + 2 * kvw
+        h = self.emb[tokens]                                             # [B, n, hidden]
+        for layer, lw in enumerate(self.layers):
+            x = self._norm(h, lw["ln1"])
+            qkv = F.linear(x, lw["qkv"], lw["qkv_b"]).float().contiguous()   # [B, n, row]
+            kp, vp = self._kv_ptrs[layer]
+            _lib.call("bgtq_append_kv_rope", g.kv_heads, kp, vp, C.c_void_p(qkv.data_ptr()), row, n * row, qw,
+                      qw + kvw, n, 0, B, self.inv_freq.ctypes.data, C.c_void_p(st))
             if n == 1:
-                att = self.attn[layer].attend(qr.view(B, g.kv_heads, g.gqa, g.head_dim).contiguous())
+                q = qkv[:, 0, :qw].reshape(B, g.kv_heads, g.gqa, g.head_dim).contiguous()
+                att = self.attn[layer].attend(q)
             else:
-                att = self.attn[layer].prefill(qr.contiguous(), start)
-            att = att.reshape(B, n, g.hidden).to(self.compute)
-            h = h + self._lin(att, p + "self_attn.o_proj.weight")
-            x = self._norm(h, self.w[p + "post_attention_layernorm.weight"])
-            gate = self._lin(x, p + "mlp.gate_proj.weight")
-            up = self._lin(x, p + "mlp.up_proj.weight")
-            h = h + self._lin(torch.nn.functional.silu(gate) * up, p + "mlp.down_proj.weight")
-        last = self._norm(h[:, -1], self.w["model.norm.weight"])
+                q = qkv[:, :, :qw].reshape(B, n, g.q_heads, g.head_dim).contiguous()
+                att = self.attn[layer].prefill(q, start)
+            att = att.reshape(B * n, g.hidden).to(self.compute)
+            h = torch.addmm(h.reshape(B * n, g.hidden), att, lw["o"].t()).view(B, n, g.hidden)
+            x = self._norm(h, lw["ln2"])
+            gate, up = F.linear(x, lw["gate_up"]).chunk(2, dim=-1)
+            act = (F.silu(gate) * up).reshape(B * n, -1)
+            h = torch.addmm(h.reshape(B * n, g.hidden), act, lw["down"].t()).view(B, n, g.hidden)
+        last = self._norm(h[:, -1], self.final_norm)
         self.length += n
-        return (last @ self.w["model.embed_tokens.weight"].t()).float()
+        return (last @ self.emb.t()).float()
 
     def prefill(self, tokens, chunk: int | None = None):
         """decoder.ts:82: the prompt in chunks; returns the last chunk's logits."""
@@ -202,9 +210,8 @@ class Decoder:
         return self.forward(token)
 
     def destroy(self):
-        for objs in (self.attn,):
-            for a in objs:
-                a.destroy()
+        for a in self.attn:
+            a.destroy()
         for layer in self.keys + self.values:
             for o in layer:
                 o.destroy()

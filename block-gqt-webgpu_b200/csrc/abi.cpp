@@ -425,6 +425,65 @@ bgtq_status bgtq_keys_append(bgtq_keys *k, const void *src, bgtq_dtype dtype, in
     return BGTQ_OK;
 }
 
+bgtq_status bgtq_append_kv_rope(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, const float *src,
+                                uint64_t row_stride, uint64_t seq_stride, uint32_t k_offset, uint32_t v_offset,
+                                uint32_t count, uint32_t seq_first, uint32_t seq_count, const float *inv_freq,
+                                void *stream_) {
+    if (!keys || !values || !src || !inv_freq || heads < 1 || heads > (uint32_t)kMaxHeads)
+        return fail(BGTQ_EINVAL, "Invalid K/V append");
+    const bgtq_keys *k0 = keys[0];
+    if (!k0) return fail(BGTQ_EINVAL, "Invalid K/V append");
+    const uint32_t d = k0->dim;
+    if (d % 2 || !count || !seq_count || (uint64_t)seq_first + seq_count > k0->sequences ||
+        reinterpret_cast<uintptr_t>(src) % 4 || row_stride < (uint64_t)std::max(k_offset, v_offset) + heads * d)
+        return fail(BGTQ_EINVAL, "Invalid K/V append");
+    for (uint32_t h = 0; h < heads; ++h) {
+        const bgtq_keys *k = keys[h];
+        const bgtq_values *v = values[h];
+        if (!k || !v || k->kind != BGTQ_KEYS_PACKED || k->dim != d || v->dim != d || v->dtype != BGTQ_F16 ||
+            k->device != k0->device || v->device != k0->device || k->sequences != k0->sequences ||
+            v->sequences != k0->sequences)
+            return fail(BGTQ_EINVAL, "K/V append needs packed keys and FP16 values of one head dim");
+        for (uint32_t s = 0; s < seq_count; ++s) {
+            const uint32_t seq = seq_first + s, L = k0->lengths[seq];
+            if (k->lengths[seq] != L || v->lengths[seq] != L) return fail(BGTQ_EBUSY, "K/V lengths must match");
+            if ((uint64_t)L + count > std::min(k->capacity, v->capacity))
+                return fail(BGTQ_ECAPACITY, "K capacity exceeded");
+        }
+    }
+    DeviceGuard g(k0->device);
+    if (!g.ok) return fail(BGTQ_ECUDA, "cannot select device");
+    KvRopeArgs a;
+    std::memset(&a, 0, sizeof(a));
+    for (uint32_t h = 0; h < heads; ++h) {
+        fill_encode_head(keys[h], a.head[h]);
+        a.v[h] = values[h]->data;
+        a.v_lengths[h] = values[h]->d_lengths;
+        a.v_seq_stride[h] = (uint64_t)values[h]->cap_alloc * values[h]->D;
+    }
+    a.src = src;
+    a.start = k0->d_lengths;
+    a.row_stride = row_stride;
+    a.seq_stride = seq_stride;
+    a.k_offset = k_offset;
+    a.v_offset = v_offset;
+    a.count = count;
+    a.seq_first = seq_first;
+    a.seq_count = seq_count;
+    a.heads = heads;
+    a.vD = values[0]->D;
+    a.v_swizzle = values_swizzled(0, values[0]->D) ? 1u : 0u;
+    for (uint32_t p = 0; p < d / 2; ++p) a.inv_freq[p] = inv_freq[p];
+    cudaError_t e = launch_kv_rope_append(a, d, static_cast<cudaStream_t>(stream_));
+    if (e != cudaSuccess) return cuda_fail(e, "K/V append launch");
+    for (uint32_t h = 0; h < heads; ++h)
+        for (uint32_t s = 0; s < seq_count; ++s) {
+            keys[h]->lengths[seq_first + s] += count;
+            values[h]->lengths[seq_first + s] += count;
+        }
+    return BGTQ_OK;
+}
+
 bgtq_status bgtq_keys_length(const bgtq_keys *k, uint32_t seq, uint32_t *out) {
     if (!k || !out || seq >= k->sequences) return fail(BGTQ_EINVAL, "invalid argument");
     *out = k->lengths[seq];
@@ -673,6 +732,8 @@ void bgtq_attention_destroy(bgtq_attention *a) {
     a->out_dev.release();
     a->logits_dev.release();
     a->probs_dev.release();
+    a->prefill_qt.release();
+    a->rope.release();
     delete a;
 }
 
@@ -818,6 +879,7 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
     a.lse = (logits || probs) ? at->lse : nullptr;
     a.part = at->part;
     a.counters = at->counters + 0;
+    a.rope = at->use_rope ? static_cast<const float *>(at->rope.p) : nullptr;
     a.status = device_status_word(at->device);
     a.seq_first = seq_first;
     a.seq_count = seq_count;
@@ -894,6 +956,7 @@ bgtq_status bgtq_attend_prefill(bgtq_attention *at, const float *q, uint32_t pos
     a.out = dout;
     a.lengths = at->keys[0]->d_lengths;
     a.status = device_status_word(at->device);
+    a.rope = at->use_rope ? static_cast<const float *>(at->rope.p) : nullptr;
     a.seq_first = seq_first;
     a.seq_count = seq_count;
     a.heads = H;
@@ -922,6 +985,20 @@ bgtq_status bgtq_attention_set_splits(bgtq_attention *a, uint32_t splits) {
     a->forced_splits = splits;
     return BGTQ_OK;
 }
+bgtq_status bgtq_attention_set_rope(bgtq_attention *a, const float *inv_freq, uint32_t n) {
+    if (!a || (n && (!inv_freq || n != a->dim / 2))) return fail(BGTQ_EINVAL, "RoPE table must hold dim/2 entries");
+    if (!n) {
+        a->use_rope = false;
+        return BGTQ_OK;
+    }
+    DeviceGuard g(a->device);
+    if (!g.ok) return fail(BGTQ_ECUDA, "cannot select device");
+    CK(a->rope.ensure((size_t)n * 4), "RoPE table allocation");
+    CK(cudaMemcpy(a->rope.p, inv_freq, (size_t)n * 4, cudaMemcpyHostToDevice), "RoPE table upload");
+    a->use_rope = true;
+    return BGTQ_OK;
+}
+
 bgtq_status bgtq_attention_set_prefill_kernel(bgtq_attention *a, uint32_t kernel) {
     if (!a || kernel > 1) return fail(BGTQ_EINVAL, "invalid prefill kernel");
     a->prefill_kernel = kernel;

@@ -813,6 +813,17 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
     }
 }
 
+// Element j of query row q after split-half RoPE at position pos (src/model/kernels.wgsl:
+// 49-54) with the table inv[d/2], rounded like separate multiplies and adds; without a
+// table the element itself.
+__device__ __forceinline__ float rope_elem(const float *q, uint32_t j, uint32_t d, uint32_t pos, const float *inv) {
+    if (!inv) return q[j];
+    const uint32_t pairs = d / 2, p = j < pairs ? j : j - pairs;
+    const float ang = __fmul_rn((float)pos, inv[p]);
+    const float c = cosf(ang), sn = sinf(ang), x = q[p], y = q[p + pairs];
+    return j < pairs ? __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn)) : __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+}
+
 // Query records for one (sequence, KV head): qt[j][r] = sum_{i in group(j)} R[j][i] *
 // q_r[perm[i]] / sqrt(d) for packed keys (the query rotated into the code domain), or
 // q_r[j] / sqrt(d) for dense keys; zero for j >= d and r >= rows.  One CTA per
@@ -823,9 +834,12 @@ static __global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant_
     const uint32_t hd = blockIdx.x, s = blockIdx.y, R = a.rows;
     const AttnHead &h = a.head[hd];
     const float *qg = a.q + ((uint64_t)s * a.heads + hd) * (uint64_t)R * d;
+    const uint32_t len = a.lengths[a.seq_first + s];
     for (uint32_t idx = threadIdx.x; idx < R * d; idx += blockDim.x) {
         const uint32_t r = idx / d, i = idx % d;
-        qraw[idx] = packed ? qg[r * d + h.perm[i]] : qg[r * d + i];
+        // a query sits at its position (default: the last appended row)
+        const uint32_t pos = a.positions ? a.positions[s * R + r] : (len ? len - 1 : 0);
+        qraw[idx] = rope_elem(qg + r * d, packed ? h.perm[i] : i, d, pos, a.rope);
     }
     __syncthreads();
     const float qscale = kLog2e / sqrtf((float)d);  // scores in log2 units

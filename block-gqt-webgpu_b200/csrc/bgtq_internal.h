@@ -78,6 +78,21 @@ struct EncodeArgs {
     int src_f32;
 };
 
+// Model-path append: RoPE'd K and V of `count` tokens per sequence for `heads` KV heads,
+// read from FP32 projections (src + s*seq_stride + t*row_stride; K of head h at k_offset +
+// h*d, V at v_offset + h*d, in floats).
+struct KvRopeArgs {
+    EncodeHead head[kMaxHeads];
+    void *v[kMaxHeads];             // FP16 value rows, sequence 0 row 0
+    uint32_t *v_lengths[kMaxHeads];
+    const float *src;
+    const uint32_t *start;          // device lengths of the first key store (start rows)
+    uint64_t v_seq_stride[kMaxHeads];  // halves between sequences of each value store
+    uint64_t row_stride, seq_stride;   // floats
+    uint32_t k_offset, v_offset, count, seq_first, seq_count, heads, vD, v_swizzle;
+    float inv_freq[kMaxDim / 2];
+};
+
 // Per-head constants of the attention kernels.
 struct AttnHead {
     const uint8_t *k;          // packed rows | FP16 K rows | FP32 K rows, sequence 0 row 0
@@ -109,6 +124,7 @@ struct AttnArgs {
     float *part;               // [splits][S][H][R][D + 2]
     uint32_t *counters;        // [S][H], zero between launches
     uint32_t *status;
+    const float *rope;         // optional [d/2] RoPE table: queries arrive before RoPE
     uint32_t seq_first, seq_count, heads, rows, splits, tokens_per_split, causal, logit_stride;
 };
 
@@ -120,6 +136,7 @@ struct PrefillArgs {
     float *out;                // [S][n][heads*gqa][d]
     const uint32_t *lengths;   // [sequences] key lengths (device), indexed seq_first + s
     uint32_t *status;
+    const float *rope;         // optional [d/2] RoPE table: queries arrive before RoPE
     uint32_t seq_first, seq_count, heads, gqa, n, pos_first, d;
 };
 
@@ -134,6 +151,7 @@ struct ReconArgs {
 // Kernel launchers (return cudaError_t of the launch).
 cudaError_t launch_encode(const EncodeArgs &a, uint32_t d, uint32_t smem_cent_floats, uint32_t max_ncb,
                           cudaStream_t s);
+cudaError_t launch_kv_rope_append(const KvRopeArgs &a, uint32_t d, cudaStream_t s);
 cudaError_t launch_copy_rows(void *dst, uint64_t dst_seq_stride, uint32_t dst_row_elems, int dst_f32,
                              const void *src, uint64_t src_row_stride, uint64_t src_seq_stride, int src_f32,
                              const uint32_t *row0, uint32_t row0_scalar, uint32_t count, uint32_t seq_first,

@@ -221,24 +221,86 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant_
     }
 }
 
+// Shared-memory scratch of one warp's key in the warp-per-key kernels.
+struct WarpKey {
+    float xs[kMaxDim];         // permuted FP16 key as FP32, then normalised
+    float nrm[kMaxGroups];
+    uint8_t codes[kMaxDim];
+    uint32_t orow[kMaxDim / 4 + 1];
+    uint16_t srow[8];
+};
+
+// The encode of one key held in wk.xs (already permuted, FP16-exact values) by one warp,
+// written to row dst_row of sequence dseq: same arithmetic and order as encode_kernel,
+// bit for bit - group sums and scales sequential per group (one lane per group), every
+// y_j one lane's sequential FMA chain over its group, ascending.
+__device__ __forceinline__ void warp_encode(const EncodeHead &h, uint32_t d, WarpKey &wk, uint32_t dseq,
+                                            uint32_t dst_row, int lane) {
+    const uint32_t ns = h.ns, ng = h.ng;
+    const uint32_t row_words = h.row_stride / 4, sc_words = h.scale_stride / 2;
+    uint8_t *ob = reinterpret_cast<uint8_t *>(wk.orow);
+    __syncwarp();
+    if ((uint32_t)lane < ng) {
+        float acc = 0.0f;
+        for (uint32_t i = h.group_off[lane]; i < h.group_off[lane + 1]; ++i) acc = fmaf(wk.xs[i], wk.xs[i], acc);
+        wk.nrm[lane] = sqrtf(acc + 1e-30f);
+    }
+    __syncwarp();
+    for (uint32_t i = lane; i < d; i += 32) {
+        const float n = wk.nrm[h.t.group_of[i]];
+        wk.xs[i] = wk.xs[i] / (n > 1e-10f ? n : 1.0f);
+    }
+    __syncwarp();
+    for (uint32_t j = lane; j < d; j += 32) {
+        const uint32_t g = h.t.group_of[j];
+        const float *rj = h.t.rot + (uint64_t)j * d;
+        float y = 0.0f;
+#pragma unroll 4
+        for (uint32_t i = h.group_off[g]; i < h.group_off[g + 1]; ++i) y = fmaf(wk.xs[i], __ldg(rj + i), y);
+        float t = (y - h.t.off[j]) * h.t.inv[j];
+        t = fminf(fmaxf(t, 0.0f), 255.0f);
+        wk.codes[j] = h.t.lut[(uint32_t)h.t.cbidx[j] * 256u + (uint32_t)t];
+    }
+    __syncwarp();
+    if ((uint32_t)lane < ng) {
+        float cl = 0.0f;
+        for (uint32_t j = h.group_off[lane]; j < h.group_off[lane + 1]; ++j) {
+            const float cv = h.t.cent[h.t.cb_base[j] + wk.codes[j]];
+            cl = fmaf(cv, cv, cl);
+        }
+        wk.srow[lane] = __half_as_ushort(__float2half_rn(wk.nrm[lane] / fmaxf(sqrtf(cl), 1e-10f)));
+    } else if ((uint32_t)lane < 8) {
+        wk.srow[lane] = 0;
+    }
+    for (uint32_t b = lane; b < row_words * 4; b += 32) {
+        uint32_t v = 0;
+        if (b < ns / 2) v = (uint32_t)wk.codes[2 * b] | ((uint32_t)wk.codes[2 * b + 1] << 4);
+        else if (b < ns / 2 + (d - ns)) v = wk.codes[ns + (b - ns / 2)];
+        ob[b] = (uint8_t)v;
+    }
+    __syncwarp();
+    uint32_t *dst = reinterpret_cast<uint32_t *>(h.packed + (uint64_t)dseq * h.k_seq_stride +
+                                                 (uint64_t)dst_row * h.row_stride);
+    for (uint32_t c = lane; c < row_words; c += 32) dst[c] = wk.orow[c];
+    if ((uint32_t)lane < sc_words) {
+        uint32_t *sdst = reinterpret_cast<uint32_t *>(h.scales + (uint64_t)dseq * h.s_seq_stride +
+                                                      (uint64_t)dst_row * h.scale_stride);
+        sdst[lane] = (uint32_t)wk.srow[2 * lane] | ((uint32_t)wk.srow[2 * lane + 1] << 16);
+    }
+    __syncwarp();
+}
+
 // Few keys (a decode step appends one token per sequence): one warp per key, lanes over
 // dimensions, so a launch of a few hundred keys spreads over many SMs instead of a couple
-// of threads-per-key CTAs.  Same arithmetic and order as encode_kernel, bit for bit: group
-// sums and scales are still sequential per group (one lane per group), every y_j is still
-// one lane's sequential FMA chain over its group, ascending.
+// of threads-per-key CTAs.
 __global__ void __launch_bounds__(kThreads) encode_warp_kernel(const __grid_constant__ EncodeArgs a, uint32_t d,
                                                                uint32_t total) {
     constexpr int W = kThreads / 32;
     const EncodeHead &h = a.head[blockIdx.y];
-    __shared__ float xs[W][kMaxDim];            // permuted key, then normalised
-    __shared__ float nrm[W][kMaxGroups];
-    __shared__ uint8_t codes[W][kMaxDim];
-    __shared__ uint32_t orow[W][kMaxDim / 4 + 1];
-    __shared__ uint16_t srow[W][8];
+    __shared__ WarpKey wks[W];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t ns = h.ns, ng = h.ng, count = a.count;
-    const uint32_t row_words = h.row_stride / 4, sc_words = h.scale_stride / 2;
-    uint8_t *ob = reinterpret_cast<uint8_t *>(orow[w]);
+    const uint32_t count = a.count;
+    WarpKey &wk = wks[w];
     for (uint32_t q = blockIdx.x * W + w; q < total; q += gridDim.x * W) {
         const uint32_t s = q / count, rr = q % count;
         const uint64_t e0 = (uint64_t)s * a.seq_stride + (uint64_t)rr * a.row_stride + h.src_head_offset;
@@ -246,63 +308,67 @@ __global__ void __launch_bounds__(kThreads) encode_warp_kernel(const __grid_cons
             const uint64_t e = e0 + h.t.perm[i];
             const __half x = a.src_f32 ? __float2half_rn(static_cast<const float *>(a.src)[e])
                                        : __ushort_as_half(static_cast<const uint16_t *>(a.src)[e]);
-            xs[w][i] = __half2float(x);
+            wk.xs[i] = __half2float(x);
         }
-        __syncwarp();
-        if ((uint32_t)lane < ng) {
-            float acc = 0.0f;
-            for (uint32_t i = h.group_off[lane]; i < h.group_off[lane + 1]; ++i) acc = fmaf(xs[w][i], xs[w][i], acc);
-            nrm[w][lane] = sqrtf(acc + 1e-30f);
-        }
-        __syncwarp();
-        for (uint32_t i = lane; i < d; i += 32) {
-            const float n = nrm[w][h.t.group_of[i]];
-            xs[w][i] = xs[w][i] / (n > 1e-10f ? n : 1.0f);
-        }
-        __syncwarp();
-        for (uint32_t j = lane; j < d; j += 32) {
-            const uint32_t g = h.t.group_of[j];
-            const float *rj = h.t.rot + (uint64_t)j * d;
-            float y = 0.0f;
-#pragma unroll 4
-            for (uint32_t i = h.group_off[g]; i < h.group_off[g + 1]; ++i) y = fmaf(xs[w][i], __ldg(rj + i), y);
-            float t = (y - h.t.off[j]) * h.t.inv[j];
-            t = fminf(fmaxf(t, 0.0f), 255.0f);
-            codes[w][j] = h.t.lut[(uint32_t)h.t.cbidx[j] * 256u + (uint32_t)t];
-        }
-        __syncwarp();
-        if ((uint32_t)lane < ng) {
-            float cl = 0.0f;
-            for (uint32_t j = h.group_off[lane]; j < h.group_off[lane + 1]; ++j) {
-                const float cv = h.t.cent[h.t.cb_base[j] + codes[w][j]];
-                cl = fmaf(cv, cv, cl);
-            }
-            srow[w][lane] = __half_as_ushort(__float2half_rn(nrm[w][lane] / fmaxf(sqrtf(cl), 1e-10f)));
-        } else if ((uint32_t)lane < 8) {
-            srow[w][lane] = 0;
-        }
-        for (uint32_t b = lane; b < row_words * 4; b += 32) {
-            uint32_t v = 0;
-            if (b < ns / 2) v = (uint32_t)codes[w][2 * b] | ((uint32_t)codes[w][2 * b + 1] << 4);
-            else if (b < ns / 2 + (d - ns)) v = codes[w][ns + (b - ns / 2)];
-            ob[b] = (uint8_t)v;
-        }
-        __syncwarp();
-        const uint32_t dst_row = (a.row0 ? a.row0[s] : a.row0_scalar) + rr;
-        uint32_t *dst = reinterpret_cast<uint32_t *>(h.packed + (uint64_t)(a.seq_first + s) * h.k_seq_stride +
-                                                     (uint64_t)dst_row * h.row_stride);
-        for (uint32_t c = lane; c < row_words; c += 32) dst[c] = orow[w][c];
-        if ((uint32_t)lane < sc_words) {
-            uint32_t *sdst = reinterpret_cast<uint32_t *>(h.scales + (uint64_t)(a.seq_first + s) * h.s_seq_stride +
-                                                          (uint64_t)dst_row * h.scale_stride);
-            sdst[lane] = (uint32_t)srow[w][2 * lane] | ((uint32_t)srow[w][2 * lane + 1] << 16);
-        }
-        __syncwarp();
+        warp_encode(h, d, wk, a.seq_first + s, (a.row0 ? a.row0[s] : a.row0_scalar) + rr, lane);
     }
     if (blockIdx.x == 0 && h.lengths) {
         for (uint32_t s = threadIdx.x; s < a.seq_count; s += kThreads)
             h.lengths[a.seq_first + s] = (a.row0 ? a.row0[s] : a.row0_scalar) + count;
     }
+}
+
+// Model-path append (src/model/decoder.ts:44-50: rope(K), encode_k per KV head, V append):
+// one warp per (new token, KV head) reads the FP32 K and V projections of the token, applies
+// split-half RoPE to K at the token's cache row (src/model/kernels.wgsl:49-54, rounded like
+// separate multiplies and adds), encodes it into the packed store and writes V to the FP16
+// value store.  Start rows come from the first key store's device lengths, so the launch is
+// stream-ordered against earlier appends without host round trips; lengths are bumped by
+// bump_lengths_kernel afterwards.
+__global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_constant__ KvRopeArgs a, uint32_t d,
+                                                                  uint32_t total) {
+    constexpr int W = kThreads / 32;
+    const uint32_t hd = blockIdx.y;
+    const EncodeHead &h = a.head[hd];
+    __shared__ WarpKey wks[W];
+    __shared__ float kr[W][kMaxDim];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    WarpKey &wk = wks[w];
+    const uint32_t pairs = d / 2;
+    for (uint32_t q = blockIdx.x * W + w; q < total; q += gridDim.x * W) {
+        const uint32_t s = q / a.count, rr = q % a.count, seq = a.seq_first + s;
+        const uint32_t pos = a.start[seq] + rr;
+        const float *src = a.src + (uint64_t)s * a.seq_stride + (uint64_t)rr * a.row_stride;
+        const float *ks = src + a.k_offset + (uint64_t)hd * d, *vs = src + a.v_offset + (uint64_t)hd * d;
+        for (uint32_t p = lane; p < pairs; p += 32) {
+            const float ang = __fmul_rn((float)pos, a.inv_freq[p]);
+            const float c = cosf(ang), sn = sinf(ang), x = ks[p], y = ks[p + pairs];
+            kr[w][p] = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
+            kr[w][p + pairs] = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+        }
+        __syncwarp();
+        for (uint32_t i = lane; i < d; i += 32) wk.xs[i] = __half2float(__float2half_rn(kr[w][h.t.perm[i]]));
+        warp_encode(h, d, wk, seq, pos, lane);
+        // V row: FP32 -> FP16, chunk-swizzled for head dims 64 / 128
+        __half *vrow = reinterpret_cast<__half *>(a.v[hd]) + (uint64_t)seq * a.v_seq_stride[hd] + (uint64_t)pos * a.vD;
+        for (uint32_t e = lane; e < a.vD; e += 32) {
+            const float x = e < d ? vs[e] : 0.0f;
+            uint32_t de = e;
+            if (a.v_swizzle) {
+                const uint32_t c = e >> 3;
+                de = (((c & ~7u) | ((c ^ pos) & 7u)) << 3) | (e & 7u);
+            }
+            vrow[de] = __float2half_rn(x);
+        }
+    }
+}
+
+__global__ void bump_lengths_kernel(const __grid_constant__ KvRopeArgs a) {
+    for (uint32_t s = threadIdx.x; s < a.seq_count; s += blockDim.x)
+        for (uint32_t hd = 0; hd < a.heads; ++hd) {
+            a.head[hd].lengths[a.seq_first + s] += a.count;
+            a.v_lengths[hd][a.seq_first + s] += a.count;
+        }
 }
 
 template <int D>
@@ -344,6 +410,17 @@ cudaError_t run_encode(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uin
 }
 
 }  // namespace
+
+cudaError_t launch_kv_rope_append(const KvRopeArgs &a, uint32_t d, cudaStream_t s) {
+    const uint32_t total = a.count * a.seq_count;
+    if (!total) return cudaSuccess;
+    const uint32_t blocks = (total + kThreads / 32 - 1) / (kThreads / 32);
+    kv_rope_append_kernel<<<dim3(blocks, a.heads), kThreads, 0, s>>>(a, d, total);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    bump_lengths_kernel<<<1, 128, 0, s>>>(a);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_encode(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uint32_t max_ncb, cudaStream_t s) {
     if (a.count == 0 || a.seq_count == 0) return cudaSuccess;

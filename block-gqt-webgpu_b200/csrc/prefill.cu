@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(128) prefill_qrot_kernel(const __grid_constant
     const float *qg = a.q + (((uint64_t)s * a.n + t) * HQ + (uint64_t)h * G) * d;
     for (uint32_t idx = threadIdx.x; idx < G * d; idx += blockDim.x) {
         const uint32_t r = idx / d, i = idx % d;
-        qraw[r][i] = qg[(uint64_t)r * d + hd.perm[i]];
+        qraw[r][i] = attn::rope_elem(qg + (uint64_t)r * d, hd.perm[i], d, a.pos_first + t, a.rope);
     }
     __syncthreads();
     const float qscale = kLog2e / sqrtf((float)d);

@@ -134,6 +134,18 @@ bgtq_status bgtq_keys_append(bgtq_keys *k, const void *src, bgtq_dtype dtype, in
                              uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
                              void *stream);
 bgtq_status bgtq_keys_length(const bgtq_keys *k, uint32_t seq, uint32_t *length_out);
+/* Model-path append of one layer (src/model/decoder.ts:44-50: RoPE on K, encode_k per KV
+ * head, V append) in one launch: for `count` new tokens of sequences [seq_first,
+ * seq_first+seq_count), reads the FP32 projections at src + s*seq_stride + t*row_stride
+ * (floats; K of KV head h at k_offset + h*dim, V at v_offset + h*dim), applies split-half
+ * RoPE (src/model/kernels.wgsl:49-54) to K at each token's cache row with the host table
+ * inv_freq[dim/2], encodes it into keys[h] and writes V as FP16 into values[h].  Needs
+ * packed keys and FP16 values of one head dim with equal lengths; src is device memory;
+ * stream-ordered (start rows are read from the device). */
+bgtq_status bgtq_append_kv_rope(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, const float *src,
+                                uint64_t row_stride, uint64_t seq_stride, uint32_t k_offset, uint32_t v_offset,
+                                uint32_t count, uint32_t seq_first, uint32_t seq_count, const float *inv_freq,
+                                void *stream);
 /* Start every sequence of the store over (lengths 0), keeping its capacity: a new request
  * reusing the cache.  Rows past a length are never attended, so their old contents stay
  * until appends overwrite them.  No counterpart in the reference (its stores only grow);
@@ -213,6 +225,11 @@ bgtq_status bgtq_attend_prefill(bgtq_attention *a, const float *q, uint32_t pos_
 bgtq_status bgtq_attention_last_splits(const bgtq_attention *a, uint32_t *splits_out);
 /* Force a split-KV factor (0 = automatic). */
 bgtq_status bgtq_attention_set_splits(bgtq_attention *a, uint32_t splits);
+/* Queries arrive before RoPE (the model path's raw Q projection): bgtq_attend and
+ * bgtq_attend_prefill apply split-half RoPE (src/model/kernels.wgsl:49-54) with the table
+ * inv_freq[n], n = dim/2, at each query's position (positions[], else the last appended
+ * row; prefill: pos_first + t) before attending.  n = 0 turns it off. */
+bgtq_status bgtq_attention_set_rope(bgtq_attention *a, const float *inv_freq, uint32_t n);
 /* Which tensor-core kernel bgtq_attend_prefill runs: 0 = tcgen05 UMMA with TMEM
  * accumulators (default), 1 = mma.sync (diagnostics, A/B comparisons).  Both compute the
  * same causal attention to the same tolerance. */

@@ -119,3 +119,52 @@ def test_decoder_rejects_bad_requests(cuda):
     with pytest.raises(ValueError, match="tokens"):
         dec.decode(np.array([[g.vocab]]))
     dec.destroy()
+
+
+def test_fused_rope_append_equals_separate_steps(cuda):
+    """bgtq_append_kv_rope (one launch: RoPE on K, encode, FP16 V append for every KV head)
+    writes the bytes that torch RoPE followed by PackedKeys / Values appends write."""
+    import ctypes as C
+    import torch
+    from bgtq import GroupedAttention, PackedKeys, Values, _lib
+    zh = np.load(GOLDEN / "smollm2_heads.npz")
+    H, G, B, d = 2, 3, 3, 64
+    pairs = d // 2
+    inv = torch.pow(torch.tensor(1e5, dtype=torch.float32), -torch.arange(pairs, dtype=torch.float32) / pairs)
+    rng = np.random.default_rng(8)
+    tabs = [(zh[f"h{h}_config"], zh[f"h{h}_table"]) for h in range(H)]
+    fused_k = [PackedKeys(t, 64, sequences=B) for t in tabs]
+    fused_v = [Values(d, 64, "f16", sequences=B) for _ in range(H)]
+    ref_k = [PackedKeys(t, 64, sequences=B) for t in tabs]
+    ref_v = [Values(d, 64, "f16", sequences=B) for _ in range(H)]
+    row = (H * G + 2 * H) * d
+    kp = (C.c_void_p * H)(*[k._handle for k in fused_k])
+    vp = (C.c_void_p * H)(*[v._handle for v in fused_v])
+    start = 0
+    for n in (5, 1, 1, 7):
+        qkv = torch.from_numpy(rng.standard_normal((B, n, row)).astype(np.float32) * 3).to(cuda)
+        _lib.call("bgtq_append_kv_rope", H, kp, vp, C.c_void_p(qkv.data_ptr()), row, n * row, H * G * d,
+                  H * G * d + H * d, n, 0, B, inv.numpy().ctypes.data, None)
+        pos = torch.arange(start, start + n, device=cuda, dtype=torch.float32)
+        ang = pos[:, None] * inv.to(cuda)[None, :]
+        c, s = torch.cos(ang), torch.sin(ang)
+        for h in range(H):
+            k = qkv[:, :, H * G * d + h * d:H * G * d + (h + 1) * d]
+            a, b = k[..., :pairs], k[..., pairs:]
+            kr = torch.cat([a * c - b * s, b * c + a * s], -1).contiguous()
+            ref_k[h].append(kr)
+            ref_v[h].append(qkv[:, :, H * G * d + H * d + h * d:H * G * d + H * d + (h + 1) * d].contiguous())
+        start += n
+    torch.cuda.synchronize()
+    for h in range(H):
+        for s_ in range(B):
+            assert fused_k[h].lengths(s_) == ref_k[h].lengths(s_) == start
+            np.testing.assert_array_equal(fused_k[h].read(s_)[0], ref_k[h].read(s_)[0])
+            np.testing.assert_array_equal(fused_k[h].read(s_)[1], ref_k[h].read(s_)[1])
+    # values: attention with the same keys sees the same V rows
+    q = torch.from_numpy(rng.standard_normal((B, H, G, d)).astype(np.float32)).to(cuda)
+    o1 = GroupedAttention(fused_k, fused_v, G).attend(q)
+    o2 = GroupedAttention(fused_k, ref_v, G).attend(q)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(o1.cpu().numpy(), o2.cpu().numpy())
+    assert device_status(0) == 0
