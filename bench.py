@@ -397,12 +397,13 @@ def run_model(args, rank, world, local_rank):
     dec.prefill(torch.from_numpy(rng.integers(0, g.vocab, (1, prefix))).to(dev), chunk=1024)
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t_pre
-    toks = [torch.from_numpy(rng.integers(0, g.vocab, (1, 1))).to(dev) for _ in range(warmup + steps)]
+    toks = [torch.from_numpy(rng.integers(0, g.vocab, (1, 1))).to(dev) for _ in range(warmup + steps + 1)]
     it = iter(toks)
     logits = []
+    dec.capture_decode(next(it))   # one eager decode step, then the step recorded as a CUDA graph
 
     def step():
-        logits.append(dec.decode(next(it)))
+        logits.append(dec.decode_graph(next(it)).clone())
 
     def barrier():
         sharding.barrier(dist, torch.cuda.synchronize)
@@ -420,7 +421,7 @@ def run_model(args, rank, world, local_rank):
     finite = all(bool(torch.isfinite(x).all()) for x in logits)
     if rank == 0:
         print(json.dumps({
-            "metric": f"{g.family} whole-model decode tokens/s (batch 1 per GPU, 4096-token prefix)",
+            "metric": f"{g.family} whole-model decode tokens/s (batch 1 per GPU, 4096-token prefix, CUDA graph)",
             "value": world * 1e3 / ms, "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (random-init FP16 weights N(0,0.02), uniform random token ids)",

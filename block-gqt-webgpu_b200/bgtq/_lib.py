@@ -90,6 +90,9 @@ SIGNATURES = {
     "bgtq_append_kv_rope": (I32, [U32, P, P, P, C.c_uint64, C.c_uint64, U32, U32, U32, U32, U32, P, P]),
     "bgtq_attention_set_prefill_kernel": (I32, [P, U32]),
     "bgtq_attention_set_rope": (I32, [P, P, U32]),
+    "bgtq_attention_plan_for_capacity": (I32, [P, C.c_int]),
+    "bgtq_keys_sync_lengths": (I32, [P]),
+    "bgtq_values_sync_lengths": (I32, [P]),
     "bgtq_values_reset": (I32, [P, P]),
 }
 

@@ -153,7 +153,7 @@ class Decoder:
         import torch
         return torch.nn.functional.rms_norm(x, (self.g.hidden,), w, self.g.rms_eps)
 
-    def forward(self, tokens):
+    def forward(self, tokens, _check: bool = True):
         """decoder.ts:31-81 for a [batch, n] chunk: returns the last position's logits
         [batch, vocab] (FP32)."""
         import ctypes as C
@@ -163,8 +163,10 @@ class Decoder:
         g = self.g
         tokens = torch.as_tensor(tokens, device=self.dev).reshape(self.batch, -1).long()
         B, n = tokens.shape
-        if n < 1 or self.length + n > self.capacity or int(tokens.max()) >= g.vocab or int(tokens.min()) < 0:
-            raise ValueError("Invalid tokens/capacity")  # decoder.ts:33
+        if _check:
+            self._sync_lengths()
+            if n < 1 or self.length + n > self.capacity or int(tokens.max()) >= g.vocab or int(tokens.min()) < 0:
+                raise ValueError("Invalid tokens/capacity")  # decoder.ts:33
         start = self.length
         st = torch.cuda.current_stream(self.dev).cuda_stream
         qw, kvw = g.q_heads * g.head_dim, g.kv_heads * g.head_dim
@@ -209,7 +211,51 @@ class Decoder:
         """decoder.ts:83: one token per sequence."""
         return self.forward(token)
 
+    # ---- CUDA graph of one decode step ----
+    def capture_decode(self, token):
+        """Decode `token` eagerly, then record the whole decode step (every layer's GEMMs,
+        norms, K/V append and attention) as one CUDA graph; decode_graph() replays it.
+        Attention plans its split-KV factor for the capacity, so replays stay exact while
+        the sequences grow; appends inside replays move the device lengths only."""
+        import torch
+        from . import _lib
+        for a in self.attn:
+            _lib.call("bgtq_attention_plan_for_capacity", a._handle, 1)
+        out = self.forward(token)                      # eager step: warms every kernel up
+        torch.cuda.synchronize(self.dev)
+        self._tok = torch.as_tensor(token, device=self.dev).reshape(self.batch, 1).long().clone()
+        self._graph = torch.cuda.CUDAGraph()
+        length = self.length
+        with torch.cuda.graph(self._graph):
+            self._logits = self.forward(self._tok, _check=False)
+        self.length = length                           # recording appended nothing
+        self._host_stale = True
+        self._sync_lengths()
+        return out
+
+    def decode_graph(self, token):
+        """Replay the recorded decode step for `token` [batch, 1]; returns the graph's
+        logits buffer (overwritten by the next replay)."""
+        if self.length + 1 > self.capacity:
+            raise ValueError("Invalid tokens/capacity")
+        self._tok.copy_(token.reshape(self.batch, 1))
+        self._graph.replay()
+        self.length += 1
+        self._host_stale = True
+        return self._logits
+
+    def _sync_lengths(self):
+        from . import _lib
+        if getattr(self, "_host_stale", False):
+            for ks, vs in zip(self.keys, self.values):
+                for k in ks:
+                    _lib.call("bgtq_keys_sync_lengths", k._handle)
+                for v in vs:
+                    _lib.call("bgtq_values_sync_lengths", v._handle)
+            self._host_stale = False
+
     def destroy(self):
+        self._graph = None
         for a in self.attn:
             a.destroy()
         for layer in self.keys + self.values:

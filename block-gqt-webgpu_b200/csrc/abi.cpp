@@ -473,6 +473,10 @@ bgtq_status bgtq_append_kv_rope(uint32_t heads, bgtq_keys *const *keys, bgtq_val
     a.heads = heads;
     a.vD = values[0]->D;
     a.v_swizzle = values_swizzled(0, values[0]->D) ? 1u : 0u;
+    a.capacity = ~0u;
+    for (uint32_t h = 0; h < heads; ++h) a.capacity = std::min(a.capacity, std::min(keys[h]->capacity, values[h]->capacity));
+    a.status = device_status_word(k0->device);
+    if (!a.status) return fail(BGTQ_ECUDA, "no status word");
     for (uint32_t p = 0; p < d / 2; ++p) a.inv_freq[p] = inv_freq[p];
     cudaError_t e = launch_kv_rope_append(a, d, static_cast<cudaStream_t>(stream_));
     if (e != cudaSuccess) return cuda_fail(e, "K/V append launch");
@@ -787,6 +791,9 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
         min_len = std::min(min_len, L);
     }
     if (logits && min_len != max_len) return fail(BGTQ_EINVAL, "logit capture needs equal lengths");
+    // a launch recorded once and replayed while the sequences grow plans its splits for the
+    // longest length it may meet
+    const uint32_t plan_len = at->plan_capacity && !logits ? at->keys[0]->capacity : max_len;
     if (host) {
         const size_t nq = (size_t)seq_count * H * rows * d;
         for (size_t i = 0; i < nq; ++i)
@@ -888,7 +895,7 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
     a.causal = causal ? 1u : 0u;
     a.logit_stride = max_len;
     uint32_t splits = 1;
-    cudaError_t e = launch_attention(a, kk, at->values[0]->dtype == BGTQ_F32, d, max_cent, max_len, at->forced_splits,
+    cudaError_t e = launch_attention(a, kk, at->values[0]->dtype == BGTQ_F32, d, max_cent, plan_len, at->forced_splits,
                                      at->max_splits, &splits, stream);
     if (e != cudaSuccess) return cuda_fail(e, "attention launch");
     launches += 2;  // query rotation + attention
@@ -985,6 +992,26 @@ bgtq_status bgtq_attention_set_splits(bgtq_attention *a, uint32_t splits) {
     a->forced_splits = splits;
     return BGTQ_OK;
 }
+bgtq_status bgtq_attention_plan_for_capacity(bgtq_attention *a, int on) {
+    if (!a) return fail(BGTQ_EINVAL, "null attention");
+    a->plan_capacity = on != 0;
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_keys_sync_lengths(bgtq_keys *k) {
+    if (!k) return fail(BGTQ_EINVAL, "null keys");
+    DeviceGuard g(k->device);
+    CK(cudaMemcpy(k->lengths.data(), k->d_lengths, (size_t)k->sequences * 4, cudaMemcpyDeviceToHost), "lengths");
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_values_sync_lengths(bgtq_values *v) {
+    if (!v) return fail(BGTQ_EINVAL, "null values");
+    DeviceGuard g(v->device);
+    CK(cudaMemcpy(v->lengths.data(), v->d_lengths, (size_t)v->sequences * 4, cudaMemcpyDeviceToHost), "lengths");
+    return BGTQ_OK;
+}
+
 bgtq_status bgtq_attention_set_rope(bgtq_attention *a, const float *inv_freq, uint32_t n) {
     if (!a || (n && (!inv_freq || n != a->dim / 2))) return fail(BGTQ_EINVAL, "RoPE table must hold dim/2 entries");
     if (!n) {

@@ -877,12 +877,25 @@ cudaError_t run(const AttnArgs &a, const Plan &pl, uint32_t d, dim3 grid, cudaSt
     return cudaGetLastError();
 }
 
+// Resident CTAs per SM for a plan; remembered per (device, shared-memory size), so launches
+// after the first make no attribute calls (nothing but the launch itself while a stream is
+// being captured).
 template <int D, int QM, KKind KK, bool VF32>
 int occupancy(const Plan &pl) {
     auto kern = attn_kernel<D, QM, KK, VF32>;
+    static int cached_dev[8] = {-1, -1, -1, -1, -1, -1, -1, -1};
+    static uint32_t cached_smem[8] = {};
+    static int cached_n[8] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int slot = dev & 7;
+    if (cached_dev[slot] == dev && cached_smem[slot] == pl.total) return cached_n[slot];
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.total);
     int n = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, pl.total);
+    cached_dev[slot] = dev;
+    cached_smem[slot] = pl.total;
+    cached_n[slot] = n;
     return n;
 }
 

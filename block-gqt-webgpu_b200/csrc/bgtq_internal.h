@@ -90,6 +90,8 @@ struct KvRopeArgs {
     uint64_t v_seq_stride[kMaxHeads];  // halves between sequences of each value store
     uint64_t row_stride, seq_stride;   // floats
     uint32_t k_offset, v_offset, count, seq_first, seq_count, heads, vD, v_swizzle;
+    uint32_t capacity;              // rows every store can hold: rows at or past it are refused
+    uint32_t *status;               // device status word (kStatusBadLength on a refusal)
     float inv_freq[kMaxDim / 2];
 };
 

@@ -338,6 +338,10 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
     for (uint32_t q = blockIdx.x * W + w; q < total; q += gridDim.x * W) {
         const uint32_t s = q / a.count, rr = q % a.count, seq = a.seq_first + s;
         const uint32_t pos = a.start[seq] + rr;
+        if (pos >= a.capacity) {  // replayed past the capacity the host checked: refuse, report
+            if (lane == 0) atomicOr(a.status, kStatusBadLength);
+            continue;
+        }
         const float *src = a.src + (uint64_t)s * a.seq_stride + (uint64_t)rr * a.row_stride;
         const float *ks = src + a.k_offset + (uint64_t)hd * d, *vs = src + a.v_offset + (uint64_t)hd * d;
         for (uint32_t p = lane; p < pairs; p += 32) {
@@ -366,8 +370,9 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
 __global__ void bump_lengths_kernel(const __grid_constant__ KvRopeArgs a) {
     for (uint32_t s = threadIdx.x; s < a.seq_count; s += blockDim.x)
         for (uint32_t hd = 0; hd < a.heads; ++hd) {
-            a.head[hd].lengths[a.seq_first + s] += a.count;
-            a.v_lengths[hd][a.seq_first + s] += a.count;
+            const uint32_t kl = a.head[hd].lengths[a.seq_first + s], vl = a.v_lengths[hd][a.seq_first + s];
+            a.head[hd].lengths[a.seq_first + s] = min(kl + a.count, a.capacity);
+            a.v_lengths[hd][a.seq_first + s] = min(vl + a.count, a.capacity);
         }
 }
 

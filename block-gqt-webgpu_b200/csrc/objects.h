@@ -73,4 +73,5 @@ struct bgtq_attention {
     uint32_t prefill_kernel = 0;  // 0: tcgen05 / TMEM kernel, 1: mma.sync kernel
     bgtq::DevBuf rope;            // RoPE table when queries arrive before RoPE (else empty)
     bool use_rope = false;
+    bool plan_capacity = false;   // split plan for the keys' capacity (graph replays)
 };

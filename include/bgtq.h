@@ -225,6 +225,14 @@ bgtq_status bgtq_attend_prefill(bgtq_attention *a, const float *q, uint32_t pos_
 bgtq_status bgtq_attention_last_splits(const bgtq_attention *a, uint32_t *splits_out);
 /* Force a split-KV factor (0 = automatic). */
 bgtq_status bgtq_attention_set_splits(bgtq_attention *a, uint32_t splits);
+/* For launches recorded once (CUDA graph capture) and replayed while sequences grow: on != 0
+ * makes bgtq_attend plan its split-KV factor for the keys' capacity instead of the current
+ * lengths, so a replay covers every row appended since.  No counterpart in the reference. */
+bgtq_status bgtq_attention_plan_for_capacity(bgtq_attention *a, int on);
+/* Replayed appends (bgtq_append_kv_rope inside a graph) advance the device lengths only;
+ * these copy them back to the host-side bookkeeping that later calls validate against. */
+bgtq_status bgtq_keys_sync_lengths(bgtq_keys *k);
+bgtq_status bgtq_values_sync_lengths(bgtq_values *v);
 /* Queries arrive before RoPE (the model path's raw Q projection): bgtq_attend and
  * bgtq_attend_prefill apply split-half RoPE (src/model/kernels.wgsl:49-54) with the table
  * inv_freq[n], n = dim/2, at each query's position (positions[], else the last appended

@@ -168,3 +168,34 @@ def test_fused_rope_append_equals_separate_steps(cuda):
     torch.cuda.synchronize()
     np.testing.assert_array_equal(o1.cpu().numpy(), o2.cpu().numpy())
     assert device_status(0) == 0
+
+
+def test_graph_replayed_decode_matches_eager(cuda):
+    """A CUDA graph of the decode step (capture_decode / decode_graph) gives the eager
+    decoder's logits while the caches grow across replays."""
+    import torch
+    g = GEOMS["qwen-like"]
+    w = random_weights(g, seed=5, device=cuda, std=0.08)
+    B = 2
+    eager = Decoder(w, g, 200, _tables(g), batch=B)
+    graph = Decoder(w, g, 200, _tables(g), batch=B)
+    rng = np.random.default_rng(4)
+    prompt = torch.from_numpy(rng.integers(0, g.vocab, (B, 60))).to(cuda)
+    eager.prefill(prompt)
+    graph.prefill(prompt)
+    toks = [torch.from_numpy(rng.integers(0, g.vocab, (B, 1))).to(cuda) for _ in range(6)]
+    np.testing.assert_allclose(graph.capture_decode(toks[0]).cpu().numpy(), eager.decode(toks[0]).cpu().numpy(),
+                               atol=1e-5, rtol=1e-4)
+    for t in toks[1:]:
+        got = graph.decode_graph(t).clone()
+        ref = eager.decode(t)
+        np.testing.assert_allclose(got.cpu().numpy(), ref.cpu().numpy(), atol=1e-5, rtol=1e-4)
+    assert graph.length == eager.length == 66
+    graph._sync_lengths()
+    assert graph.keys[0][0].lengths(1) == 66
+    # an eager step after replays continues from the device lengths
+    t = torch.from_numpy(rng.integers(0, g.vocab, (B, 1))).to(cuda)
+    np.testing.assert_allclose(graph.decode(t).cpu().numpy(), eager.decode(t).cpu().numpy(), atol=1e-5, rtol=1e-4)
+    assert device_status(0) == 0
+    eager.destroy()
+    graph.destroy()
