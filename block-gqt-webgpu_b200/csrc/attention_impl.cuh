@@ -193,6 +193,15 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// 2^x on the special-function unit (PTX ex2.approx.ftz: relative error below 2^-22,
+// 2^-inf = +0, results below 2^-126 flushed to 0, which is far below any probability that
+// matters here).
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -614,15 +623,16 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
 #pragma unroll
                 for (int tt = 1; tt < TPL; ++tt) tm = fmaxf(tm, lg[tt]);
                 const float mnew = fmaxf(m[r], warp_max(tm));
-                alpha[r] = exp2f(m[r] - mnew);  // 0 on the first live tile: l and O are still 0
+                alpha[r] = ex2(m[r] - mnew);  // 0 on the first live tile: l and O are still 0
                 m[r] = mnew;
                 rescale = true;
             }
-            const float mref = m[r] - kPShift;
+            // no live score yet keeps m at -inf and every score at -inf: 2^(-inf - 0) = 0
+            const float mref = m[r] == -INFINITY ? 0.0f : m[r] - kPShift;
             float ps = 0.0f;
 #pragma unroll
             for (int tt = 0; tt < TPL; ++tt) {
-                const float p = lg[tt] == -INFINITY ? 0.0f : exp2f(lg[tt] - mref);
+                const float p = ex2(lg[tt] - mref);
                 pbuf[r * TT + tt * 32 + lane] = p;
                 ps += p;
             }
@@ -660,8 +670,9 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
                 }
                 const __half2 ha = __floats2half2_rn(pa.x, pa.y), hb = __floats2half2_rn(pb.x, pb.y);
                 const float2 fa = __half22float2(ha), fb = __half22float2(hb);
-                const __half2 la = __floats2half2_rn(pa.x - fa.x, pa.y - fa.y);
-                const __half2 lb = __floats2half2_rn(pb.x - fb.x, pb.y - fb.y);
+                const float2 m1 = make_float2(-1.0f, -1.0f);
+                const float2 ra = __ffma2_rn(fa, m1, pa), rb = __ffma2_rn(fb, m1, pb);  // exact p - hi
+                const __half2 la = __floats2half2_rn(ra.x, ra.y), lb = __floats2half2_rn(rb.x, rb.y);
                 const uint32_t ahi0 = h2_bits(ha), ahi2 = h2_bits(hb), alo0 = h2_bits(la), alo2 = h2_bits(lb);
                 // ldmatrix row address of this lane: matrix mi (tokens +8*(mi&1), chunk +(mi>>1)), row ri
                 const uint32_t tok = (uint32_t)(kb16 * 16 + (mi & 1) * 8 + ri);
@@ -769,7 +780,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
 #pragma unroll
         for (int ww = 0; ww < kWarps; ++ww) {
             const float mw = mm[ww * QP + r];
-            const float f = mw == -INFINITY ? 0.0f : exp2f(mw - M);
+            const float f = mw == -INFINITY ? 0.0f : ex2(mw - M);
             L = fmaf(ml[ww * QP + r], f, L);
             Ov = fmaf(mO[(ww * QP + r) * D + dd], f, Ov);
         }
@@ -801,7 +812,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
                 float L = 0.0f, Ov = 0.0f;
                 for (uint32_t sp = 0; sp < a.splits; ++sp) {
                     const float ms = __ldcg(pp + sp * sstride + d);
-                    const float f = ms == -INFINITY ? 0.0f : exp2f(ms - M);
+                    const float f = ms == -INFINITY ? 0.0f : ex2(ms - M);
                     L = fmaf(__ldcg(pp + sp * sstride + d + 1), f, L);
                     Ov = fmaf(__ldcg(pp + sp * sstride + dd), f, Ov);
                 }

@@ -95,7 +95,8 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r
 __device__ __forceinline__ void split2(float x, float y, uint32_t &hi, uint32_t &lo) {
     const __half2 h = __floats2half2_rn(x, y);
     const float2 f = __half22float2(h);
-    const __half2 l = __floats2half2_rn(x - f.x, y - f.y);
+    const float2 r = __ffma2_rn(f, make_float2(-1.0f, -1.0f), make_float2(x, y));  // exact x - f
+    const __half2 l = __floats2half2_rn(r.x, r.y);
     hi = *reinterpret_cast<const uint32_t *>(&h);
     lo = *reinterpret_cast<const uint32_t *>(&l);
 }
@@ -328,7 +329,7 @@ __global__ void __launch_bounds__(Shape<G>::W * 32, 2) prefill_kernel(const __gr
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
                 const float mnew = fmaxf(m[hr], mx);
-                alpha[hr] = mnew == -INFINITY ? 1.0f : exp2f(m[hr] - mnew);
+                alpha[hr] = mnew == -INFINITY ? 1.0f : attn::ex2(m[hr] - mnew);
                 m[hr] = mnew;
                 const float mref = mnew == -INFINITY ? 0.0f : mnew - kPShift;
                 float ps = 0.0f;
@@ -337,7 +338,7 @@ __global__ void __launch_bounds__(Shape<G>::W * 32, 2) prefill_kernel(const __gr
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         const float x = sf[nt][2 * hr + e];
-                        const float p = x == -INFINITY ? 0.0f : exp2f(x - mref);
+                        const float p = attn::ex2(x - mref);  // masked: 2^-inf = 0
                         sf[nt][2 * hr + e] = p;
                         ps += p;
                     }

@@ -127,7 +127,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 __device__ __forceinline__ void split2(float x, float y, uint32_t &hi, uint32_t &lo) {
     const __half2 h = __floats2half2_rn(x, y);
     const float2 f = __half22float2(h);
-    const __half2 l = __floats2half2_rn(x - f.x, y - f.y);
+    const float2 r = __ffma2_rn(f, make_float2(-1.0f, -1.0f), make_float2(x, y));  // exact x - f
+    const __half2 l = __floats2half2_rn(r.x, r.y);
     hi = *reinterpret_cast<const uint32_t *>(&h);
     lo = *reinterpret_cast<const uint32_t *>(&l);
 }
@@ -323,26 +324,28 @@ __global__ void __launch_bounds__(NTH, 2) prefill_tc_kernel(const __grid_constan
             for (int i = 0; i < 32; ++i) sv[i] += t[i];
         }
         const uint32_t k0 = j * BN + c0;
+        if (!live || k0 + 31u > pos || k0 + 32u > len) {  // keys past the row's position or the length
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const uint32_t key = k0 + i;
+                sv[i] = live && key <= pos && key < len ? sv[i] : -INFINITY;
+            }
+        }
         float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const uint32_t key = k0 + i;
-            const bool ok = live && key <= pos && key < len;
-            sv[i] = ok ? sv[i] : -INFINITY;
-            mx = fmaxf(mx, sv[i]);
-        }
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, sv[i]);
         red[hf * M + row] = mx;
         tc_before_sync();
         __syncthreads();
         mx = fmaxf(red[row], red[M + row]);
         const float mnew = fmaxf(m_run, mx);
-        const float alpha = mnew == -INFINITY ? 1.0f : exp2f(m_run - mnew);
+        const float alpha = mnew == -INFINITY ? 1.0f : attn::ex2(m_run - mnew);
         m_run = mnew;
         const float mref = mnew == -INFINITY ? 0.0f : mnew - kPShift;
         float ps = 0.0f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-            const float p = sv[i] == -INFINITY ? 0.0f : exp2f(sv[i] - mref);
+            const float p = attn::ex2(sv[i] - mref);  // masked: 2^-inf = 0
             sv[i] = p;
             ps += p;
         }
