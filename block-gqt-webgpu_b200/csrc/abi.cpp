@@ -87,6 +87,8 @@ cudaError_t upload_tables(const Layout &L, DeviceTables &dt) {
     const size_t o_grp = off; off = a16(off + L.d);
     const size_t o_cbi = off; off = a16(off + L.d);
     const size_t o_cbb = off; off = a16(off + 2 * L.d);
+    const size_t o_lk = off; off = a16(off + 4 * L.lookup.size());
+    const size_t o_lko = off; off = a16(off + 2 * L.d);
     std::vector<unsigned char> host(off, 0);
     std::memcpy(host.data() + o_rot, L.rot.data(), 4 * n_rot);
     if (n_cent) std::memcpy(host.data() + o_cent, L.cent_compact.data(), 4 * n_cent);
@@ -97,6 +99,8 @@ cudaError_t upload_tables(const Layout &L, DeviceTables &dt) {
     std::memcpy(host.data() + o_grp, L.group_of.data(), L.d);
     std::memcpy(host.data() + o_cbi, L.pos_to_cb.data(), L.d);
     std::memcpy(host.data() + o_cbb, L.cb_base.data(), 2 * L.d);
+    std::memcpy(host.data() + o_lk, L.lookup.data(), 4 * L.lookup.size());
+    std::memcpy(host.data() + o_lko, L.lookup_off.data(), 2 * L.d);
     void *blob = nullptr;
     cudaError_t e = cudaMalloc(&blob, off);
     if (e != cudaSuccess) return e;
@@ -117,6 +121,8 @@ cudaError_t upload_tables(const Layout &L, DeviceTables &dt) {
     dt.group_of = b + o_grp;
     dt.cbidx = b + o_cbi;
     dt.cb_base = reinterpret_cast<const uint16_t *>(b + o_cbb);
+    dt.lookup = reinterpret_cast<const float *>(b + o_lk);
+    dt.lookup_off = reinterpret_cast<const uint16_t *>(b + o_lko);
     return cudaSuccess;
 }
 
@@ -762,6 +768,9 @@ void fill_packed_head(AttnHead &ah, const bgtq_keys *k, const bgtq_values *v) {
     ah.ns = k->L.ns;
     ah.ng = k->L.ng;
     ah.n_cent = (uint32_t)k->L.cent_compact.size();
+    ah.lookup = k->dt.lookup;
+    ah.lookup_off = k->dt.lookup_off;
+    ah.n_lookup = (uint32_t)k->L.lookup.size();
     for (int i = 0; i < 4; ++i) ah.bound_mask[i] = k->L.bound_mask[i];
     for (int gi = 0; gi <= kMaxGroups; ++gi) ah.group_off[gi] = k->L.group_off[gi];
     for (uint32_t j = 0; j < (uint32_t)kMaxDim; ++j) ah.cb_base[j] = j < k->dim ? k->L.cb_base[j] : (uint16_t)ah.n_cent;
@@ -848,7 +857,7 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
         ah.v_seq_stride = (uint64_t)v->cap_alloc * v->D * vsz;
         if (kk == KKind::Packed) {
             fill_packed_head(ah, k, v);
-            max_cent = std::max(max_cent, ah.n_cent);
+            max_cent = std::max(max_cent, ah.n_lookup);
         } else if (kk == KKind::F16) {
             ah.k = k->rows;
             ah.k_seq_stride = (uint64_t)k->cap_alloc * k->row_stride;

@@ -107,6 +107,9 @@ inline Plan make_plan(KKind kk, int v_f32, uint32_t D, uint32_t QP, uint32_t TT,
     Plan p{};
     p.stages = stages;
     uint32_t off = 0;
+    // the lookup table first: its slots' byte offsets must keep their 256-byte (nibble runs)
+    // and size (byte dims) alignment; the 256 zero floats after it cover any code byte of
+    // a padding record
     p.cent = off;
     p.cent_alloc = kk == KKind::Packed ? n_cent + 256u : 0u;
     off = align16(off + 4u * p.cent_alloc);
@@ -232,9 +235,10 @@ __device__ __forceinline__ void load_q(const float *p, float (&q)[QP]) {
 }
 
 // Build the packed-path pair records for one (sequence, head) from the query records qt
-// [D][QP] and the head's codebook offsets: group g's pairs [off_g/2, off_{g+1}/2) padded
-// to 4*ceil(pairs/4) records; padding records carry zero query values (their codebook
-// offsets stay in range, so whatever code bytes they meet contribute exactly 0).
+// [D][QP] and the head's lookup-layout offsets: group g's pairs [off_g/2, off_{g+1}/2)
+// padded to 4*ceil(pairs/4) records; padding records carry zero query values (their
+// lookups stay inside the table and its zero tail, so whatever code bytes they meet
+// contribute exactly 0).
 template <int D, int QM, int QP>
 __device__ __forceinline__ void build_tables(const AttnHead &h, const float *qt, unsigned char *rec, uint32_t d,
                                              uint32_t cent_off, int tid) {
@@ -252,26 +256,27 @@ __device__ __forceinline__ void build_tables(const AttnHead &h, const float *qt,
                 rp[2 * r] = __float_as_uint(live ? __ldg(qt + j0 * QP + r) : 0.0f);
                 rp[2 * r + 1] = __float_as_uint(live ? __ldg(qt + (j0 + 1) * QP + r) : 0.0f);
             }
-            const uint32_t ja = min(j0, 127u), jb = min(j0 + 1, 127u);
-            rp[2 * QM] = cent_off + 4u * h.cb_base[ja];
-            rp[2 * QM + 1] = cent_off + 4u * h.cb_base[jb];
+            const uint32_t ja = min(j0, d - 1u), jb = min(j0 + 1, d - 1u);
+            rp[2 * QM] = cent_off + 4u * __ldg(h.lookup_off + ja);
+            rp[2 * QM + 1] = cent_off + 4u * __ldg(h.lookup_off + jb);
             for (int x = 2 * QM + 2; x < G::RP; ++x) rp[x] = 0u;
         }
         base += n;
     }
-    (void)d;
 }
 
 // Dequantise + QK for the TPL tokens of this lane (see the file comment).  Groups are
 // walked in order; inside a group, straight-line blocks of 4 dimension pairs (no branches)
 // accumulate each pair into a float2 (even, odd dims) with one packed FMA per query row,
-// and the group's FP16 scale is applied once at the group's end.  A lookup is one byte
-// extract of an index word pre-scaled by 4, one add of the record's codebook offset and one
-// shared load.  Code bytes are read as (unaligned) words: a nibble block needs 4 bytes, a
-// byte block 8.
+// and the group's FP16 scale is applied once at the group's end.  Codebooks sit in the
+// lookup layout (layout.cpp, build_lookup_layout), so a lookup address is one instruction
+// from the code word: a nibble lookup is a byte permute of (code * 4, run slot address) plus
+// a constant offset, a byte lookup an OR (or shifted add) of code * 4 into the dimension's
+// size-aligned slot address from the pair record.  Code bytes are read as (unaligned)
+// words: a nibble block needs 4 bytes, a byte block 8.
 template <int D, int QM>
 __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char *sm, uint32_t kb_s,
-                                          const uint16_t *sb, const unsigned char *rec, uint32_t d, int lane,
+                                          const uint16_t *sb, const unsigned char *rec, uint32_t cb_s, int lane,
                                           float (&acc)[Geo<D>::TPL][QM]) {
     using G = RecGeo<D, QM>;
     constexpr int TPL = Geo<D>::TPL, RP = G::RP;
@@ -294,18 +299,19 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
 #pragma unroll
         for (int r = 0; r < QM; ++r) { acc2[tt][r] = make_float2(0.0f, 0.0f); part[tt][r] = make_float2(0.0f, 0.0f); }
     }
-    // one dimension pair: record + the two pre-scaled indices of each token
-    auto pair = [&](const uint32_t *rp, const uint32_t (&ia)[TPL], const uint32_t (&ib)[TPL]) {
+    // one dimension pair: the record's query values against the two codebook entries of each
+    // token at byte addresses ia + OA, ib + OB
+    auto pair = [&](const uint32_t *rp, const uint32_t (&ia)[TPL], const uint32_t (&ib)[TPL], uint32_t OA,
+                    uint32_t OB) {
         uint32_t v[RP];
 #pragma unroll
         for (int x = 0; x < RP; x += 4) {
             const uint4 t = *reinterpret_cast<const uint4 *>(rp + x);
             v[x] = t.x; v[x + 1] = t.y; v[x + 2] = t.z; v[x + 3] = t.w;
         }
-        const uint32_t ba = v[2 * QM], bb = v[2 * QM + 1];
 #pragma unroll
         for (int tt = 0; tt < TPL; ++tt) {
-            const float2 c = make_float2(lds_f32(sm, ba + ia[tt]), lds_f32(sm, bb + ib[tt]));
+            const float2 c = make_float2(lds_f32(sm, ia[tt] + OA), lds_f32(sm, ib[tt] + OB));
 #pragma unroll
             for (int r = 0; r < QM; ++r)
                 part[tt][r] = __ffma2_rn(make_float2(__uint_as_float(v[2 * r]), __uint_as_float(v[2 * r + 1])), c,
@@ -313,8 +319,9 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
         }
     };
     // a run of cnt <= 4 pairs starting at pair record rp0 whose codes start at byte a of the
-    // row (nibble run: pair b = byte b; byte run: pair b = bytes 2b, 2b+1)
-    auto nib_run = [&](uint32_t a, const uint32_t *rp0, uint32_t cnt) {
+    // row (nibble run: pair b = byte b; byte run: pair b = bytes 2b, 2b+1).  slot: the nibble
+    // run's 256-byte aligned lookup slot.
+    auto nib_run = [&](uint32_t a, const uint32_t *rp0, uint32_t cnt, uint32_t slot) {
         const uint32_t al = a & ~3u, sh = (a & 3u) * 8u;
         uint32_t lo4[TPL], hi4[TPL];
 #pragma unroll
@@ -329,10 +336,10 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
                 uint32_t ia[TPL], ib[TPL];
 #pragma unroll
                 for (int tt = 0; tt < TPL; ++tt) {
-                    ia[tt] = __byte_perm(lo4[tt], 0u, 0x4440u | p);
-                    ib[tt] = __byte_perm(hi4[tt], 0u, 0x4440u | p);
+                    ia[tt] = __byte_perm(lo4[tt], slot, 0x7650u | p);  // slot + code * 4
+                    ib[tt] = __byte_perm(hi4[tt], slot, 0x7650u | p);
                 }
-                pair(rp0 + p * RP, ia, ib);
+                pair(rp0 + p * RP, ia, ib, 64u * p, 256u + 64u * p);
             }
         }
     };
@@ -352,14 +359,17 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
             if ((uint32_t)p < cnt) {
+                const uint32_t *rp = rp0 + p * RP;
+                const uint2 base = *reinterpret_cast<const uint2 *>(rp + 2 * QM);
                 uint32_t ia[TPL], ib[TPL];
 #pragma unroll
                 for (int tt = 0; tt < TPL; ++tt) {
                     const uint32_t e = x4[tt][(p >> 1) * 2], o = x4[tt][(p >> 1) * 2 + 1];
-                    ia[tt] = (p & 1) ? e >> 16 : e & 0xffffu;
-                    ib[tt] = (p & 1) ? o >> 16 : o & 0xffffu;
+                    // slots are aligned to their size: OR / add of code * 4 is the address
+                    ia[tt] = (p & 1) ? base.x + (e >> 16) : base.x | (e & 0xffffu);
+                    ib[tt] = (p & 1) ? base.y + (o >> 16) : base.y | (o & 0xffffu);
                 }
-                pair(rp0 + p * RP, ia, ib);
+                pair(rp, ia, ib, 0u, 0u);
             }
         }
     };
@@ -370,9 +380,11 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
         const uint32_t nfull = np / 4, rem = np & 3u;
         const uint32_t *rg = recs + rix * RP;
         if (go < ns) {
+            // run b of the head owns lookup slot b (512 bytes); the group's first run is rix / 4
+            const uint32_t slot0 = cb_s + (rix >> 2) * 512u;
 #pragma unroll 1
-            for (uint32_t k = 0; k < nfull; ++k) nib_run(p0 + 4 * k, rg + 4 * k * RP, 4);
-            if (rem) nib_run(p0 + 4 * nfull, rg + 4 * nfull * RP, rem);
+            for (uint32_t k = 0; k < nfull; ++k) nib_run(p0 + 4 * k, rg + 4 * k * RP, 4, slot0 + k * 512u);
+            if (rem) nib_run(p0 + 4 * nfull, rg + 4 * nfull * RP, rem, slot0 + nfull * 512u);
         } else {
             // byte group: dim 2*p0 sits at byte ns/2 + (2*p0 - ns)
             const uint32_t ob = 2 * p0 - ns / 2;
@@ -401,7 +413,6 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
     for (int tt = 0; tt < TPL; ++tt)
 #pragma unroll
         for (int r = 0; r < QM; ++r) acc[tt][r] = acc2[tt][r].x + acc2[tt][r].y;
-    (void)d;
 }
 
 // Minimum resident CTAs per SM the register allocation must allow: the packed kernels of
@@ -460,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
     // ---- prologue: codebooks, query tables, barriers ----
     const float *qt = a.qt + ((uint64_t)s * a.heads + hd) * (uint64_t)(D * QP);
     if constexpr (KK == KKind::Packed) {
-        for (uint32_t i = tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < h.n_cent ? h.cent[i] : 0.0f;
+        for (uint32_t i = tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < h.n_lookup ? h.lookup[i] : 0.0f;
         build_tables<D, QM, QP>(h, qt, rec, d, pl.cent, tid);
     } else {
         const float4 *src = reinterpret_cast<const float4 *>(qt);
@@ -549,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
         // ---- logits for this lane's TPL tokens ----
         float acc[TPL][QM];
         if constexpr (KK == KKind::Packed) {
-            packed_qk<D, QM>(h, smem, (uint32_t)(kb - smem), sb, rec, d, lane, acc);
+            packed_qk<D, QM>(h, smem, (uint32_t)(kb - smem), sb, rec, pl.cent, lane, acc);
         } else {
             const uint32_t steps = (n + TPSK - 1) / TPSK;
             for (uint32_t st2 = 0; st2 < steps; ++st2) {

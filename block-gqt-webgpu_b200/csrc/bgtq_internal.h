@@ -33,6 +33,10 @@ struct Layout {
     uint32_t bound_mask[4] = {};                           // bit j: a group starts at dim j (j > 0)
     std::vector<uint16_t> cb_base;                         // compact centroid base per dim
     std::vector<float> cent_compact;                       // per-dim codebooks, 2^w entries each
+    // Decode-attention lookup layout (build_lookup_layout): nibble dimensions in 512-byte
+    // run slots, byte dimensions in power-of-two slots aligned to their size.
+    std::vector<float> lookup;                             // the table, slot by slot
+    std::vector<uint16_t> lookup_off;                      // per dim: float offset of its slot
     std::vector<uint32_t> ranges;                          // [2d] PackedKeys group ranges
 };
 
@@ -50,6 +54,8 @@ struct DeviceTables {
     const uint8_t *lut = nullptr;      // [ncb][256]
     const uint8_t *perm = nullptr, *group_of = nullptr, *cbidx = nullptr;
     const uint16_t *cb_base = nullptr;
+    const float *lookup = nullptr;     // Layout::lookup
+    const uint16_t *lookup_off = nullptr;
 };
 
 // Per-head constants of the encode kernel.
@@ -102,13 +108,15 @@ struct AttnHead {
     const void *v;
     const float *rot;          // dense rotation (packed path)
     const float *cent;         // compact codebooks (packed path)
+    const float *lookup;       // decode-attention lookup layout of the codebooks
+    const uint16_t *lookup_off;
     const uint8_t *perm, *group_of;
     uint64_t k_seq_stride;     // bytes
     uint64_t s_seq_stride;     // halves
     uint64_t v_seq_stride;     // bytes
     uint32_t row_stride;       // bytes between K rows
     uint32_t scale_stride;     // halves
-    uint32_t ns, ng, n_cent;
+    uint32_t ns, ng, n_cent, n_lookup;
     uint32_t bound_mask[4];
     uint32_t group_off[kMaxGroups + 1];
     uint16_t cb_base[kMaxDim];

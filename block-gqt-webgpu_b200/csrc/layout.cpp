@@ -5,6 +5,7 @@
 // (src/runtime/packed-keys.ts:15-23), raising the same classes of error.  It additionally
 // requires what the CUDA kernels rely on and every reference table satisfies: group ids
 // increase along the (head-permuted) dimension order, codes are whole bytes or nibbles.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <set>
@@ -13,6 +14,8 @@
 #include "bgtq_internal.h"
 
 namespace bgtq {
+
+void build_lookup_layout(Layout &L, const std::vector<uint32_t> &cb_size);
 
 static bgtq_status fail(std::string &err, bgtq_status s, const char *msg) {
     err = msg;
@@ -123,7 +126,60 @@ bgtq_status parse_layout(const uint32_t *config, size_t n_config, const float *t
     L.cent_compact.resize(total);
     for (uint32_t i = 0; i < d; ++i)
         for (uint32_t c = 0; c < cb_size[i]; ++c) L.cent_compact[L.cb_base[i] + c] = L.cent[(size_t)i * maxc + c];
+    build_lookup_layout(L, cb_size);
     return BGTQ_OK;
+}
+
+// The decode-attention kernel walks each group's dimension pairs in runs of four (one
+// 32-bit word of nibble codes, two words of byte codes) and forms a lookup address without
+// a separate add:
+//  - nibble groups: run b (numbered over all groups, each group starting a new run) owns the
+//    512-byte slot b; the even dimension of its pair p has its 16-entry codebook at float
+//    128 b + 16 p, the odd one at 128 b + 64 + 16 p.  With the slot 256-byte aligned, one
+//    byte permute of (code * 4, slot address) is the address, and p's offset is a constant.
+//  - byte groups: each dimension gets a slot of P = next power of two >= its group's largest
+//    codebook, aligned to P floats (groups placed in descending P, after the nibble slots),
+//    so slot | code * 4 is the address.
+// Slots are zero past each codebook's reachable codes.
+void build_lookup_layout(Layout &L, const std::vector<uint32_t> &cb_size) {
+    const uint32_t d = L.d;
+    L.lookup_off.assign(d, 0);
+    uint32_t runs = 0, g_first_run[kMaxGroups] = {}, pmax = 1, pg[kMaxGroups] = {};
+    for (uint32_t g = 0; g < L.ng; ++g) {
+        const uint32_t a = L.group_off[g], b = L.group_off[g + 1];
+        g_first_run[g] = runs;
+        if (a < L.ns) {
+            runs += ((b - a) / 2 + 3) / 4;
+        } else {
+            uint32_t m = 1;
+            for (uint32_t j = a; j < b; ++j) m = std::max(m, cb_size[j]);
+            uint32_t p = 1;
+            while (p < m) p *= 2;
+            pg[g] = p;
+            pmax = std::max(pmax, p);
+        }
+    }
+    uint32_t cursor = runs * 128u;
+    cursor = (cursor + pmax - 1) / pmax * pmax;
+    for (uint32_t g = 0; g < L.ng; ++g) {
+        const uint32_t a = L.group_off[g], b = L.group_off[g + 1];
+        if (a >= L.ns) continue;
+        for (uint32_t j = a; j < b; ++j) {
+            const uint32_t q = j / 2 - a / 2;
+            L.lookup_off[j] = (uint16_t)((g_first_run[g] + q / 4) * 128u + (j & 1u) * 64u + (q % 4) * 16u);
+        }
+    }
+    for (uint32_t p = pmax; p >= 1; p /= 2)
+        for (uint32_t g = 0; g < L.ng; ++g) {
+            if (L.group_off[g] < L.ns || pg[g] != p) continue;
+            for (uint32_t j = L.group_off[g]; j < L.group_off[g + 1]; ++j) {
+                L.lookup_off[j] = (uint16_t)cursor;
+                cursor += p;
+            }
+        }
+    L.lookup.assign(cursor, 0.0f);
+    for (uint32_t j = 0; j < d; ++j)
+        for (uint32_t c = 0; c < cb_size[j]; ++c) L.lookup[L.lookup_off[j] + c] = L.cent_compact[L.cb_base[j] + c];
 }
 
 }  // namespace bgtq

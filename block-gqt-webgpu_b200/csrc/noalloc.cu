@@ -137,10 +137,13 @@ extern "C" bgtq_status bgtq_attend_static(uint32_t heads, bgtq_keys *const *keys
         ah.ns = k->L.ns;
         ah.ng = k->L.ng;
         ah.n_cent = (uint32_t)k->L.cent_compact.size();
+        ah.lookup = k->dt.lookup;
+        ah.lookup_off = k->dt.lookup_off;
+        ah.n_lookup = (uint32_t)k->L.lookup.size();
         for (int i = 0; i < 4; ++i) ah.bound_mask[i] = k->L.bound_mask[i];
         for (int g = 0; g <= kMaxGroups; ++g) ah.group_off[g] = k->L.group_off[g];
         for (uint32_t j = 0; j < (uint32_t)kMaxDim; ++j) ah.cb_base[j] = j < d ? k->L.cb_base[j] : (uint16_t)ah.n_cent;
-        max_cent = std::max(max_cent, ah.n_cent);
+        max_cent = std::max(max_cent, ah.n_lookup);
     }
     a.q = q;
     a.qt = qt;
