@@ -36,8 +36,10 @@
 //                  the rescale of O unless a score exceeds the running maximum by 2^3.
 //   P.V            tensor cores (mma.sync m16n8k16, FP16 in, FP32 accumulate) for FP16 V of
 //                  64/128 dims: P is scaled by 2^12 and split into high and low FP16 parts
-//                  (about 22 significant bits) that occupy fragment rows 0-7 and 8-15 of
-//                  one MMA; V tiles arrive chunk-swizzled from the value
+//                  (about 22 significant bits).  Up to 4 query rows compute O^T = V^T P^T
+//                  with the parts in B columns 0-3 and 4-7 (16 dims per MMA); up to 8 rows
+//                  put them in A rows 0-7 and 8-15 (8 dims per MMA).  V tiles arrive
+//                  chunk-swizzled from the value
 //                  store so ldmatrix reads them without bank conflicts.  FP32 V and small
 //                  head dims use FP32 FMAs with lane = 16-byte slice of V.
 #pragma once
@@ -432,6 +434,10 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
     constexpr int KSZ = KK == KKind::F32 ? 4 : 2, KVEC = 16 / KSZ, LPTK = D / KVEC, TPSK = 32 / LPTK;
     static_assert(KK == KKind::Packed || (LPTK >= 1 && LPTK <= 32), "K slice layout");
     constexpr int NT = D / 8;  // MMA n-tiles (8 dims each)
+    // Up to 4 query rows: P.V as O^T = V^T P^T, V^T in the 16-row A operand (16 dims per
+    // tile) and P^T in the 8 B columns (high parts of rows 0-3 in columns 0-3, low parts in
+    // 4-7): half the MMAs and accumulators of the P-as-A form, which up to 8 rows use.
+    constexpr bool TMMA = MMA && QM <= 4;
 
     const uint32_t split = blockIdx.x, hd = blockIdx.y, s = blockIdx.z;
     const AttnHead &h = a.head[hd];
@@ -486,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
     float m[QM], l[QM];
 #pragma unroll
     for (int r = 0; r < QM; ++r) { m[r] = -INFINITY; l[r] = 0.0f; }
-    constexpr int OS = MMA ? NT * 4 : QM * VEC;  // output accumulators per lane
+    constexpr int OS = TMMA ? (D / 16) * 4 : MMA ? NT * 4 : QM * VEC;  // output accumulators per lane
     float O[OS];
 #pragma unroll
     for (int i = 0; i < OS; ++i) O[i] = 0.0f;
@@ -659,7 +665,50 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
         pending &= ~4u;
 
         // ---- P.V ----
-        if constexpr (MMA) {
+        if constexpr (TMMA) {
+            // C fragment: row g / g + 8 = dim (16 per tile), column pair 2c / 2c + 1 = P column;
+            // column j holds the high (j < 4) or low (j >= 4) part of query row j & 3
+            const int g = lane >> 2, c = lane & 3;
+            if (rescale) {
+                // columns 2c, 2c + 1 hold rows 0, 1 (c even) or 2, 3 (c odd)
+                float al[4];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) al[r] = r < QM ? alpha[r < QM ? r : 0] : 1.0f;
+                const bool odd = c & 1;
+                const float a0 = odd ? al[2] : al[0], a1 = odd ? al[3] : al[1];
+#pragma unroll
+                for (int i = 0; i < OS; i += 2) { O[i] *= a0; O[i + 1] *= a1; }
+            }
+            const uint32_t vb_s = smem_u32(vb);
+            const int mi = lane >> 3, ri = lane & 7;
+            const int qg = g & 3;
+            const bool lo_col = g >= 4, live_col = qg < QM;
+#pragma unroll
+            for (int kb16 = 0; kb16 < TT / 16; ++kb16) {
+                float2 pa = make_float2(0.0f, 0.0f), pb = make_float2(0.0f, 0.0f);
+                if (live_col) {
+                    pa = *reinterpret_cast<const float2 *>(pbuf + qg * TT + kb16 * 16 + 2 * c);
+                    pb = *reinterpret_cast<const float2 *>(pbuf + qg * TT + kb16 * 16 + 2 * c + 8);
+                }
+                const __half2 ha = __floats2half2_rn(pa.x, pa.y), hb = __floats2half2_rn(pb.x, pb.y);
+                const float2 fa = __half22float2(ha), fb = __half22float2(hb);
+                const float2 m1 = make_float2(-1.0f, -1.0f);
+                const float2 ra = __ffma2_rn(fa, m1, pa), rb = __ffma2_rn(fb, m1, pb);  // exact p - hi
+                const __half2 la = __floats2half2_rn(ra.x, ra.y), lb = __floats2half2_rn(rb.x, rb.y);
+                const uint32_t b0 = lo_col ? h2_bits(la) : h2_bits(ha), b1 = lo_col ? h2_bits(lb) : h2_bits(hb);
+                // ldmatrix (transposed) row address of this lane: matrix mi = tokens +8*(mi>>1),
+                // dims +8*(mi&1) of the 16-dim tile; row ri
+                const uint32_t tok = (uint32_t)(kb16 * 16 + (mi >> 1) * 8 + ri);
+#pragma unroll
+                for (int mt = 0; mt < D / 16; ++mt) {
+                    const uint32_t chunk = (uint32_t)(2 * mt + (mi & 1));
+                    const uint32_t pos_c = (chunk & ~7u) | ((chunk ^ tok) & 7u);
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4_trans(vb_s + tok * (D * 2) + pos_c * 16, a0, a1, a2, a3);
+                    mma_16816(*reinterpret_cast<float(*)[4]>(&O[mt * 4]), a0, a1, a2, a3, b0, b1);
+                }
+            }
+        } else if constexpr (MMA) {
             // fragment row g = query (high part of P), row g + 8 = the same query (low part);
             // column pair 2c/2c+1 (+8) = token (A) or dim (C)
             const int g = lane >> 2, c = lane & 3;
@@ -758,7 +807,26 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
     float *mO = reinterpret_cast<float *>(smem + pl.stage);  // [kWarps][QP][D]
     float *mm = mO + kWarps * QP * D;                        // [kWarps][QP]
     float *ml = mm + kWarps * QP;
-    if constexpr (MMA) {
+    if constexpr (TMMA) {
+        // add each low column into its high column (lane ^ 2 holds columns 2c ^ 4, 2c+1 ^ 4)
+#pragma unroll
+        for (int i = 0; i < OS; ++i) O[i] += __shfl_xor_sync(0xffffffffu, O[i], 2);
+        const int g = lane >> 2, c = lane & 3;
+        if (c < 2) {
+            const int q0 = 2 * c, q1 = 2 * c + 1;
+#pragma unroll
+            for (int mt = 0; mt < D / 16; ++mt) {
+                if (q0 < QM) {
+                    mO[(w * QP + q0) * D + mt * 16 + g] = O[mt * 4 + 0];
+                    mO[(w * QP + q0) * D + mt * 16 + g + 8] = O[mt * 4 + 2];
+                }
+                if (q1 < QM) {
+                    mO[(w * QP + q1) * D + mt * 16 + g] = O[mt * 4 + 1];
+                    mO[(w * QP + q1) * D + mt * 16 + g + 8] = O[mt * 4 + 3];
+                }
+            }
+        }
+    } else if constexpr (MMA) {
         const int g = lane >> 2, c = lane & 3;
         if (g < QM) {
 #pragma unroll
