@@ -129,7 +129,7 @@ inline Plan make_plan(KKind kk, int v_f32, uint32_t D, uint32_t QP, uint32_t TT,
     p.stage = off;
     off += kWarps * p.warp_bytes;
     p.pbuf = off;
-    off = align16(off + kWarps * TT * (QM ? QM : QP) * 4u);
+    off = align16(off + kWarps * (TT + 8u) * (QM ? QM : QP) * 4u);
     p.bars = off;
     off += kWarps * 4u * 8u;  // per warp: K barriers 0, 1 and the V barrier
     p.total = align16(off);
@@ -450,7 +450,10 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
     float *cent_s = reinterpret_cast<float *>(smem + pl.cent);
     unsigned char *rec = smem + pl.qrec;
     float *qrec_s = reinterpret_cast<float *>(rec);
-    float *pbuf = reinterpret_cast<float *>(smem + pl.pbuf) + w * TT * QM;  // [QM][TT]
+    // P rows of TT floats at a stride of TT + 8: the P.V operand loads of four rows fall in
+    // different banks
+    constexpr int PS = TT + 8;
+    float *pbuf = reinterpret_cast<float *>(smem + pl.pbuf) + w * PS * QM;  // [QM][PS]
     const uint32_t bar0 = smem_u32(smem + pl.bars) + (uint32_t)w * 32u, vbar = bar0 + 16u;
     __shared__ uint32_t s_last;
 
@@ -596,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
                     for (int e = 0; e < KVEC; ++e) sum = fmaf(qreg[r][e], kv[e], sum);
 #pragma unroll
                     for (int o = 1; o < LPTK; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-                    if ((lane % LPTK) == 0 && tl < n) pbuf[r * TT + tl] = sum;
+                    if ((lane % LPTK) == 0 && tl < n) pbuf[r * PS + tl] = sum;
                 }
             }
             __syncwarp();
@@ -604,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
             for (int tt = 0; tt < TPL; ++tt) {
                 const uint32_t tl = tt * 32 + lane;
 #pragma unroll
-                for (int r = 0; r < QM; ++r) acc[tt][r] = tl < n ? pbuf[r * TT + tl] : 0.0f;
+                for (int r = 0; r < QM; ++r) acc[tt][r] = tl < n ? pbuf[r * PS + tl] : 0.0f;
             }
             __syncwarp();
         }
@@ -650,7 +653,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
 #pragma unroll
             for (int tt = 0; tt < TPL; ++tt) {
                 const float p = ex2(lg[tt] - mref);
-                pbuf[r * TT + tt * 32 + lane] = p;
+                pbuf[r * PS + tt * 32 + lane] = p;
                 ps += p;
             }
             l[r] = fmaf(l[r], alpha[r], ps);  // this lane's share; summed over lanes at the end
@@ -687,8 +690,8 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
             for (int kb16 = 0; kb16 < TT / 16; ++kb16) {
                 float2 pa = make_float2(0.0f, 0.0f), pb = make_float2(0.0f, 0.0f);
                 if (live_col) {
-                    pa = *reinterpret_cast<const float2 *>(pbuf + qg * TT + kb16 * 16 + 2 * c);
-                    pb = *reinterpret_cast<const float2 *>(pbuf + qg * TT + kb16 * 16 + 2 * c + 8);
+                    pa = *reinterpret_cast<const float2 *>(pbuf + qg * PS + kb16 * 16 + 2 * c);
+                    pb = *reinterpret_cast<const float2 *>(pbuf + qg * PS + kb16 * 16 + 2 * c + 8);
                 }
                 const __half2 ha = __floats2half2_rn(pa.x, pa.y), hb = __floats2half2_rn(pb.x, pb.y);
                 const float2 fa = __half22float2(ha), fb = __half22float2(hb);
@@ -725,8 +728,8 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
             for (int kb16 = 0; kb16 < TT / 16; ++kb16) {
                 float2 pa = make_float2(0.0f, 0.0f), pb = make_float2(0.0f, 0.0f);
                 if (g < QM) {
-                    pa = *reinterpret_cast<const float2 *>(pbuf + g * TT + kb16 * 16 + 2 * c);
-                    pb = *reinterpret_cast<const float2 *>(pbuf + g * TT + kb16 * 16 + 2 * c + 8);
+                    pa = *reinterpret_cast<const float2 *>(pbuf + g * PS + kb16 * 16 + 2 * c);
+                    pb = *reinterpret_cast<const float2 *>(pbuf + g * PS + kb16 * 16 + 2 * c + 8);
                 }
                 const __half2 ha = __floats2half2_rn(pa.x, pa.y), hb = __floats2half2_rn(pb.x, pb.y);
                 const float2 fa = __half22float2(ha), fb = __half22float2(hb);
@@ -776,7 +779,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
                     }
 #pragma unroll
                     for (int r = 0; r < QM; ++r) {
-                        const float p = pbuf[r * TT + tl];
+                        const float p = pbuf[r * PS + tl];
 #pragma unroll
                         for (int e = 0; e < VEC; ++e) O[r * VEC + e] = fmaf(p, vv[e], O[r * VEC + e]);
                     }
