@@ -61,6 +61,9 @@ SIGNATURES = {
     "bgtq_last_error": (C.c_char_p, []),
     "bgtq_version": (C.c_char_p, []),
     "bgtq_allocate_bits": (I32, [P, U32, I64, I32, I32, P]),
+    "bgtq_tables_build": (I32, [U32, P, P, U32, U32, U32, P, SZ, P, P, SZ, P]),
+    "bgtq_haar_rotation": (I32, [U32, U64, P]),
+    "bgtq_optimal_centroids": (I32, [U32, U32, P]),
     "bgtq_layout_validate": (I32, [P, SZ, P, SZ, P, C.POINTER(LayoutInfo)]),
     "bgtq_tables_create": (I32, [P, SZ, P, SZ, C.c_int, C.POINTER(P)]),
     "bgtq_tables_info": (I32, [P, C.POINTER(LayoutInfo)]),

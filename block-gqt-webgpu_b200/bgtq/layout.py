@@ -94,6 +94,40 @@ def validate_layout(config: np.ndarray, table: np.ndarray) -> tuple[_lib.LayoutI
     return info, ranges[:2 * dim]
 
 
+def build_tables(widths, rotation_threshold: int = 3, row_pad: int = 0, norm_stride: int = 0,
+                 pair_order=None) -> tuple[np.ndarray, np.ndarray]:
+    """Flattened (config u32, table f32) of one head from per-pair widths, built natively
+    the way the reference's calibration builds them (block_gtq_pipeline.py:151-246,
+    quant_kernels.py:276-364, quantizer.py:34-106; see bgtq_tables_build).  pair_order: an
+    optional width-ascending permutation of the pairs to use instead of the argsort order."""
+    w = np.ascontiguousarray(widths, dtype=np.int64)
+    dim = 2 * len(w)
+    po = None if pair_order is None else np.ascontiguousarray(pair_order, dtype=np.int64)
+    pp = None if po is None else po.ctypes.data
+    nc, nt = C.c_size_t(0), C.c_size_t(0)
+    _lib.call("bgtq_tables_build", dim, w.ctypes.data, pp, rotation_threshold, row_pad, norm_stride, None, 0,
+              C.byref(nc), None, 0, C.byref(nt))
+    config = np.zeros(nc.value, np.uint32)
+    table = np.zeros(nt.value, np.float32)
+    _lib.call("bgtq_tables_build", dim, w.ctypes.data, pp, rotation_threshold, row_pad, norm_stride,
+              config.ctypes.data, config.size, C.byref(nc), table.ctypes.data, table.size, C.byref(nt))
+    return config, table
+
+
+def haar_rotation(n: int, seed: int) -> np.ndarray:
+    """NumPy default_rng(seed) Haar rotation of size n in FP32 (block_gtq_pipeline.py:81-92)."""
+    out = np.zeros((n, n), np.float32)
+    _lib.call("bgtq_haar_rotation", n, seed, out.ctypes.data)
+    return out
+
+
+def optimal_centroids(bits: int, n: int) -> np.ndarray:
+    """Lloyd-Max centroids for N(0, 1/n) in FP32 (block_gtq_pipeline.py:24-78)."""
+    out = np.zeros(1 << bits, np.float32)
+    _lib.call("bgtq_optimal_centroids", bits, n, out.ctypes.data)
+    return out
+
+
 def allocate_bits(scores, budget: int, min_bits: int = 1, max_bits: int = 8) -> np.ndarray:
     """Greedy per-pair widths (src/reference/allocator.py:4-17), computed natively."""
     s = np.ascontiguousarray(scores, dtype=np.float32)

@@ -98,6 +98,31 @@ const char *bgtq_version(void);
 bgtq_status bgtq_allocate_bits(const float *scores, uint32_t n, int64_t budget, int32_t min_bits,
                                int32_t max_bits, int64_t *widths_out);
 
+/* Table builder: per-pair widths[dim/2] (1..8) -> the flattened config (u32) and table (f32)
+ * of src/webgpu/layout.ts:24-31, as the reference's calibration builds them:
+ * BlockGTQPipeline._post_allocation_setup (vendor/blockgtq/block_gtq_pipeline.py:151-246:
+ * pairs ordered by width, one group per width, identity blocks below rotation_threshold and
+ * NumPy-seeded Haar rotations (seed 42 + width) at or above it, Lloyd-Max centroids),
+ * build_code_lut (vendor/blockgtq/quant_kernels.py:276-364) and build_pack_meta
+ * (vendor/blockgtq/quantizer.py:34-106).  Pairs are ordered by width as torch.argsort
+ * orders them (equal widths by libstdc++ std::sort over (width, index)), or by pair_order
+ * when it is given (a width-ascending permutation of the pairs, e.g. an existing
+ * calibration's).  row_pad bytes are added to the packed row;
+ * norm_stride 0 means the group count.  With config or table NULL only the lengths are
+ * returned (size query). */
+bgtq_status bgtq_tables_build(uint32_t dim, const int64_t *widths, const int64_t *pair_order,
+                              uint32_t rotation_threshold, uint32_t row_pad, uint32_t norm_stride, uint32_t *config,
+                              size_t config_capacity, size_t *config_len, float *table, size_t table_capacity,
+                              size_t *table_len);
+
+/* The Haar rotation of size n that NumPy gives for default_rng(seed) (standard normals, QR,
+ * columns signed by diag(R), det +1), row-major FP32 (block_gtq_pipeline.py:81-92). */
+bgtq_status bgtq_haar_rotation(uint32_t n, uint64_t seed, float *out);
+
+/* MSE-optimal scalar centroids (2^bits values, ascending, FP32) for N(0, 1/n)
+ * (block_gtq_pipeline.py:24-78). */
+bgtq_status bgtq_optimal_centroids(uint32_t bits, uint32_t n, float *out);
+
 /* validateLayout() plus the PackedKeys inverse-group check, on host memory only.
  * config/table are the flattened tables() output (src/webgpu/layout.ts:24-31).
  * ranges_out (nullable, 2*dim entries) receives the [start,end) group bounds of each
