@@ -235,9 +235,7 @@ def run_ours(args, rank, world, local_rank):
 
     def step(record=False):
         for layer in range(L):
-            for h in range(H):
-                keys[layer][h].append(knew[layer][:, h:h + 1, :])
-                values[layer][h].append(vnew[layer][:, h:h + 1, :])
+            bgtq.append_kv(keys[layer], values[layer], knew[layer], vnew[layer])  # every KV head, one launch
             if record:
                 ev[layer][0].record(stream)
             atts[layer].attend(q[layer], out=outs[layer])
@@ -265,7 +263,7 @@ def run_ours(args, rank, world, local_rank):
     clk = clocks.stop()
     elapsed = t_start.elapsed_time(t_end) / 1e3
     launch_ms = [a.elapsed_time(b) for evs in attn_ms for a, b in evs]
-    launches = steps * L * (2 * H + 2)  # per layer: H encodes + H V appends + query rotation + attention
+    launches = steps * L * 4  # per layer: fused K/V append + length bump + query rotation + attention
 
     # ---- e2e through the C ABI with host buffers ----
     e2e = None

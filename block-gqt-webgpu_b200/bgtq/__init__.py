@@ -8,11 +8,11 @@ no CPU fallback - a missing library raises ImportError on first use.
 from ._lib import (BGTQError, DeviceError, LayoutError, RangeError, StateError, LIB_PATH, lib)
 from .layout import (BlockGTQParameters, allocate_bits, build_tables, haar_rotation, optimal_centroids, tables,
                      validate_layout)
-from .runtime import CompressedKeys, FP16Keys, PackedKeys, Values
+from .runtime import CompressedKeys, FP16Keys, PackedKeys, Values, append_kv
 from .attention import AttentionEngine, AttentionSession, GroupedAttention, OptimizedAttention
 
 __all__ = ["BGTQError", "DeviceError", "LayoutError", "RangeError", "StateError", "LIB_PATH", "lib",
-           "BlockGTQParameters", "allocate_bits", "build_tables", "haar_rotation", "optimal_centroids", "tables", "validate_layout", "CompressedKeys", "FP16Keys",
+           "BlockGTQParameters", "allocate_bits", "build_tables", "haar_rotation", "optimal_centroids", "tables", "validate_layout", "CompressedKeys", "FP16Keys", "append_kv",
            "PackedKeys", "Values", "AttentionEngine", "AttentionSession", "GroupedAttention", "OptimizedAttention",
            "device_status"]
 

@@ -431,17 +431,15 @@ bgtq_status bgtq_keys_append(bgtq_keys *k, const void *src, bgtq_dtype dtype, in
     return BGTQ_OK;
 }
 
-bgtq_status bgtq_append_kv_rope(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, const float *src,
-                                uint64_t row_stride, uint64_t seq_stride, uint32_t k_offset, uint32_t v_offset,
-                                uint32_t count, uint32_t seq_first, uint32_t seq_count, const float *inv_freq,
-                                void *stream_) {
-    if (!keys || !values || !src || !inv_freq || heads < 1 || heads > (uint32_t)kMaxHeads)
-        return fail(BGTQ_EINVAL, "Invalid K/V append");
+namespace {
+// Shared checks and launch of the one-launch K/V appends (bgtq_append_kv_rope, bgtq_append_kv).
+bgtq_status append_kv_common(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, KvRopeArgs &a,
+                             uint32_t count, uint32_t seq_first, uint32_t seq_count, void *stream_) {
+    if (!keys || !values || heads < 1 || heads > (uint32_t)kMaxHeads) return fail(BGTQ_EINVAL, "Invalid K/V append");
     const bgtq_keys *k0 = keys[0];
     if (!k0) return fail(BGTQ_EINVAL, "Invalid K/V append");
     const uint32_t d = k0->dim;
-    if (d % 2 || !count || !seq_count || (uint64_t)seq_first + seq_count > k0->sequences ||
-        reinterpret_cast<uintptr_t>(src) % 4 || row_stride < (uint64_t)std::max(k_offset, v_offset) + heads * d)
+    if (d % 2 || !count || !seq_count || (uint64_t)seq_first + seq_count > k0->sequences)
         return fail(BGTQ_EINVAL, "Invalid K/V append");
     for (uint32_t h = 0; h < heads; ++h) {
         const bgtq_keys *k = keys[h];
@@ -459,20 +457,13 @@ bgtq_status bgtq_append_kv_rope(uint32_t heads, bgtq_keys *const *keys, bgtq_val
     }
     DeviceGuard g(k0->device);
     if (!g.ok) return fail(BGTQ_ECUDA, "cannot select device");
-    KvRopeArgs a;
-    std::memset(&a, 0, sizeof(a));
     for (uint32_t h = 0; h < heads; ++h) {
         fill_encode_head(keys[h], a.head[h]);
         a.v[h] = values[h]->data;
         a.v_lengths[h] = values[h]->d_lengths;
         a.v_seq_stride[h] = (uint64_t)values[h]->cap_alloc * values[h]->D;
     }
-    a.src = src;
     a.start = k0->d_lengths;
-    a.row_stride = row_stride;
-    a.seq_stride = seq_stride;
-    a.k_offset = k_offset;
-    a.v_offset = v_offset;
     a.count = count;
     a.seq_first = seq_first;
     a.seq_count = seq_count;
@@ -483,7 +474,6 @@ bgtq_status bgtq_append_kv_rope(uint32_t heads, bgtq_keys *const *keys, bgtq_val
     for (uint32_t h = 0; h < heads; ++h) a.capacity = std::min(a.capacity, std::min(keys[h]->capacity, values[h]->capacity));
     a.status = device_status_word(k0->device);
     if (!a.status) return fail(BGTQ_ECUDA, "no status word");
-    for (uint32_t p = 0; p < d / 2; ++p) a.inv_freq[p] = inv_freq[p];
     cudaError_t e = launch_kv_rope_append(a, d, static_cast<cudaStream_t>(stream_));
     if (e != cudaSuccess) return cuda_fail(e, "K/V append launch");
     for (uint32_t h = 0; h < heads; ++h)
@@ -492,6 +482,45 @@ bgtq_status bgtq_append_kv_rope(uint32_t heads, bgtq_keys *const *keys, bgtq_val
             values[h]->lengths[seq_first + s] += count;
         }
     return BGTQ_OK;
+}
+}  // namespace
+
+bgtq_status bgtq_append_kv_rope(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, const float *src,
+                                uint64_t row_stride, uint64_t seq_stride, uint32_t k_offset, uint32_t v_offset,
+                                uint32_t count, uint32_t seq_first, uint32_t seq_count, const float *inv_freq,
+                                void *stream_) {
+    if (!keys || !keys[0] || !src || !inv_freq || reinterpret_cast<uintptr_t>(src) % 4 ||
+        row_stride < (uint64_t)std::max(k_offset, v_offset) + heads * keys[0]->dim)
+        return fail(BGTQ_EINVAL, "Invalid K/V append");
+    KvRopeArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.k_src = src + k_offset;
+    a.v_src = src + v_offset;
+    a.row_stride = row_stride;
+    a.seq_stride = seq_stride;
+    a.rope = 1;
+    for (uint32_t p = 0; p < keys[0]->dim / 2 && p < kMaxDim / 2; ++p) a.inv_freq[p] = inv_freq[p];
+    return append_kv_common(heads, keys, values, a, count, seq_first, seq_count, stream_);
+}
+
+bgtq_status bgtq_append_kv(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, const void *k_src,
+                           bgtq_dtype k_dtype, const void *v_src, bgtq_dtype v_dtype, uint32_t count,
+                           uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
+                           void *stream_) {
+    if (!keys || !keys[0] || !k_src || !v_src || (k_dtype != BGTQ_F16 && k_dtype != BGTQ_F32) ||
+        (v_dtype != BGTQ_F16 && v_dtype != BGTQ_F32) || row_stride < (uint64_t)heads * keys[0]->dim ||
+        reinterpret_cast<uintptr_t>(k_src) % (k_dtype == BGTQ_F16 ? 2 : 4) ||
+        reinterpret_cast<uintptr_t>(v_src) % (v_dtype == BGTQ_F16 ? 2 : 4))
+        return fail(BGTQ_EINVAL, "Invalid K/V append");
+    KvRopeArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.k_src = k_src;
+    a.v_src = v_src;
+    a.k_f16 = k_dtype == BGTQ_F16 ? 1u : 0u;
+    a.v_f16 = v_dtype == BGTQ_F16 ? 1u : 0u;
+    a.row_stride = row_stride;
+    a.seq_stride = seq_stride;
+    return append_kv_common(heads, keys, values, a, count, seq_first, seq_count, stream_);
 }
 
 bgtq_status bgtq_keys_length(const bgtq_keys *k, uint32_t seq, uint32_t *out) {

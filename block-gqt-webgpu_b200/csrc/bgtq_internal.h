@@ -91,11 +91,12 @@ struct KvRopeArgs {
     EncodeHead head[kMaxHeads];
     void *v[kMaxHeads];             // FP16 value rows, sequence 0 row 0
     uint32_t *v_lengths[kMaxHeads];
-    const float *src;
+    const void *k_src, *v_src;      // head h of token t of sequence s at + s*seq_stride + t*row_stride + h*dim
     const uint32_t *start;          // device lengths of the first key store (start rows)
     uint64_t v_seq_stride[kMaxHeads];  // halves between sequences of each value store
-    uint64_t row_stride, seq_stride;   // floats
-    uint32_t k_offset, v_offset, count, seq_first, seq_count, heads, vD, v_swizzle;
+    uint64_t row_stride, seq_stride;   // source elements
+    uint32_t k_f16, v_f16, rope;       // FP16 (else FP32) sources; RoPE on K with inv_freq
+    uint32_t count, seq_first, seq_count, heads, vD, v_swizzle;
     uint32_t capacity;              // rows every store can hold: rows at or past it are refused
     uint32_t *status;               // device status word (kStatusBadLength on a refusal)
     float inv_freq[kMaxDim / 2];

@@ -318,13 +318,20 @@ __global__ void __launch_bounds__(kThreads) encode_warp_kernel(const __grid_cons
     }
 }
 
-// Model-path append (src/model/decoder.ts:44-50: rope(K), encode_k per KV head, V append):
-// one warp per (new token, KV head) reads the FP32 K and V projections of the token, applies
-// split-half RoPE to K at the token's cache row (src/model/kernels.wgsl:49-54, rounded like
-// separate multiplies and adds), encodes it into the packed store and writes V to the FP16
-// value store.  Start rows come from the first key store's device lengths, so the launch is
+// Element i of an FP16 or FP32 source.
+__device__ __forceinline__ float src_elem(const void *p, uint64_t i, uint32_t f16) {
+    return f16 ? __half2float(static_cast<const __half *>(p)[i]) : static_cast<const float *>(p)[i];
+}
+
+// K/V append of one layer for every KV head in one launch.  One warp per (new token, KV
+// head) reads the token's K and V (FP16 or FP32), optionally applies split-half RoPE to K at
+// the token's cache row (the model path, src/model/decoder.ts:44-50 and
+// src/model/kernels.wgsl:49-54, rounded like separate multiplies and adds), encodes K into
+// the packed store (FP16-rounded first, as every append is) and writes V to the FP16 value
+// store.  Start rows come from the first key store's device lengths, so the launch is
 // stream-ordered against earlier appends without host round trips; lengths are bumped by
 // bump_lengths_kernel afterwards.
+
 __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_constant__ KvRopeArgs a, uint32_t d,
                                                                   uint32_t total) {
     constexpr int W = kThreads / 32;
@@ -342,13 +349,17 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
             if (lane == 0) atomicOr(a.status, kStatusBadLength);
             continue;
         }
-        const float *src = a.src + (uint64_t)s * a.seq_stride + (uint64_t)rr * a.row_stride;
-        const float *ks = src + a.k_offset + (uint64_t)hd * d, *vs = src + a.v_offset + (uint64_t)hd * d;
-        for (uint32_t p = lane; p < pairs; p += 32) {
-            const float ang = __fmul_rn((float)pos, a.inv_freq[p]);
-            const float c = cosf(ang), sn = sinf(ang), x = ks[p], y = ks[p + pairs];
-            kr[w][p] = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
-            kr[w][p + pairs] = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+        const uint64_t at = (uint64_t)s * a.seq_stride + (uint64_t)rr * a.row_stride + (uint64_t)hd * d;
+        if (a.rope) {
+            for (uint32_t p = lane; p < pairs; p += 32) {
+                const float ang = __fmul_rn((float)pos, a.inv_freq[p]);
+                const float c = cosf(ang), sn = sinf(ang);
+                const float x = src_elem(a.k_src, at + p, a.k_f16), y = src_elem(a.k_src, at + p + pairs, a.k_f16);
+                kr[w][p] = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
+                kr[w][p + pairs] = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+            }
+        } else {
+            for (uint32_t i = lane; i < d; i += 32) kr[w][i] = src_elem(a.k_src, at + i, a.k_f16);
         }
         __syncwarp();
         for (uint32_t i = lane; i < d; i += 32) wk.xs[i] = __half2float(__float2half_rn(kr[w][h.t.perm[i]]));
@@ -356,7 +367,7 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
         // V row: FP32 -> FP16, chunk-swizzled for head dims 64 / 128
         __half *vrow = reinterpret_cast<__half *>(a.v[hd]) + (uint64_t)seq * a.v_seq_stride[hd] + (uint64_t)pos * a.vD;
         for (uint32_t e = lane; e < a.vD; e += 32) {
-            const float x = e < d ? vs[e] : 0.0f;
+            const float x = e < d ? src_elem(a.v_src, at + e, a.v_f16) : 0.0f;
             uint32_t de = e;
             if (a.v_swizzle) {
                 const uint32_t c = e >> 3;

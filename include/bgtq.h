@@ -171,6 +171,16 @@ bgtq_status bgtq_append_kv_rope(uint32_t heads, bgtq_keys *const *keys, bgtq_val
                                 uint64_t row_stride, uint64_t seq_stride, uint32_t k_offset, uint32_t v_offset,
                                 uint32_t count, uint32_t seq_first, uint32_t seq_count, const float *inv_freq,
                                 void *stream);
+/* K/V append of one layer for `heads` KV heads in one launch (the per-head
+ * PackedKeys.append + Values.append of src/runtime/packed-keys.ts:39-48 and
+ * src/runtime/values.ts:9-14, batched): K and V of head h, token t, sequence s at
+ * src + s*seq_stride + t*row_stride + h*dim elements (FP16 or FP32, device memory, no
+ * RoPE); K is FP16-rounded and encoded into keys[h], V written as FP16 into values[h].
+ * Needs packed keys and FP16 values of one head dim with equal lengths; stream-ordered. */
+bgtq_status bgtq_append_kv(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, const void *k_src,
+                           bgtq_dtype k_dtype, const void *v_src, bgtq_dtype v_dtype, uint32_t count,
+                           uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
+                           void *stream);
 /* Start every sequence of the store over (lengths 0), keeping its capacity: a new request
  * reusing the cache.  Rows past a length are never attended, so their old contents stay
  * until appends overwrite them.  No counterpart in the reference (its stores only grow);

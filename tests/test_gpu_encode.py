@@ -218,3 +218,43 @@ def test_reset_starts_every_sequence_over(cuda):
     kh = oracle.reconstruct(cfg, tab, *keys.read(0))
     _, _, ref = oracle.attention(q[0, 0], kh, vb[0].astype(np.float32))
     np.testing.assert_allclose(att.attend(q)[0, 0], ref, atol=1e-5, rtol=1e-4)
+
+
+@pytest.mark.parametrize("dtype", ["float16", "float32"])
+def test_append_kv_equals_per_head_appends(cuda, dtype):
+    """bgtq_append_kv (every KV head's K encode + V append in one launch) writes the bytes
+    of per-head PackedKeys.append / Values.append, and attention over the stores agrees
+    exactly, across appends of 4, 1, 1 and 3 tokens on 5 sequences (one of them offset)."""
+    import torch
+    from bgtq import GroupedAttention, Values, append_kv
+    zh = np.load(GOLDEN / "smollm2_heads.npz")
+    H, B, d = 3, 5, 64
+    tabs = [(zh[f"h{h}_config"], zh[f"h{h}_table"]) for h in range(H)]
+    fk = [PackedKeys(t, 64, sequences=B + 1) for t in tabs]
+    fv = [Values(d, 64, "f16", sequences=B + 1) for _ in range(H)]
+    rk = [PackedKeys(t, 64, sequences=B + 1) for t in tabs]
+    rv = [Values(d, 64, "f16", sequences=B + 1) for _ in range(H)]
+    gen = torch.Generator(device=cuda).manual_seed(5)
+    dt = getattr(torch, dtype)
+    for n in (4, 1, 1, 3):
+        k = (torch.randn((B, n, H, d), device=cuda, generator=gen) * 2).to(dt)
+        v = torch.randn((B, n, H, d), device=cuda, generator=gen).to(dt)
+        append_kv(fk, fv, k, v, seq_first=1)
+        for h in range(H):
+            rk[h].append(k[:, :, h, :].contiguous(), seq_first=1)
+            rv[h].append(v[:, :, h, :].contiguous(), seq_first=1)
+    torch.cuda.synchronize()
+    for h in range(H):
+        assert fk[h].lengths(0) == 0 and fv[h].lengths(0) == 0
+        for s in range(1, B + 1):
+            assert fk[h].lengths(s) == rk[h].lengths(s) == 9 == fv[h].lengths(s)
+            np.testing.assert_array_equal(fk[h].read(s)[0], rk[h].read(s)[0])
+            np.testing.assert_array_equal(fk[h].read(s)[1], rk[h].read(s)[1])
+    q = torch.randn((B, H, 3, d), device=cuda, generator=gen)
+    o1 = GroupedAttention(fk, fv, 3).attend(q, seq_first=1)
+    o2 = GroupedAttention(rk, rv, 3).attend(q, seq_first=1)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(o1.cpu().numpy(), o2.cpu().numpy())
+    with pytest.raises(ValueError):
+        append_kv(fk, fv, k, v[:, :, :2])
+    assert device_status(0) == 0
