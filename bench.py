@@ -279,9 +279,7 @@ def run_ours(args, rank, world, local_rank):
 
         def step_host():
             for layer in range(L):
-                for h in range(H):
-                    keys[layer][h].append(kn[layer][:, h:h + 1, :])
-                    values[layer][h].append(vn[layer][:, h:h + 1, :])
+                bgtq.append_kv(keys[layer], values[layer], kn[layer], vn[layer])  # host K/V, every KV head
                 atts[layer].attend(qn[layer], out=on[layer])
 
         step_host()
@@ -350,8 +348,8 @@ def run_ours(args, rank, world, local_rank):
             h2d = L * (q[0].numel() * 4 + knew[0].numel() * 2 + vnew[0].numel() * 2)
             line["e2e"] = {"value": B * world * e2e[1] / e2e_max, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                            "d2h_bytes_per_step": L * outs[0].numel() * 4,
-                           "path": "bgtq C ABI (PackedKeys/Values.append + GroupedAttention.attend) on pinned host "
-                                   "NumPy buffers"}
+                           "path": "bgtq C ABI (bgtq_append_kv of every KV head + GroupedAttention.attend, one "
+                                   "synchronising attend per layer) on pinned host NumPy buffers"}
         print(json.dumps(line), flush=True)
     for a in atts:
         a.destroy()

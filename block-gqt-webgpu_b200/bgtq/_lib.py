@@ -91,7 +91,7 @@ SIGNATURES = {
     "bgtq_attend_prefill": (I32, [P, P, U32, U32, U32, U32, U32, P, C.c_int, P]),
     "bgtq_keys_reset": (I32, [P, P]),
     "bgtq_append_kv_rope": (I32, [U32, P, P, P, C.c_uint64, C.c_uint64, U32, U32, U32, U32, U32, P, P]),
-    "bgtq_append_kv": (I32, [U32, P, P, P, I32, P, I32, U32, C.c_uint64, U32, U32, C.c_uint64, P]),
+    "bgtq_append_kv": (I32, [U32, P, P, P, I32, P, I32, I32, U32, C.c_uint64, U32, U32, C.c_uint64, P]),
     "bgtq_attention_set_prefill_kernel": (I32, [P, U32]),
     "bgtq_attention_set_rope": (I32, [P, P, U32]),
     "bgtq_attention_plan_for_capacity": (I32, [P, C.c_int]),

@@ -250,23 +250,48 @@ class Values(_Store):
 def append_kv(keys, values, k, v, seq_first: int = 0, stream=None) -> None:
     """One layer's K/V append for every KV head in one launch (bgtq_append_kv): the per-head
     PackedKeys.append + Values.append of the reference (src/runtime/packed-keys.ts:39-48,
-    src/runtime/values.ts:9-14), batched.  k, v: CUDA tensors [seq_count, n, heads, dim] or
-    [seq_count, heads, dim] (one new token), float16 or float32, the last two dimensions
-    contiguous; keys[h] packed stores, values[h] FP16 stores of the same head dim."""
-    import torch
-    if k.dim() == 3:
-        k, v = k.unsqueeze(1), v.unsqueeze(1)
-    if k.shape != v.shape or k.dim() != 4 or not k.is_cuda or not v.is_cuda:
-        raise ValueError("k and v must be CUDA tensors of one shape [seq_count, n, heads, dim]")
-    heads, dim = k.shape[2], k.shape[3]
-    if heads != len(keys) or heads != len(values) or k.stride(3) != 1 or k.stride(2) != dim or v.stride(3) != 1 \
-            or v.stride(2) != dim or k.stride() != v.stride():
-        raise ValueError("k / v layout: [seq_count, n, heads, dim] with contiguous heads x dim")
-    dt = {torch.float16: 1, torch.float32: 2}
-    if k.dtype not in dt or v.dtype not in dt:
-        raise ValueError("k / v must be float16 or float32")
+    src/runtime/values.ts:9-14), batched.  k, v: [seq_count, n, heads, dim] or
+    [seq_count, heads, dim] (one new token), either CUDA tensors (float16 / float32, the last
+    two dimensions contiguous) or host NumPy arrays (uint16 FP16 bits, float16 or float32,
+    C-contiguous; uploaded in stream order, so page-locked buffers must not change until the
+    stream has passed the call).  keys[h] packed stores, values[h] FP16 stores of one dim."""
+    host = isinstance(k, np.ndarray)
+    if host != isinstance(v, np.ndarray):
+        raise ValueError("k and v must both be host arrays or both CUDA tensors")
+    if host:
+        def norm(a):
+            a = np.ascontiguousarray(a)
+            if a.dtype == np.float16:
+                a = a.view(np.uint16)
+            if a.dtype not in (np.uint16, np.float32):
+                raise ValueError("host k / v must be FP16 bits (uint16), float16 or float32")
+            return a if a.ndim == 4 else a[:, None]
+        k, v = norm(k), norm(v)
+        if k.shape != v.shape or k.ndim != 4:
+            raise ValueError("k and v must share one shape [seq_count, n, heads, dim]")
+        S, n, heads, dim = k.shape
+        ptr_k, ptr_v = k.ctypes.data, v.ctypes.data
+        dk, dv = (1 if k.dtype == np.uint16 else 2), (1 if v.dtype == np.uint16 else 2)
+        rs, ss = heads * dim, n * heads * dim
+        st = stream
+    else:
+        import torch
+        if k.dim() == 3:
+            k, v = k.unsqueeze(1), v.unsqueeze(1)
+        if k.shape != v.shape or k.dim() != 4 or not k.is_cuda or not v.is_cuda:
+            raise ValueError("k and v must be CUDA tensors of one shape [seq_count, n, heads, dim]")
+        S, n, heads, dim = k.shape
+        if k.stride(3) != 1 or k.stride(2) != dim or v.stride(3) != 1 or v.stride(2) != dim or k.stride() != v.stride():
+            raise ValueError("k / v layout: [seq_count, n, heads, dim] with contiguous heads x dim")
+        dt = {torch.float16: 1, torch.float32: 2}
+        if k.dtype not in dt or v.dtype not in dt:
+            raise ValueError("k / v must be float16 or float32")
+        ptr_k, ptr_v, dk, dv = k.data_ptr(), v.data_ptr(), dt[k.dtype], dt[v.dtype]
+        rs, ss = k.stride(1), k.stride(0)
+        st = stream if stream is not None else _torch_stream(k)
+    if heads != len(keys) or heads != len(values):
+        raise ValueError("one key and one value store per head")
     kp = (C.c_void_p * heads)(*[x._handle for x in keys])
     vp = (C.c_void_p * heads)(*[x._handle for x in values])
-    st = stream if stream is not None else _torch_stream(k)
-    _lib.call("bgtq_append_kv", heads, kp, vp, C.c_void_p(k.data_ptr()), dt[k.dtype], C.c_void_p(v.data_ptr()),
-              dt[v.dtype], k.shape[1], k.stride(1), seq_first, k.shape[0], k.stride(0), _stream_ptr(st))
+    _lib.call("bgtq_append_kv", heads, kp, vp, C.c_void_p(ptr_k), dk, C.c_void_p(ptr_v), dv, 1 if host else 0, n, rs,
+              seq_first, S, ss, _stream_ptr(st))

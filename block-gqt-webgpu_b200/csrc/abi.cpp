@@ -126,20 +126,22 @@ cudaError_t upload_tables(const Layout &L, DeviceTables &dt) {
     return cudaSuccess;
 }
 
+// Branch-free per row (the exponent field all ones marks Inf / NaN), so the compiler
+// vectorises it: host appends are checked on every call.
 bool host_finite(const void *src, bgtq_dtype dt, uint32_t dim, uint32_t count, uint64_t row_stride, uint32_t seq_count,
                  uint64_t seq_stride) {
     for (uint32_t s = 0; s < seq_count; ++s)
         for (uint32_t r = 0; r < count; ++r) {
             const uint64_t base = s * seq_stride + r * row_stride;
+            uint32_t bad = 0;
             if (dt == BGTQ_F16) {
                 const uint16_t *p = static_cast<const uint16_t *>(src) + base;
-                for (uint32_t i = 0; i < dim; ++i)
-                    if ((p[i] & 0x7c00u) == 0x7c00u) return false;
+                for (uint32_t i = 0; i < dim; ++i) bad |= (uint32_t)((p[i] & 0x7c00u) == 0x7c00u);
             } else {
-                const float *p = static_cast<const float *>(src) + base;
-                for (uint32_t i = 0; i < dim; ++i)
-                    if (!std::isfinite(p[i])) return false;
+                const uint32_t *p = static_cast<const uint32_t *>(src) + base;
+                for (uint32_t i = 0; i < dim; ++i) bad |= (uint32_t)((p[i] & 0x7f800000u) == 0x7f800000u);
             }
+            if (bad) return false;
         }
     return true;
 }
@@ -504,14 +506,39 @@ bgtq_status bgtq_append_kv_rope(uint32_t heads, bgtq_keys *const *keys, bgtq_val
 }
 
 bgtq_status bgtq_append_kv(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, const void *k_src,
-                           bgtq_dtype k_dtype, const void *v_src, bgtq_dtype v_dtype, uint32_t count,
+                           bgtq_dtype k_dtype, const void *v_src, bgtq_dtype v_dtype, int host, uint32_t count,
                            uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
                            void *stream_) {
-    if (!keys || !keys[0] || !k_src || !v_src || (k_dtype != BGTQ_F16 && k_dtype != BGTQ_F32) ||
+    if (!keys || !keys[0] || !values || !values[0] || !k_src || !v_src || (k_dtype != BGTQ_F16 && k_dtype != BGTQ_F32) ||
         (v_dtype != BGTQ_F16 && v_dtype != BGTQ_F32) || row_stride < (uint64_t)heads * keys[0]->dim ||
         reinterpret_cast<uintptr_t>(k_src) % (k_dtype == BGTQ_F16 ? 2 : 4) ||
         reinterpret_cast<uintptr_t>(v_src) % (v_dtype == BGTQ_F16 ? 2 : 4))
         return fail(BGTQ_EINVAL, "Invalid K/V append");
+    if (host) {
+        // host sources: one dense [seq_count][count][heads][dim] block each, checked, then
+        // uploaded to the first stores' staging buffers in stream order (no host wait: a later
+        // upload into the same buffer is queued behind this launch on the same stream)
+        const uint32_t d = keys[0]->dim;
+        const uint64_t n = (uint64_t)seq_count * count * heads * d;
+        if (row_stride != (uint64_t)heads * d || (seq_count > 1 && seq_stride != (uint64_t)count * row_stride) ||
+            !count || !seq_count)
+            return fail(BGTQ_EINVAL, "host K/V append needs dense [sequences][count][heads][dim] sources");
+        if (!host_finite(k_src, k_dtype, (uint32_t)(n / seq_count), 1, 0, seq_count, (uint64_t)count * row_stride))
+            return fail(BGTQ_ENONFINITE, "Finite FP16 K required");
+        if (!host_finite(v_src, v_dtype, (uint32_t)(n / seq_count), 1, 0, seq_count, (uint64_t)count * row_stride))
+            return fail(BGTQ_ENONFINITE, "finite inputs required");
+        DeviceGuard g(keys[0]->device);
+        if (!g.ok) return fail(BGTQ_ECUDA, "cannot select device");
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+        const size_t kb = n * (k_dtype == BGTQ_F16 ? 2 : 4), vb = n * (v_dtype == BGTQ_F16 ? 2 : 4);
+        CK(keys[0]->staging.ensure(kb), "staging allocation");
+        CK(values[0]->staging.ensure(vb), "staging allocation");
+        CK(cudaMemcpyAsync(keys[0]->staging.p, k_src, kb, cudaMemcpyHostToDevice, stream), "K upload");
+        CK(cudaMemcpyAsync(values[0]->staging.p, v_src, vb, cudaMemcpyHostToDevice, stream), "V upload");
+        k_src = keys[0]->staging.p;
+        v_src = values[0]->staging.p;
+        seq_stride = (uint64_t)count * row_stride;
+    }
     KvRopeArgs a;
     std::memset(&a, 0, sizeof(a));
     a.k_src = k_src;
@@ -833,9 +860,8 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
     // longest length it may meet
     const uint32_t plan_len = at->plan_capacity && !logits ? at->keys[0]->capacity : max_len;
     if (host) {
-        const size_t nq = (size_t)seq_count * H * rows * d;
-        for (size_t i = 0; i < nq; ++i)
-            if (!std::isfinite(q[i])) return fail(BGTQ_ENONFINITE, "Q: finite inputs required");
+        if (!host_finite(q, BGTQ_F32, d, seq_count * H * rows, d, 1, 0))
+            return fail(BGTQ_ENONFINITE, "Q: finite inputs required");
         if (positions)
             for (uint32_t s = 0; s < seq_count; ++s)
                 for (uint32_t r = 0; r < rows; ++r)
@@ -973,9 +999,8 @@ bgtq_status bgtq_attend_prefill(bgtq_attention *at, const float *q, uint32_t pos
         if ((uint64_t)pos_first + n > L) return fail(BGTQ_EINVAL, "Invalid Q/K/V shape or positions");
     }
     const size_t nq = (size_t)seq_count * n * H * gqa * d;
-    if (host)
-        for (size_t i = 0; i < nq; ++i)
-            if (!std::isfinite(q[i])) return fail(BGTQ_ENONFINITE, "Q: finite inputs required");
+    if (host && !host_finite(q, BGTQ_F32, d, seq_count * n * H * gqa, d, 1, 0))
+        return fail(BGTQ_ENONFINITE, "Q: finite inputs required");
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     DeviceGuard g(at->device);
     if (!g.ok) return fail(BGTQ_ECUDA, "cannot select device");

@@ -174,11 +174,15 @@ bgtq_status bgtq_append_kv_rope(uint32_t heads, bgtq_keys *const *keys, bgtq_val
 /* K/V append of one layer for `heads` KV heads in one launch (the per-head
  * PackedKeys.append + Values.append of src/runtime/packed-keys.ts:39-48 and
  * src/runtime/values.ts:9-14, batched): K and V of head h, token t, sequence s at
- * src + s*seq_stride + t*row_stride + h*dim elements (FP16 or FP32, device memory, no
- * RoPE); K is FP16-rounded and encoded into keys[h], V written as FP16 into values[h].
- * Needs packed keys and FP16 values of one head dim with equal lengths; stream-ordered. */
+ * src + s*seq_stride + t*row_stride + h*dim elements (FP16 or FP32, no RoPE); K is
+ * FP16-rounded and encoded into keys[h], V written as FP16 into values[h].  Needs packed
+ * keys and FP16 values of one head dim with equal lengths.  host != 0: the sources are host
+ * memory holding dense [seq_count][count][heads][dim] blocks, checked for finite values
+ * (BGTQ_ENONFINITE) and uploaded in stream order without a host wait - page-locked sources
+ * must stay unchanged until the stream has passed the call, and host appends to the same
+ * first store share its staging buffer, so issue them on one stream.  Stream-ordered. */
 bgtq_status bgtq_append_kv(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, const void *k_src,
-                           bgtq_dtype k_dtype, const void *v_src, bgtq_dtype v_dtype, uint32_t count,
+                           bgtq_dtype k_dtype, const void *v_src, bgtq_dtype v_dtype, int host, uint32_t count,
                            uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
                            void *stream);
 /* Start every sequence of the store over (lengths 0), keeping its capacity: a new request

@@ -258,3 +258,36 @@ def test_append_kv_equals_per_head_appends(cuda, dtype):
     with pytest.raises(ValueError):
         append_kv(fk, fv, k, v[:, :, :2])
     assert device_status(0) == 0
+
+
+def test_append_kv_host_sources(cuda):
+    """bgtq_append_kv from host NumPy buffers (FP16 bits / float32, uploaded in stream order)
+    writes what the device-source call writes; a non-finite host value is refused with the
+    stores unchanged."""
+    import torch
+    from bgtq import RangeError, Values, append_kv
+    zh = np.load(GOLDEN / "smollm2_heads.npz")
+    H, B, d = 2, 4, 64
+    tabs = [(zh[f"h{h}_config"], zh[f"h{h}_table"]) for h in range(H)]
+    hk = [PackedKeys(t, 32, sequences=B) for t in tabs]
+    hv = [Values(d, 32, "f16", sequences=B) for _ in range(H)]
+    dk = [PackedKeys(t, 32, sequences=B) for t in tabs]
+    dv = [Values(d, 32, "f16", sequences=B) for _ in range(H)]
+    rng = np.random.default_rng(9)
+    for n in (3, 1):
+        k = (rng.standard_normal((B, n, H, d)) * 2).astype(np.float16)
+        v = rng.standard_normal((B, n, H, d)).astype(np.float32)
+        append_kv(hk, hv, k.view(np.uint16), v)
+        append_kv(dk, dv, torch.from_numpy(k).to(cuda), torch.from_numpy(v).to(cuda))
+    torch.cuda.synchronize()
+    for h in range(H):
+        for s in range(B):
+            assert hk[h].lengths(s) == dk[h].lengths(s) == 4 == hv[h].lengths(s)
+            np.testing.assert_array_equal(hk[h].read(s)[0], dk[h].read(s)[0])
+            np.testing.assert_array_equal(hk[h].read(s)[1], dk[h].read(s)[1])
+    bad = np.zeros((B, 1, H, d), np.float32)
+    bad[1, 0, 1, 5] = np.inf
+    with pytest.raises(RangeError):
+        append_kv(hk, hv, np.zeros((B, 1, H, d), np.float16), bad)
+    assert hk[0].lengths(0) == 4 and hv[1].lengths(3) == 4
+    assert device_status(0) == 0
