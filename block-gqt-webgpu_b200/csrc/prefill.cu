@@ -102,30 +102,46 @@ __device__ __forceinline__ void split2(float x, float y, uint32_t &hi, uint32_t 
 }
 
 // Code-domain queries: qt[s][t][hq][i] = sum_{j in group(i)} R[i][j] q[perm[j]] * log2(e)/sqrt(d)
-// for the G query heads of KV head blockIdx.y at query t = blockIdx.x of sequence blockIdx.z.
-__global__ void __launch_bounds__(128) prefill_qrot_kernel(const __grid_constant__ PrefillArgs a) {
-    __shared__ float qraw[kMaxRows][kMaxDim];
-    const uint32_t t = blockIdx.x, h = blockIdx.y, s = blockIdx.z, G = a.gqa, d = a.d;
+// (after split-half RoPE at the query's position when a table is given).  One CTA rotates
+// kQrotTokens positions x G query heads of KV head blockIdx.y of sequence blockIdx.z: the
+// head's rotation rows are staged in shared memory once, the permuted query rows next to
+// them, and thread (i, row group) sums each output over its group in ascending j - the
+// order and rounding of a per-row loop.
+constexpr uint32_t kQrotTokens = 32, kQrotThreads = 256;
+
+__global__ void __launch_bounds__(kQrotThreads) prefill_qrot_kernel(const __grid_constant__ PrefillArgs a) {
+    extern __shared__ float qsm[];
+    const uint32_t t0 = blockIdx.x * kQrotTokens, h = blockIdx.y, s = blockIdx.z, G = a.gqa, d = a.d;
     const AttnHead &hd = a.head[h];
     const uint64_t HQ = (uint64_t)a.heads * G;
-    const float *qg = a.q + (((uint64_t)s * a.n + t) * HQ + (uint64_t)h * G) * d;
-    for (uint32_t idx = threadIdx.x; idx < G * d; idx += blockDim.x) {
-        const uint32_t r = idx / d, i = idx % d;
-        qraw[r][i] = attn::rope_elem(qg + (uint64_t)r * d, hd.perm[i], d, a.pos_first + t, a.rope);
+    const uint32_t nt = min(kQrotTokens, a.n - t0), rows = nt * G;
+    float *rs = qsm;                   // [d][d + 1] rotation rows
+    float *qp = qsm + d * (d + 1);     // [rows][d] permuted (and RoPE'd) query rows
+    for (uint32_t idx = threadIdx.x; idx < d * d; idx += blockDim.x) rs[(idx / d) * (d + 1) + idx % d] = hd.rot[idx];
+    const float *qg = a.q + (((uint64_t)s * a.n + t0) * HQ + (uint64_t)h * G) * d;
+    for (uint32_t idx = threadIdx.x; idx < rows * d; idx += blockDim.x) {
+        const uint32_t row = idx / d, i = idx % d, t = row / G, g = row % G;
+        qp[idx] = attn::rope_elem(qg + ((uint64_t)t * HQ + g) * d, hd.perm[i], d, a.pos_first + t0 + t, a.rope);
     }
     __syncthreads();
     const float qscale = kLog2e / sqrtf((float)d);
-    float *out = a.qt + (((uint64_t)s * a.n + t) * HQ + (uint64_t)h * G) * D;
-    for (uint32_t idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-        const uint32_t r = idx / D, i = idx % D;
-        float v = 0.0f;
+    const uint32_t nrg = blockDim.x / D;  // row groups
+    for (uint32_t c = threadIdx.x; c < nrg * D; c += blockDim.x) {
+        const uint32_t i = c % D, rg = c / D;
+        uint32_t lo = 0, hi = 0;
         if (i < d) {
-            const uint32_t g = hd.group_of[i], lo = hd.group_off[g], hi = hd.group_off[g + 1];
-            const float *ri = hd.rot + (uint64_t)i * d;
-            for (uint32_t j = lo; j < hi; ++j) v = fmaf(ri[j], qraw[r][j], v);
-            v *= qscale;
+            const uint32_t g = hd.group_of[i];
+            lo = hd.group_off[g];
+            hi = hd.group_off[g + 1];
         }
-        out[(uint64_t)r * D + i] = v;
+        const float *ri = rs + i * (d + 1);
+        for (uint32_t row = rg; row < rows; row += nrg) {
+            const float *q = qp + row * d;
+            float v = 0.0f;
+            for (uint32_t j = lo; j < hi; ++j) v = fmaf(ri[j], q[j], v);
+            const uint32_t t = row / G, g = row % G;
+            a.qt[(((uint64_t)s * a.n + t0 + t) * HQ + (uint64_t)h * G + g) * D + i] = i < d ? v * qscale : 0.0f;
+        }
     }
 }
 
@@ -442,7 +458,20 @@ cudaError_t launch_prefill(const PrefillArgs &a, uint32_t max_cent, int umma, cu
     }
     // one plan for all heads, sized for the widest; each head copies its own tile sizes
     const pre::Plan pl = pre::make_plan(row_stride, scale_stride, max_cent);
-    pre::prefill_qrot_kernel<<<dim3(a.n, a.heads, a.seq_count), 128, 0, s>>>(a);
+    {
+        const size_t qsmem = sizeof(float) * ((size_t)a.d * (a.d + 1) + (size_t)pre::kQrotTokens * a.gqa * a.d);
+        static int configured[64] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 0 || dev >= 64 || (int)qsmem > configured[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(pre::prefill_qrot_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)qsmem);
+            if (e != cudaSuccess) return e;
+            if (dev >= 0 && dev < 64) configured[dev] = (int)qsmem;
+        }
+        pre::prefill_qrot_kernel<<<dim3((a.n + pre::kQrotTokens - 1) / pre::kQrotTokens, a.heads, a.seq_count),
+                                   pre::kQrotThreads, qsmem, s>>>(a);
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if (umma) return launch_prefill_tc(a, max_cent, s);
