@@ -104,43 +104,76 @@ __device__ __forceinline__ void split2(float x, float y, uint32_t &hi, uint32_t 
 // Code-domain queries: qt[s][t][hq][i] = sum_{j in group(i)} R[i][j] q[perm[j]] * log2(e)/sqrt(d)
 // (after split-half RoPE at the query's position when a table is given).  One CTA rotates
 // kQrotTokens positions x G query heads of KV head blockIdx.y of sequence blockIdx.z: the
-// head's rotation rows are staged in shared memory once, the permuted query rows next to
-// them, and thread (i, row group) sums each output over its group in ascending j - the
-// order and rounding of a per-row loop.
-constexpr uint32_t kQrotTokens = 32, kQrotThreads = 256;
+// head's rotation (transposed) and the query rows (row-major, odd stride: conflict-free
+// stores and reads) are staged in shared memory, and each thread accumulates 4 outputs x 8
+// rows over all j in ascending order.  R[i][j] is exactly 0 outside group(i) (the layout
+// check enforces it), so the dense sum rounds exactly like the sum over the group alone.
+constexpr uint32_t kQrotTokens = 16, kQrotThreads = 256, kQrotRowsMax = kQrotTokens * kMaxRows;  // 128 rows
+constexpr uint32_t kQrotStride = D + 1;  // floats per staged query row
 
 __global__ void __launch_bounds__(kQrotThreads) prefill_qrot_kernel(const __grid_constant__ PrefillArgs a) {
-    extern __shared__ float qsm[];
+    extern __shared__ __align__(16) float qsm[];
     const uint32_t t0 = blockIdx.x * kQrotTokens, h = blockIdx.y, s = blockIdx.z, G = a.gqa, d = a.d;
     const AttnHead &hd = a.head[h];
     const uint64_t HQ = (uint64_t)a.heads * G;
     const uint32_t nt = min(kQrotTokens, a.n - t0), rows = nt * G;
-    float *rs = qsm;                   // [d][d + 1] rotation rows
-    float *qp = qsm + d * (d + 1);     // [rows][d] permuted (and RoPE'd) query rows
-    for (uint32_t idx = threadIdx.x; idx < d * d; idx += blockDim.x) rs[(idx / d) * (d + 1) + idx % d] = hd.rot[idx];
-    const float *qg = a.q + (((uint64_t)s * a.n + t0) * HQ + (uint64_t)h * G) * d;
-    for (uint32_t idx = threadIdx.x; idx < rows * d; idx += blockDim.x) {
-        const uint32_t row = idx / d, i = idx % d, t = row / G, g = row % G;
-        qp[idx] = attn::rope_elem(qg + ((uint64_t)t * HQ + g) * d, hd.perm[i], d, a.pos_first + t0 + t, a.rope);
+    const uint32_t tid = threadIdx.x;
+    float *rt = qsm;                                            // [D][D]: rt[j][i] = R[i][j] (0 past d)
+    float *qs = qsm + D * D;                                    // [kQrotRowsMax][kQrotStride] query rows
+    uint32_t *perm = reinterpret_cast<uint32_t *>(qs + kQrotRowsMax * kQrotStride);  // [D]
+    for (uint32_t idx = tid; idx < (uint32_t)(D * D); idx += kQrotThreads) {
+        const uint32_t j = idx / D, i = idx % D;
+        rt[idx] = (i < d && j < d) ? hd.rot[(uint64_t)i * d + j] : 0.0f;
+    }
+    if (tid < (uint32_t)D) perm[tid] = tid < d ? hd.perm[tid] : 0u;
+    {
+        const float *qg = a.q + (((uint64_t)s * a.n + t0) * HQ + (uint64_t)h * G) * d;
+#pragma unroll 8
+        for (uint32_t idx = tid; idx < kQrotRowsMax * D; idx += kQrotThreads) {
+            const uint32_t row = idx / D, i = idx % D;
+            float v = 0.0f;
+            if (row < rows && i < d) {
+                const uint32_t t = row / G, g = row - t * G;
+                v = attn::rope_elem(qg + ((uint64_t)t * HQ + g) * d, i, d, a.pos_first + t0 + t, a.rope);
+            }
+            qs[row * kQrotStride + i] = v;
+        }
     }
     __syncthreads();
-    const float qscale = kLog2e / sqrtf((float)d);
-    const uint32_t nrg = blockDim.x / D;  // row groups
-    for (uint32_t c = threadIdx.x; c < nrg * D; c += blockDim.x) {
-        const uint32_t i = c % D, rg = c / D;
-        uint32_t lo = 0, hi = 0;
-        if (i < d) {
-            const uint32_t g = hd.group_of[i];
-            lo = hd.group_off[g];
-            hi = hd.group_off[g + 1];
+    // thread tile: outputs 4*ib .. 4*ib+3, rows 8*rb .. 8*rb+7
+    const uint32_t ib = tid % 16, rb = tid / 16;
+    float acc[4][8];
+#pragma unroll
+    for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int r = 0; r < 8; ++r) acc[x][r] = 0.0f;
+    if (8 * rb < rows) {
+        const float *qr = qs + 8 * rb * kQrotStride;
+        for (uint32_t j = 0; j < d; ++j) {
+            const float4 rv = *reinterpret_cast<const float4 *>(rt + j * D + 4 * ib);
+            const uint32_t pj = perm[j];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                const float qv = qr[r * kQrotStride + pj];
+                acc[0][r] = fmaf(rv.x, qv, acc[0][r]);
+                acc[1][r] = fmaf(rv.y, qv, acc[1][r]);
+                acc[2][r] = fmaf(rv.z, qv, acc[2][r]);
+                acc[3][r] = fmaf(rv.w, qv, acc[3][r]);
+            }
         }
-        const float *ri = rs + i * (d + 1);
-        for (uint32_t row = rg; row < rows; row += nrg) {
-            const float *q = qp + row * d;
-            float v = 0.0f;
-            for (uint32_t j = lo; j < hi; ++j) v = fmaf(ri[j], q[j], v);
-            const uint32_t t = row / G, g = row % G;
-            a.qt[(((uint64_t)s * a.n + t0 + t) * HQ + (uint64_t)h * G + g) * D + i] = i < d ? v * qscale : 0.0f;
+    }
+    const float qscale = kLog2e / sqrtf((float)d);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const uint32_t row = 8 * rb + r;
+        if (row < rows) {
+            const uint32_t t = row / G, g = row - t * G;
+            float4 o;
+            o.x = 4 * ib + 0 < d ? acc[0][r] * qscale : 0.0f;
+            o.y = 4 * ib + 1 < d ? acc[1][r] * qscale : 0.0f;
+            o.z = 4 * ib + 2 < d ? acc[2][r] * qscale : 0.0f;
+            o.w = 4 * ib + 3 < d ? acc[3][r] * qscale : 0.0f;
+            *reinterpret_cast<float4 *>(a.qt + (((uint64_t)s * a.n + t0 + t) * HQ + (uint64_t)h * G + g) * D + 4 * ib) = o;
         }
     }
 }
@@ -459,7 +492,7 @@ cudaError_t launch_prefill(const PrefillArgs &a, uint32_t max_cent, int umma, cu
     // one plan for all heads, sized for the widest; each head copies its own tile sizes
     const pre::Plan pl = pre::make_plan(row_stride, scale_stride, max_cent);
     {
-        const size_t qsmem = sizeof(float) * ((size_t)a.d * (a.d + 1) + (size_t)pre::kQrotTokens * a.gqa * a.d);
+        const size_t qsmem = sizeof(float) * ((size_t)pre::D * pre::D + (size_t)pre::kQrotRowsMax * pre::kQrotStride + pre::D);
         static int configured[64] = {};
         int dev = 0;
         cudaGetDevice(&dev);
