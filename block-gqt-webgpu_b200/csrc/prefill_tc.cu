@@ -9,7 +9,8 @@
 //   1. the packed tile (rows + FP16 scales) and the V tile arrive by cp.async.bulk (TMA
 //      bulk copies, no multicast) on mbarriers, two tiles in flight;
 //   2. all threads dequantise the packed tile into shared memory as code-domain values
-//      s_g * cent split into FP16 high / low halves (K-major, 128-byte swizzle);
+//      s_g * cent split into FP16 high / low halves (K-major, 128-byte swizzle), a thread per
+//      key and eight dimension pairs, decoded from a per-pair table;
 //   3. one thread issues S = Q_hi C_hi + Q_hi C_lo + Q_lo C_hi as 12 UMMAs (M 128, N 64,
 //      K 16) into three TMEM accumulators - the large high x high term over dims 0-31 and
 //      32-63 separately, the two small cross terms together - so the tensor cores' running
@@ -48,7 +49,10 @@ constexpr uint32_t kCTile = BN * kRow;          // 8 KB
 constexpr uint32_t kTmemCols = 256;
 // TMEM columns: S_hh over dims 0-31, S_hh over dims 32-63, S cross terms, O tile
 constexpr uint32_t kColHH0 = 0, kColHH1 = 64, kColX = 128, kColO = 192;
-constexpr uint32_t kMetaHigh = 1u << 8, kMetaByte = 1u << 9, kMetaZero = 1u << 10;
+// Per dimension pair decode word (x): byte of the codes in the packed row, bit 8: the pair
+// is two raw bytes (else the low / high nibbles of one byte), bits 16-18: group; (y): the
+// compact codebook offsets of the two dimensions.  Pairs past the head dim decode zeros.
+constexpr uint32_t kPairByte = 1u << 8;
 
 struct Plan {
     uint32_t qhi, qlo, chi, clo, phi, plo, vst, kst, cent, meta, bars, slot, red, total;
@@ -168,7 +172,7 @@ __global__ void __launch_bounds__(NTH, 2) prefill_tc_kernel(const __grid_constan
     unsigned char *sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(sm);
     float *cent_s = reinterpret_cast<float *>(sm + pl.cent);
-    uint32_t *meta_s = reinterpret_cast<uint32_t *>(sm + pl.meta);
+    uint2 *pair_s = reinterpret_cast<uint2 *>(sm + pl.meta);
     const uint32_t bars = sbase + pl.bars;
     const uint32_t bar_s = bars + 32u, bar_o = bars + 40u;
     volatile uint32_t *slot = reinterpret_cast<volatile uint32_t *>(sm + pl.slot);
@@ -182,15 +186,16 @@ __global__ void __launch_bounds__(NTH, 2) prefill_tc_kernel(const __grid_constan
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
     }
     for (uint32_t i = tid; i < pl.cent_alloc; i += NTH) cent_s[i] = i < hd.n_cent ? hd.cent[i] : 0.0f;
-    if (tid < (uint32_t)D) {
-        uint32_t m = kMetaZero;
-        if (tid < a.d) {
-            const uint32_t grp = hd.group_of[tid];
-            if (tid < hd.ns) m = (tid >> 1) | ((tid & 1u) ? kMetaHigh : 0u);
-            else m = (hd.ns / 2 + (tid - hd.ns)) | kMetaByte;
-            m |= grp << 12 | (uint32_t)hd.cb_base[tid] << 16;
+    if (tid < (uint32_t)D / 2) {
+        const uint32_t j0 = 2 * tid;
+        // zero pair: nibble byte 0 against the zero tail of the codebooks (codes <= 15)
+        uint2 pw = make_uint2(0u, hd.n_cent | hd.n_cent << 16);
+        if (j0 < a.d) {
+            const bool nib = j0 < hd.ns;
+            pw.x = (nib ? tid : hd.ns / 2 + (j0 - hd.ns)) | (nib ? 0u : kPairByte) | (uint32_t)hd.group_of[j0] << 16;
+            pw.y = (uint32_t)hd.cb_base[j0] | (uint32_t)hd.cb_base[j0 + 1] << 16;
         }
-        meta_s[tid] = m;
+        pair_s[tid] = pw;
     }
     {
         // this thread's query row (code domain, log2 units) as FP16 high / low halves
@@ -268,20 +273,33 @@ __global__ void __launch_bounds__(NTH, 2) prefill_tc_kernel(const __grid_constan
         phase ^= 1u << st;
         pending &= ~(1u << st);
         const unsigned char *kt = sm + pl.kst + st * pl.kstage;
-        for (uint32_t it = tid; it < BN * 8u; it += NTH) {
-            const uint32_t key = it & (BN - 1), ch = it >> 6;
-            const unsigned char *row = kt + key * row_stride;
+        {
+            // thread = key (lanes: consecutive keys, one codebook per instruction) x pairs
+            // 8r .. 8r+7 (chunks 2r, 2r+1); the pair's kind is uniform over the warp
+            const uint32_t key = tid & (BN - 1), r = tid >> 6;
+            const unsigned char *krow = kt + key * row_stride;
             const uint16_t *sc = reinterpret_cast<const uint16_t *>(kt + soff + key * srow);
-            float v[8];
+            float v0[8], v1[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const uint32_t mt = meta_s[ch * 8 + e];
-                const uint32_t byte = row[mt & 0xffu];
-                const uint32_t code = (mt & kMetaByte) ? byte : ((mt & kMetaHigh) ? byte >> 4 : byte & 15u);
-                const float scale = __half2float(__ushort_as_half(sc[(mt >> 12) & 7u]));
-                v[e] = (mt & kMetaZero) ? 0.0f : cent_s[(mt >> 16) + code] * scale;
+            for (uint32_t q = 0; q < 8; ++q) {
+                const uint2 pw = pair_s[8 * r + q];
+                const uint32_t boff = pw.x & 0xffu;
+                uint32_t c0, c1;
+                if (pw.x & kPairByte) {
+                    c0 = krow[boff];
+                    c1 = krow[boff + 1];
+                } else {
+                    const uint32_t b = krow[boff];
+                    c0 = b & 15u;
+                    c1 = b >> 4;
+                }
+                const float scale = __half2float(__ushort_as_half(sc[pw.x >> 16]));
+                float &x0 = q < 4 ? v0[2 * q] : v1[2 * q - 8], &x1 = q < 4 ? v0[2 * q + 1] : v1[2 * q - 7];
+                x0 = cent_s[(pw.y & 0xffffu) + c0] * scale;
+                x1 = cent_s[(pw.y >> 16) + c1] * scale;
             }
-            put8(sm + pl.chi, sm + pl.clo, key, ch, v);
+            put8(sm + pl.chi, sm + pl.clo, key, 2 * r, v0);
+            put8(sm + pl.chi, sm + pl.clo, key, 2 * r + 1, v1);
         }
         fence_proxy_async();
         tc_before_sync();
