@@ -64,6 +64,12 @@ SIGNATURES = {
     "bgtq_tables_build": (I32, [U32, P, P, U32, U32, U32, P, SZ, P, P, SZ, P]),
     "bgtq_haar_rotation": (I32, [U32, U64, P]),
     "bgtq_optimal_centroids": (I32, [U32, U32, P]),
+    "bgtq_fixture_read": (I32, [C.c_char_p, P]),
+    "bgtq_fixture_array_count": (I32, [P, P]),
+    "bgtq_fixture_array": (I32, [P, U32, P, P, P, P, P, P]),
+    "bgtq_fixture_manifest": (I32, [P, P]),
+    "bgtq_fixture_destroy": (None, [P]),
+    "bgtq_fixture_write": (I32, [C.c_char_p, C.c_char_p, U32, P, P, P, P, P]),
     "bgtq_layout_validate": (I32, [P, SZ, P, SZ, P, C.POINTER(LayoutInfo)]),
     "bgtq_tables_create": (I32, [P, SZ, P, SZ, C.c_int, C.POINTER(P)]),
     "bgtq_tables_info": (I32, [P, C.POINTER(LayoutInfo)]),

@@ -123,6 +123,27 @@ bgtq_status bgtq_haar_rotation(uint32_t n, uint64_t seed, float *out);
  * (block_gtq_pipeline.py:24-78). */
 bgtq_status bgtq_optimal_centroids(uint32_t bits, uint32_t n, float *out);
 
+/* Fixture files of the reference's tests (tests/oracles/fixture.py:13-49): a JSON manifest
+ * (metadata + array descriptors dtype f32/u32/u8/f16/u16, shape, offset, nbytes) beside a
+ * little-endian payload checked by length and SHA-256.  Read errors are BGTQ_ELAYOUT with
+ * read_fixture's messages ("Unsupported fixture format", "Fixture payload length/hash
+ * mismatch", "Invalid array descriptor: <name>"). */
+typedef struct bgtq_fixture bgtq_fixture;
+bgtq_status bgtq_fixture_read(const char *json_path, bgtq_fixture **out);
+bgtq_status bgtq_fixture_array_count(const bgtq_fixture *f, uint32_t *n);
+/* Array `index` in manifest order; data points into the fixture (valid until destroy). */
+bgtq_status bgtq_fixture_array(const bgtq_fixture *f, uint32_t index, const char **name, const char **dtype,
+                               uint32_t *ndim, const uint64_t **shape, const void **data, uint64_t *nbytes);
+/* The manifest text as read (metadata included). */
+bgtq_status bgtq_fixture_manifest(const bgtq_fixture *f, const char **json);
+void bgtq_fixture_destroy(bgtq_fixture *f);
+/* write_fixture: arrays (C order) into <json_path stem>.bin, each on a 4-byte boundary, and
+ * the manifest = metadata_json (a JSON object, may be NULL) + version (kept if given, else
+ * 1), endianness, binary, byte_length, sha256, arrays. */
+bgtq_status bgtq_fixture_write(const char *json_path, const char *metadata_json, uint32_t n_arrays,
+                               const char *const *names, const char *const *dtypes, const uint32_t *ndims,
+                               const uint64_t *const *shapes, const void *const *data);
+
 /* validateLayout() plus the PackedKeys inverse-group check, on host memory only.
  * config/table are the flattened tables() output (src/webgpu/layout.ts:24-31).
  * ranges_out (nullable, 2*dim entries) receives the [start,end) group bounds of each
