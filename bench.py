@@ -340,6 +340,8 @@ def run_ours(args, rank, world, local_rank):
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             "clocks": clk,
+            "attention_kernel": ("layout-specialised (compiled at run time for the config-4 group structure)"
+                                 if bgtq.layout_jit_stats()[0] else "generic"),
             "checks": {"outputs_finite": finite, "device_status": status, "setup_s": setup_s,
                        "output_checksums": checksums,
                        "sequences": [sharding.sequence_range(B, r)[0] for r in range(world)]},

@@ -14,7 +14,22 @@ from .attention import AttentionEngine, AttentionSession, GroupedAttention, Opti
 __all__ = ["BGTQError", "DeviceError", "LayoutError", "RangeError", "StateError", "LIB_PATH", "lib",
            "BlockGTQParameters", "allocate_bits", "build_tables", "haar_rotation", "optimal_centroids", "tables", "validate_layout", "CompressedKeys", "FP16Keys", "append_kv",
            "PackedKeys", "Values", "AttentionEngine", "AttentionSession", "GroupedAttention", "OptimizedAttention",
-           "device_status"]
+           "device_status", "set_layout_jit", "layout_jit_stats"]
+
+
+def set_layout_jit(on: bool) -> None:
+    """Use (default) or bypass the layout-specialised decode attention kernels (bgtq_set_layout_jit)."""
+    from . import _lib
+    _lib.call("bgtq_set_layout_jit", 1 if on else 0)
+
+
+def layout_jit_stats() -> tuple[int, int]:
+    """(specialised kernels built, layouts that failed to build) in this process."""
+    import ctypes as C
+    from . import _lib
+    b, f = C.c_uint32(), C.c_uint32()
+    _lib.call("bgtq_layout_jit_stats", C.byref(b), C.byref(f))
+    return b.value, f.value
 
 
 def device_status(device: int = 0) -> int:

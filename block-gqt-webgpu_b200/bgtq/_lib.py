@@ -64,6 +64,8 @@ SIGNATURES = {
     "bgtq_tables_build": (I32, [U32, P, P, U32, U32, U32, P, SZ, P, P, SZ, P]),
     "bgtq_haar_rotation": (I32, [U32, U64, P]),
     "bgtq_optimal_centroids": (I32, [U32, U32, P]),
+    "bgtq_set_layout_jit": (I32, [I32]),
+    "bgtq_layout_jit_stats": (I32, [P, P]),
     "bgtq_fixture_read": (I32, [C.c_char_p, P]),
     "bgtq_fixture_array_count": (I32, [P, P]),
     "bgtq_fixture_array": (I32, [P, U32, P, P, P, P, P, P]),

@@ -1,5 +1,6 @@
 // Instantiation table and host launch logic for the attention kernels.
 #include <algorithm>
+#include <mutex>
 
 #include "attention_impl.cuh"
 
@@ -54,6 +55,24 @@ Entry pick_entry(KKind kk, int v_f32, uint32_t D, uint32_t rows) {
 }
 
 uint32_t dim_template(uint32_t d) { return d <= 16 ? 16u : d <= 32 ? 32u : d <= 64 ? 64u : 128u; }
+
+// Resident CTAs per SM of a specialised kernel (the dynamic shared-memory limit set first),
+// remembered per (kernel, device, shared-memory size).
+int jit_occupancy(const void *k, int dev, uint32_t smem) {
+    struct Slot { const void *k; int dev; uint32_t smem; int n; };
+    static Slot slots[16] = {};
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Slot &sl : slots)
+        if (sl.k == k && sl.dev == dev && sl.smem == smem) return sl.n;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int n = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, attn::kThreads, smem);
+    static int next = 0;
+    slots[next] = Slot{k, dev, smem, n};
+    next = (next + 1) % 16;
+    return n;
+}
 
 __global__ void probs_kernel(const float *logits, const float *lse, float *probs, uint64_t rows, uint32_t tokens,
                              uint32_t stride) {
@@ -143,7 +162,28 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
     const Plan pl =
         attn::make_plan(kk, v_f32, D, e.qp, TT, row_stride, scale_stride, max_cent, (uint32_t)optin - 64u, 2, e.qm);
     if (pl.total > (uint32_t)optin) return cudaErrorInvalidConfiguration;
-    int per_sm = e.occ(pl);
+    // packed keys whose heads share one group structure: the kernel specialised for it
+    const void *jk = nullptr;
+    if (kk == KKind::Packed) {
+        const AttnHead &h0 = a.head[0];
+        bool same = h0.ng >= 1 && h0.ng <= (uint32_t)kMaxGroups;
+        for (uint32_t h = 1; h < a.heads && same; ++h) {
+            same = a.head[h].ns == h0.ns && a.head[h].ng == h0.ng;
+            for (uint32_t g = 0; g <= h0.ng && same; ++g) same = a.head[h].group_off[g] == h0.group_off[g];
+        }
+        if (same) {
+            JitKey key{};
+            key.D = D;
+            key.QM = e.qm;
+            key.vf32 = v_f32 ? 1u : 0u;
+            key.ns = h0.ns;
+            key.ng = h0.ng;
+            key.scale_stride = scale_stride;
+            for (uint32_t g = 0; g <= h0.ng; ++g) key.group_off[g] = h0.group_off[g];
+            jk = jit_attention_kernel(key, dev);
+        }
+    }
+    int per_sm = jk ? jit_occupancy(jk, dev, pl.total) : e.occ(pl);
     if (per_sm < 1) per_sm = 1;
     uint32_t splits = 1, tps = 0;
     choose_splits(a.seq_count * a.heads, max_len, attn::kWarps * TT, (uint32_t)(sms * per_sm), forced_splits,
@@ -155,6 +195,12 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
     attn::qrot_kernel<<<dim3(a.heads, a.seq_count), 128, 0, s>>>(a, d, D, e.qp, kk == KKind::Packed ? 1 : 0);
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
+    if (jk) {
+        uint32_t dd = d;
+        Plan plc = pl;
+        void *args[] = {&a, &plc, &dd};
+        return cudaLaunchKernel(jk, grid, dim3(attn::kThreads), args, pl.total, s);
+    }
     return e.run(a, pl, d, grid, s);
 }
 

@@ -90,6 +90,17 @@ struct UseMma {
     static constexpr bool value = !VF32 && (D == 64 || D == 128);
 };
 
+// Group structure of the packed keys.  RuntimeGroups reads it from the head at run time; a
+// kernel specialised for one layout (built by NVRTC, jit.cpp) supplies a policy with
+// kStatic = true and the layout as constants (kNG groups, kNS nibble dims, group offsets
+// go(g) as a constexpr function, which folds where an array might be placed in memory), so
+// every group and run loop unrolls.
+struct RuntimeGroups {
+    static constexpr bool kStatic = false;
+    static constexpr uint32_t kNG = 0, kNS = 0;
+    static __host__ __device__ constexpr uint32_t go(uint32_t) { return 0; }
+};
+
 // Shared-memory plan of one CTA.  Each warp owns a V tile buffer and a ring of `stages`
 // K tile buffers (packed rows + FP16 scales, or dense rows): the next tile's keys are
 // fetched while the current tile is computed, and the next tile's values are fetched as
@@ -103,6 +114,7 @@ struct Plan {
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
 __host__ __device__ inline uint32_t align128(uint32_t x) { return (x + 127u) & ~127u; }
 
+#ifndef __CUDACC_RTC__
 inline Plan make_plan(KKind kk, int v_f32, uint32_t D, uint32_t QP, uint32_t TT, uint32_t row_stride,
                       uint32_t scale_stride, uint32_t n_cent, uint32_t smem_limit = 227u * 1024u,
                       uint32_t stages = 2, uint32_t QM = 0) {
@@ -137,6 +149,7 @@ inline Plan make_plan(KKind kk, int v_f32, uint32_t D, uint32_t QP, uint32_t TT,
         return make_plan(kk, v_f32, D, QP, TT, row_stride, scale_stride, n_cent, smem_limit, 1, QM);
     return p;
 }
+#endif  // __CUDACC_RTC__
 
 // ---- PTX helpers: mbarrier + bulk async copies (sm_90+, no multicast), tensor cores ----
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -205,6 +218,18 @@ __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// Packed FP32 FMA (two lanes, round to nearest) in PTX, so kernels built by nvcc and by
+// NVRTC (whose headers declare the intrinsic differently) get the same instruction.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -276,7 +301,7 @@ __device__ __forceinline__ void build_tables(const AttnHead &h, const float *qt,
 // a constant offset, a byte lookup an OR (or shifted add) of code * 4 into the dimension's
 // size-aligned slot address from the pair record.  Code bytes are read as (unaligned)
 // words: a nibble block needs 4 bytes, a byte block 8.
-template <int D, int QM>
+template <int D, int QM, class LP>
 __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char *sm, uint32_t kb_s,
                                           const uint16_t *sb, const unsigned char *rec, uint32_t cb_s, int lane,
                                           float (&acc)[Geo<D>::TPL][QM]) {
@@ -316,7 +341,7 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
             const float2 c = make_float2(lds_f32(sm, ia[tt] + OA), lds_f32(sm, ib[tt] + OB));
 #pragma unroll
             for (int r = 0; r < QM; ++r)
-                part[tt][r] = __ffma2_rn(make_float2(__uint_as_float(v[2 * r]), __uint_as_float(v[2 * r + 1])), c,
+                part[tt][r] = ffma2(make_float2(__uint_as_float(v[2 * r]), __uint_as_float(v[2 * r + 1])), c,
                                          part[tt][r]);
         }
     };
@@ -375,23 +400,33 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
             }
         }
     };
+    // one group: its runs of four pairs, then the group-end scale step
     uint32_t rix = 0;  // first record of the current group
-#pragma unroll 1
-    for (uint32_t g = 0; g < h.ng; ++g) {
-        const uint32_t go = h.group_off[g], p0 = go / 2, np = h.group_off[g + 1] / 2 - p0;
+    auto group = [&](uint32_t go, uint32_t gnext, uint32_t nsv, bool unrolled) {
+        const uint32_t p0 = go / 2, np = gnext / 2 - p0;
         const uint32_t nfull = np / 4, rem = np & 3u;
         const uint32_t *rg = recs + rix * RP;
-        if (go < ns) {
+        if (go < nsv) {
             // run b of the head owns lookup slot b (512 bytes); the group's first run is rix / 4
             const uint32_t slot0 = cb_s + (rix >> 2) * 512u;
+            if (unrolled) {
+#pragma unroll
+                for (uint32_t k = 0; k < nfull; ++k) nib_run(p0 + 4 * k, rg + 4 * k * RP, 4, slot0 + k * 512u);
+            } else {
 #pragma unroll 1
-            for (uint32_t k = 0; k < nfull; ++k) nib_run(p0 + 4 * k, rg + 4 * k * RP, 4, slot0 + k * 512u);
+                for (uint32_t k = 0; k < nfull; ++k) nib_run(p0 + 4 * k, rg + 4 * k * RP, 4, slot0 + k * 512u);
+            }
             if (rem) nib_run(p0 + 4 * nfull, rg + 4 * nfull * RP, rem, slot0 + nfull * 512u);
         } else {
             // byte group: dim 2*p0 sits at byte ns/2 + (2*p0 - ns)
-            const uint32_t ob = 2 * p0 - ns / 2;
+            const uint32_t ob = 2 * p0 - nsv / 2;
+            if (unrolled) {
+#pragma unroll
+                for (uint32_t k = 0; k < nfull; ++k) byte_run(ob + 8 * k, rg + 4 * k * RP, 4);
+            } else {
 #pragma unroll 1
-            for (uint32_t k = 0; k < nfull; ++k) byte_run(ob + 8 * k, rg + 4 * k * RP, 4);
+                for (uint32_t k = 0; k < nfull; ++k) byte_run(ob + 8 * k, rg + 4 * k * RP, 4);
+            }
             if (rem) byte_run(ob + 8 * nfull, rg + 4 * nfull * RP, rem);
         }
         const uint32_t nblk = nfull + (rem ? 1u : 0u);
@@ -404,12 +439,19 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
             const float ds = half_lo(sw[tt][0]) - half_lo(sw[tt][0] >> 16);
             const float2 ds2 = make_float2(ds, ds);
 #pragma unroll
-            for (int r = 0; r < QM; ++r) acc2[tt][r] = __ffma2_rn(ds2, part[tt][r], acc2[tt][r]);
+            for (int r = 0; r < QM; ++r) acc2[tt][r] = ffma2(ds2, part[tt][r], acc2[tt][r]);
             sw[tt][0] = __funnelshift_r(sw[tt][0], sw[tt][1], 16);
             sw[tt][1] = __funnelshift_r(sw[tt][1], sw[tt][2], 16);
             sw[tt][2] = __funnelshift_r(sw[tt][2], sw[tt][3], 16);
             sw[tt][3] >>= 16;
         }
+    };
+    if constexpr (LP::kStatic) {
+#pragma unroll
+        for (uint32_t g = 0; g < LP::kNG; ++g) group(LP::go(g), LP::go(g + 1), LP::kNS, true);
+    } else {
+#pragma unroll 1
+        for (uint32_t g = 0; g < h.ng; ++g) group(h.group_off[g], h.group_off[g + 1], ns, false);
     }
 #pragma unroll
     for (int tt = 0; tt < TPL; ++tt)
@@ -425,8 +467,8 @@ struct MinBlocks {
     static constexpr int value = (KK == KKind::Packed && D <= 64 && QM <= 4) ? 3 : 1;
 };
 
-template <int D, int QM, KKind KK, bool VF32>
-__global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_kernel(const __grid_constant__ AttnArgs a, const Plan pl, uint32_t d) {
+template <int D, int QM, KKind KK, bool VF32, class LP>
+__device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uint32_t d) {
     constexpr int TPL = Geo<D>::TPL, TT = Geo<D>::TT, QP = QPad<QM>::QP;
     constexpr bool MMA = UseMma<D, VF32>::value;
     constexpr int VSZ = VF32 ? 4 : 2, VEC = 16 / VSZ, LPT = D / VEC, TPS = 32 / LPT;
@@ -569,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
         // ---- logits for this lane's TPL tokens ----
         float acc[TPL][QM];
         if constexpr (KK == KKind::Packed) {
-            packed_qk<D, QM>(h, smem, (uint32_t)(kb - smem), sb, rec, pl.cent, lane, acc);
+            packed_qk<D, QM, LP>(h, smem, (uint32_t)(kb - smem), sb, rec, pl.cent, lane, acc);
         } else {
             const uint32_t steps = (n + TPSK - 1) / TPSK;
             for (uint32_t st2 = 0; st2 < steps; ++st2) {
@@ -696,7 +738,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
                 const __half2 ha = __floats2half2_rn(pa.x, pa.y), hb = __floats2half2_rn(pb.x, pb.y);
                 const float2 fa = __half22float2(ha), fb = __half22float2(hb);
                 const float2 m1 = make_float2(-1.0f, -1.0f);
-                const float2 ra = __ffma2_rn(fa, m1, pa), rb = __ffma2_rn(fb, m1, pb);  // exact p - hi
+                const float2 ra = ffma2(fa, m1, pa), rb = ffma2(fb, m1, pb);  // exact p - hi
                 const __half2 la = __floats2half2_rn(ra.x, ra.y), lb = __floats2half2_rn(rb.x, rb.y);
                 const uint32_t b0 = lo_col ? h2_bits(la) : h2_bits(ha), b1 = lo_col ? h2_bits(lb) : h2_bits(hb);
                 // ldmatrix (transposed) row address of this lane: matrix mi = tokens +8*(mi>>1),
@@ -734,7 +776,7 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
                 const __half2 ha = __floats2half2_rn(pa.x, pa.y), hb = __floats2half2_rn(pb.x, pb.y);
                 const float2 fa = __half22float2(ha), fb = __half22float2(hb);
                 const float2 m1 = make_float2(-1.0f, -1.0f);
-                const float2 ra = __ffma2_rn(fa, m1, pa), rb = __ffma2_rn(fb, m1, pb);  // exact p - hi
+                const float2 ra = ffma2(fa, m1, pa), rb = ffma2(fb, m1, pb);  // exact p - hi
                 const __half2 la = __floats2half2_rn(ra.x, ra.y), lb = __floats2half2_rn(rb.x, rb.y);
                 const uint32_t ahi0 = h2_bits(ha), ahi2 = h2_bits(hb), alo0 = h2_bits(la), alo2 = h2_bits(lb);
                 // ldmatrix row address of this lane: matrix mi (tokens +8*(mi&1), chunk +(mi>>1)), row ri
@@ -906,6 +948,12 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value) attn_ke
     }
 }
 
+template <int D, int QM, KKind KK, bool VF32>
+__global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value)
+    attn_kernel(const __grid_constant__ AttnArgs a, const Plan pl, uint32_t d) {
+    attn_body<D, QM, KK, VF32, RuntimeGroups>(a, pl, d);
+}
+
 // Element j of query row q after split-half RoPE at position pos (src/model/kernels.wgsl:
 // 49-54) with the table inv[d/2], rounded like separate multiplies and adds; without a
 // table the element itself.
@@ -954,6 +1002,7 @@ static __global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant_
     }
 }
 
+#ifndef __CUDACC_RTC__
 // Host-side dispatch helper for one (D, QM, KK, VF32) instantiation.
 template <int D, int QM, KKind KK, bool VF32>
 cudaError_t run(const AttnArgs &a, const Plan &pl, uint32_t d, dim3 grid, cudaStream_t s) {
@@ -991,6 +1040,7 @@ int occupancy(const Plan &pl) {
     cached_n[slot] = n;
     return n;
 }
+#endif  // __CUDACC_RTC__
 
 }  // namespace attn
 }  // namespace bgtq

@@ -1,6 +1,10 @@
 // Internal declarations shared by the C ABI (abi.cpp) and the kernels (*.cu).
 #pragma once
 
+// The kernel structs and constants below also compile under NVRTC (__CUDACC_RTC__), which
+// builds layout-specialised attention kernels at run time (jit.cpp); host-only parts are
+// guarded.
+#ifndef __CUDACC_RTC__
 #include <cstddef>
 #include <cstdint>
 #include <string>
@@ -9,6 +13,18 @@
 #include <cuda_runtime.h>
 
 #include "../../include/bgtq.h"
+#else
+typedef unsigned char uint8_t;
+typedef unsigned short uint16_t;
+typedef unsigned int uint32_t;
+typedef unsigned long long uint64_t;
+typedef int int32_t;
+typedef long long int64_t;
+typedef unsigned long size_t;
+#ifndef INFINITY
+#define INFINITY (1.0f / 0.0f)
+#endif
+#endif
 
 namespace bgtq {
 
@@ -22,6 +38,7 @@ constexpr uint32_t kTileRows = 64; // capacity is padded to a multiple of this
 constexpr uint32_t kStatusWaitTimeout = 1u;   // an mbarrier wait hit its iteration bound
 constexpr uint32_t kStatusBadLength = 2u;     // a kernel saw a length beyond capacity
 
+#ifndef __CUDACC_RTC__
 // Host copy of one validated layout (src/webgpu/layout.ts:2-31) plus what the kernels
 // derive from it once: compact per-dimension codebooks and group boundaries.
 struct Layout {
@@ -43,6 +60,7 @@ struct Layout {
 // Parse + validate the flattened tables.  Returns BGTQ_OK or an error with message.
 bgtq_status parse_layout(const uint32_t *config, size_t n_config, const float *table, size_t n_table, Layout &out,
                          std::string &err);
+#endif  // __CUDACC_RTC__
 
 // Device copy of one head's tables (one allocation, 16-byte aligned sections).
 struct DeviceTables {
@@ -159,6 +177,9 @@ struct ReconArgs {
     float *out;
 };
 
+enum class KKind { Packed, F16, F32 };
+
+#ifndef __CUDACC_RTC__
 // Kernel launchers (return cudaError_t of the launch).
 cudaError_t launch_encode(const EncodeArgs &a, uint32_t d, uint32_t smem_cent_floats, uint32_t max_ncb,
                           cudaStream_t s);
@@ -171,7 +192,7 @@ cudaError_t launch_copy_rows(void *dst, uint64_t dst_seq_stride, uint32_t dst_ro
 inline bool values_swizzled(int f32, uint32_t D) { return !f32 && (D == 64 || D == 128); }
 cudaError_t launch_reconstruct(const ReconArgs &a, uint32_t n_cent, cudaStream_t s);
 
-enum class KKind { Packed, F16, F32 };
+
 // Attention over a.seq_count sequences x a.heads KV heads; picks the split-KV factor
 // (forced_splits = 0: automatic) and writes it to *splits_out.
 cudaError_t launch_attention(const AttnArgs &a, KKind kk, int v_f32, uint32_t d, uint32_t max_cent,
@@ -187,9 +208,22 @@ cudaError_t launch_probs(const float *logits, const float *lse, float *probs, ui
 size_t attention_smem_bytes(KKind kk, int v_f32, uint32_t d, uint32_t rows_bound, uint32_t row_stride,
                             uint32_t scale_stride, uint32_t max_cent);
 uint32_t attention_tile_tokens(uint32_t d);
+// Layout-specialised decode attention (jit.cpp): the kernel for one group structure of
+// packed keys, compiled once per device by NVRTC; null when disabled or not compilable.
+struct JitKey {
+    uint32_t D, QM, vf32, ns, ng, scale_stride;
+    uint32_t group_off[kMaxGroups + 1];
+};
+const void *jit_attention_kernel(const JitKey &key, int device);
+void jit_set_enabled(int on);
+// The calling thread's launches keep the generic kernel while on != 0 (an entry point that
+// promises no allocation at attention time: loading a specialised kernel allocates).
+void jit_suppress_on_thread(int on);
 
 uint32_t *device_status_word(int device);  // lazily allocated per device
 uint32_t *device_status_word_if_present(int device);  // never allocates; null if absent
 void set_last_error(const std::string &message);     // message of bgtq_last_error()
+
+#endif  // __CUDACC_RTC__
 
 }  // namespace bgtq

@@ -1,0 +1,293 @@
+// Layout-specialised decode attention: the kernel of attention_impl.cuh compiled at run time
+// by NVRTC for one group structure of packed keys (nibble dims, group offsets).  With the
+// layout as compile-time constants every group and run loop of the dequant + QK phase
+// unrolls, which removes the loop and per-group bookkeeping of the generic kernel; the
+// arithmetic and its order are the same, so outputs are identical.
+//
+// The toolkit's nvcc (run as a child process, device code only, the build's flags) compiles
+// the package's own kernel source (csrc/, found next to this library) to an sm_100a cubin,
+// loaded with cudaLibraryLoadData; about two seconds per layout.  Without nvcc, NVRTC (loaded
+// with dlopen) is the fallback: its kernels are correct but its headers declare some
+// intrinsics differently, so they are a few percent slower than nvcc's.
+// One kernel per layout key, built on the first launch that needs it and kept for the life
+// of the process (at most kMaxEntries).  Anything that fails (no NVRTC, no sources, a compile
+// or load error) leaves the generic kernel in use.  BGTQ_LAYOUT_JIT=0 in the environment or
+// bgtq_set_layout_jit(0) turns it off.
+#include <dlfcn.h>
+#include <spawn.h>
+#include <sys/wait.h>
+#include <unistd.h>
+#include <fcntl.h>
+#include <cerrno>
+
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <fstream>
+#include <sstream>
+#include <map>
+#include <mutex>
+#include <string>
+#include <sys/stat.h>
+#include <vector>
+
+#include "bgtq_internal.h"
+
+extern char **environ;
+
+namespace bgtq {
+namespace {
+
+constexpr size_t kMaxEntries = 16;
+
+typedef int (*nvrtcCreateProgram_t)(void **, const char *, const char *, int, const char *const *,
+                                    const char *const *);
+typedef int (*nvrtcCompileProgram_t)(void *, int, const char *const *);
+typedef int (*nvrtcGetSize_t)(void *, size_t *);
+typedef int (*nvrtcGetData_t)(void *, char *);
+typedef int (*nvrtcDestroyProgram_t)(void **);
+
+struct Nvrtc {
+    bool ok = false;
+    nvrtcCreateProgram_t create = nullptr;
+    nvrtcCompileProgram_t compile = nullptr;
+    nvrtcGetSize_t log_size = nullptr, cubin_size = nullptr;
+    nvrtcGetData_t log = nullptr, cubin = nullptr;
+    nvrtcDestroyProgram_t destroy = nullptr;
+};
+
+std::string cuda_home() {
+    for (const char *v : {"CUDA_HOME", "CUDA_PATH"}) {
+        const char *e = std::getenv(v);
+        if (e && *e) return e;
+    }
+    return "/usr/local/cuda";
+}
+
+bool exists(const std::string &p) {
+    struct stat st;
+    return stat(p.c_str(), &st) == 0;
+}
+
+const Nvrtc &nvrtc() {
+    static Nvrtc n;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = nullptr;
+        for (const std::string &name : {std::string("libnvrtc.so.12"), std::string("libnvrtc.so"),
+                                         cuda_home() + "/lib64/libnvrtc.so.12", cuda_home() + "/lib64/libnvrtc.so"}) {
+            h = dlopen(name.c_str(), RTLD_NOW | RTLD_LOCAL);
+            if (h) break;
+        }
+        if (!h) return;
+        n.create = reinterpret_cast<nvrtcCreateProgram_t>(dlsym(h, "nvrtcCreateProgram"));
+        n.compile = reinterpret_cast<nvrtcCompileProgram_t>(dlsym(h, "nvrtcCompileProgram"));
+        n.log_size = reinterpret_cast<nvrtcGetSize_t>(dlsym(h, "nvrtcGetProgramLogSize"));
+        n.log = reinterpret_cast<nvrtcGetData_t>(dlsym(h, "nvrtcGetProgramLog"));
+        n.cubin_size = reinterpret_cast<nvrtcGetSize_t>(dlsym(h, "nvrtcGetCUBINSize"));
+        n.cubin = reinterpret_cast<nvrtcGetData_t>(dlsym(h, "nvrtcGetCUBIN"));
+        n.destroy = reinterpret_cast<nvrtcDestroyProgram_t>(dlsym(h, "nvrtcDestroyProgram"));
+        n.ok = n.create && n.compile && n.log_size && n.log && n.cubin_size && n.cubin && n.destroy;
+    });
+    return n;
+}
+
+// csrc/ of this package: the library sits in bgtq/, the sources in ../csrc
+std::string source_dir() {
+    Dl_info info{};
+    if (!dladdr(reinterpret_cast<void *>(&jit_set_enabled), &info) || !info.dli_fname) return "";
+    std::string p(info.dli_fname);
+    const size_t slash = p.find_last_of('/');
+    p = slash == std::string::npos ? std::string(".") : p.substr(0, slash);
+    for (const std::string dir : {p + "/../csrc", p + "/csrc"})
+        if (exists(dir + "/attention_impl.cuh")) return dir;
+    return "";
+}
+
+struct Entry {
+    bool failed = false;
+    cudaLibrary_t lib = nullptr;
+    cudaKernel_t kernel = nullptr;
+};
+
+std::mutex g_mu;
+std::map<std::string, Entry> g_cache;
+std::atomic<int> g_enabled{-1};  // -1: not read from the environment yet
+std::atomic<uint32_t> g_built{0}, g_failed{0};
+
+std::string key_string(const JitKey &k) {
+    std::string s = std::to_string(k.D) + "/" + std::to_string(k.QM) + "/" + std::to_string(k.vf32) + "/" +
+                    std::to_string(k.ns) + "/" + std::to_string(k.ng) + ":";
+    for (uint32_t g = 0; g <= k.ng && g <= (uint32_t)kMaxGroups; ++g) s += std::to_string(k.group_off[g]) + ",";
+    return s;
+}
+
+std::string kernel_source(const JitKey &k) {
+    // go(g) as nested conditionals over g = 0 .. ng
+    std::string go = "0u";
+    for (int g = (int)k.ng; g >= 0; --g)
+        go = "g == " + std::to_string(g) + "u ? " + std::to_string(k.group_off[g]) + "u : (" + go + ")";
+    const std::string D = std::to_string(k.D), QM = std::to_string(k.QM), VF = k.vf32 ? "true" : "false";
+    return "#include \"attention_impl.cuh\"\n"
+           "struct JitGroups {\n"
+           "    static constexpr bool kStatic = true;\n"
+           "    static constexpr uint32_t kNG = " + std::to_string(k.ng) + "u, kNS = " + std::to_string(k.ns) + "u;\n"
+           "    static __host__ __device__ constexpr uint32_t go(uint32_t g) { return " + go + "; }\n"
+           "};\n"
+           "extern \"C\" __global__ void __launch_bounds__(bgtq::attn::kThreads, bgtq::attn::MinBlocks<" + D + ", " +
+           QM + ", bgtq::KKind::Packed>::value)\n"
+           "bgtq_attn_jit(const __grid_constant__ bgtq::AttnArgs a, const bgtq::attn::Plan pl, uint32_t d) {\n"
+           "    bgtq::attn::attn_body<" + D + ", " + QM + ", bgtq::KKind::Packed, " + VF + ", JitGroups>(a, pl, d);\n"
+           "}\n";
+}
+
+// nvcc -cubin of `src` in a private temporary directory; false if nvcc is absent or fails.
+bool nvcc_cubin(const std::string &src, const std::string &src_dir, std::vector<char> &cubin) {
+    const std::string nvcc = cuda_home() + "/bin/nvcc";
+    if (!exists(nvcc)) return false;
+    const char *tmp = std::getenv("TMPDIR");
+    std::string tmpl = std::string(tmp && *tmp ? tmp : "/tmp") + "/bgtq_jit_XXXXXX";
+    std::vector<char> tbuf(tmpl.begin(), tmpl.end());
+    tbuf.push_back('\0');
+    if (!mkdtemp(tbuf.data())) return false;
+    const std::string dir(tbuf.data()), cu = dir + "/k.cu", out = dir + "/k.cubin", log = dir + "/log.txt";
+    bool ok = false;
+    {
+        std::ofstream f(cu);
+        f << src;
+    }
+    std::vector<std::string> args = {nvcc, "-cubin", "-gencode", "arch=compute_100a,code=sm_100a", "-O3",
+                                     "-std=c++17", "-I" + src_dir, "-o", out, cu};
+    std::vector<char *> argv;
+    for (auto &a : args) argv.push_back(&a[0]);
+    argv.push_back(nullptr);
+    posix_spawn_file_actions_t fa;
+    posix_spawn_file_actions_init(&fa);
+    posix_spawn_file_actions_addopen(&fa, 1, log.c_str(), O_WRONLY | O_CREAT | O_TRUNC, 0644);
+    posix_spawn_file_actions_adddup2(&fa, 1, 2);
+    pid_t pid = 0;
+    if (posix_spawn(&pid, nvcc.c_str(), &fa, nullptr, argv.data(), environ) == 0) {
+        int status = 0;
+        while (waitpid(pid, &status, 0) < 0 && errno == EINTR) {
+        }
+        ok = WIFEXITED(status) && WEXITSTATUS(status) == 0;
+    }
+    posix_spawn_file_actions_destroy(&fa);
+    if (ok) {
+        std::ifstream f(out, std::ios::binary);
+        std::stringstream ss;
+        ss << f.rdbuf();
+        const std::string b = ss.str();
+        cubin.assign(b.begin(), b.end());
+        ok = !cubin.empty();
+    } else if (std::getenv("BGTQ_LAYOUT_JIT_LOG")) {
+        std::ifstream f(log);
+        std::stringstream ss;
+        ss << f.rdbuf();
+        std::fprintf(stderr, "bgtq layout JIT: nvcc failed:\n%s\n", ss.str().c_str());
+    }
+    for (const std::string &p : {cu, out, log}) unlink(p.c_str());
+    rmdir(dir.c_str());
+    return ok;
+}
+
+bool load(const std::vector<char> &cubin, Entry &e) {
+    if (cudaLibraryLoadData(&e.lib, cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    if (cudaLibraryGetKernel(&e.kernel, e.lib, "bgtq_attn_jit") != cudaSuccess) {
+        cudaGetLastError();
+        cudaLibraryUnload(e.lib);
+        e.lib = nullptr;
+        return false;
+    }
+    return true;
+}
+
+bool build(const JitKey &k, Entry &e) {
+    const std::string src_dir = source_dir(), inc = cuda_home() + "/include";
+    if (src_dir.empty()) return false;
+    const std::string src = kernel_source(k);
+    std::vector<char> cubin;
+    if (nvcc_cubin(src, src_dir, cubin) && load(cubin, e)) return true;
+    const Nvrtc &n = nvrtc();
+    if (!n.ok || !exists(inc + "/cuda_fp16.h")) return false;
+    void *prog = nullptr;
+    if (n.create(&prog, src.c_str(), "bgtq_attn_jit.cu", 0, nullptr, nullptr) != 0) return false;
+    const std::string i1 = "-I" + src_dir, i2 = "-I" + inc;
+    const char *opts[] = {"--gpu-architecture=sm_100a", "-std=c++17", i1.c_str(), i2.c_str()};
+    const int rc = n.compile(prog, 4, opts);
+    cubin.clear();
+    if (rc == 0) {
+        size_t sz = 0;
+        if (n.cubin_size(prog, &sz) == 0 && sz) {
+            cubin.resize(sz);
+            if (n.cubin(prog, cubin.data()) != 0) cubin.clear();
+        }
+    } else if (std::getenv("BGTQ_LAYOUT_JIT_LOG")) {
+        size_t sz = 0;
+        n.log_size(prog, &sz);
+        std::string log(sz, '\0');
+        n.log(prog, &log[0]);
+        std::fprintf(stderr, "bgtq layout JIT: compile failed:\n%s\n", log.c_str());
+    }
+    n.destroy(&prog);
+    return !cubin.empty() && load(cubin, e);
+}
+
+bool enabled() {
+    int v = g_enabled.load();
+    if (v < 0) {
+        const char *e = std::getenv("BGTQ_LAYOUT_JIT");
+        v = (e && e[0] == '0') ? 0 : 1;
+        g_enabled.store(v);
+    }
+    return v != 0;
+}
+
+}  // namespace
+
+void jit_set_enabled(int on) { g_enabled.store(on ? 1 : 0); }
+
+namespace {
+thread_local int t_suppressed = 0;
+}
+void jit_suppress_on_thread(int on) { t_suppressed = on; }
+
+const void *jit_attention_kernel(const JitKey &key, int device) {
+    (void)device;  // a cudaLibrary_t serves every device
+    if (t_suppressed || !enabled() || key.ng < 1 || key.ng > (uint32_t)kMaxGroups) return nullptr;
+    const std::string ks = key_string(key);
+    std::lock_guard<std::mutex> lock(g_mu);
+    auto it = g_cache.find(ks);
+    if (it == g_cache.end()) {
+        if (g_cache.size() >= kMaxEntries) return nullptr;
+        Entry e;
+        if (build(key, e)) {
+            g_built.fetch_add(1);
+        } else {
+            e.failed = true;
+            g_failed.fetch_add(1);
+        }
+        it = g_cache.emplace(ks, e).first;
+    }
+    return it->second.failed ? nullptr : reinterpret_cast<const void *>(it->second.kernel);
+}
+
+}  // namespace bgtq
+
+extern "C" {
+
+bgtq_status bgtq_set_layout_jit(int on) {
+    bgtq::jit_set_enabled(on);
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_layout_jit_stats(uint32_t *built, uint32_t *failed) {
+    if (built) *built = bgtq::g_built.load();
+    if (failed) *failed = bgtq::g_failed.load();
+    return BGTQ_OK;
+}
+
+}  // extern "C"
