@@ -6,12 +6,15 @@ Workload per GPU (weak scaling: every rank holds its own batch):
   (config-4 tables: allocator widths for the synthetic pair-energy profile at budget 128,
   built by the reference's table code) + FP16 V, synthetic data drawn on the device.
 One step = one decode step of the whole batch through all 30 layers' attention: per
-layer, append the new token's K (encode kernel) and V for every sequence and KV head,
-then compressed-K GQA attention over the cache.  Metric: decoded tokens/s (whole job).
+layer, append the new token's K (encode) and V for every sequence and KV head in one
+launch (bgtq_append_kv), then compressed-K GQA attention over the cache (the kernel
+specialised for the config-4 group structure, compiled on the first warm-up step).
+Metric: decoded tokens/s (whole job).
 
   value  inputs resident in HBM, device-timed with CUDA events (max over ranks)
   e2e    the same step through the C ABI with host buffers: Q / new K / new V copied
-         from pinned host memory and attention outputs copied back, inside the timed region
+         from pinned host memory (one host bgtq_append_kv and one host bgtq_attend per
+         layer) and attention outputs copied back, inside the timed region
   roofline  attention launch (query rotation + attention kernel) timed with CUDA events
          inside the timed region, algorithmic bytes = tokens x KV heads x (row bytes +
          2 x groups + 2 x head_dim) at logical row size, against MEASURED_PEAKS.json HBM
