@@ -402,7 +402,7 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
     };
     // one group: its runs of four pairs, then the group-end scale step
     uint32_t rix = 0;  // first record of the current group
-    auto group = [&](uint32_t go, uint32_t gnext, uint32_t nsv, bool unrolled) {
+    auto group = [&](uint32_t g, uint32_t go, uint32_t gnext, uint32_t nsv, bool unrolled) {
         const uint32_t p0 = go / 2, np = gnext / 2 - p0;
         const uint32_t nfull = np / 4, rem = np & 3u;
         const uint32_t *rg = recs + rix * RP;
@@ -436,22 +436,31 @@ __device__ __forceinline__ void packed_qk(const AttnHead &h, const unsigned char
         // = 0 (the scale rows are zero-padded), so no per-group reset is needed.
 #pragma unroll
         for (int tt = 0; tt < TPL; ++tt) {
-            const float ds = half_lo(sw[tt][0]) - half_lo(sw[tt][0] >> 16);
+            float ds;
+            if constexpr (LP::kStatic) {
+                // g is a constant here: read s_g and s_{g+1} from their fixed halves
+                const uint32_t w0 = sw[tt][(g >> 1) & 3u], w1 = g + 1 < 8u ? sw[tt][((g + 1) >> 1) & 3u] : 0u;
+                ds = half_lo(w0 >> (16u * (g & 1u))) - half_lo(w1 >> (16u * ((g + 1) & 1u)));
+            } else {
+                ds = half_lo(sw[tt][0]) - half_lo(sw[tt][0] >> 16);
+            }
             const float2 ds2 = make_float2(ds, ds);
 #pragma unroll
             for (int r = 0; r < QM; ++r) acc2[tt][r] = ffma2(ds2, part[tt][r], acc2[tt][r]);
-            sw[tt][0] = __funnelshift_r(sw[tt][0], sw[tt][1], 16);
-            sw[tt][1] = __funnelshift_r(sw[tt][1], sw[tt][2], 16);
-            sw[tt][2] = __funnelshift_r(sw[tt][2], sw[tt][3], 16);
-            sw[tt][3] >>= 16;
+            if constexpr (!LP::kStatic) {
+                sw[tt][0] = __funnelshift_r(sw[tt][0], sw[tt][1], 16);
+                sw[tt][1] = __funnelshift_r(sw[tt][1], sw[tt][2], 16);
+                sw[tt][2] = __funnelshift_r(sw[tt][2], sw[tt][3], 16);
+                sw[tt][3] >>= 16;
+            }
         }
     };
     if constexpr (LP::kStatic) {
 #pragma unroll
-        for (uint32_t g = 0; g < LP::kNG; ++g) group(LP::go(g), LP::go(g + 1), LP::kNS, true);
+        for (uint32_t g = 0; g < LP::kNG; ++g) group(g, LP::go(g), LP::go(g + 1), LP::kNS, true);
     } else {
 #pragma unroll 1
-        for (uint32_t g = 0; g < h.ng; ++g) group(h.group_off[g], h.group_off[g + 1], ns, false);
+        for (uint32_t g = 0; g < h.ng; ++g) group(g, h.group_off[g], h.group_off[g + 1], ns, false);
     }
 #pragma unroll
     for (int tt = 0; tt < TPL; ++tt)
