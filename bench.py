@@ -266,7 +266,7 @@ def run_ours(args, rank, world, local_rank):
     clk = clocks.stop()
     elapsed = t_start.elapsed_time(t_end) / 1e3
     launch_ms = [a.elapsed_time(b) for evs in attn_ms for a, b in evs]
-    launches = steps * L * 4  # per layer: fused K/V append + length bump + query rotation + attention
+    launches = steps * L * 3  # per layer: fused K/V append (bumps the lengths too) + query rotation + attention
 
     # ---- e2e through the C ABI with host buffers ----
     e2e = None

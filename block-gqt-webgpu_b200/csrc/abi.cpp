@@ -355,9 +355,10 @@ bgtq_status bgtq_keys_create(bgtq_keys_kind kind, const bgtq_tables *tables, uin
         cudaMemset(k->scales, 0, sb);
         k->ledger.push_back({"K FP16 scale capacity", "persistent-k", sb});
     }
-    if (cudaMalloc(&k->d_lengths, sizeof(uint32_t) * sequences) != cudaSuccess)
+    // per-sequence lengths, then one word the K/V append kernel counts its finished CTAs in
+    if (cudaMalloc(&k->d_lengths, sizeof(uint32_t) * (sequences + 1)) != cudaSuccess)
         return cleanup(BGTQ_ENOMEM, "length allocation failed");
-    cudaMemset(k->d_lengths, 0, sizeof(uint32_t) * sequences);
+    cudaMemset(k->d_lengths, 0, sizeof(uint32_t) * (sequences + 1));
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return cleanup(BGTQ_ECUDA, std::string("K init: ") + cudaGetErrorString(e));
     k->lengths.assign(sequences, 0);
@@ -466,6 +467,7 @@ bgtq_status append_kv_common(uint32_t heads, bgtq_keys *const *keys, bgtq_values
         a.v_seq_stride[h] = (uint64_t)values[h]->cap_alloc * values[h]->D;
     }
     a.start = k0->d_lengths;
+    a.ticket = k0->d_lengths + k0->sequences;
     a.count = count;
     a.seq_first = seq_first;
     a.seq_count = seq_count;

@@ -117,6 +117,7 @@ struct KvRopeArgs {
     uint32_t count, seq_first, seq_count, heads, vD, v_swizzle;
     uint32_t capacity;              // rows every store can hold: rows at or past it are refused
     uint32_t *status;               // device status word (kStatusBadLength on a refusal)
+    uint32_t *ticket;               // zero between launches: counts finished CTAs
     float inv_freq[kMaxDim / 2];
 };
 

@@ -329,8 +329,8 @@ __device__ __forceinline__ float src_elem(const void *p, uint64_t i, uint32_t f1
 // src/model/kernels.wgsl:49-54, rounded like separate multiplies and adds), encodes K into
 // the packed store (FP16-rounded first, as every append is) and writes V to the FP16 value
 // store.  Start rows come from the first key store's device lengths, so the launch is
-// stream-ordered against earlier appends without host round trips; lengths are bumped by
-// bump_lengths_kernel afterwards.
+// stream-ordered against earlier appends without host round trips; the last CTA to finish
+// bumps the lengths.
 
 __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_constant__ KvRopeArgs a, uint32_t d,
                                                                   uint32_t total) {
@@ -376,15 +376,26 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
             vrow[de] = __float2half_rn(x);
         }
     }
-}
-
-__global__ void bump_lengths_kernel(const __grid_constant__ KvRopeArgs a) {
-    for (uint32_t s = threadIdx.x; s < a.seq_count; s += blockDim.x)
-        for (uint32_t hd = 0; hd < a.heads; ++hd) {
-            const uint32_t kl = a.head[hd].lengths[a.seq_first + s], vl = a.v_lengths[hd][a.seq_first + s];
-            a.head[hd].lengths[a.seq_first + s] = min(kl + a.count, a.capacity);
-            a.v_lengths[hd][a.seq_first + s] = min(vl + a.count, a.capacity);
-        }
+    // The last CTA to finish moves every store's lengths on.  Each CTA read its start rows
+    // before taking a ticket, so none reads a bumped length; the ticket is left at zero for
+    // the next launch (or graph replay).
+    __shared__ uint32_t s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(a.ticket, 1u) == gridDim.x * gridDim.y - 1 ? 1u : 0u;
+    }
+    __syncthreads();
+    if (s_last) {
+        __threadfence();
+        for (uint32_t s = threadIdx.x; s < a.seq_count; s += blockDim.x)
+            for (uint32_t hh = 0; hh < a.heads; ++hh) {
+                const uint32_t kl = a.head[hh].lengths[a.seq_first + s], vl = a.v_lengths[hh][a.seq_first + s];
+                a.head[hh].lengths[a.seq_first + s] = min(kl + a.count, a.capacity);
+                a.v_lengths[hh][a.seq_first + s] = min(vl + a.count, a.capacity);
+            }
+        if (threadIdx.x == 0) *a.ticket = 0u;
+    }
 }
 
 template <int D>
@@ -432,9 +443,6 @@ cudaError_t launch_kv_rope_append(const KvRopeArgs &a, uint32_t d, cudaStream_t 
     if (!total) return cudaSuccess;
     const uint32_t blocks = (total + kThreads / 32 - 1) / (kThreads / 32);
     kv_rope_append_kernel<<<dim3(blocks, a.heads), kThreads, 0, s>>>(a, d, total);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    bump_lengths_kernel<<<1, 128, 0, s>>>(a);
     return cudaGetLastError();
 }
 
