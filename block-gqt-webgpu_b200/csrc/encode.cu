@@ -224,6 +224,7 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant_
 // Shared-memory scratch of one warp's key in the warp-per-key kernels.
 struct WarpKey {
     float xs[kMaxDim];         // permuted FP16 key as FP32, then normalised
+    float cv[kMaxDim];         // codebook value of each dimension's code
     float nrm[kMaxGroups];
     uint8_t codes[kMaxDim];
     uint32_t orow[kMaxDim / 4 + 1];
@@ -255,19 +256,20 @@ __device__ __forceinline__ void warp_encode(const EncodeHead &h, uint32_t d, War
         const uint32_t g = h.t.group_of[j];
         const float *rj = h.t.rot + (uint64_t)j * d;
         float y = 0.0f;
-#pragma unroll 4
+#pragma unroll 8
         for (uint32_t i = h.group_off[g]; i < h.group_off[g + 1]; ++i) y = fmaf(wk.xs[i], __ldg(rj + i), y);
         float t = (y - h.t.off[j]) * h.t.inv[j];
         t = fminf(fmaxf(t, 0.0f), 255.0f);
         wk.codes[j] = h.t.lut[(uint32_t)h.t.cbidx[j] * 256u + (uint32_t)t];
     }
     __syncwarp();
+    // every lane fetches its dimensions' codebook values first, so the sequential per-group
+    // sums below read shared memory instead of waiting on two dependent loads per dimension
+    for (uint32_t j = lane; j < d; j += 32) wk.cv[j] = h.t.cent[h.t.cb_base[j] + wk.codes[j]];
+    __syncwarp();
     if ((uint32_t)lane < ng) {
         float cl = 0.0f;
-        for (uint32_t j = h.group_off[lane]; j < h.group_off[lane + 1]; ++j) {
-            const float cv = h.t.cent[h.t.cb_base[j] + wk.codes[j]];
-            cl = fmaf(cv, cv, cl);
-        }
+        for (uint32_t j = h.group_off[lane]; j < h.group_off[lane + 1]; ++j) cl = fmaf(wk.cv[j], wk.cv[j], cl);
         wk.srow[lane] = __half_as_ushort(__float2half_rn(wk.nrm[lane] / fmaxf(sqrtf(cl), 1e-10f)));
     } else if ((uint32_t)lane < 8) {
         wk.srow[lane] = 0;
@@ -388,12 +390,14 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
     __syncthreads();
     if (s_last) {
         __threadfence();
-        for (uint32_t s = threadIdx.x; s < a.seq_count; s += blockDim.x)
-            for (uint32_t hh = 0; hh < a.heads; ++hh) {
-                const uint32_t kl = a.head[hh].lengths[a.seq_first + s], vl = a.v_lengths[hh][a.seq_first + s];
-                a.head[hh].lengths[a.seq_first + s] = min(kl + a.count, a.capacity);
-                a.v_lengths[hh][a.seq_first + s] = min(vl + a.count, a.capacity);
-            }
+        // independent (sequence, head) updates, unrolled so their loads overlap
+#pragma unroll 8
+        for (uint32_t idx = threadIdx.x; idx < a.seq_count * a.heads; idx += blockDim.x) {
+            const uint32_t s = a.seq_first + idx / a.heads, hh = idx % a.heads;
+            const uint32_t kl = a.head[hh].lengths[s], vl = a.v_lengths[hh][s];
+            a.head[hh].lengths[s] = min(kl + a.count, a.capacity);
+            a.v_lengths[hh][s] = min(vl + a.count, a.capacity);
+        }
         if (threadIdx.x == 0) *a.ticket = 0u;
     }
 }
