@@ -34,8 +34,10 @@ class GroupedAttention:
         self.device = keys[0].device
 
     def attend(self, q, positions=None, causal: bool = False, rows: int | None = None, seq_first: int = 0,
-               seq_count: int | None = None, out=None, logits=None, probs=None, stream=None):
-        """q: [seq_count, heads, rows, dim] (or [rows, dim] for one head / one sequence)."""
+               seq_count: int | None = None, out=None, logits=None, probs=None, stream=None, wait: bool = True):
+        """q: [seq_count, heads, rows, dim] (or [rows, dim] for one head / one sequence).
+        Host (NumPy) inputs with wait=False: the output download is queued without waiting;
+        `out` (page-locked) holds the result once the stream has been synchronised."""
         rows = self.rows if rows is None else int(rows)
         if isinstance(q, np.ndarray) or not hasattr(q, "data_ptr"):
             qa = np.ascontiguousarray(np.asarray(q, dtype=np.float32))
@@ -52,7 +54,7 @@ class GroupedAttention:
             _lib.call("bgtq_attend", self._handle, qa.ctypes.data, None if pos is None else pos.ctypes.data,
                       int(bool(causal)), rows, seq_first, seq_count, o.ctypes.data,
                       None if logits is None else logits.ctypes.data, None if probs is None else probs.ctypes.data,
-                      1, None)
+                      1 if wait else 2, None)
             return o
         import torch
         seq_count = q.shape[0] if seq_count is None else seq_count

@@ -976,7 +976,7 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
         CK(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, stream), "output download");
         if (logits) CK(cudaMemcpyAsync(logits, dlogits, nl * 4, cudaMemcpyDeviceToHost, stream), "logit download");
         if (probs) CK(cudaMemcpyAsync(probs, dprobs, nl * 4, cudaMemcpyDeviceToHost, stream), "probability download");
-        CK(cudaStreamSynchronize(stream), "attend");
+        if (host != 2) CK(cudaStreamSynchronize(stream), "attend");  // 2: the caller waits on the stream
     }
     return BGTQ_OK;
 }

@@ -269,7 +269,11 @@ void bgtq_attention_destroy(bgtq_attention *a);
  *   logits   optional [seq_count][heads][rows][length] FP32 (inspect(): raw q.k/sqrt(d),
  *            -inf where masked); needs equal lengths across the sequences
  *   probs    optional, same shape as logits (requires logits)
- * host=1: q/positions/out/logits/probs are host memory, copied inside the call.
+ * host=1: q/positions/out/logits/probs are host memory, copied inside the call, which
+ * returns with the outputs in place.  host=2: the same, but the call does not wait: the
+ * downloads are queued on the stream and the outputs are valid once the caller has
+ * synchronised it (page-locked outputs; q may be reused on return).  Calls on one attention
+ * object share its staging buffers, so issue them on one stream.
  * Errors (optimized.ts:29-35): empty or mismatched K/V lengths, rows out of range,
  * positions >= length, non-finite host Q.  Mirrors setQueries()+attend(). */
 bgtq_status bgtq_attend(bgtq_attention *a, const float *q, const uint32_t *positions, int causal, uint32_t rows,

@@ -190,6 +190,14 @@ def test_device_io_matches_host_io(cuda):
     dev = att.attend(torch.from_numpy(q).to(cuda))
     torch.cuda.synchronize()
     np.testing.assert_array_equal(dev.cpu().numpy(), host)
+    # host buffers without the per-call wait: two calls queued, one synchronisation
+    outs = [torch.empty((S, 3, 3, 64), pin_memory=True).numpy() for _ in range(2)]
+    q2 = synthetic.profiled(rng, S * 9, 64).reshape(S, 3, 3, 64)
+    att.attend(q, out=outs[0], wait=False)
+    att.attend(q2, out=outs[1], wait=False)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(outs[0], host)
+    np.testing.assert_array_equal(outs[1], att.attend(q2))
 
 
 def test_config1_full_decode_matches_reference(cuda):
