@@ -162,26 +162,23 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
     const Plan pl =
         attn::make_plan(kk, v_f32, D, e.qp, TT, row_stride, scale_stride, max_cent, (uint32_t)optin - 64u, 2, e.qm);
     if (pl.total > (uint32_t)optin) return cudaErrorInvalidConfiguration;
-    // packed keys whose heads share one group structure: the kernel specialised for it
+    // packed keys: the kernel specialised for the heads' group structures, once available
     const void *jk = nullptr;
     if (kk == KKind::Packed) {
-        const AttnHead &h0 = a.head[0];
-        bool same = h0.ng >= 1 && h0.ng <= (uint32_t)kMaxGroups;
-        for (uint32_t h = 1; h < a.heads && same; ++h) {
-            same = a.head[h].ns == h0.ns && a.head[h].ng == h0.ng;
-            for (uint32_t g = 0; g <= h0.ng && same; ++g) same = a.head[h].group_off[g] == h0.group_off[g];
+        JitKey key{};
+        key.D = D;
+        key.QM = e.qm;
+        key.vf32 = v_f32 ? 1u : 0u;
+        key.heads = a.heads;
+        bool ok = true;
+        for (uint32_t h = 0; h < a.heads; ++h) {
+            const AttnHead &hh = a.head[h];
+            ok &= hh.ng >= 1 && hh.ng <= (uint32_t)kMaxGroups;
+            key.head[h].ns = hh.ns;
+            key.head[h].ng = hh.ng;
+            for (uint32_t g = 0; g <= hh.ng && g <= (uint32_t)kMaxGroups; ++g) key.head[h].group_off[g] = hh.group_off[g];
         }
-        if (same) {
-            JitKey key{};
-            key.D = D;
-            key.QM = e.qm;
-            key.vf32 = v_f32 ? 1u : 0u;
-            key.ns = h0.ns;
-            key.ng = h0.ng;
-            key.scale_stride = scale_stride;
-            for (uint32_t g = 0; g <= h0.ng; ++g) key.group_off[g] = h0.group_off[g];
-            jk = jit_attention_kernel(key, dev);
-        }
+        if (ok) jk = jit_attention_kernel(key, s);
     }
     int per_sm = jk ? jit_occupancy(jk, dev, pl.total) : e.occ(pl);
     if (per_sm < 1) per_sm = 1;

@@ -91,7 +91,7 @@ struct UseMma {
 };
 
 // Group structure of the packed keys.  RuntimeGroups reads it from the head at run time; a
-// kernel specialised for one layout (built by NVRTC, jit.cpp) supplies a policy with
+// kernel specialised for one layout (compiled at run time, jit.cpp) supplies a policy with
 // kStatic = true and the layout as constants (kNG groups, kNS nibble dims, group offsets
 // go(g) as a constexpr function, which folds where an array might be placed in memory), so
 // every group and run loop unrolls.

@@ -209,13 +209,18 @@ cudaError_t launch_probs(const float *logits, const float *lse, float *probs, ui
 size_t attention_smem_bytes(KKind kk, int v_f32, uint32_t d, uint32_t rows_bound, uint32_t row_stride,
                             uint32_t scale_stride, uint32_t max_cent);
 uint32_t attention_tile_tokens(uint32_t d);
-// Layout-specialised decode attention (jit.cpp): the kernel for one group structure of
-// packed keys, compiled once per device by NVRTC; null when disabled or not compilable.
-struct JitKey {
-    uint32_t D, QM, vf32, ns, ng, scale_stride;
+// Layout-specialised decode attention (jit.cpp): the kernel for the heads' group structures
+// of packed keys, compiled at run time; null while it is not (yet) available, in which case
+// the generic kernel runs.
+struct JitLayout {
+    uint32_t ns, ng;
     uint32_t group_off[kMaxGroups + 1];
 };
-const void *jit_attention_kernel(const JitKey &key, int device);
+struct JitKey {
+    uint32_t D, QM, vf32, heads;
+    JitLayout head[kMaxHeads];
+};
+const void *jit_attention_kernel(const JitKey &key, cudaStream_t stream);
 void jit_set_enabled(int on);
 // The calling thread's launches keep the generic kernel while on != 0 (an entry point that
 // promises no allocation at attention time: loading a specialised kernel allocates).

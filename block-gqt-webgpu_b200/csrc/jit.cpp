@@ -1,18 +1,22 @@
 // Layout-specialised decode attention: the kernel of attention_impl.cuh compiled at run time
-// by NVRTC for one group structure of packed keys (nibble dims, group offsets).  With the
-// layout as compile-time constants every group and run loop of the dequant + QK phase
+// for the group structures of a launch's packed key heads (nibble dims, group offsets).  With
+// the layout as compile-time constants every group and run loop of the dequant + QK phase
 // unrolls, which removes the loop and per-group bookkeeping of the generic kernel; the
-// arithmetic and its order are the same, so outputs are identical.
+// arithmetic and its order are the same, so outputs are identical.  Heads with different
+// structures get one inlined body each, chosen per CTA by its head index (blockIdx.y).
 //
 // The toolkit's nvcc (run as a child process, device code only, the build's flags) compiles
 // the package's own kernel source (csrc/, found next to this library) to an sm_100a cubin,
-// loaded with cudaLibraryLoadData; about two seconds per layout.  Without nvcc, NVRTC (loaded
-// with dlopen) is the fallback: its kernels are correct but its headers declare some
-// intrinsics differently, so they are a few percent slower than nvcc's.
-// One kernel per layout key, built on the first launch that needs it and kept for the life
-// of the process (at most kMaxEntries).  Anything that fails (no NVRTC, no sources, a compile
-// or load error) leaves the generic kernel in use.  BGTQ_LAYOUT_JIT=0 in the environment or
-// bgtq_set_layout_jit(0) turns it off.
+// loaded with cudaLibraryLoadData; about two seconds per distinct structure.  Without nvcc,
+// NVRTC (loaded with dlopen) is the fallback: its kernels are correct but its headers declare
+// some intrinsics differently, so they are a few percent slower than nvcc's.
+// One kernel per key (dims, query rows, value type, the heads' structures), kept for the life
+// of the process (at most kMaxEntries).  A key whose heads share one structure compiles on the
+// launch that first needs it; a key with several compiles on a background thread (host work
+// only, no CUDA calls) while the generic kernel serves the launches.  The cubin is loaded by
+// the first launch after that whose stream is not capturing a graph.  Anything that fails
+// (no compiler, no sources, a compile or load error) leaves the generic kernel in use.
+// BGTQ_LAYOUT_JIT=0 in the environment or bgtq_set_layout_jit(0) turns it off.
 #include <dlfcn.h>
 #include <spawn.h>
 #include <sys/wait.h>
@@ -29,6 +33,7 @@
 #include <mutex>
 #include <string>
 #include <sys/stat.h>
+#include <thread>
 #include <vector>
 
 #include "bgtq_internal.h"
@@ -105,40 +110,80 @@ std::string source_dir() {
 }
 
 struct Entry {
-    bool failed = false;
+    enum State { Compiling, Compiled, Ready, Failed } state = Compiling;
+    std::vector<char> cubin;  // Compiled: waiting for a launch outside a capture to load it
     cudaLibrary_t lib = nullptr;
     cudaKernel_t kernel = nullptr;
 };
 
-std::mutex g_mu;
-std::map<std::string, Entry> g_cache;
+// Never destroyed: a compile thread may still be running when the process exits.
+std::mutex &g_mu = *new std::mutex;
+std::map<std::string, Entry> &g_cache = *new std::map<std::string, Entry>;
 std::atomic<int> g_enabled{-1};  // -1: not read from the environment yet
 std::atomic<uint32_t> g_built{0}, g_failed{0};
 
+bool same_layout(const JitLayout &x, const JitLayout &y) {
+    if (x.ns != y.ns || x.ng != y.ng) return false;
+    for (uint32_t g = 0; g <= x.ng; ++g)
+        if (x.group_off[g] != y.group_off[g]) return false;
+    return true;
+}
+
+// The distinct structures of the key's heads (in first-use order) and each head's index into them.
+uint32_t layout_classes(const JitKey &k, uint32_t (&cls)[kMaxHeads], uint32_t (&first)[kMaxHeads]) {
+    uint32_t n = 0;
+    for (uint32_t h = 0; h < k.heads; ++h) {
+        uint32_t c = 0;
+        while (c < n && !same_layout(k.head[first[c]], k.head[h])) ++c;
+        if (c == n) first[n++] = h;
+        cls[h] = c;
+    }
+    return n;
+}
+
 std::string key_string(const JitKey &k) {
     std::string s = std::to_string(k.D) + "/" + std::to_string(k.QM) + "/" + std::to_string(k.vf32) + "/" +
-                    std::to_string(k.ns) + "/" + std::to_string(k.ng) + ":";
-    for (uint32_t g = 0; g <= k.ng && g <= (uint32_t)kMaxGroups; ++g) s += std::to_string(k.group_off[g]) + ",";
+                    std::to_string(k.heads);
+    for (uint32_t h = 0; h < k.heads; ++h) {
+        const JitLayout &l = k.head[h];
+        s += ";" + std::to_string(l.ns) + "/" + std::to_string(l.ng) + ":";
+        for (uint32_t g = 0; g <= l.ng; ++g) s += std::to_string(l.group_off[g]) + ",";
+    }
     return s;
 }
 
 std::string kernel_source(const JitKey &k) {
-    // go(g) as nested conditionals over g = 0 .. ng
-    std::string go = "0u";
-    for (int g = (int)k.ng; g >= 0; --g)
-        go = "g == " + std::to_string(g) + "u ? " + std::to_string(k.group_off[g]) + "u : (" + go + ")";
+    uint32_t cls[kMaxHeads] = {}, first[kMaxHeads] = {};
+    const uint32_t n = layout_classes(k, cls, first);
     const std::string D = std::to_string(k.D), QM = std::to_string(k.QM), VF = k.vf32 ? "true" : "false";
-    return "#include \"attention_impl.cuh\"\n"
-           "struct JitGroups {\n"
-           "    static constexpr bool kStatic = true;\n"
-           "    static constexpr uint32_t kNG = " + std::to_string(k.ng) + "u, kNS = " + std::to_string(k.ns) + "u;\n"
-           "    static __host__ __device__ constexpr uint32_t go(uint32_t g) { return " + go + "; }\n"
-           "};\n"
-           "extern \"C\" __global__ void __launch_bounds__(bgtq::attn::kThreads, bgtq::attn::MinBlocks<" + D + ", " +
+    std::string src = "#include \"attention_impl.cuh\"\n";
+    for (uint32_t c = 0; c < n; ++c) {
+        const JitLayout &l = k.head[first[c]];
+        // go(g) as nested conditionals over g = 0 .. ng
+        std::string go = "0u";
+        for (int g = (int)l.ng; g >= 0; --g)
+            go = "g == " + std::to_string(g) + "u ? " + std::to_string(l.group_off[g]) + "u : (" + go + ")";
+        src += "struct JitGroups" + std::to_string(c) + " {\n"
+               "    static constexpr bool kStatic = true;\n"
+               "    static constexpr uint32_t kNG = " + std::to_string(l.ng) + "u, kNS = " + std::to_string(l.ns) + "u;\n"
+               "    static __host__ __device__ constexpr uint32_t go(uint32_t g) { return " + go + "; }\n"
+               "};\n";
+    }
+    src += "extern \"C\" __global__ void __launch_bounds__(bgtq::attn::kThreads, bgtq::attn::MinBlocks<" + D + ", " +
            QM + ", bgtq::KKind::Packed>::value)\n"
-           "bgtq_attn_jit(const __grid_constant__ bgtq::AttnArgs a, const bgtq::attn::Plan pl, uint32_t d) {\n"
-           "    bgtq::attn::attn_body<" + D + ", " + QM + ", bgtq::KKind::Packed, " + VF + ", JitGroups>(a, pl, d);\n"
-           "}\n";
+           "bgtq_attn_jit(const __grid_constant__ bgtq::AttnArgs a, const bgtq::attn::Plan pl, uint32_t d) {\n";
+    if (n > 1) src += "    const uint32_t hd = blockIdx.y;\n";
+    for (uint32_t c = 0; c < n; ++c) {
+        std::string cond;
+        for (uint32_t h = 0; h < k.heads; ++h)
+            if (cls[h] == c) cond += std::string(cond.empty() ? "" : " || ") + "hd == " + std::to_string(h) + "u";
+        const std::string body = "bgtq::attn::attn_body<" + D + ", " + QM + ", bgtq::KKind::Packed, " + VF +
+                                 ", JitGroups" + std::to_string(c) + ">(a, pl, d);\n";
+        if (n == 1) src += "    " + body;
+        else if (c + 1 < n) src += std::string(c ? "    else if (" : "    if (") + cond + ") " + body;
+        else src += "    else " + body;
+    }
+    return src + "}\n";
 }
 
 // nvcc -cubin of `src` in a private temporary directory; false if nvcc is absent or fails.
@@ -191,9 +236,10 @@ bool nvcc_cubin(const std::string &src, const std::string &src_dir, std::vector<
     return ok;
 }
 
-bool load(const std::vector<char> &cubin, Entry &e) {
-    if (cudaLibraryLoadData(&e.lib, cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0) != cudaSuccess) {
+bool load(Entry &e) {
+    if (cudaLibraryLoadData(&e.lib, e.cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0) != cudaSuccess) {
         cudaGetLastError();
+        e.lib = nullptr;
         return false;
     }
     if (cudaLibraryGetKernel(&e.kernel, e.lib, "bgtq_attn_jit") != cudaSuccess) {
@@ -205,20 +251,21 @@ bool load(const std::vector<char> &cubin, Entry &e) {
     return true;
 }
 
-bool build(const JitKey &k, Entry &e) {
-    const std::string src_dir = source_dir(), inc = cuda_home() + "/include";
-    if (src_dir.empty()) return false;
-    const std::string src = kernel_source(k);
+// The key's kernel as an sm_100a cubin (host work only: nvcc, else NVRTC); empty on failure.
+std::vector<char> compile(const JitKey &k) {
     std::vector<char> cubin;
-    if (nvcc_cubin(src, src_dir, cubin) && load(cubin, e)) return true;
+    const std::string src_dir = source_dir(), inc = cuda_home() + "/include";
+    if (src_dir.empty()) return cubin;
+    const std::string src = kernel_source(k);
+    if (nvcc_cubin(src, src_dir, cubin)) return cubin;
+    cubin.clear();
     const Nvrtc &n = nvrtc();
-    if (!n.ok || !exists(inc + "/cuda_fp16.h")) return false;
+    if (!n.ok || !exists(inc + "/cuda_fp16.h")) return cubin;
     void *prog = nullptr;
-    if (n.create(&prog, src.c_str(), "bgtq_attn_jit.cu", 0, nullptr, nullptr) != 0) return false;
+    if (n.create(&prog, src.c_str(), "bgtq_attn_jit.cu", 0, nullptr, nullptr) != 0) return cubin;
     const std::string i1 = "-I" + src_dir, i2 = "-I" + inc;
     const char *opts[] = {"--gpu-architecture=sm_100a", "-std=c++17", i1.c_str(), i2.c_str()};
     const int rc = n.compile(prog, 4, opts);
-    cubin.clear();
     if (rc == 0) {
         size_t sz = 0;
         if (n.cubin_size(prog, &sz) == 0 && sz) {
@@ -233,7 +280,14 @@ bool build(const JitKey &k, Entry &e) {
         std::fprintf(stderr, "bgtq layout JIT: compile failed:\n%s\n", log.c_str());
     }
     n.destroy(&prog);
-    return !cubin.empty() && load(cubin, e);
+    return cubin;
+}
+
+// A compiled entry's cubin moved into a library, or marked failed (caller holds g_mu).
+void finish(Entry &e, std::vector<char> &&cubin) {
+    e.cubin = std::move(cubin);
+    e.state = e.cubin.empty() ? Entry::Failed : Entry::Compiled;
+    if (e.state == Entry::Failed) g_failed.fetch_add(1);
 }
 
 bool enabled() {
@@ -255,24 +309,47 @@ thread_local int t_suppressed = 0;
 }
 void jit_suppress_on_thread(int on) { t_suppressed = on; }
 
-const void *jit_attention_kernel(const JitKey &key, int device) {
-    (void)device;  // a cudaLibrary_t serves every device
-    if (t_suppressed || !enabled() || key.ng < 1 || key.ng > (uint32_t)kMaxGroups) return nullptr;
+const void *jit_attention_kernel(const JitKey &key, cudaStream_t stream) {
+    if (t_suppressed || !enabled() || key.heads < 1 || key.heads > (uint32_t)kMaxHeads) return nullptr;
+    for (uint32_t h = 0; h < key.heads; ++h)
+        if (key.head[h].ng < 1 || key.head[h].ng > (uint32_t)kMaxGroups) return nullptr;
     const std::string ks = key_string(key);
     std::lock_guard<std::mutex> lock(g_mu);
     auto it = g_cache.find(ks);
     if (it == g_cache.end()) {
         if (g_cache.size() >= kMaxEntries) return nullptr;
-        Entry e;
-        if (build(key, e)) {
+        it = g_cache.emplace(ks, Entry{}).first;
+        uint32_t cls[kMaxHeads], first[kMaxHeads];
+        if (layout_classes(key, cls, first) == 1) {
+            finish(it->second, compile(key));
+        } else {
+            std::thread([key, ks] {
+                std::vector<char> cubin = compile(key);
+                std::lock_guard<std::mutex> l(g_mu);
+                finish(g_cache[ks], std::move(cubin));
+            }).detach();
+            return nullptr;
+        }
+    }
+    Entry &e = it->second;
+    if (e.state == Entry::Compiled) {
+        // loading is not a stream operation: keep it out of graph captures
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        if (cs != cudaStreamCaptureStatusNone) return nullptr;
+        if (load(e)) {
+            e.state = Entry::Ready;
             g_built.fetch_add(1);
         } else {
-            e.failed = true;
+            e.state = Entry::Failed;
             g_failed.fetch_add(1);
         }
-        it = g_cache.emplace(ks, e).first;
+        std::vector<char>().swap(e.cubin);
     }
-    return it->second.failed ? nullptr : reinterpret_cast<const void *>(it->second.kernel);
+    return e.state == Entry::Ready ? reinterpret_cast<const void *>(e.kernel) : nullptr;
 }
 
 }  // namespace bgtq

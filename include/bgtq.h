@@ -123,12 +123,15 @@ bgtq_status bgtq_haar_rotation(uint32_t n, uint64_t seed, float *out);
  * (block_gtq_pipeline.py:24-78). */
 bgtq_status bgtq_optimal_centroids(uint32_t bits, uint32_t n, float *out);
 
-/* Layout-specialised decode attention: launches over packed keys whose heads share one group
- * structure use a kernel compiled for that structure at run time (NVRTC, once per layout and
- * process; identical results, fewer instructions).  on = 0 keeps the generic kernel (also
- * BGTQ_LAYOUT_JIT=0 in the environment).  No counterpart in the reference. */
+/* Layout-specialised decode attention: launches over packed keys use a kernel compiled at run
+ * time for their heads' group structures (the toolkit's nvcc, else NVRTC; once per key and
+ * process; identical results, fewer instructions).  Heads sharing one structure compile on the
+ * first launch; heads with several compile on a background thread while the generic kernel
+ * runs, and a later launch outside a graph capture loads the result.  on = 0 keeps the
+ * generic kernel (also BGTQ_LAYOUT_JIT=0 in the environment).  No counterpart in the
+ * reference. */
 bgtq_status bgtq_set_layout_jit(int on);
-/* Specialised kernels built / layouts that failed to build (and use the generic kernel). */
+/* Specialised kernels loaded / keys that failed to build (and use the generic kernel). */
 bgtq_status bgtq_layout_jit_stats(uint32_t *built, uint32_t *failed);
 
 /* Fixture files of the reference's tests (tests/oracles/fixture.py:13-49): a JSON manifest

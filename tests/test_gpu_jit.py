@@ -1,13 +1,17 @@
 """Layout-specialised decode attention (bgtq_set_layout_jit): the kernel compiled at run
 time for one group structure gives the generic kernel's outputs bit for bit - rows 1-4 and
 7, FP16 and FP32 values, head dims 64 and 128, one and several splits, causal positions,
-logit / log-sum-exp capture - and is what runs by default when the heads share a layout."""
+logit / log-sum-exp capture - and is what runs by default when the heads share a layout.
+Heads with different structures (the SmolLM2 calibration) get a kernel compiled in the
+background: every launch before and after it is ready gives the generic outputs."""
+import time
+
 import numpy as np
 import pytest
 
 import bgtq
 from bgtq import GroupedAttention, PackedKeys, Values, device_status
-from conftest import load_config
+from conftest import GOLDEN, load_config
 
 pytestmark = pytest.mark.gpu
 
@@ -70,4 +74,46 @@ def test_specialised_logits_and_lse(cuda):
     bgtq.set_layout_jit(True)
     for a, b in zip(*res):
         np.testing.assert_array_equal(a, b)
+    assert device_status(0) == 0
+
+
+@pytest.mark.parametrize("rows", [2, 7])
+def test_mixed_layouts_compile_in_background(cuda, rows):
+    import torch
+    z = np.load(GOLDEN / "smollm2_heads.npz")
+    S, T, H, d = 2, 900, 6, 64
+    gen = torch.Generator(device=cuda).manual_seed(40 + rows)
+    keys = [PackedKeys((z[f"h{h}_config"], z[f"h{h}_table"]), T, sequences=S) for h in range(H)]
+    vals = [Values(d, T, "f16", sequences=S) for _ in range(H)]
+    for h in range(H):
+        keys[h].append((torch.randn((S, T, d), device=cuda, generator=gen) * 0.4).half())
+        vals[h].append(torch.randn((S, T, d), device=cuda, generator=gen).half())
+    att = GroupedAttention(keys, vals, rows)
+    q = torch.randn((S, H, rows, d), device=cuda, generator=gen)
+    pos = torch.from_numpy(np.random.default_rng(rows).integers(0, T, (S, rows)).astype(np.uint32)).to(cuda)
+
+    def run():
+        o1 = att.attend(q).clone()
+        o2 = att.attend(q, positions=pos, causal=True).clone()
+        torch.cuda.synchronize()
+        return o1.cpu().numpy(), o2.cpu().numpy()
+
+    bgtq.set_layout_jit(False)
+    ref = run()
+    bgtq.set_layout_jit(True)
+    built0, failed0 = bgtq.layout_jit_stats()
+    deadline = time.monotonic() + 240
+    while True:
+        got = run()                      # generic until the specialised kernel is loaded
+        np.testing.assert_array_equal(got[0], ref[0])
+        np.testing.assert_array_equal(got[1], ref[1])
+        built, failed = bgtq.layout_jit_stats()
+        assert failed == failed0
+        if built > built0:
+            break
+        assert time.monotonic() < deadline, "background compile did not finish"
+        time.sleep(0.25)
+    got = run()                          # the specialised kernel
+    np.testing.assert_array_equal(got[0], ref[0])
+    np.testing.assert_array_equal(got[1], ref[1])
     assert device_status(0) == 0
