@@ -65,7 +65,9 @@ def build(jobs: int | None = None, force: bool = False, verbose: bool = False) -
     srcs = sources()
     with cf.ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as ex:
         objs = list(ex.map(lambda s: compile_one(s, force, verbose), srcs))
-    stamp = hashlib.sha256("".join(str(o) for o in objs).encode()).hexdigest()[:16]
+    for old in set(OUT_DIR.glob("*.o")) - set(objs):   # objects of earlier source versions
+        old.unlink()
+    stamp =hashlib.sha256("".join(str(o) for o in objs).encode()).hexdigest()[:16]
     stamp_file = OUT_DIR / "lib.stamp"
     if LIB.exists() and not force and stamp_file.exists() and stamp_file.read_text() == stamp:
         return LIB

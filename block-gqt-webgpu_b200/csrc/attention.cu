@@ -164,6 +164,7 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
     if (pl.total > (uint32_t)optin) return cudaErrorInvalidConfiguration;
     // packed keys: the kernel specialised for the heads' group structures, once available
     const void *jk = nullptr;
+    bool head_major = false;
     if (kk == KKind::Packed) {
         JitKey key{};
         key.D = D;
@@ -178,7 +179,7 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
             key.head[h].ng = hh.ng;
             for (uint32_t g = 0; g <= hh.ng && g <= (uint32_t)kMaxGroups; ++g) key.head[h].group_off[g] = hh.group_off[g];
         }
-        if (ok) jk = jit_attention_kernel(key, s);
+        if (ok) jk = jit_attention_kernel(key, s, &head_major);
     }
     int per_sm = jk ? jit_occupancy(jk, dev, pl.total) : e.occ(pl);
     if (per_sm < 1) per_sm = 1;
@@ -196,6 +197,7 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
         uint32_t dd = d;
         Plan plc = pl;
         void *args[] = {&a, &plc, &dd};
+        if (head_major) grid = dim3(splits, a.seq_count, a.heads);
         return cudaLaunchKernel(jk, grid, dim3(attn::kThreads), args, pl.total, s);
     }
     return e.run(a, pl, d, grid, s);

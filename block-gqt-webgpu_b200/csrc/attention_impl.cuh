@@ -477,7 +477,8 @@ struct MinBlocks {
 };
 
 template <int D, int QM, KKind KK, bool VF32, class LP>
-__device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uint32_t d) {
+__device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uint32_t d, uint32_t split, uint32_t hd,
+                                          uint32_t s) {
     constexpr int TPL = Geo<D>::TPL, TT = Geo<D>::TT, QP = QPad<QM>::QP;
     constexpr bool MMA = UseMma<D, VF32>::value;
     constexpr int VSZ = VF32 ? 4 : 2, VEC = 16 / VSZ, LPT = D / VEC, TPS = 32 / LPT;
@@ -490,7 +491,6 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     // 4-7): half the MMAs and accumulators of the P-as-A form, which up to 8 rows use.
     constexpr bool TMMA = MMA && QM <= 4;
 
-    const uint32_t split = blockIdx.x, hd = blockIdx.y, s = blockIdx.z;
     const AttnHead &h = a.head[hd];
     const uint32_t seq = a.seq_first + s;
     const uint32_t len = a.lengths[seq];
@@ -960,7 +960,7 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
 template <int D, int QM, KKind KK, bool VF32>
 __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value)
     attn_kernel(const __grid_constant__ AttnArgs a, const Plan pl, uint32_t d) {
-    attn_body<D, QM, KK, VF32, RuntimeGroups>(a, pl, d);
+    attn_body<D, QM, KK, VF32, RuntimeGroups>(a, pl, d, blockIdx.x, blockIdx.y, blockIdx.z);
 }
 
 // Element j of query row q after split-half RoPE at position pos (src/model/kernels.wgsl:

@@ -211,7 +211,8 @@ size_t attention_smem_bytes(KKind kk, int v_f32, uint32_t d, uint32_t rows_bound
 uint32_t attention_tile_tokens(uint32_t d);
 // Layout-specialised decode attention (jit.cpp): the kernel for the heads' group structures
 // of packed keys, compiled at run time; null while it is not (yet) available, in which case
-// the generic kernel runs.
+// the generic kernel runs.  *head_major: the kernel takes the grid (splits, sequences, heads)
+// instead of (splits, heads, sequences).
 struct JitLayout {
     uint32_t ns, ng;
     uint32_t group_off[kMaxGroups + 1];
@@ -220,7 +221,7 @@ struct JitKey {
     uint32_t D, QM, vf32, heads;
     JitLayout head[kMaxHeads];
 };
-const void *jit_attention_kernel(const JitKey &key, cudaStream_t stream);
+const void *jit_attention_kernel(const JitKey &key, cudaStream_t stream, bool *head_major);
 void jit_set_enabled(int on);
 // The calling thread's launches keep the generic kernel while on != 0 (an entry point that
 // promises no allocation at attention time: loading a specialised kernel allocates).

@@ -3,7 +3,10 @@
 // the layout as compile-time constants every group and run loop of the dequant + QK phase
 // unrolls, which removes the loop and per-group bookkeeping of the generic kernel; the
 // arithmetic and its order are the same, so outputs are identical.  Heads with different
-// structures get one inlined body each, chosen per CTA by its head index (blockIdx.y).
+// structures get one inlined body each, chosen per CTA by its head index; their grid is
+// (splits, sequences, heads), so the CTAs resident on an SM at one time mostly run one body
+// (the usual (splits, heads, sequences) order ran every body on every SM at once and
+// thrashed the instruction cache: twice the time).
 //
 // The toolkit's nvcc (run as a child process, device code only, the build's flags) compiles
 // the package's own kernel source (csrc/, found next to this library) to an sm_100a cubin,
@@ -43,7 +46,7 @@ extern char **environ;
 namespace bgtq {
 namespace {
 
-constexpr size_t kMaxEntries = 16;
+constexpr size_t kMaxEntries = 64;  // a cubin is a few hundred KB
 
 typedef int (*nvrtcCreateProgram_t)(void **, const char *, const char *, int, const char *const *,
                                     const char *const *);
@@ -141,6 +144,12 @@ uint32_t layout_classes(const JitKey &k, uint32_t (&cls)[kMaxHeads], uint32_t (&
     return n;
 }
 
+// Heads with more than one structure: the kernel's grid is (splits, sequences, heads).
+bool multi_layout(const JitKey &k) {
+    uint32_t cls[kMaxHeads], first[kMaxHeads];
+    return layout_classes(k, cls, first) > 1;
+}
+
 std::string key_string(const JitKey &k) {
     std::string s = std::to_string(k.D) + "/" + std::to_string(k.QM) + "/" + std::to_string(k.vf32) + "/" +
                     std::to_string(k.heads);
@@ -172,13 +181,16 @@ std::string kernel_source(const JitKey &k) {
     src += "extern \"C\" __global__ void __launch_bounds__(bgtq::attn::kThreads, bgtq::attn::MinBlocks<" + D + ", " +
            QM + ", bgtq::KKind::Packed>::value)\n"
            "bgtq_attn_jit(const __grid_constant__ bgtq::AttnArgs a, const bgtq::attn::Plan pl, uint32_t d) {\n";
-    if (n > 1) src += "    const uint32_t hd = blockIdx.y;\n";
+    // several structures: the grid is (splits, sequences, heads), so that the CTAs resident
+    // on an SM at one time mostly run one head's body (instruction cache)
+    if (n > 1) src += "    const uint32_t hd = blockIdx.z;\n";
+    const std::string blk = n > 1 ? "blockIdx.x, hd, blockIdx.y" : "blockIdx.x, blockIdx.y, blockIdx.z";
     for (uint32_t c = 0; c < n; ++c) {
         std::string cond;
         for (uint32_t h = 0; h < k.heads; ++h)
             if (cls[h] == c) cond += std::string(cond.empty() ? "" : " || ") + "hd == " + std::to_string(h) + "u";
         const std::string body = "bgtq::attn::attn_body<" + D + ", " + QM + ", bgtq::KKind::Packed, " + VF +
-                                 ", JitGroups" + std::to_string(c) + ">(a, pl, d);\n";
+                                 ", JitGroups" + std::to_string(c) + ">(a, pl, d, " + blk + ");\n";
         if (n == 1) src += "    " + body;
         else if (c + 1 < n) src += std::string(c ? "    else if (" : "    if (") + cond + ") " + body;
         else src += "    else " + body;
@@ -309,7 +321,8 @@ thread_local int t_suppressed = 0;
 }
 void jit_suppress_on_thread(int on) { t_suppressed = on; }
 
-const void *jit_attention_kernel(const JitKey &key, cudaStream_t stream) {
+const void *jit_attention_kernel(const JitKey &key, cudaStream_t stream, bool *head_major) {
+    *head_major = false;
     if (t_suppressed || !enabled() || key.heads < 1 || key.heads > (uint32_t)kMaxHeads) return nullptr;
     for (uint32_t h = 0; h < key.heads; ++h)
         if (key.head[h].ng < 1 || key.head[h].ng > (uint32_t)kMaxGroups) return nullptr;
@@ -319,8 +332,7 @@ const void *jit_attention_kernel(const JitKey &key, cudaStream_t stream) {
     if (it == g_cache.end()) {
         if (g_cache.size() >= kMaxEntries) return nullptr;
         it = g_cache.emplace(ks, Entry{}).first;
-        uint32_t cls[kMaxHeads], first[kMaxHeads];
-        if (layout_classes(key, cls, first) == 1) {
+        if (!multi_layout(key)) {
             finish(it->second, compile(key));
         } else {
             std::thread([key, ks] {
@@ -349,7 +361,9 @@ const void *jit_attention_kernel(const JitKey &key, cudaStream_t stream) {
         }
         std::vector<char>().swap(e.cubin);
     }
-    return e.state == Entry::Ready ? reinterpret_cast<const void *>(e.kernel) : nullptr;
+    if (e.state != Entry::Ready) return nullptr;
+    *head_major = multi_layout(key);
+    return reinterpret_cast<const void *>(e.kernel);
 }
 
 }  // namespace bgtq
