@@ -334,7 +334,9 @@ def run_ours(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s", "traffic": traffic,
-                         "kernel": "query rotation + attn_kernel<64,3,packed,f16> per layer (CUDA events)",
+                         "kernel": "query rotation + " + ("bgtq_attn_jit" if bgtq.layout_jit_stats()[0]
+                                                          else "attn_kernel<64,3,packed,f16>")
+                                   + " per layer (CUDA events)",
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "bytes_per_token_head": bpt, "mean_launch_ms": mean_launch_s * 1e3},
             "k_encode": {"value": enc_rate / 1e6, "unit": "Mkeys/s", "keys_per_launch": enc_keys,
