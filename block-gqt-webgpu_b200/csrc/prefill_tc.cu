@@ -177,7 +177,6 @@ __global__ void __launch_bounds__(NTH, 2) prefill_tc_kernel(const __grid_constan
     const uint32_t bar_s = bars + 32u, bar_o = bars + 40u;
     volatile uint32_t *slot = reinterpret_cast<volatile uint32_t *>(sm + pl.slot);
     float *red = reinterpret_cast<float *>(sm + pl.red);  // [2][M]
-    __shared__ uint32_t s_err;
 
     // ---- prologue: TMEM, codebooks, decode words, query tile, barriers ----
     if (warp == 0) {
@@ -218,7 +217,6 @@ __global__ void __launch_bounds__(NTH, 2) prefill_tc_kernel(const __grid_constan
         }
     }
     if (tid < 6) mbar_init(bars + 8u * tid, 1u);
-    if (tid == 0) s_err = 0;
     fence_barrier_init();
     fence_proxy_async();
     tc_before_sync();
@@ -265,66 +263,76 @@ __global__ void __launch_bounds__(NTH, 2) prefill_tc_kernel(const __grid_constan
     for (int i = 0; i < 32; ++i) o[i] = 0.0f;
     float m_run = -INFINITY, l_run = 0.0f;
     uint32_t phase = 0;  // bit b: parity of barrier b (K0, K1, V0, V1, S, O)
+    bool err = false;    // this thread saw a wait time out; CTA-wide decisions use __syncthreads_or
 
-    for (uint32_t j = 0; j < ntiles; ++j) {
-        const uint32_t st = j & 1u;
-        // ---- 1-2: dequantise packed tile j ----
-        if (!mbar_wait_bounded(bars + 8u * st, (phase >> st) & 1u)) s_err = 1u;
+    // packed tile t (stage t & 1) -> code-domain FP16 high / low halves in the C tile
+    auto dequant = [&](uint32_t t) {
+        const uint32_t st = t & 1u;
+        if (!mbar_wait_bounded(bars + 8u * st, (phase >> st) & 1u)) err = true;
         phase ^= 1u << st;
         pending &= ~(1u << st);
         const unsigned char *kt = sm + pl.kst + st * pl.kstage;
-        {
-            // thread = key (lanes: consecutive keys, one codebook per instruction) x pairs
-            // 8r .. 8r+7 (chunks 2r, 2r+1); the pair's kind is uniform over the warp
-            const uint32_t key = tid & (BN - 1), r = tid >> 6;
-            const unsigned char *krow = kt + key * row_stride;
-            const uint16_t *sc = reinterpret_cast<const uint16_t *>(kt + soff + key * srow);
-            float v0[8], v1[8];
+        // thread = key (lanes: consecutive keys, one codebook per instruction) x pairs
+        // 8r .. 8r+7 (chunks 2r, 2r+1); the pair's kind is uniform over the warp
+        const uint32_t key = tid & (BN - 1), r = tid >> 6;
+        const unsigned char *krow = kt + key * row_stride;
+        const uint16_t *sc = reinterpret_cast<const uint16_t *>(kt + soff + key * srow);
+        float v0[8], v1[8];
 #pragma unroll
-            for (uint32_t q = 0; q < 8; ++q) {
-                const uint2 pw = pair_s[8 * r + q];
-                const uint32_t boff = pw.x & 0xffu;
-                uint32_t c0, c1;
-                if (pw.x & kPairByte) {
-                    c0 = krow[boff];
-                    c1 = krow[boff + 1];
-                } else {
-                    const uint32_t b = krow[boff];
-                    c0 = b & 15u;
-                    c1 = b >> 4;
-                }
-                const float scale = __half2float(__ushort_as_half(sc[pw.x >> 16]));
-                float &x0 = q < 4 ? v0[2 * q] : v1[2 * q - 8], &x1 = q < 4 ? v0[2 * q + 1] : v1[2 * q - 7];
-                x0 = cent_s[(pw.y & 0xffffu) + c0] * scale;
-                x1 = cent_s[(pw.y >> 16) + c1] * scale;
+        for (uint32_t q = 0; q < 8; ++q) {
+            const uint2 pw = pair_s[8 * r + q];
+            const uint32_t boff = pw.x & 0xffu;
+            uint32_t c0, c1;
+            if (pw.x & kPairByte) {
+                c0 = krow[boff];
+                c1 = krow[boff + 1];
+            } else {
+                const uint32_t b = krow[boff];
+                c0 = b & 15u;
+                c1 = b >> 4;
             }
-            put8(sm + pl.chi, sm + pl.clo, key, 2 * r, v0);
-            put8(sm + pl.chi, sm + pl.clo, key, 2 * r + 1, v1);
+            const float scale = __half2float(__ushort_as_half(sc[pw.x >> 16]));
+            float &x0 = q < 4 ? v0[2 * q] : v1[2 * q - 8], &x1 = q < 4 ? v0[2 * q + 1] : v1[2 * q - 7];
+            x0 = cent_s[(pw.y & 0xffffu) + c0] * scale;
+            x1 = cent_s[(pw.y >> 16) + c1] * scale;
         }
+        put8(sm + pl.chi, sm + pl.clo, key, 2 * r, v0);
+        put8(sm + pl.chi, sm + pl.clo, key, 2 * r + 1, v1);
+    };
+    // S = Q C^T of the tile in the C tile (issued by thread 0; the caller tracks the commit)
+    auto issue_s = [&]() {
+#pragma unroll
+        for (uint32_t ks = 0; ks < 4; ++ks) {
+            const uint64_t ko = (ks * 32u) >> 4;  // 16 dims = 32 bytes along the swizzled row
+            umma(tmem + kColX, dq_lo + ko, dc_hi + ko, ID_QK, ks > 0 ? 1u : 0u);
+            umma(tmem + kColX, dq_hi + ko, dc_lo + ko, ID_QK, 1u);
+            umma(tmem + (ks < 2 ? kColHH0 : kColHH1), dq_hi + ko, dc_hi + ko, ID_QK, (ks & 1u) ? 1u : 0u);
+        }
+        umma_commit(bar_s);
+    };
+
+    // Software pipeline: tile j + 1 is dequantised while the tensor cores run tile j's P.V,
+    // and its S is issued before tile j's output fold, so each tile takes three CTA barriers.
+    if (ntiles > 0) {
+        dequant(0);
         fence_proxy_async();
         tc_before_sync();
         __syncthreads();
         tc_after_sync();
-        if (s_err) break;
-        // ---- 3: S on the tensor cores ----
         if (tid == 0) {
-            if (j + 2 < ntiles) issue_k(j + 2, st);
-#pragma unroll
-            for (uint32_t ks = 0; ks < 4; ++ks) {
-                const uint64_t ko = (ks * 32u) >> 4;  // 16 dims = 32 bytes along the swizzled row
-                umma(tmem + kColX, dq_lo + ko, dc_hi + ko, ID_QK, ks > 0 ? 1u : 0u);
-                umma(tmem + kColX, dq_hi + ko, dc_lo + ko, ID_QK, 1u);
-                umma(tmem + (ks < 2 ? kColHH0 : kColHH1), dq_hi + ko, dc_hi + ko, ID_QK, (ks & 1u) ? 1u : 0u);
-            }
-            umma_commit(bar_s);
+            if (2 < ntiles) issue_k(2, 0);
+            issue_s();
         }
-        if (j + 2 < ntiles) pending |= 1u << st;
+        if (2 < ntiles) pending |= 1u;
         pending |= 16u;
-        if (!mbar_wait_bounded(bar_s, (phase >> 4) & 1u)) s_err = 1u;
+    }
+    for (uint32_t j = 0; j < ntiles; ++j) {
+        const uint32_t st = j & 1u;
+        if (!mbar_wait_bounded(bar_s, (phase >> 4) & 1u)) err = true;
         phase ^= 16u;
         pending &= ~16u;
         tc_after_sync();
-        // ---- 4: this half row's scores, mask, online softmax, P halves ----
+        // ---- this half row's scores, mask, online softmax, P halves ----
         float sv[32];
         {
             float t[32];
@@ -377,13 +385,12 @@ __global__ void __launch_bounds__(NTH, 2) prefill_tc_kernel(const __grid_constan
         }
         fence_proxy_async();
         tc_before_sync();
-        __syncthreads();
+        if (__syncthreads_or(err)) break;
         tc_after_sync();
-        if (s_err) break;
-        // ---- 5: O tile = P_hi V + P_lo V ----
+        // ---- O tile = P_hi V + P_lo V on the tensor cores ----
         if (tid == 0) {
             if (!mbar_wait_bounded(bars + 16u + 8u * st, (phase >> (2 + st)) & 1u)) {
-                s_err = 1u;
+                err = true;
             } else {
                 const uint64_t dv = sdesc(sbase + pl.vst + st * kCTile, kCTile);
 #pragma unroll
@@ -398,10 +405,23 @@ __global__ void __launch_bounds__(NTH, 2) prefill_tc_kernel(const __grid_constan
         }
         phase ^= 4u << st;
         pending &= ~(4u << st);
-        __syncthreads();
-        if (s_err) break;
-        pending |= 32u;
-        if (!mbar_wait_bounded(bar_o, (phase >> 5) & 1u)) s_err = 1u;
+        pending |= 32u;  // on a failed V wait nothing commits: the error path's wait times out
+        // ---- meanwhile: dequantise tile j + 1 (the C tile is free: S of tile j is done) ----
+        if (j + 1 < ntiles) dequant(j + 1);
+        fence_proxy_async();
+        tc_before_sync();
+        if (__syncthreads_or(err)) break;
+        tc_after_sync();
+        if (j + 1 < ntiles) {
+            if (tid == 0) {
+                if (j + 3 < ntiles) issue_k(j + 3, st ^ 1u);
+                issue_s();
+            }
+            if (j + 3 < ntiles) pending |= 1u << (st ^ 1u);
+            pending |= 16u;
+        }
+        // ---- fold tile j's output while the tensor cores compute S of tile j + 1 ----
+        if (!mbar_wait_bounded(bar_o, (phase >> 5) & 1u)) err = true;
         phase ^= 32u;
         pending &= ~32u;
         tc_after_sync();
@@ -412,29 +432,25 @@ __global__ void __launch_bounds__(NTH, 2) prefill_tc_kernel(const __grid_constan
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = fmaf(o[i], alpha, t[i]);
         }
-        tc_before_sync();
-        __syncthreads();
-        if (s_err) break;
-        if (tid == 0 && j + 2 < ntiles) issue_v(j + 2, st);
+        // the V stage is free once P.V is done (read by the tensor cores only)
+        if (tid == 0 && j + 2 < ntiles && !err) issue_v(j + 2, st);
         if (j + 2 < ntiles) pending |= 4u << st;
     }
 
-    if (s_err) {
+    red[hf * M + row] = l_run;
+    tc_before_sync();
+    if (__syncthreads_or(err)) {
         // report, then give copies and tensor-core work in flight a bounded chance to finish
         if (tid == 0) atomicOr(a.status, kStatusWaitTimeout);
         for (uint32_t b = 0; b < 6; ++b)
             if (pending & (1u << b)) mbar_wait_bounded(bars + 8u * b, (phase >> b) & 1u);
-    } else {
-        red[hf * M + row] = l_run;
-        __syncthreads();
-        if (live) {
-            const float inv = 1.0f / (red[row] + red[M + row]);
-            const uint64_t HQ = (uint64_t)a.heads * G;
-            float *dst = a.out + (((uint64_t)s * a.n + qi) * HQ + (uint64_t)h * G + gq) * a.d;
+    } else if (live) {
+        const float inv = 1.0f / (red[row] + red[M + row]);
+        const uint64_t HQ = (uint64_t)a.heads * G;
+        float *dst = a.out + (((uint64_t)s * a.n + qi) * HQ + (uint64_t)h * G + gq) * a.d;
 #pragma unroll
-            for (uint32_t i = 0; i < 32; ++i)
-                if (c0 + i < a.d) dst[c0 + i] = o[i] * inv;
-        }
+        for (uint32_t i = 0; i < 32; ++i)
+            if (c0 + i < a.d) dst[c0 + i] = o[i] * inv;
     }
     tc_before_sync();
     __syncthreads();
