@@ -206,7 +206,6 @@ __global__ void __launch_bounds__(Shape<G>::W * 32, 2) prefill_kernel(const __gr
     uint32_t *meta_s = reinterpret_cast<uint32_t *>(smem + pl.meta);
     const uint32_t chi = smem_u32(smem + pl.chi), clo = smem_u32(smem + pl.clo);
     const uint32_t bars = smem_u32(smem + pl.bars);
-    __shared__ uint32_t s_err;
 
     // ---- prologue: codebooks, decode words, barriers ----
     for (uint32_t i = tid; i < pl.cent_alloc; i += NTH) cent_s[i] = i < hd.n_cent ? hd.cent[i] : 0.0f;
@@ -222,7 +221,6 @@ __global__ void __launch_bounds__(Shape<G>::W * 32, 2) prefill_kernel(const __gr
         meta_s[i] = m;
     }
     if (tid < 4) mbar_init(bars + 8u * tid, 1u);
-    if (tid == 0) s_err = 0;
     fence_barrier_init();
     __syncthreads();
 
@@ -285,11 +283,12 @@ __global__ void __launch_bounds__(Shape<G>::W * 32, 2) prefill_kernel(const __gr
     float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
     const int mi = lane >> 3, ri = lane & 7;
     uint32_t phase = 0;
+    bool err = false;  // this thread saw a wait time out; CTA-wide decisions use __syncthreads_or
 
     for (uint32_t j = 0; j < ntiles; ++j) {
         const uint32_t st = j & 1u;
         // ---- dequantise packed tile j into FP16 high / low code-domain values ----
-        if (!mbar_wait_bounded(bars + 8u * st, (phase >> st) & 1u)) s_err = 1u;
+        if (!mbar_wait_bounded(bars + 8u * st, (phase >> st) & 1u)) err = true;
         phase ^= 1u << st;
         pending &= ~(1u << st);
         const unsigned char *kt = smem + pl.kst + st * pl.kstage;
@@ -315,8 +314,7 @@ __global__ void __launch_bounds__(Shape<G>::W * 32, 2) prefill_kernel(const __gr
             *reinterpret_cast<uint4 *>(smem + pl.chi + at) = hi;
             *reinterpret_cast<uint4 *>(smem + pl.clo + at) = lo;
         }
-        __syncthreads();
-        if (s_err) break;
+        if (__syncthreads_or(err)) break;
         if (tid == 0 && j + 2 < ntiles) issue_k(j + 2, st);
         if (j + 2 < ntiles) pending |= 1u << st;
 
@@ -397,7 +395,7 @@ __global__ void __launch_bounds__(Shape<G>::W * 32, 2) prefill_kernel(const __gr
             float tv[8][4];
 #pragma unroll
             for (int nt = 0; nt < 8; ++nt) tv[nt][0] = tv[nt][1] = tv[nt][2] = tv[nt][3] = 0.0f;
-            if (!mbar_wait_bounded(bars + 16u + 8u * st, (phase >> (2 + st)) & 1u)) s_err = 1u;
+            if (!mbar_wait_bounded(bars + 16u + 8u * st, (phase >> (2 + st)) & 1u)) err = true;
             const uint32_t vs = smem_u32(smem + pl.vst + st * kCTile);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
@@ -428,12 +426,11 @@ __global__ void __launch_bounds__(Shape<G>::W * 32, 2) prefill_kernel(const __gr
         }
         phase ^= 4u << st;
         pending &= ~(4u << st);
-        __syncthreads();
-        if (s_err) break;
+        if (__syncthreads_or(err)) break;
         if (tid == 0 && j + 2 < ntiles) issue_v(j + 2, st);
         if (j + 2 < ntiles) pending |= 4u << st;
     }
-    if (s_err) {
+    if (__syncthreads_or(err)) {
         // report, then give the copies still in flight a bounded chance to land
         if (tid == 0) atomicOr(a.status, kStatusWaitTimeout);
         for (uint32_t b = 0; b < 4; ++b)
