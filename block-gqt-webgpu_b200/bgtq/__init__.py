@@ -14,7 +14,8 @@ from .attention import AttentionEngine, AttentionSession, GroupedAttention, Opti
 __all__ = ["BGTQError", "DeviceError", "LayoutError", "RangeError", "StateError", "LIB_PATH", "lib",
            "BlockGTQParameters", "allocate_bits", "build_tables", "haar_rotation", "optimal_centroids", "tables", "validate_layout", "CompressedKeys", "FP16Keys", "append_kv",
            "PackedKeys", "Values", "AttentionEngine", "AttentionSession", "GroupedAttention", "OptimizedAttention",
-           "device_status", "set_layout_jit", "layout_jit_stats"]
+           "device_status", "set_layout_jit", "layout_jit_stats",
+           "layout_jit_counts"]
 
 
 def set_layout_jit(on: bool) -> None:
@@ -30,6 +31,16 @@ def layout_jit_stats() -> tuple[int, int]:
     b, f = C.c_uint32(), C.c_uint32()
     _lib.call("bgtq_layout_jit_stats", C.byref(b), C.byref(f))
     return b.value, f.value
+
+
+def layout_jit_counts() -> dict:
+    """{"compiled": cubins ready, "loaded": kernels loaded by a launch, "failed": keys that
+    failed to build} for the layout-specialised attention kernels of this process."""
+    import ctypes as C
+    from . import _lib
+    c, l, f = C.c_uint32(), C.c_uint32(), C.c_uint32()
+    _lib.call("bgtq_layout_jit_counts", C.byref(c), C.byref(l), C.byref(f))
+    return {"compiled": c.value, "loaded": l.value, "failed": f.value}
 
 
 def device_status(device: int = 0) -> int:

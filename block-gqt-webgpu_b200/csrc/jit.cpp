@@ -123,7 +123,7 @@ struct Entry {
 std::mutex &g_mu = *new std::mutex;
 std::map<std::string, Entry> &g_cache = *new std::map<std::string, Entry>;
 std::atomic<int> g_enabled{-1};  // -1: not read from the environment yet
-std::atomic<uint32_t> g_built{0}, g_failed{0};
+std::atomic<uint32_t> g_compiled{0}, g_built{0}, g_failed{0};  // cubins made, kernels loaded, failures
 
 bool same_layout(const JitLayout &x, const JitLayout &y) {
     if (x.ns != y.ns || x.ng != y.ng) return false;
@@ -299,7 +299,7 @@ std::vector<char> compile(const JitKey &k) {
 void finish(Entry &e, std::vector<char> &&cubin) {
     e.cubin = std::move(cubin);
     e.state = e.cubin.empty() ? Entry::Failed : Entry::Compiled;
-    if (e.state == Entry::Failed) g_failed.fetch_add(1);
+    (e.state == Entry::Failed ? g_failed : g_compiled).fetch_add(1);
 }
 
 bool enabled() {
@@ -377,6 +377,13 @@ bgtq_status bgtq_set_layout_jit(int on) {
 
 bgtq_status bgtq_layout_jit_stats(uint32_t *built, uint32_t *failed) {
     if (built) *built = bgtq::g_built.load();
+    if (failed) *failed = bgtq::g_failed.load();
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_layout_jit_counts(uint32_t *compiled, uint32_t *loaded, uint32_t *failed) {
+    if (compiled) *compiled = bgtq::g_compiled.load();
+    if (loaded) *loaded = bgtq::g_built.load();
     if (failed) *failed = bgtq::g_failed.load();
     return BGTQ_OK;
 }

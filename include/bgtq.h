@@ -133,6 +133,9 @@ bgtq_status bgtq_optimal_centroids(uint32_t bits, uint32_t n, float *out);
 bgtq_status bgtq_set_layout_jit(int on);
 /* Specialised kernels loaded / keys that failed to build (and use the generic kernel). */
 bgtq_status bgtq_layout_jit_stats(uint32_t *built, uint32_t *failed);
+/* The same counters with the compile step apart: kernels compiled (cubins ready, whether or
+ * not a launch has loaded them yet), loaded, and failed.  Any pointer may be NULL. */
+bgtq_status bgtq_layout_jit_counts(uint32_t *compiled, uint32_t *loaded, uint32_t *failed);
 
 /* Fixture files of the reference's tests (tests/oracles/fixture.py:13-49): a JSON manifest
  * (metadata + array descriptors dtype f32/u32/u8/f16/u16, shape, offset, nbytes) beside a

@@ -3,7 +3,8 @@ time for one group structure gives the generic kernel's outputs bit for bit - ro
 7, FP16 and FP32 values, head dims 64 and 128, one and several splits, causal positions,
 logit / log-sum-exp capture - and is what runs by default when the heads share a layout.
 Heads with different structures (the SmolLM2 calibration) get a kernel compiled in the
-background: every launch before and after it is ready gives the generic outputs."""
+background: every launch before and after it is ready gives the generic outputs, and a
+launch inside a CUDA graph capture never loads it (the graph records the generic kernel)."""
 import time
 
 import numpy as np
@@ -116,4 +117,48 @@ def test_mixed_layouts_compile_in_background(cuda, rows):
     got = run()                          # the specialised kernel
     np.testing.assert_array_equal(got[0], ref[0])
     np.testing.assert_array_equal(got[1], ref[1])
+    assert device_status(0) == 0
+
+
+def test_no_kernel_load_inside_graph_capture(cuda):
+    import torch
+    from bgtq import _lib
+    z = np.load(GOLDEN / "smollm2_heads.npz")
+    S, T, d, rows, heads = 2, 500, 64, 1, (0, 3, 1)   # three structures: a key no other test uses
+    gen = torch.Generator(device=cuda).manual_seed(77)
+    keys = [PackedKeys((z[f"h{h}_config"], z[f"h{h}_table"]), T, sequences=S) for h in heads]
+    vals = [Values(d, T, "f16", sequences=S) for _ in heads]
+    for k, v in zip(keys, vals):
+        k.append((torch.randn((S, T, d), device=cuda, generator=gen) * 0.4).half())
+        v.append(torch.randn((S, T, d), device=cuda, generator=gen).half())
+    att = GroupedAttention(keys, vals, rows)
+    _lib.call("bgtq_attention_plan_for_capacity", att._handle, 1)
+    q = torch.randn((S, len(heads), rows, d), device=cuda, generator=gen)
+    bgtq.set_layout_jit(False)
+    ref = att.attend(q).clone()
+    torch.cuda.synchronize()
+    bgtq.set_layout_jit(True)
+    c0 = bgtq.layout_jit_counts()
+    att.attend(q)                                     # starts the background compile
+    torch.cuda.synchronize()
+    deadline = time.monotonic() + 240
+    while bgtq.layout_jit_counts()["compiled"] == c0["compiled"]:   # no launches meanwhile
+        assert bgtq.layout_jit_counts()["failed"] == c0["failed"]
+        assert time.monotonic() < deadline, "background compile did not finish"
+        time.sleep(0.25)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = att.attend(q)
+    assert bgtq.layout_jit_counts()["loaded"] == c0["loaded"]        # not loaded while capturing
+    graph.replay()
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), ref.cpu().numpy())
+    got = att.attend(q).clone()                       # outside a capture: loads and runs it
+    torch.cuda.synchronize()
+    assert bgtq.layout_jit_counts()["loaded"] == c0["loaded"] + 1
+    np.testing.assert_array_equal(got.cpu().numpy(), ref.cpu().numpy())
+    graph.replay()                                    # the recorded generic kernel still replays
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), ref.cpu().numpy())
+    del graph
     assert device_status(0) == 0
