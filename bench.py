@@ -393,8 +393,7 @@ def run_model(args, rank, world, local_rank):
     dist = sharding.init_from_env("nccl", timeout_s=300.0, device=dev)
     g = SMOLLM2_135M if args.workload == "model-smollm2" else QWEN25_05B
     prefix, steps, warmup = 4096, args.steps, max(3, args.warmup)
-    z = np.load(ROOT / "tests" / "golden" / "smollm2_heads.npz")
-    tables = [(z[f"h{i % 6}_config"], z[f"h{i % 6}_table"]) for i in range(g.layers * g.kv_heads)]
+    tables = calibration_tables(g.layers * g.kv_heads)
     dec = Decoder(random_weights(g, seed=7 + rank, device=dev), g, prefix + warmup + steps + 4, tables, batch=1)
     rng = np.random.default_rng(rank)
     t_pre = time.perf_counter()
@@ -431,13 +430,31 @@ def run_model(args, rank, world, local_rank):
             "data": "synthetic (random-init FP16 weights N(0,0.02), uniform random token ids)",
             "config": {"workload": f"config {2 if g.family == 'smollm2' else 3}: {g.family} geometry, {g.layers} layers, "
                                    f"{g.q_heads}/{g.kv_heads} heads, head_dim 64, Block-GTQ K + FP16 V",
-                       "model": g.family, "global_batch": world, "seq_len": prefix, "parallelism": f"replicas x{world}"},
+                       "model": g.family, "global_batch": world, "seq_len": prefix, "parallelism": f"replicas x{world}",
+                       "tables": "SmolLM2 calibration heads (reference calibration widths, native table builder)"
+                                 + ("" if g.family == "smollm2" else "; stand-ins: no Qwen calibration exists")},
+            "attention_kernels": bgtq.layout_jit_counts(),
             "prefill_s": prefill_s, "reference_webgpu_ms_per_token": 375.6 if g.family == "smollm2" else 348.4,
             "checks": {"logits_finite": finite, "device_status": bgtq.device_status(local_rank)}}), flush=True)
     dec.destroy()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def calibration_tables(n):
+    """Tables of the first n heads of the reference's SmolLM2 calibration (30 layers x 3 KV
+    heads), built by the native table builder from the calibrated bit widths (pair order,
+    row padding and scale stride as calibrated; the same bytes as the reference's tables)."""
+    import bgtq
+    z = np.load(ROOT / "tests" / "golden" / "smollm2_calibration.npz")
+    out = []
+    for i in range(n):
+        j = i % len(z["widths"])
+        out.append(bgtq.build_tables(z["widths"][j].astype(np.int64), pair_order=z["pair_order"][j].astype(np.int64),
+                                     rotation_threshold=int(z["rotation_threshold"]), row_pad=int(z["row_pad"][j]),
+                                     norm_stride=int(z["norm_stride"][j])))
+    return out
 
 
 def run_prefill(args, rank, world, local_rank):

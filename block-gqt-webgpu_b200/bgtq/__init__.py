@@ -15,7 +15,7 @@ __all__ = ["BGTQError", "DeviceError", "LayoutError", "RangeError", "StateError"
            "BlockGTQParameters", "allocate_bits", "build_tables", "haar_rotation", "optimal_centroids", "tables", "validate_layout", "CompressedKeys", "FP16Keys", "append_kv",
            "PackedKeys", "Values", "AttentionEngine", "AttentionSession", "GroupedAttention", "OptimizedAttention",
            "device_status", "set_layout_jit", "layout_jit_stats",
-           "layout_jit_counts"]
+           "layout_jit_counts", "layout_jit_wait"]
 
 
 def set_layout_jit(on: bool) -> None:
@@ -41,6 +41,17 @@ def layout_jit_counts() -> dict:
     c, l, f = C.c_uint32(), C.c_uint32(), C.c_uint32()
     _lib.call("bgtq_layout_jit_counts", C.byref(c), C.byref(l), C.byref(f))
     return {"compiled": c.value, "loaded": l.value, "failed": f.value}
+
+
+def layout_jit_wait(timeout_s: float = 300.0) -> bool:
+    """Wait for the queued background compiles of layout-specialised attention kernels and
+    load what they built (call outside a graph capture); False if the time ran out."""
+    from . import _lib
+    status = _lib.lib().bgtq_layout_jit_wait(max(0, min(int(timeout_s * 1000), 2**32 - 1)))
+    if status == _lib.ETIMEOUT:
+        return False
+    _lib.check(status)
+    return True
 
 
 def device_status(device: int = 0) -> int:

@@ -67,6 +67,7 @@ SIGNATURES = {
     "bgtq_set_layout_jit": (I32, [I32]),
     "bgtq_layout_jit_stats": (I32, [P, P]),
     "bgtq_layout_jit_counts": (I32, [P, P, P]),
+    "bgtq_layout_jit_wait": (I32, [U32]),
     "bgtq_fixture_read": (I32, [C.c_char_p, P]),
     "bgtq_fixture_array_count": (I32, [P, P]),
     "bgtq_fixture_array": (I32, [P, U32, P, P, P, P, P, P]),

@@ -212,17 +212,20 @@ class Decoder:
         return self.forward(token)
 
     # ---- CUDA graph of one decode step ----
-    def capture_decode(self, token):
+    def capture_decode(self, token, jit_wait_s=300.0):
         """Decode `token` eagerly, then record the whole decode step (every layer's GEMMs,
         norms, K/V append and attention) as one CUDA graph; decode_graph() replays it.
         Attention plans its split-KV factor for the capacity, so replays stay exact while
-        the sequences grow; appends inside replays move the device lengths only."""
+        the sequences grow; appends inside replays move the device lengths only.  The
+        layout-specialised attention kernels the eager step queued are waited for (up to
+        `jit_wait_s`) and loaded first, so the graph records them."""
         import torch
-        from . import _lib
+        from . import _lib, layout_jit_wait
         for a in self.attn:
             _lib.call("bgtq_attention_plan_for_capacity", a._handle, 1)
         out = self.forward(token)                      # eager step: warms every kernel up
         torch.cuda.synchronize(self.dev)
+        layout_jit_wait(jit_wait_s)
         self._tok = torch.as_tensor(token, device=self.dev).reshape(self.batch, 1).long().clone()
         self._graph = torch.cuda.CUDAGraph()
         length = self.length

@@ -15,9 +15,10 @@
 // some intrinsics differently, so they are a few percent slower than nvcc's.
 // One kernel per key (dims, query rows, value type, the heads' structures), kept for the life
 // of the process (at most kMaxEntries).  A key whose heads share one structure compiles on the
-// launch that first needs it; a key with several compiles on a background thread (host work
-// only, no CUDA calls) while the generic kernel serves the launches.  The cubin is loaded by
-// the first launch after that whose stream is not capturing a graph.  Anything that fails
+// launch that first needs it; a key with several is queued for background worker threads
+// (host work only, no CUDA calls; at most kWorkers compiles at a time) while the generic
+// kernel serves the launches.  The cubin is loaded by the first launch after that whose stream is not capturing
+// a graph, or by bgtq_layout_jit_wait.  Anything that fails
 // (no compiler, no sources, a compile or load error) leaves the generic kernel in use.
 // BGTQ_LAYOUT_JIT=0 in the environment or bgtq_set_layout_jit(0) turns it off.
 #include <dlfcn.h>
@@ -28,6 +29,9 @@
 #include <cerrno>
 
 #include <atomic>
+#include <chrono>
+#include <condition_variable>
+#include <deque>
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
@@ -124,6 +128,18 @@ std::mutex &g_mu = *new std::mutex;
 std::map<std::string, Entry> &g_cache = *new std::map<std::string, Entry>;
 std::atomic<int> g_enabled{-1};  // -1: not read from the environment yet
 std::atomic<uint32_t> g_compiled{0}, g_built{0}, g_failed{0};  // cubins made, kernels loaded, failures
+
+// Background compiles: a FIFO served by up to kWorkers threads (started as jobs arrive, never
+// joined); g_cv signals both a queued job and a finished one.  Guarded by g_mu.
+struct Job {
+    JitKey key;
+    std::string ks;
+};
+std::deque<Job> &g_queue = *new std::deque<Job>;
+std::condition_variable &g_cv = *new std::condition_variable;
+constexpr uint32_t kWorkers = 4;
+uint32_t g_busy = 0;     // jobs queued or compiling
+uint32_t g_workers = 0;  // worker threads started
 
 bool same_layout(const JitLayout &x, const JitLayout &y) {
     if (x.ns != y.ns || x.ng != y.ng) return false;
@@ -302,6 +318,34 @@ void finish(Entry &e, std::vector<char> &&cubin) {
     (e.state == Entry::Failed ? g_failed : g_compiled).fetch_add(1);
 }
 
+void worker() {
+    std::unique_lock<std::mutex> l(g_mu);
+    for (;;) {
+        g_cv.wait(l, [] { return !g_queue.empty(); });
+        Job j = std::move(g_queue.front());
+        g_queue.pop_front();
+        l.unlock();
+        std::vector<char> cubin = compile(j.key);
+        l.lock();
+        finish(g_cache[j.ks], std::move(cubin));
+        --g_busy;
+        g_cv.notify_all();
+    }
+}
+
+// A compiled entry's library loaded (caller holds g_mu, outside any graph capture).
+void load_compiled(Entry &e) {
+    if (e.state != Entry::Compiled) return;
+    if (load(e)) {
+        e.state = Entry::Ready;
+        g_built.fetch_add(1);
+    } else {
+        e.state = Entry::Failed;
+        g_failed.fetch_add(1);
+    }
+    std::vector<char>().swap(e.cubin);
+}
+
 bool enabled() {
     int v = g_enabled.load();
     if (v < 0) {
@@ -335,11 +379,13 @@ const void *jit_attention_kernel(const JitKey &key, cudaStream_t stream, bool *h
         if (!multi_layout(key)) {
             finish(it->second, compile(key));
         } else {
-            std::thread([key, ks] {
-                std::vector<char> cubin = compile(key);
-                std::lock_guard<std::mutex> l(g_mu);
-                finish(g_cache[ks], std::move(cubin));
-            }).detach();
+            g_queue.push_back(Job{key, ks});
+            ++g_busy;
+            if (g_workers < kWorkers && g_workers < g_busy) {
+                std::thread(worker).detach();
+                ++g_workers;
+            }
+            g_cv.notify_all();
             return nullptr;
         }
     }
@@ -352,14 +398,7 @@ const void *jit_attention_kernel(const JitKey &key, cudaStream_t stream, bool *h
             return nullptr;
         }
         if (cs != cudaStreamCaptureStatusNone) return nullptr;
-        if (load(e)) {
-            e.state = Entry::Ready;
-            g_built.fetch_add(1);
-        } else {
-            e.state = Entry::Failed;
-            g_failed.fetch_add(1);
-        }
-        std::vector<char>().swap(e.cubin);
+        load_compiled(e);
     }
     if (e.state != Entry::Ready) return nullptr;
     *head_major = multi_layout(key);
@@ -379,6 +418,13 @@ bgtq_status bgtq_layout_jit_stats(uint32_t *built, uint32_t *failed) {
     if (built) *built = bgtq::g_built.load();
     if (failed) *failed = bgtq::g_failed.load();
     return BGTQ_OK;
+}
+
+bgtq_status bgtq_layout_jit_wait(uint32_t timeout_ms) {
+    std::unique_lock<std::mutex> l(bgtq::g_mu);
+    const bool idle = bgtq::g_cv.wait_for(l, std::chrono::milliseconds(timeout_ms), [] { return bgtq::g_busy == 0; });
+    for (auto &kv : bgtq::g_cache) bgtq::load_compiled(kv.second);
+    return idle ? BGTQ_OK : BGTQ_ETIMEOUT;
 }
 
 bgtq_status bgtq_layout_jit_counts(uint32_t *compiled, uint32_t *loaded, uint32_t *failed) {

@@ -136,6 +136,11 @@ bgtq_status bgtq_layout_jit_stats(uint32_t *built, uint32_t *failed);
 /* The same counters with the compile step apart: kernels compiled (cubins ready, whether or
  * not a launch has loaded them yet), loaded, and failed.  Any pointer may be NULL. */
 bgtq_status bgtq_layout_jit_counts(uint32_t *compiled, uint32_t *loaded, uint32_t *failed);
+/* Wait up to timeout_ms for the background compiles queued so far, then load every compiled
+ * kernel, so the next launches (and a graph recorded after this call) use them.  Call it
+ * outside a graph capture.  BGTQ_ETIMEOUT if compiles were still running at the limit (what
+ * had finished is loaded). */
+bgtq_status bgtq_layout_jit_wait(uint32_t timeout_ms);
 
 /* Fixture files of the reference's tests (tests/oracles/fixture.py:13-49): a JSON manifest
  * (metadata + array descriptors dtype f32/u32/u8/f16/u16, shape, offset, nbytes) beside a

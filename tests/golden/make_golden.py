@@ -23,6 +23,9 @@ What it writes, all derived from the reference's own Python CPU code and fixture
   tests regenerate them bit-identically; their SHA-256 is stored beside the outputs.
 * ``smollm2_heads.npz`` - the flattened ``config`` / ``table`` / ``ranges`` of the first
   six SmolLM2 calibration heads from ``fixtures/model/calibration.json`` (format check).
+* ``smollm2_calibration.npz`` - all 90 heads of that calibration (30 layers x 3 KV heads) as
+  table-builder inputs - widths, pair order, row padding, scale stride - with the SHA-256 of
+  each head's reference ``config`` and ``table`` (``--only calibration`` writes just this).
 """
 from __future__ import annotations
 
@@ -157,9 +160,32 @@ def export_smollm2(ref_root, read_fixture, count=6):
     save(HERE / "smollm2_heads.npz", **out)
 
 
+def export_calibration(ref_root, read_fixture):
+    meta, a = read_fixture(ref_root / "fixtures/model/calibration.json")
+    n = len(meta["heads"])
+    widths, order, pad, stride, cfg_sha, tab_sha = [], [], [], [], [], []
+    for i in range(n):
+        cfg, tab = a[f"h{i}_config"], a[f"h{i}_table"]
+        d, ns = int(cfg[0]), int(cfg[4])
+        perm = cfg[int(cfg[6]):int(cfg[6]) + d]
+        widths.append(a[f"h{i}_widths"].astype(np.int8))
+        order.append(perm[0::2].astype(np.int16))
+        pad.append(int(cfg[2]) - (ns // 2 + d - ns))
+        stride.append(int(cfg[3]))
+        cfg_sha.append(sha(cfg.astype(np.uint32)))
+        tab_sha.append(sha(tab.astype(np.float32)))
+    save(HERE / "smollm2_calibration.npz", widths=np.stack(widths), pair_order=np.stack(order),
+         row_pad=np.array(pad, np.int32), norm_stride=np.array(stride, np.int32),
+         layer=np.array([h["layer"] for h in meta["heads"]], np.int32),
+         kv_head=np.array([h["kv_head"] for h in meta["heads"]], np.int32),
+         rotation_threshold=np.int32(meta["rotation_threshold"]),
+         config_sha256=np.array(cfg_sha), table_sha256=np.array(tab_sha))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
+    ap.add_argument("--only", choices=["calibration"], default=None)
     args = ap.parse_args()
     ref_root = args.reference.resolve()
     os.environ["PYTHONDONTWRITEBYTECODE"] = "1"
@@ -168,6 +194,9 @@ def main():
     import torch
     torch.set_num_threads(1)
     from tests.oracles.fixture import read_fixture
+    if args.only == "calibration":
+        export_calibration(ref_root, read_fixture)
+        return
     from tests.oracles import production_oracle as oracle
     from tests.oracles.oracle import load
     from reference.production_math import encode, reconstruct
@@ -182,6 +211,7 @@ def main():
     export_config("config1", dim=128, tokens=4096, budget=256, seed=0, sample=512, attention=True, ref=ref)
     export_config("config4", dim=64, tokens=4096, budget=128, seed=4, sample=512, attention=False, ref=ref)
     export_smollm2(ref_root, read_fixture)
+    export_calibration(ref_root, read_fixture)
     print("golden vectors written to", HERE)
 
 

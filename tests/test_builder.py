@@ -9,6 +9,9 @@ Pins, all bit-exact:
   norm stride = groups + 1, as export_mixed.py writes them) and the six SmolLM2 calibration
   heads: tables exact from the widths; configs exact given the fixtures' pair order (they were
   made by torch builds whose unstable argsort orders equal widths differently).
+* all 90 heads of the SmolLM2 calibration (tests/golden/smollm2_calibration.npz: widths,
+  pair order, row padding, scale stride and the SHA-256 of the reference's config / table):
+  tables exact from the widths alone, configs exact given the pair order.
 * the Haar rotation against NumPy's own generator + QR (the reference's
   _random_rotation_dense_torch, vendor/blockgtq/block_gtq_pipeline.py:81-92), and the
   builder's pair order against torch.argsort.
@@ -73,6 +76,25 @@ def test_tables_match_smollm2_calibration(head):
     cfg, tab = bgtq.build_tables(w, pair_order=perm[0::2], **kw)
     np.testing.assert_array_equal(cfg, rcfg)
     np.testing.assert_array_equal(tab, rtab)
+
+
+def _sha(a):
+    import hashlib
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def test_tables_match_full_smollm2_calibration():
+    z = np.load(GOLDEN / "smollm2_calibration.npz")
+    assert z["widths"].shape == (90, 32) and int(z["rotation_threshold"]) == 2
+    for i in range(90):
+        w = z["widths"][i].astype(np.int64)
+        kw = dict(rotation_threshold=int(z["rotation_threshold"]), row_pad=int(z["row_pad"][i]),
+                  norm_stride=int(z["norm_stride"][i]))
+        _, tab = bgtq.build_tables(w, **kw)
+        assert _sha(tab.astype(np.float32)) == z["table_sha256"][i], i
+        cfg, tab = bgtq.build_tables(w, pair_order=z["pair_order"][i].astype(np.int64), **kw)
+        assert _sha(cfg.astype(np.uint32)) == z["config_sha256"][i], i
+        assert _sha(tab.astype(np.float32)) == z["table_sha256"][i], i
 
 
 def test_pair_order_is_torch_argsort():

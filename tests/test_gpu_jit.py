@@ -162,3 +162,40 @@ def test_no_kernel_load_inside_graph_capture(cuda):
     np.testing.assert_array_equal(out.cpu().numpy(), ref.cpu().numpy())
     del graph
     assert device_status(0) == 0
+
+
+def test_wait_loads_and_graph_records_specialised_kernel(cuda):
+    import torch
+    from bgtq import _lib
+    z = np.load(GOLDEN / "smollm2_heads.npz")
+    S, T, d, rows, heads = 3, 400, 64, 4, (2, 4, 5, 3)   # four structures: a key no other test uses
+    gen = torch.Generator(device=cuda).manual_seed(78)
+    keys = [PackedKeys((z[f"h{h}_config"], z[f"h{h}_table"]), T, sequences=S) for h in heads]
+    vals = [Values(d, T, "f16", sequences=S) for _ in heads]
+    for k, v in zip(keys, vals):
+        k.append((torch.randn((S, T, d), device=cuda, generator=gen) * 0.4).half())
+        v.append(torch.randn((S, T, d), device=cuda, generator=gen).half())
+    att = GroupedAttention(keys, vals, rows)
+    _lib.call("bgtq_attention_plan_for_capacity", att._handle, 1)
+    q = torch.randn((S, len(heads), rows, d), device=cuda, generator=gen)
+    bgtq.set_layout_jit(False)
+    ref = att.attend(q).clone()
+    torch.cuda.synchronize()
+    bgtq.set_layout_jit(True)
+    c0 = bgtq.layout_jit_counts()
+    att.attend(q)                                     # queues the compile
+    torch.cuda.synchronize()
+    assert bgtq.layout_jit_wait(240.0)
+    c1 = bgtq.layout_jit_counts()
+    assert c1["loaded"] == c0["loaded"] + 1 and c1["failed"] == c0["failed"]   # loaded without a launch
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = att.attend(q)                           # records the specialised kernel
+    for _ in range(2):
+        graph.replay()
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy(), ref.cpu().numpy())
+    assert bgtq.layout_jit_counts() == c1
+    assert bgtq.layout_jit_wait(0.0)                  # nothing queued: returns at once
+    del graph
+    assert device_status(0) == 0
