@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--tables", choices=["config4", "calibration"], default="config4",
+                    help="decode: config-4 tables for every head (the headline), or the 90 heads of the "
+                         "reference's SmolLM2 calibration (30 layers x 3 KV heads)")
     ap.add_argument("--workload", choices=["decode", "model-smollm2", "model-qwen", "prefill"], default="decode",
                     help="decode: config 4 (the headline); model-*: configs 2/3; prefill: config 5")
     return ap.parse_args()
@@ -193,6 +196,11 @@ def run_ours(args, rank, world, local_rank):
     p, cfg, tab = tables()
     B, T, L, H, R, d = args.batch, args.context, args.layers, KV_HEADS, GQA, HEAD_DIM
     steps, warmup = args.steps, args.warmup
+    calib = args.tables == "calibration"
+    head_tables = calibration_tables(L * H) if calib else [(cfg, tab)] * (L * H)
+    head_params = [bgtq.BlockGTQParameters.from_tables(*t) for t in head_tables] if calib else [p] * (L * H)
+    if calib:
+        p, (cfg, tab) = head_params[0], head_tables[0]   # the CPU baseline's sample head
     e2e_steps = 0 if args.no_e2e else max(2, steps // 2)
     capacity = T + warmup + steps + 2 * e2e_steps + 8
     sig = torch.from_numpy(synthetic.pair_sigma(d // 2).astype(np.float32)).to(dev)
@@ -212,7 +220,7 @@ def run_ours(args, rank, world, local_rank):
     for layer in range(L):
         lk, lv = [], []
         for h in range(H):
-            k = bgtq.PackedKeys((cfg, tab), capacity, sequences=B, device=local_rank)
+            k = bgtq.PackedKeys(head_tables[layer * H + h], capacity, sequences=B, device=local_rank)
             v = bgtq.Values(d, capacity, "f16", sequences=B, device=local_rank)
             kk = profiled_keys(B, T)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -248,8 +256,12 @@ def run_ours(args, rank, world, local_rank):
     def barrier():
         sharding.barrier(dist, torch.cuda.synchronize)
 
-    for _ in range(warmup):
+    for i in range(warmup):
         step()
+        if i == 0 and calib:
+            # the first step queued each layer's layout-specialised kernel: wait for them
+            torch.cuda.synchronize()
+            bgtq.layout_jit_wait(600.0)
     barrier()
     clocks = Clocks(local_rank)
     clocks.start()
@@ -305,19 +317,21 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0:
         hbm, peak_kind = peaks()
         ctx_mean = T + warmup + (steps + 1) / 2.0
-        bpt = bytes_per_token_head(p)
+        bpt = float(np.mean([bytes_per_token_head(ph) for ph in head_params]))
         alg_bytes = B * ctx_mean * H * bpt
         mean_launch_s = float(np.mean(launch_ms)) / 1e3
         achieved = alg_bytes / mean_launch_s / 1e9
         traffic = None
         tf = ROOT / "profiles" / "attention_traffic.json"
-        if tf.exists():
+        if tf.exists() and not calib:   # captured on the config-4 tables
             per_token_head = json.loads(tf.read_text())["dram_bytes_per_token_head"]
             traffic = per_token_head * B * ctx_mean * H
         enc_keys = B * T
         enc_ms_med = float(np.median(enc_ms))
         enc_rate = enc_keys / (enc_ms_med / 1e3)
-        enc_bytes = 2 * d + (p.nibble_dims // 2 + d - p.nibble_dims) + 2 * p.groups
+        enc_bytes = float(np.mean([2 * d + (ph.nibble_dims // 2 + d - ph.nibble_dims) + 2 * ph.groups
+                                   for ph in head_params]))
+        enc_flops = float(np.mean([encode_flops_per_key(ph) for ph in head_params]))
         cpu = cpu_baseline(p, cfg, tab, T, B, L, args.cpu_seconds, os.cpu_count() or 1)
         value = B * world * steps / elapsed_max
         line = {
@@ -326,8 +340,10 @@ def run_ours(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (device-drawn K with the pair-energy profile, N(0,1) V and Q)",
             "config": {"workload": "config4: SmolLM2 attention geometry, 30 layers x 3 KV / 9 Q heads (GQA 3), "
-                                   "head_dim 64, batch 256 x context 32768 per GPU, Block-GTQ K (config-4 tables) "
+                                   "head_dim 64, batch 256 x context 32768 per GPU, Block-GTQ K ("
+                                   + ("the 90 SmolLM2 calibration heads" if calib else "config-4 tables") + ") "
                                    "+ FP16 V; step = append new K/V + attention for every layer",
+                       "tables": args.tables,
                        "layers": L, "kv_heads": H, "q_heads": H * R, "head_dim": d, "global_batch": B * world,
                        "seq_len": T, "parallelism": f"sequence-sharded x{world} (independent batches, no collective)",
                        "l2": "inputs larger than L2: ~139 GB cache resident per GPU, no flush needed"},
@@ -341,13 +357,16 @@ def run_ours(args, rank, world, local_rank):
                          "bytes_per_token_head": bpt, "mean_launch_ms": mean_launch_s * 1e3},
             "k_encode": {"value": enc_rate / 1e6, "unit": "Mkeys/s", "keys_per_launch": enc_keys,
                          "ms_per_launch": enc_ms_med, "hbm_frac": enc_rate * enc_bytes / 1e9 / hbm,
-                         "fp32_tflops": enc_rate * encode_flops_per_key(p) / 1e12,
-                         "bytes_per_key": enc_bytes, "flops_per_key": encode_flops_per_key(p)},
+                         "fp32_tflops": enc_rate * enc_flops / 1e12,
+                         "bytes_per_key": enc_bytes, "flops_per_key": enc_flops},
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             "clocks": clk,
-            "attention_kernel": ("layout-specialised (compiled at run time for the config-4 group structure)"
+            "attention_kernel": (("layout-specialised (compiled at run time for each layer's heads' group "
+                                  "structures)" if calib else
+                                  "layout-specialised (compiled at run time for the config-4 group structure)")
                                  if bgtq.layout_jit_stats()[0] else "generic"),
+            "layout_jit": bgtq.layout_jit_counts(),
             "checks": {"outputs_finite": finite, "device_status": status, "setup_s": setup_s,
                        "output_checksums": checksums,
                        "sequences": [sharding.sequence_range(B, r)[0] for r in range(world)]},
@@ -473,7 +492,7 @@ def run_prefill(args, rank, world, local_rank):
     dist = sharding.init_from_env("nccl", timeout_s=300.0, device=dev)
     g = QWEN25_05B
     S, T, L, H, G, d = 16, 8192, args.layers if args.layers != LAYERS else g.layers, g.kv_heads, g.gqa, 64
-    z = np.load(ROOT / "tests" / "golden" / "smollm2_heads.npz")
+    heads = calibration_tables(L * H)
     gen = torch.Generator(device=dev).manual_seed(11 + rank)
     x = torch.randn((S * T, g.hidden), device=dev, generator=gen, dtype=torch.bfloat16)
     wqkv = [(torch.randn((g.hidden, (g.q_heads + 2 * H) * d), device=dev, generator=gen) * 0.05).bfloat16()
@@ -490,7 +509,7 @@ def run_prefill(args, rank, world, local_rank):
     steps, warmup = args.steps, max(3, args.warmup)
     stores = []
     for layer in range(L):
-        ks = [bgtq.PackedKeys((z[f"h{(layer * H + h) % 6}_config"], z[f"h{(layer * H + h) % 6}_table"]), T,
+        ks = [bgtq.PackedKeys(heads[layer * H + h], T,
                               sequences=S, device=local_rank) for h in range(H)]
         vs = [bgtq.Values(d, T, "f16", sequences=S, device=local_rank) for _ in range(H)]
         stores.append((ks, vs, bgtq.GroupedAttention(ks, vs, G)))
@@ -540,7 +559,8 @@ def run_prefill(args, rank, world, local_rank):
             "data": "synthetic (N(0,1) BF16 activations, random-init BF16 projections)",
             "config": {"workload": f"config 5: Qwen2.5-0.5B attention geometry, {L} layers, 14/2 heads, head_dim 64, "
                                    f"{S} sequences x {T} tokens, causal", "global_batch": S * world, "seq_len": T,
-                       "parallelism": f"sequence-sharded x{world}"},
+                       "parallelism": f"sequence-sharded x{world}",
+                       "tables": "SmolLM2 calibration heads as stand-ins (no Qwen calibration exists)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak or None, "unit": "TFLOP/s",
                          "frac": achieved / peak if peak else None,
                          "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)",
