@@ -138,6 +138,7 @@ def test_no_kernel_load_inside_graph_capture(cuda):
     ref = att.attend(q).clone()
     torch.cuda.synchronize()
     bgtq.set_layout_jit(True)
+    assert bgtq.layout_jit_wait(240.0)                # no compile of an earlier test still pending
     c0 = bgtq.layout_jit_counts()
     att.attend(q)                                     # starts the background compile
     torch.cuda.synchronize()
@@ -182,6 +183,7 @@ def test_wait_loads_and_graph_records_specialised_kernel(cuda):
     ref = att.attend(q).clone()
     torch.cuda.synchronize()
     bgtq.set_layout_jit(True)
+    assert bgtq.layout_jit_wait(240.0)                # loads what earlier tests left compiled
     c0 = bgtq.layout_jit_counts()
     att.attend(q)                                     # queues the compile
     torch.cuda.synchronize()
