@@ -27,6 +27,17 @@ constexpr int kThreads = 128;
 constexpr uint32_t kWarpKeysMax = 4096;
 
 __device__ __forceinline__ bool bit_set(const uint32_t (&m)[4], int j) { return (m[j >> 5] >> (j & 31)) & 1u; }
+// The same bit at a run-time index, chosen from the four registers by selects (an indexed
+// register array would be placed in local memory).
+__device__ __forceinline__ bool bit_set_rt(const uint32_t (&m)[4], uint32_t j) {
+    const uint32_t w = j >> 5;
+    const uint32_t word = w == 0 ? m[0] : w == 1 ? m[1] : w == 2 ? m[2] : m[3];
+    return (word >> (j & 31)) & 1u;
+}
+// Quotient n / d for n * d < 2^32 from one high multiply by m = ceil(2^32 / d) (d > 1):
+// n * m / 2^32 = n / d + n * e / (d * 2^32) with e = m * d - 2^32 < d, whose second term
+// stays below 1 / d, so the floor is exact.
+__device__ __forceinline__ uint32_t div_small(uint32_t n, uint32_t d, uint32_t m) { return d == 1 ? n : __umulhi(n, m); }
 
 template <int D>
 __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant__ EncodeArgs a, uint32_t d,
@@ -75,20 +86,45 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant_
 #pragma unroll
     for (int w = 0; w < 4; ++w) bm[w] = h.bound_mask[w];
     const uint32_t ns = h.ns, ng = h.ng, count = a.count;
+    // row-word and scale-word quotients by high multiplies (w < kThreads * 64 words)
+    const uint32_t rw_magic = row_words > 1 ? (uint32_t)((0x100000000ull + row_words - 1) / row_words) : 0u;
+    const uint32_t sw_magic = sc_words > 1 ? (uint32_t)((0x100000000ull + sc_words - 1) / sc_words) : 0u;
+    const bool vec16 = !a.src_f32 && d == (uint32_t)D &&
+                       (((uintptr_t)a.src | ((a.seq_stride | a.row_stride | h.src_head_offset) * 2u)) & 15u) == 0;
+    __shared__ uint64_t rsrc_s[kThreads], rdst_s[kThreads], rsc_s[kThreads];
     __syncthreads();
 
     const uint32_t n_tiles = (total + kThreads - 1) / kThreads;
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
         const uint32_t first = tile * kThreads;
         const uint32_t nrows = min((uint32_t)kThreads, total - first);
+        // ---- per-row source element and destination offsets (one division per row) ----
+        if ((uint32_t)tid < nrows) {
+            const uint32_t q = first + tid, s = q / count, rr = q % count;
+            const uint64_t dseq = a.seq_first + s, dst_row = (a.row0 ? a.row0[s] : a.row0_scalar) + rr;
+            rsrc_s[tid] = (uint64_t)s * a.seq_stride + (uint64_t)rr * a.row_stride + h.src_head_offset;
+            rdst_s[tid] = dseq * h.k_seq_stride + dst_row * h.row_stride;
+            rsc_s[tid] = dseq * h.s_seq_stride + dst_row * h.scale_stride;
+        }
+        __syncthreads();
         // ---- stage the input rows as FP16 words (coalesced) ----
         const uint32_t in_words = d / 2;
-        for (uint32_t w = tid; w < nrows * (uint32_t)(D / 2); w += kThreads) {
+        if (vec16) {
+            // full-width FP16 rows on 16-byte boundaries: one 16-byte load per 8 elements
+            for (uint32_t w = tid; w < nrows * (uint32_t)(D / 8); w += kThreads) {
+                const uint32_t r = w / (D / 8), c = w % (D / 8);
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.src) + rsrc_s[r] + 8u * c));
+                uint32_t *dst = stage_s + r * SW + 4u * c;
+                dst[0] = v.x;
+                dst[1] = v.y;
+                dst[2] = v.z;
+                dst[3] = v.w;
+            }
+        } else for (uint32_t w = tid; w < nrows * (uint32_t)(D / 2); w += kThreads) {
             const uint32_t r = w / (D / 2), c = w % (D / 2);
             uint32_t word = 0;
             if (c < in_words) {
-                const uint32_t q = first + r, s = q / count, rr = q % count;
-                const uint64_t e = (uint64_t)s * a.seq_stride + (uint64_t)rr * a.row_stride + h.src_head_offset + 2u * c;
+                const uint64_t e = rsrc_s[r] + 2u * c;
                 if (a.src_f32) {
                     const float2 f = *reinterpret_cast<const float2 *>(static_cast<const float *>(a.src) + e);
                     word = (uint32_t)__half_as_ushort(__float2half_rn(f.x)) |
@@ -184,7 +220,7 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant_
                         ob[(ns >> 1) + (j - ns)] = (uint8_t)code;
                     }
                     const uint32_t jn = j + 1;
-                    if (jn == d || ((bm[jn >> 5] >> (jn & 31)) & 1u)) {
+                    if (jn == d || bit_set_rt(bm, jn)) {
                         const float s = n / fmaxf(sqrtf(cl), 1e-10f);
                         srow[g] = __half_as_ushort(__float2half_rn(s));
                         ++g;
@@ -197,20 +233,12 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant_
         __syncthreads();
         // ---- write packed rows and scales (coalesced words) ----
         for (uint32_t w = tid; w < nrows * row_words; w += kThreads) {
-            const uint32_t r = w / row_words, c = w % row_words;
-            const uint32_t q = first + r, s = q / count, rr = q % count;
-            const uint32_t dst_row = (a.row0 ? a.row0[s] : a.row0_scalar) + rr;
-            uint32_t *dst = reinterpret_cast<uint32_t *>(h.packed + (uint64_t)(a.seq_first + s) * h.k_seq_stride +
-                                                         (uint64_t)dst_row * h.row_stride);
-            dst[c] = out_s[r * ow + c];
+            const uint32_t r = div_small(w, row_words, rw_magic), c = w - r * row_words;
+            reinterpret_cast<uint32_t *>(h.packed + rdst_s[r])[c] = out_s[r * ow + c];
         }
         for (uint32_t w = tid; w < nrows * sc_words; w += kThreads) {
-            const uint32_t r = w / sc_words, c = w % sc_words;
-            const uint32_t q = first + r, s = q / count, rr = q % count;
-            const uint32_t dst_row = (a.row0 ? a.row0[s] : a.row0_scalar) + rr;
-            uint32_t *dst = reinterpret_cast<uint32_t *>(h.scales + (uint64_t)(a.seq_first + s) * h.s_seq_stride +
-                                                         (uint64_t)dst_row * h.scale_stride);
-            dst[c] = sc_s[r * sw + c];
+            const uint32_t r = div_small(w, sc_words, sw_magic), c = w - r * sc_words;
+            reinterpret_cast<uint32_t *>(h.scales + rsc_s[r])[c] = sc_s[r * sw + c];
         }
         __syncthreads();
     }
