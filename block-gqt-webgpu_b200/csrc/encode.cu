@@ -263,6 +263,15 @@ struct WarpKey {
 // written to row dst_row of sequence dseq: same arithmetic and order as encode_kernel,
 // bit for bit - group sums and scales sequential per group (one lane per group), every
 // y_j one lane's sequential FMA chain over its group, ascending.
+// kSmem: the table pointers of h point into shared memory (plain loads; __ldg is for global
+// memory only).
+template <bool kSmem>
+__device__ __forceinline__ float table_load(const float *p) {
+    if constexpr (kSmem) return *p;
+    else return __ldg(p);
+}
+
+template <bool kSmem>
 __device__ __forceinline__ void warp_encode(const EncodeHead &h, uint32_t d, WarpKey &wk, uint32_t dseq,
                                             uint32_t dst_row, int lane) {
     const uint32_t ns = h.ns, ng = h.ng;
@@ -285,7 +294,7 @@ __device__ __forceinline__ void warp_encode(const EncodeHead &h, uint32_t d, War
         const float *rj = h.t.rot + (uint64_t)j * d;
         float y = 0.0f;
 #pragma unroll 8
-        for (uint32_t i = h.group_off[g]; i < h.group_off[g + 1]; ++i) y = fmaf(wk.xs[i], __ldg(rj + i), y);
+        for (uint32_t i = h.group_off[g]; i < h.group_off[g + 1]; ++i) y = fmaf(wk.xs[i], table_load<kSmem>(rj + i), y);
         float t = (y - h.t.off[j]) * h.t.inv[j];
         t = fminf(fmaxf(t, 0.0f), 255.0f);
         wk.codes[j] = h.t.lut[(uint32_t)h.t.cbidx[j] * 256u + (uint32_t)t];
@@ -340,7 +349,7 @@ __global__ void __launch_bounds__(kThreads) encode_warp_kernel(const __grid_cons
                                        : __ushort_as_half(static_cast<const uint16_t *>(a.src)[e]);
             wk.xs[i] = __half2float(x);
         }
-        warp_encode(h, d, wk, a.seq_first + s, (a.row0 ? a.row0[s] : a.row0_scalar) + rr, lane);
+        warp_encode<false>(h, d, wk, a.seq_first + s, (a.row0 ? a.row0[s] : a.row0_scalar) + rr, lane);
     }
     if (blockIdx.x == 0 && h.lengths) {
         for (uint32_t s = threadIdx.x; s < a.seq_count; s += kThreads)
@@ -362,13 +371,44 @@ __device__ __forceinline__ float src_elem(const void *p, uint64_t i, uint32_t f1
 // stream-ordered against earlier appends without host round trips; the last CTA to finish
 // bumps the lengths.
 
+//
+// stage_bytes != 0: every head's encode tables (rotation, codebooks, offsets, inverse scales,
+// code LUT, permutation, group and codebook indices: the leading part of its table blob, up to
+// the attention lookup) fit in stage_bytes of dynamic shared memory.  Each CTA copies its
+// head's part once with 16-byte loads and encodes from shared memory, so a key's dependent
+// table lookups cost shared-memory latency instead of one L2 round trip each.  The arithmetic
+// and its order are the same either way.
 __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_constant__ KvRopeArgs a, uint32_t d,
-                                                                  uint32_t total) {
+                                                                  uint32_t total, uint32_t stage_bytes) {
     constexpr int W = kThreads / 32;
     const uint32_t hd = blockIdx.y;
-    const EncodeHead &h = a.head[hd];
     __shared__ WarpKey wks[W];
     __shared__ float kr[W][kMaxDim];
+    extern __shared__ __align__(16) unsigned char tab_s[];
+    __shared__ __align__(16) unsigned char hs_raw[sizeof(EncodeHead)];
+    EncodeHead &hs = *reinterpret_cast<EncodeHead *>(hs_raw);
+    if (stage_bytes) {
+        const EncodeHead &g = a.head[hd];
+        const unsigned char *b = static_cast<const unsigned char *>(g.t.blob);
+        const uint32_t n16 = (uint32_t)(reinterpret_cast<const unsigned char *>(g.t.lookup) - b) / 16u;
+        for (uint32_t i = threadIdx.x; i < n16; i += kThreads)
+            reinterpret_cast<uint4 *>(tab_s)[i] = __ldg(reinterpret_cast<const uint4 *>(b) + i);
+        if (threadIdx.x == 0) {
+            hs = g;
+            hs.t.rot = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.rot) - b));
+            hs.t.cent = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.cent) - b));
+            hs.t.off = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.off) - b));
+            hs.t.inv = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.inv) - b));
+            hs.t.lut = tab_s + (g.t.lut - b);
+            hs.t.perm = tab_s + (g.t.perm - b);
+            hs.t.group_of = tab_s + (g.t.group_of - b);
+            hs.t.cbidx = tab_s + (g.t.cbidx - b);
+            hs.t.cb_base =
+                reinterpret_cast<const uint16_t *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.cb_base) - b));
+        }
+        __syncthreads();
+    }
+    const EncodeHead &h = stage_bytes ? hs : a.head[hd];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     WarpKey &wk = wks[w];
     const uint32_t pairs = d / 2;
@@ -393,7 +433,8 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
         }
         __syncwarp();
         for (uint32_t i = lane; i < d; i += 32) wk.xs[i] = __half2float(__float2half_rn(kr[w][h.t.perm[i]]));
-        warp_encode(h, d, wk, seq, pos, lane);
+        if (stage_bytes) warp_encode<true>(h, d, wk, seq, pos, lane);
+        else warp_encode<false>(h, d, wk, seq, pos, lane);
         // V row: FP32 -> FP16, chunk-swizzled for head dims 64 / 128
         __half *vrow = reinterpret_cast<__half *>(a.v[hd]) + (uint64_t)seq * a.v_seq_stride[hd] + (uint64_t)pos * a.vD;
         for (uint32_t e = lane; e < a.vD; e += 32) {
@@ -474,7 +515,28 @@ cudaError_t launch_kv_rope_append(const KvRopeArgs &a, uint32_t d, cudaStream_t 
     const uint32_t total = a.count * a.seq_count;
     if (!total) return cudaSuccess;
     const uint32_t blocks = (total + kThreads / 32 - 1) / (kThreads / 32);
-    kv_rope_append_kernel<<<dim3(blocks, a.heads), kThreads, 0, s>>>(a, d, total);
+    // Stage the tables when every head's encode part of its blob (the blob's layout puts the
+    // encode tables first, the attention lookup after them) fits in the default shared-memory
+    // window beside the kernel's static arrays.
+    constexpr uintptr_t kStageMax = 40u * 1024u;
+    uint32_t stage = 0;
+    for (uint32_t h = 0; h < a.heads; ++h) {
+        const DeviceTables &t = a.head[h].t;
+        const uintptr_t b = reinterpret_cast<uintptr_t>(t.blob), end = reinterpret_cast<uintptr_t>(t.lookup);
+        const uintptr_t ptrs[] = {reinterpret_cast<uintptr_t>(t.rot),   reinterpret_cast<uintptr_t>(t.cent),
+                                  reinterpret_cast<uintptr_t>(t.off),   reinterpret_cast<uintptr_t>(t.inv),
+                                  reinterpret_cast<uintptr_t>(t.lut),   reinterpret_cast<uintptr_t>(t.perm),
+                                  reinterpret_cast<uintptr_t>(t.group_of), reinterpret_cast<uintptr_t>(t.cbidx),
+                                  reinterpret_cast<uintptr_t>(t.cb_base)};
+        bool ok = b != 0 && end > b && end - b <= kStageMax && (b & 15u) == 0 && ((end - b) & 15u) == 0;
+        for (uintptr_t q : ptrs) ok = ok && q >= b && q < end;
+        if (!ok) {
+            stage = 0;
+            break;
+        }
+        stage = stage > (uint32_t)(end - b) ? stage : (uint32_t)(end - b);
+    }
+    kv_rope_append_kernel<<<dim3(blocks, a.heads), kThreads, stage, s>>>(a, d, total, stage);
     return cudaGetLastError();
 }
 
