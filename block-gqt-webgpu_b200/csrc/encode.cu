@@ -329,13 +329,43 @@ __device__ __forceinline__ void warp_encode(const EncodeHead &h, uint32_t d, War
     __syncwarp();
 }
 
+// Copies the encode tables of g (the leading part of its table blob, up to the attention
+// lookup) into tab_s with 16-byte loads and writes g with its table pointers moved there into
+// hs.  Called by every thread of the CTA; ends with a barrier.
+__device__ __forceinline__ void stage_head_tables(const EncodeHead &g, unsigned char *tab_s, EncodeHead &hs) {
+    const unsigned char *b = static_cast<const unsigned char *>(g.t.blob);
+    const uint32_t n16 = (uint32_t)(reinterpret_cast<const unsigned char *>(g.t.lookup) - b) / 16u;
+    for (uint32_t i = threadIdx.x; i < n16; i += blockDim.x)
+        reinterpret_cast<uint4 *>(tab_s)[i] = __ldg(reinterpret_cast<const uint4 *>(b) + i);
+    if (threadIdx.x == 0) {
+        hs = g;
+        hs.t.rot = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.rot) - b));
+        hs.t.cent = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.cent) - b));
+        hs.t.off = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.off) - b));
+        hs.t.inv = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.inv) - b));
+        hs.t.lut = tab_s + (g.t.lut - b);
+        hs.t.perm = tab_s + (g.t.perm - b);
+        hs.t.group_of = tab_s + (g.t.group_of - b);
+        hs.t.cbidx = tab_s + (g.t.cbidx - b);
+        hs.t.cb_base =
+            reinterpret_cast<const uint16_t *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.cb_base) - b));
+    }
+    __syncthreads();
+}
+
 // Few keys (a decode step appends one token per sequence): one warp per key, lanes over
 // dimensions, so a launch of a few hundred keys spreads over many SMs instead of a couple
 // of threads-per-key CTAs.
+// stage_bytes != 0: the head's encode tables are staged in shared memory first, as in
+// kv_rope_append_kernel.
 __global__ void __launch_bounds__(kThreads) encode_warp_kernel(const __grid_constant__ EncodeArgs a, uint32_t d,
-                                                               uint32_t total) {
+                                                               uint32_t total, uint32_t stage_bytes) {
     constexpr int W = kThreads / 32;
-    const EncodeHead &h = a.head[blockIdx.y];
+    extern __shared__ __align__(16) unsigned char tab_s[];
+    __shared__ __align__(16) unsigned char hs_raw[sizeof(EncodeHead)];
+    EncodeHead &hs = *reinterpret_cast<EncodeHead *>(hs_raw);
+    if (stage_bytes) stage_head_tables(a.head[blockIdx.y], tab_s, hs);
+    const EncodeHead &h = stage_bytes ? hs : a.head[blockIdx.y];
     __shared__ WarpKey wks[W];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t count = a.count;
@@ -349,7 +379,9 @@ __global__ void __launch_bounds__(kThreads) encode_warp_kernel(const __grid_cons
                                        : __ushort_as_half(static_cast<const uint16_t *>(a.src)[e]);
             wk.xs[i] = __half2float(x);
         }
-        warp_encode<false>(h, d, wk, a.seq_first + s, (a.row0 ? a.row0[s] : a.row0_scalar) + rr, lane);
+        const uint32_t dst_row = (a.row0 ? a.row0[s] : a.row0_scalar) + rr;
+        if (stage_bytes) warp_encode<true>(h, d, wk, a.seq_first + s, dst_row, lane);
+        else warp_encode<false>(h, d, wk, a.seq_first + s, dst_row, lane);
     }
     if (blockIdx.x == 0 && h.lengths) {
         for (uint32_t s = threadIdx.x; s < a.seq_count; s += kThreads)
@@ -387,27 +419,7 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
     extern __shared__ __align__(16) unsigned char tab_s[];
     __shared__ __align__(16) unsigned char hs_raw[sizeof(EncodeHead)];
     EncodeHead &hs = *reinterpret_cast<EncodeHead *>(hs_raw);
-    if (stage_bytes) {
-        const EncodeHead &g = a.head[hd];
-        const unsigned char *b = static_cast<const unsigned char *>(g.t.blob);
-        const uint32_t n16 = (uint32_t)(reinterpret_cast<const unsigned char *>(g.t.lookup) - b) / 16u;
-        for (uint32_t i = threadIdx.x; i < n16; i += kThreads)
-            reinterpret_cast<uint4 *>(tab_s)[i] = __ldg(reinterpret_cast<const uint4 *>(b) + i);
-        if (threadIdx.x == 0) {
-            hs = g;
-            hs.t.rot = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.rot) - b));
-            hs.t.cent = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.cent) - b));
-            hs.t.off = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.off) - b));
-            hs.t.inv = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.inv) - b));
-            hs.t.lut = tab_s + (g.t.lut - b);
-            hs.t.perm = tab_s + (g.t.perm - b);
-            hs.t.group_of = tab_s + (g.t.group_of - b);
-            hs.t.cbidx = tab_s + (g.t.cbidx - b);
-            hs.t.cb_base =
-                reinterpret_cast<const uint16_t *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.cb_base) - b));
-        }
-        __syncthreads();
-    }
+    if (stage_bytes) stage_head_tables(a.head[hd], tab_s, hs);
     const EncodeHead &h = stage_bytes ? hs : a.head[hd];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     WarpKey &wk = wks[w];
@@ -471,6 +483,29 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
     }
 }
 
+// Dynamic shared memory for staging every head's encode tables (the leading part of its
+// table blob: the blob puts the encode tables first, the attention lookup after them), or 0
+// when some head's part does not fit the default shared-memory window beside the warp-per-key
+// kernels' static arrays, or its pointers are not laid out that way.
+uint32_t encode_stage_bytes(const EncodeHead *heads, uint32_t n) {
+    constexpr uintptr_t kStageMax = 40u * 1024u;
+    uint32_t stage = 0;
+    for (uint32_t h = 0; h < n; ++h) {
+        const DeviceTables &t = heads[h].t;
+        const uintptr_t b = reinterpret_cast<uintptr_t>(t.blob), end = reinterpret_cast<uintptr_t>(t.lookup);
+        const uintptr_t ptrs[] = {reinterpret_cast<uintptr_t>(t.rot),   reinterpret_cast<uintptr_t>(t.cent),
+                                  reinterpret_cast<uintptr_t>(t.off),   reinterpret_cast<uintptr_t>(t.inv),
+                                  reinterpret_cast<uintptr_t>(t.lut),   reinterpret_cast<uintptr_t>(t.perm),
+                                  reinterpret_cast<uintptr_t>(t.group_of), reinterpret_cast<uintptr_t>(t.cbidx),
+                                  reinterpret_cast<uintptr_t>(t.cb_base)};
+        bool ok = b != 0 && end > b && end - b <= kStageMax && (b & 15u) == 0 && ((end - b) & 15u) == 0;
+        for (uintptr_t q : ptrs) ok = ok && q >= b && q < end;
+        if (!ok) return 0;
+        stage = stage > (uint32_t)(end - b) ? stage : (uint32_t)(end - b);
+    }
+    return stage;
+}
+
 template <int D>
 size_t encode_smem(uint32_t cent_alloc, uint32_t lut_bytes, uint32_t row_stride, uint32_t scale_stride) {
     const size_t ow = (row_stride / 4) | 1u, sw = scale_stride / 2 + 1;
@@ -515,27 +550,7 @@ cudaError_t launch_kv_rope_append(const KvRopeArgs &a, uint32_t d, cudaStream_t 
     const uint32_t total = a.count * a.seq_count;
     if (!total) return cudaSuccess;
     const uint32_t blocks = (total + kThreads / 32 - 1) / (kThreads / 32);
-    // Stage the tables when every head's encode part of its blob (the blob's layout puts the
-    // encode tables first, the attention lookup after them) fits in the default shared-memory
-    // window beside the kernel's static arrays.
-    constexpr uintptr_t kStageMax = 40u * 1024u;
-    uint32_t stage = 0;
-    for (uint32_t h = 0; h < a.heads; ++h) {
-        const DeviceTables &t = a.head[h].t;
-        const uintptr_t b = reinterpret_cast<uintptr_t>(t.blob), end = reinterpret_cast<uintptr_t>(t.lookup);
-        const uintptr_t ptrs[] = {reinterpret_cast<uintptr_t>(t.rot),   reinterpret_cast<uintptr_t>(t.cent),
-                                  reinterpret_cast<uintptr_t>(t.off),   reinterpret_cast<uintptr_t>(t.inv),
-                                  reinterpret_cast<uintptr_t>(t.lut),   reinterpret_cast<uintptr_t>(t.perm),
-                                  reinterpret_cast<uintptr_t>(t.group_of), reinterpret_cast<uintptr_t>(t.cbidx),
-                                  reinterpret_cast<uintptr_t>(t.cb_base)};
-        bool ok = b != 0 && end > b && end - b <= kStageMax && (b & 15u) == 0 && ((end - b) & 15u) == 0;
-        for (uintptr_t q : ptrs) ok = ok && q >= b && q < end;
-        if (!ok) {
-            stage = 0;
-            break;
-        }
-        stage = stage > (uint32_t)(end - b) ? stage : (uint32_t)(end - b);
-    }
+    const uint32_t stage = encode_stage_bytes(a.head, a.heads);
     kv_rope_append_kernel<<<dim3(blocks, a.heads), kThreads, stage, s>>>(a, d, total, stage);
     return cudaGetLastError();
 }
@@ -547,7 +562,8 @@ cudaError_t launch_encode(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, 
         // a warp per key: at most 4 keys per CTA, so even one sequence's token uses a CTA
         // and a decode step of a few hundred sequences spreads over the SMs
         const uint32_t blocks = (total + kThreads / 32 - 1) / (kThreads / 32);
-        encode_warp_kernel<<<dim3(blocks, a.heads), kThreads, 0, s>>>(a, d, total);
+        const uint32_t stage = encode_stage_bytes(a.head, a.heads);
+        encode_warp_kernel<<<dim3(blocks, a.heads), kThreads, stage, s>>>(a, d, total, stage);
         return cudaGetLastError();
     }
     if (d <= 16) return run_encode<16>(a, d, cent_alloc, max_ncb, s);
