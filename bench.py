@@ -23,6 +23,10 @@ Metric: decoded tokens/s (whole job).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   torchrun --nproc-per-node N bench.py --gpus N ...
+
+Other workloads (--workload): model-smollm2 / model-qwen (configs 2-3, full decode step),
+prefill (config 5, tensor-core causal prefill) and config1 (the parity case: latency of
+encoding 4096 keys at head_dim 128 plus one attention output, beside the CPU oracle).
 """
 from __future__ import annotations
 
@@ -58,7 +62,7 @@ def parse():
     ap.add_argument("--tables", choices=["config4", "calibration"], default="config4",
                     help="decode: config-4 tables for every head (the headline), or the 90 heads of the "
                          "reference's SmolLM2 calibration (30 layers x 3 KV heads)")
-    ap.add_argument("--workload", choices=["decode", "model-smollm2", "model-qwen", "prefill"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "model-smollm2", "model-qwen", "prefill", "config1"], default="decode",
                     help="decode: config 4 (the headline); model-*: configs 2/3; prefill: config 5")
     return ap.parse_args()
 
@@ -579,6 +583,95 @@ def run_prefill(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def run_config1(args, rank, world, local_rank):
+    """Config 1, the parity case: one head of 4096 keys at head_dim 128 (config-1 tables),
+    FP16 V, one FP32 query at position 4095, non-causal.  A step encodes all 4096 keys into
+    a fresh packed store, writes the 4096 V rows and computes the attention output.  It is
+    latency-bound (about 1.4 MB moved), so the metric is the step's latency.  value: device
+    inputs, CUDA-event timed; e2e: the same step from host NumPy buffers through the C ABI
+    (uploads and the output download inside the timed region).  Batch 1: replicas only."""
+    import torch
+    import bgtq
+    from bgtq import synthetic
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    z = np.load(ROOT / "tests" / "golden" / "config1.npz")
+    p = bgtq.BlockGTQParameters.from_arrays(z)
+    cfg, tab = bgtq.tables(p)
+    T, d = 4096, 128
+    k, q, v = synthetic.decode_workload(0, T, d)
+    keys, values = bgtq.PackedKeys((cfg, tab), T, device=local_rank), bgtq.Values(d, T, "f16", device=local_rank)
+    att = bgtq.GroupedAttention([keys], [values], 1)
+    k_dev = torch.from_numpy(k).to(dev)
+    v_dev = torch.from_numpy(v).to(dev)
+    q_dev = torch.from_numpy(q.reshape(1, 1, 1, d)).to(dev)
+    k_host, v_host, q_host = k.copy(), v.copy(), q.reshape(1, 1, 1, d).copy()
+    steps, warmup = max(args.steps, 20), max(args.warmup, 3)
+
+    def step_dev():
+        keys.reset()
+        values.reset()
+        keys.append(k_dev)
+        values.append(v_dev)
+        return att.attend(q_dev)
+
+    def step_host():
+        keys.reset()
+        values.reset()
+        keys.append(k_host)
+        values.append(v_host)
+        return att.attend(q_host)
+
+    dev_ms = _event_ms(step_dev, steps, warmup)
+    out_dev = step_dev().float().cpu().numpy().reshape(1, d)
+    for _ in range(warmup):
+        step_host()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        out_host = step_host()
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / steps
+    out_host = np.asarray(out_host).reshape(1, d)
+    ok = bool(np.allclose(out_dev, z["output"], atol=1e-5, rtol=1e-4) and np.array_equal(out_host, out_dev))
+    moved = T * (2 * d + p.row_bytes + 2 * p.groups) + T * (p.row_bytes + 2 * p.groups + 2 * d) + 2 * T * 2 * d
+    hbm, peak_src = peaks()
+    # the CPU oracle on the same step: encode + pack, reconstruct + attention
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    cpu = {}
+    for threads in (1, os.cpu_count() or 1):
+        t0 = time.perf_counter()
+        n = 0
+        while n < 3 or time.perf_counter() - t0 < 2.0:
+            enc = oracle.encode(cfg, tab, k.view(np.uint16), threads=threads)
+            kh = oracle.reconstruct(cfg, tab, enc["packed"], enc["scales"], threads=threads)
+            oracle.attention(q, kh, v, threads=threads)
+            n += 1
+        cpu[threads] = (time.perf_counter() - t0) * 1e3 / n
+    cores = max(cpu)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "config 1 step latency (encode 4096 keys + one attention output)", "value": dev_ms * 1e3,
+            "unit": "us", "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": dev_ms,
+            "higher_is_better": False, "scaling": "replicas only", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seed 0 decode workload, the config-1 golden fixture's inputs)",
+            "config": {"workload": "config 1: one head, 4096 keys, head_dim 128, FP16 V, one query at position 4095, "
+                                   "non-causal", "global_batch": 1, "seq_len": T, "parallelism": "replicas only",
+                       "l2": "inputs (1.4 MB) stay in L2: a latency measurement"},
+            "roofline": {"bound": "latency", "achieved": moved / (dev_ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": moved / (dev_ms * 1e-3) / 1e9 / hbm, "peak_source": peak_src,
+                         "bytes_per_step": moved},
+            "cpu_baseline": {"value": cpu[cores] * 1e3, "unit": "us", "cores": cores, "kind": "port",
+                             "single_thread_us": cpu[1] * 1e3,
+                             "sample": "the whole step (oracle encode + pack, reconstruct, attention)"},
+            "e2e": {"value": e2e_ms * 1e3, "unit": "us", "h2d_bytes_per_step": k_host.nbytes + v_host.nbytes +
+                    q_host.nbytes, "d2h_bytes_per_step": out_host.astype(np.float32).nbytes},
+            "gpu_launches": None,
+            "checks": {"output_within_1e-5_1e-4_of_golden": ok, "device_status": bgtq.device_status(local_rank)}}),
+            flush=True)
+    att.destroy()
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -591,6 +684,8 @@ def main():
         run_ours(args, rank, world, local_rank)
     elif args.workload == "prefill":
         run_prefill(args, rank, world, local_rank)
+    elif args.workload == "config1":
+        run_config1(args, rank, world, local_rank)
     else:
         run_model(args, rank, world, local_rank)
 
