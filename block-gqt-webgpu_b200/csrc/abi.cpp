@@ -323,6 +323,12 @@ bgtq_status bgtq_keys_create(bgtq_keys_kind kind, const bgtq_tables *tables, uin
         delete k;
         return fail(BGTQ_ECUDA, "cannot select device");
     }
+    // the device status word every kernel reports into exists once any store does, so
+    // entry points that must not allocate (bgtq_attend_static) always find it
+    if (!device_status_word(device)) {
+        delete k;
+        return fail(BGTQ_ENOMEM, "status word allocation failed");
+    }
     auto cleanup = [&](bgtq_status s, const std::string &m) {
         if (k->rows) cudaFree(k->rows);
         if (k->scales) cudaFree(k->scales);
@@ -420,6 +426,7 @@ bgtq_status bgtq_keys_append(bgtq_keys *k, const void *src, bgtq_dtype dtype, in
         a.seq_count = seq_count;
         a.heads = 1;
         a.src_f32 = dtype == BGTQ_F32;
+        a.status = device_status_word(k->device);
         e = launch_encode(a, k->dim, (uint32_t)k->L.cent_compact.size() + 256u, k->L.ncb, stream);
     } else {
         e = launch_copy_rows(k->rows, (uint64_t)k->cap_alloc * k->D, k->D, 0, dsrc, drow, dseq, dtype == BGTQ_F32, row0,
@@ -656,6 +663,10 @@ bgtq_status bgtq_values_create(bgtq_dtype dtype, uint32_t dim, uint32_t capacity
     v->cap_alloc = round_up(capacity, kTileRows);
     v->sequences = sequences;
     DeviceGuard g(device);
+    if (!device_status_word(device)) {
+        delete v;
+        return fail(BGTQ_ENOMEM, "status word allocation failed");
+    }
     const size_t es = dtype == BGTQ_F16 ? 2 : 4;
     const size_t bytes = (size_t)sequences * v->cap_alloc * v->D * es;
     if (cudaMalloc(&v->data, bytes) != cudaSuccess) {
@@ -807,7 +818,7 @@ void bgtq_attention_destroy(bgtq_attention *a) {
 
 }  // extern "C"
 
-namespace {
+namespace bgtq {
 // Kernel arguments of one packed-key head with its value store.
 void fill_packed_head(AttnHead &ah, const bgtq_keys *k, const bgtq_values *v) {
     const size_t vsz = v->dtype == BGTQ_F32 ? 4 : 2;
@@ -833,7 +844,7 @@ void fill_packed_head(AttnHead &ah, const bgtq_keys *k, const bgtq_values *v) {
     for (int gi = 0; gi <= kMaxGroups; ++gi) ah.group_off[gi] = k->L.group_off[gi];
     for (uint32_t j = 0; j < (uint32_t)kMaxDim; ++j) ah.cb_base[j] = j < k->dim ? k->L.cb_base[j] : (uint16_t)ah.n_cent;
 }
-}  // namespace
+}  // namespace bgtq
 
 extern "C" {
 

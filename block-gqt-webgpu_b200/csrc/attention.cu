@@ -12,13 +12,22 @@ using attn::Plan;
 struct Entry {
     cudaError_t (*run)(const AttnArgs &, const Plan &, uint32_t, dim3, cudaStream_t);
     int (*occ)(const Plan &);
+    cudaError_t (*load)();
     uint32_t qp, qm;
 };
 
+// Makes the driver load the kernel's code now (with lazy module loading it would load,
+// and take device memory, on its first launch).
+template <int D, int QM, KKind KK, bool VF32>
+cudaError_t load_kernel() {
+    cudaFuncAttributes fa;
+    return cudaFuncGetAttributes(&fa, attn::attn_kernel<D, QM, KK, VF32>);
+}
+
 template <int D, int QM, KKind KK, bool VF32>
 Entry entry() {
-    return Entry{&attn::run<D, QM, KK, VF32>, &attn::occupancy<D, QM, KK, VF32>, (uint32_t)attn::QPad<QM>::QP,
-                 (uint32_t)QM};
+    return Entry{&attn::run<D, QM, KK, VF32>, &attn::occupancy<D, QM, KK, VF32>, &load_kernel<D, QM, KK, VF32>,
+                 (uint32_t)attn::QPad<QM>::QP, (uint32_t)QM};
 }
 
 template <int D, KKind KK, bool VF32>
@@ -98,6 +107,15 @@ uint32_t attention_tile_tokens(uint32_t d) {
         case 64: return attn::Geo<64>::TT;
         default: return attn::Geo<128>::TT;
     }
+}
+
+cudaError_t preload_attention_kernels(KKind kk) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, attn::qrot_kernel);
+    for (uint32_t D : {16u, 32u, 64u, 128u})
+        for (uint32_t rows : {1u, 2u, 3u, 4u, 8u})
+            for (int vf = 0; vf < 2 && e == cudaSuccess; ++vf) e = pick_entry(kk, vf, D, rows).load();
+    return e;
 }
 
 size_t attention_smem_bytes(KKind kk, int v_f32, uint32_t d, uint32_t rows, uint32_t row_stride,

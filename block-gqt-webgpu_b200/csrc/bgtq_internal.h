@@ -100,6 +100,7 @@ struct EncodeArgs {
     uint32_t row0_scalar;
     uint32_t count, seq_first, seq_count, heads;
     int src_f32;
+    uint32_t *status;                 // device status word (bounded-wait timeouts), nullable
 };
 
 // Model-path append: RoPE'd K and V of `count` tokens per sequence for `heads` KV heads,
@@ -205,6 +206,9 @@ cudaError_t launch_prefill(const PrefillArgs &a, uint32_t max_cent, int umma, cu
 cudaError_t launch_prefill_tc(const PrefillArgs &a, uint32_t max_cent, cudaStream_t s);
 cudaError_t launch_probs(const float *logits, const float *lse, float *probs, uint64_t rows, uint32_t tokens,
                          uint32_t stride, cudaStream_t s);
+// Loads the code of every generic decode-attention kernel for keys of kind kk (and the
+// query rotation) on the current device, so that later launches load nothing.
+cudaError_t preload_attention_kernels(KKind kk);
 // Shared-memory bytes the attention kernel needs for a launch; 0 if unsupported.
 size_t attention_smem_bytes(KKind kk, int v_f32, uint32_t d, uint32_t rows_bound, uint32_t row_stride,
                             uint32_t scale_stride, uint32_t max_cent);

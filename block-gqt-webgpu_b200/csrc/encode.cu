@@ -329,15 +329,47 @@ __device__ __forceinline__ void warp_encode(const EncodeHead &h, uint32_t d, War
     __syncwarp();
 }
 
-// Copies the encode tables of g (the leading part of its table blob, up to the attention
-// lookup) into tab_s with 16-byte loads and writes g with its table pointers moved there into
-// hs.  Called by every thread of the CTA; ends with a barrier.
-__device__ __forceinline__ void stage_head_tables(const EncodeHead &g, unsigned char *tab_s, EncodeHead &hs) {
+// Bound on the polls of the table-staging mbarrier (a copy of at most 40 KB lands in
+// microseconds; the bound only keeps a broken copy from hanging the kernel).
+constexpr uint32_t kStageWaitLimit = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ bool stage_try_wait(uint32_t bar) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool stage_wait(uint32_t bar) {
+    for (uint32_t i = 0; i < kStageWaitLimit; ++i)
+        if (stage_try_wait(bar)) return true;
+    return false;
+}
+
+// Starts the copy of the encode tables of g (the leading part of its table blob, up to the
+// attention lookup; 16-byte aligned, a multiple of 16 bytes) into tab_s with one bulk
+// asynchronous copy (cp.async.bulk, no multicast) that completes on the mbarrier at bar, and
+// writes g with its table pointers moved there into hs.  Called by every thread of the CTA;
+// ends with a barrier, after which the threads wait on bar (stage_wait) before reading tab_s.
+__device__ __forceinline__ void stage_head_tables(const EncodeHead &g, unsigned char *tab_s, EncodeHead &hs,
+                                                  uint64_t *bar) {
     const unsigned char *b = static_cast<const unsigned char *>(g.t.blob);
-    const uint32_t n16 = (uint32_t)(reinterpret_cast<const unsigned char *>(g.t.lookup) - b) / 16u;
-    for (uint32_t i = threadIdx.x; i < n16; i += blockDim.x)
-        reinterpret_cast<uint4 *>(tab_s)[i] = __ldg(reinterpret_cast<const uint4 *>(b) + i);
     if (threadIdx.x == 0) {
+        const uint32_t bytes = (uint32_t)(reinterpret_cast<const unsigned char *>(g.t.lookup) - b);
+        const uint32_t ba = smem_addr(bar);
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(ba) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(ba), "r"(bytes) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         smem_addr(tab_s)),
+                     "l"(b), "r"(bytes), "r"(ba)
+                     : "memory");
         hs = g;
         hs.t.rot = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.rot) - b));
         hs.t.cent = reinterpret_cast<const float *>(tab_s + (reinterpret_cast<const unsigned char *>(g.t.cent) - b));
@@ -353,6 +385,20 @@ __device__ __forceinline__ void stage_head_tables(const EncodeHead &g, unsigned 
     __syncthreads();
 }
 
+// After stage_head_tables: true when the whole warp saw the staged tables land (then it
+// reads them from shared memory).  A warp whose bounded wait ran out reports it in status and
+// reads the global tables instead (same values, so the result is unchanged).
+__device__ __forceinline__ bool staged_tables_ready(uint64_t *bar, uint32_t *status) {
+    const bool ok = __all_sync(0xffffffffu, stage_wait(smem_addr(bar)));
+    if (!ok && (threadIdx.x & 31) == 0 && status) atomicOr(status, kStatusWaitTimeout);
+    return ok;
+}
+// Before a CTA that staged tables exits: a warp whose wait ran out waits (bounded) once more,
+// so no copy into its shared memory is left in flight when it can.
+__device__ __forceinline__ void staged_tables_drain(uint64_t *bar, bool ready) {
+    if (!ready) stage_wait(smem_addr(bar));
+}
+
 // Few keys (a decode step appends one token per sequence): one warp per key, lanes over
 // dimensions, so a launch of a few hundred keys spreads over many SMs instead of a couple
 // of threads-per-key CTAs.
@@ -364,8 +410,10 @@ __global__ void __launch_bounds__(kThreads) encode_warp_kernel(const __grid_cons
     extern __shared__ __align__(16) unsigned char tab_s[];
     __shared__ __align__(16) unsigned char hs_raw[sizeof(EncodeHead)];
     EncodeHead &hs = *reinterpret_cast<EncodeHead *>(hs_raw);
-    if (stage_bytes) stage_head_tables(a.head[blockIdx.y], tab_s, hs);
-    const EncodeHead &h = stage_bytes ? hs : a.head[blockIdx.y];
+    __shared__ __align__(8) uint64_t stage_bar;
+    if (stage_bytes) stage_head_tables(a.head[blockIdx.y], tab_s, hs, &stage_bar);
+    const bool staged = stage_bytes && staged_tables_ready(&stage_bar, a.status);
+    const EncodeHead &h = staged ? hs : a.head[blockIdx.y];
     __shared__ WarpKey wks[W];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t count = a.count;
@@ -380,9 +428,10 @@ __global__ void __launch_bounds__(kThreads) encode_warp_kernel(const __grid_cons
             wk.xs[i] = __half2float(x);
         }
         const uint32_t dst_row = (a.row0 ? a.row0[s] : a.row0_scalar) + rr;
-        if (stage_bytes) warp_encode<true>(h, d, wk, a.seq_first + s, dst_row, lane);
+        if (staged) warp_encode<true>(h, d, wk, a.seq_first + s, dst_row, lane);
         else warp_encode<false>(h, d, wk, a.seq_first + s, dst_row, lane);
     }
+    if (stage_bytes) staged_tables_drain(&stage_bar, staged);
     if (blockIdx.x == 0 && h.lengths) {
         for (uint32_t s = threadIdx.x; s < a.seq_count; s += kThreads)
             h.lengths[a.seq_first + s] = (a.row0 ? a.row0[s] : a.row0_scalar) + count;
@@ -419,8 +468,10 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
     extern __shared__ __align__(16) unsigned char tab_s[];
     __shared__ __align__(16) unsigned char hs_raw[sizeof(EncodeHead)];
     EncodeHead &hs = *reinterpret_cast<EncodeHead *>(hs_raw);
-    if (stage_bytes) stage_head_tables(a.head[hd], tab_s, hs);
-    const EncodeHead &h = stage_bytes ? hs : a.head[hd];
+    __shared__ __align__(8) uint64_t stage_bar;
+    if (stage_bytes) stage_head_tables(a.head[hd], tab_s, hs, &stage_bar);
+    const bool staged = stage_bytes && staged_tables_ready(&stage_bar, a.status);
+    const EncodeHead &h = staged ? hs : a.head[hd];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     WarpKey &wk = wks[w];
     const uint32_t pairs = d / 2;
@@ -445,7 +496,7 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
         }
         __syncwarp();
         for (uint32_t i = lane; i < d; i += 32) wk.xs[i] = __half2float(__float2half_rn(kr[w][h.t.perm[i]]));
-        if (stage_bytes) warp_encode<true>(h, d, wk, seq, pos, lane);
+        if (staged) warp_encode<true>(h, d, wk, seq, pos, lane);
         else warp_encode<false>(h, d, wk, seq, pos, lane);
         // V row: FP32 -> FP16, chunk-swizzled for head dims 64 / 128
         __half *vrow = reinterpret_cast<__half *>(a.v[hd]) + (uint64_t)seq * a.v_seq_stride[hd] + (uint64_t)pos * a.vD;
@@ -459,6 +510,7 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
             vrow[de] = __float2half_rn(x);
         }
     }
+    if (stage_bytes) staged_tables_drain(&stage_bar, staged);
     // The last CTA to finish moves every store's lengths on.  Each CTA read its start rows
     // before taking a ticket, so none reads a bumped length; the ticket is left at zero for
     // the next launch (or graph replay).

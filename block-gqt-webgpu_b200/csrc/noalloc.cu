@@ -2,22 +2,27 @@
 //
 // Who needs it: callers that run attention where they must not (or cannot) allocate -
 // a serving process that hands all free device memory to its own pool once the KV
-// caches exist, a plugin whose host framework owns every device allocation, or code
-// that runs while a stream is being captured, where cudaMalloc is not permitted.  The
-// regular path (bgtq_attention_create + bgtq_attend) keeps per-object workspace that is
-// allocated when the object is created; this entry point needs no attention object and
-// takes its scratch from one fixed array compiled into the library instead.
+// caches exist, or a plugin whose host framework owns every device allocation and
+// forbids the plugin's own cudaMalloc.  The regular path (bgtq_attention_create +
+// bgtq_attend) keeps per-object workspace that is allocated when the object is created;
+// this entry point needs no attention object and takes its scratch from one fixed array
+// compiled into the library instead.
 //
-// Scratch: g_scratch below, kScratchBytes (4 MiB + 64.25 KiB) in every GPU that loads the
+// Scratch: g_scratch below, kScratchBytes (4 MiB + 64 KiB) in every GPU that loads the
 // library, held until the process exits.  It holds the split-KV partial results, the
 // per-(sequence, head) completion tickets and the rotated query records.  Every call
 // shares it, so calls whose kernels overlap on the GPU (different streams, or different
 // host threads on one device) race and must be serialised by the caller.  The tickets
 // must start at zero and are cleared with cudaMemsetAsync at the start of every call.
+// Bounded-wait timeouts go to the library's device status word (bgtq_device_status),
+// which exists as soon as any key or value store does.
 //
-// Set-up: the first call on each device looks up the device address of g_scratch with
-// cudaGetSymbolAddress while that device is current, and caches it.  Make that first call
-// outside any stream capture.
+// Set-up: the first call on each device (that device current) looks up the device
+// address of g_scratch with cudaGetSymbolAddress and has the driver load the code of
+// every kernel this entry point can launch, so later calls load nothing; both results
+// are kept per device for the life of the process.  Make that first call before any
+// stream capture starts, and do not keep using the library on a device across a
+// cudaDeviceReset (the kept address belongs to the old context).
 #include <algorithm>
 #include <cstring>
 #include <mutex>
@@ -29,8 +34,7 @@ namespace {
 constexpr size_t kPartFloats = 3u << 18;   // split-KV partials: 786,432 floats (3 MiB)
 constexpr size_t kQtFloats = 1u << 18;     // query records: 262,144 floats (1 MiB)
 constexpr size_t kTickets = 1u << 14;      // (sequence, head) tickets: 16,384 (64 KiB)
-constexpr size_t kStatusWords = 64;        // fallback device status word (+ padding)
-constexpr size_t kScratchBytes = (kPartFloats + kQtFloats + kTickets + kStatusWords) * 4;
+constexpr size_t kScratchBytes = (kPartFloats + kQtFloats + kTickets) * 4;
 
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
@@ -45,13 +49,16 @@ bgtq_status fail(bgtq_status s, const std::string &m) {
 uint32_t dim_template(uint32_t d) { return d <= 16 ? 16u : d <= 32 ? 32u : d <= 64 ? 64u : 128u; }
 uint32_t rows_pad(uint32_t r) { return r <= 1 ? 1u : r <= 2 ? 2u : r <= 4 ? 4u : 8u; }
 
-// Device address of g_scratch on `device` (which must be current); looked up once.
+// Set-up on `device` (which must be current), once: the device address of g_scratch, and
+// the code of every generic packed-key attention kernel loaded.
 cudaError_t scratch_address(int device, void **out) {
     if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(g_mu);
     if (!g_scratch_addr[device]) {
         void *p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+        if (e != cudaSuccess) return e;
+        e = bgtq::preload_attention_kernels(bgtq::KKind::Packed);
         if (e != cudaSuccess) return e;
         g_scratch_addr[device] = p;
     }
@@ -119,31 +126,8 @@ extern "C" bgtq_status bgtq_attend_static(uint32_t heads, bgtq_keys *const *keys
     std::memset(&a, 0, sizeof(a));
     uint32_t max_cent = 0;
     for (uint32_t h = 0; h < heads; ++h) {
-        const bgtq_keys *k = keys[h];
-        const bgtq_values *v = values[h];
-        AttnHead &ah = a.head[h];
-        ah.v = v->data;
-        ah.v_seq_stride = (uint64_t)v->cap_alloc * v->D * (v->dtype == BGTQ_F32 ? 4 : 2);
-        ah.k = k->rows;
-        ah.k_seq_stride = (uint64_t)k->cap_alloc * k->row_stride;
-        ah.row_stride = k->row_stride;
-        ah.scales = k->scales;
-        ah.s_seq_stride = (uint64_t)k->cap_alloc * k->scale_stride;
-        ah.scale_stride = k->scale_stride;
-        ah.rot = k->dt.rot;
-        ah.cent = k->dt.cent;
-        ah.perm = k->dt.perm;
-        ah.group_of = k->dt.group_of;
-        ah.ns = k->L.ns;
-        ah.ng = k->L.ng;
-        ah.n_cent = (uint32_t)k->L.cent_compact.size();
-        ah.lookup = k->dt.lookup;
-        ah.lookup_off = k->dt.lookup_off;
-        ah.n_lookup = (uint32_t)k->L.lookup.size();
-        for (int i = 0; i < 4; ++i) ah.bound_mask[i] = k->L.bound_mask[i];
-        for (int g = 0; g <= kMaxGroups; ++g) ah.group_off[g] = k->L.group_off[g];
-        for (uint32_t j = 0; j < (uint32_t)kMaxDim; ++j) ah.cb_base[j] = j < d ? k->L.cb_base[j] : (uint16_t)ah.n_cent;
-        max_cent = std::max(max_cent, ah.n_lookup);
+        fill_packed_head(a.head[h], keys[h], values[h]);
+        max_cent = std::max(max_cent, a.head[h].n_lookup);
     }
     a.q = q;
     a.qt = qt;
@@ -152,10 +136,10 @@ extern "C" bgtq_status bgtq_attend_static(uint32_t heads, bgtq_keys *const *keys
     a.out = out;
     a.part = part;
     a.counters = tickets;
-    // report bounded-wait timeouts through the library's status word when it already
-    // exists (bgtq_device_status reads it); otherwise into a word of the scratch
+    // bounded-wait timeouts go to the library's status word (bgtq_device_status), which
+    // the key stores created when they were made
     a.status = device_status_word_if_present(k0->device);
-    if (!a.status) a.status = tickets + kTickets;
+    if (!a.status) return fail(BGTQ_ECUDA, "device status word missing");
     a.seq_first = seq_first;
     a.seq_count = seq_count;
     a.heads = heads;

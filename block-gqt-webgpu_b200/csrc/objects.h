@@ -75,3 +75,9 @@ struct bgtq_attention {
     bool use_rope = false;
     bool plan_capacity = false;   // split plan for the keys' capacity (graph replays)
 };
+
+namespace bgtq {
+// Kernel arguments of one packed-key head with its value store (every attention entry
+// point over packed keys fills its heads through this one function).
+void fill_packed_head(AttnHead &ah, const bgtq_keys *k, const bgtq_values *v);
+}  // namespace bgtq

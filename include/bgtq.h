@@ -331,18 +331,21 @@ bgtq_status bgtq_attention_last_launches(const bgtq_attention *a, uint32_t *laun
 /* Attention without any device allocation (no counterpart in the reference, which has
  * no such constraint).  For callers that must not allocate device memory when they run
  * attention: a server whose memory pool has taken all free device memory once the
- * caches exist, a plugin inside a framework that owns every device allocation, or work
- * recorded while a stream is being captured, where cudaMalloc is not allowed.  It needs
- * no bgtq_attention object: `heads` packed key stores and their value stores (same
- * rules as bgtq_attention_create) are attended directly, with device pointers only
- * (q/positions/out as in bgtq_attend; no logit capture).  Scratch comes from one fixed
- * 4 MiB array inside the library on every GPU that loads it, kept until the process
- * exits: at most 262,144 floats of query records (sequences x heads x padded dim x padded
- * rows; padded dim is 16/32/64/128, padded rows 1/2/4/8) - larger requests fail with
- * BGTQ_EINVAL - and the split-KV factor is limited to what 3 MiB of partials hold.  All
- * calls share that array: calls whose kernels may overlap on the GPU race, so serialise
- * them (one stream per device).  The first call on a device looks up the array's address
- * (cudaGetSymbolAddress) and should be made before any stream capture starts. */
+ * caches exist, or a plugin inside a framework that owns every device allocation and
+ * forbids the plugin's own cudaMalloc.  It needs no bgtq_attention object: `heads` packed
+ * key stores and their value stores (same rules as bgtq_attention_create) are attended
+ * directly, with device pointers only (q/positions/out as in bgtq_attend; no logit
+ * capture; always the generic, ahead-of-time compiled kernel).  Scratch comes from one
+ * fixed array of 4 MiB + 64 KiB inside the library on every GPU that loads it, kept until
+ * the process exits: at most 262,144 floats of query records (sequences x heads x padded
+ * dim x padded rows; padded dim is 16/32/64/128, padded rows 1/2/4/8) and 16,384
+ * (sequence, head) pairs - larger requests fail with BGTQ_EINVAL - and the split-KV
+ * factor is limited to what 3 MiB of partials hold.  All calls share that array and it
+ * keeps the last call's contents: calls whose kernels may overlap on the GPU race, so
+ * serialise them (one stream per device).  The first call on a device does the set-up
+ * (looks up the array's address with cudaGetSymbolAddress and loads the code of every
+ * kernel this call can launch); make it before any stream capture starts.  Do not use it
+ * on a device across a cudaDeviceReset. */
 bgtq_status bgtq_attend_static(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, const float *q,
                                const uint32_t *positions, int causal, uint32_t rows, uint32_t seq_first,
                                uint32_t seq_count, float *out, void *stream);
