@@ -94,6 +94,9 @@ class Decoder:
     each a (config u32, table f32) pair in the reference's flattened format.
     compute: torch dtype of the activations and GEMMs (float32 mirrors the reference's FP32
     shaders; float16 runs the GEMMs on FP16 tensor cores with FP32 accumulation).
+    fused: decode steps (one token per sequence, batch <= 8, FP16 weights, FP32 compute) run
+    the library's fused weight-streaming kernels on the FP16 weights (bgtq_model_gemv):
+    seven launches per layer instead of about a dozen torch / cuBLAS ones.
 
     Per layer: RMSNorm, one fused Q/K/V GEMM, one library call that applies RoPE to the new
     keys, encodes them into the packed stores and appends the FP16 values
@@ -104,7 +107,7 @@ class Decoder:
     """
 
     def __init__(self, weights, geometry: ModelGeometry, capacity: int, tables, batch: int = 1,
-                 compute=None, device: int = 0):
+                 compute=None, device: int = 0, fused: bool = True):
         import torch
         from . import _lib
         g = geometry
@@ -115,6 +118,12 @@ class Decoder:
         self.g, self.capacity, self.batch, self.length = g, int(capacity), int(batch), 0
         self.compute = compute or torch.float32
         self.dev = torch.device("cuda", device)
+        # decode steps of a few sequences run the fused weight-streaming kernels on the FP16
+        # weights (bgtq_model_gemv); they need FP16 checkpoints and FP32 compute
+        self.fused = bool(fused) and self.compute == torch.float32 and batch <= 8 and all(
+            v.dtype == torch.float16 for v in weights.values())
+        if self.fused:
+            w16 = {k: v.to(self.dev, torch.float16) for k, v in weights.items()}
         w = {k: v.to(self.dev, self.compute) for k, v in weights.items()}
         self.emb, self.final_norm = w["model.embed_tokens.weight"], w["model.norm.weight"]
         self.layers = []
@@ -127,6 +136,17 @@ class Decoder:
             self.layers.append(dict(ln1=w[p + "input_layernorm.weight"], ln2=w[p + "post_attention_layernorm.weight"],
                                     qkv=qkv, qkv_b=bias, o=w[p + "self_attn.o_proj.weight"], gate_up=gate_up,
                                     down=w[p + "mlp.down_proj.weight"]))
+        self.layers16 = []
+        if self.fused:
+            for layer in range(g.layers):
+                p = f"model.layers.{layer}."
+                self.layers16.append(dict(
+                    qkv=torch.cat([w16[p + f"self_attn.{n}.weight"] for n in ("q_proj", "k_proj", "v_proj")]).contiguous(),
+                    o=w16[p + "self_attn.o_proj.weight"].contiguous(),
+                    gate_up=torch.cat([w16[p + "mlp.gate_proj.weight"], w16[p + "mlp.up_proj.weight"]]).contiguous(),
+                    down=w16[p + "mlp.down_proj.weight"].contiguous()))
+            self.emb16 = w16["model.embed_tokens.weight"].contiguous()
+            del w16
         del w
         pairs = g.head_dim // 2
         # inv_freq as the reference's rope kernel raises theta (kernels.wgsl:52), FP32
@@ -169,6 +189,8 @@ class Decoder:
                 raise ValueError("Invalid tokens/capacity")  # decoder.ts:33
         start = self.length
         st = torch.cuda.current_stream(self.dev).cuda_stream
+        if n == 1 and self.fused:
+            return self._decode_fused(tokens, st)
         qw, kvw = g.q_heads * g.head_dim, g.kv_heads * g.head_dim
         row = qw + 2 * kvw
         h = self.emb[tokens]                                             # [B, n, hidden]
@@ -193,6 +215,45 @@ class Decoder:
         last = self._norm(h[:, -1], self.final_norm)
         self.length += n
         return (last @ self.emb.t()).float()
+
+    def _decode_fused(self, tokens, st):
+        """One token per sequence through the fused decode kernels: per layer RMSNorm + Q/K/V
+        (+ bias) in one GEMV, the RoPE + encode + V append launch, attention, o_proj with the
+        residual add, RMSNorm + gate/up + SiLU gating in one GEMV, down_proj with the residual
+        add; then the final RMSNorm + tied lm_head in one GEMV (decoder.ts:31-81,
+        kernels.wgsl:11-54)."""
+        import ctypes as C
+        import torch
+        from . import _lib
+        g = self.g
+        B = tokens.shape[0]
+        qw, kvw = g.q_heads * g.head_dim, g.kv_heads * g.head_dim
+        row = qw + 2 * kvw
+        h = self.emb[tokens[:, 0]].contiguous()                         # [B, hidden] residual stream
+        qkv = torch.empty((B, row), device=self.dev, dtype=torch.float32)
+        act = torch.empty((B, g.intermediate), device=self.dev, dtype=torch.float32)
+        sp = C.c_void_p(st)
+
+        def gemv(mode, x, in_dim, norm, w16, bias, out_dim, y):
+            _lib.call("bgtq_model_gemv", mode, C.c_void_p(x.data_ptr()), B, x.stride(0), in_dim,
+                      None if norm is None else C.c_void_p(norm.data_ptr()), C.c_float(g.rms_eps),
+                      C.c_void_p(w16.data_ptr()), None if bias is None else C.c_void_p(bias.data_ptr()), out_dim,
+                      C.c_void_p(y.data_ptr()), y.stride(0), sp)
+
+        for layer, (lw, l16) in enumerate(zip(self.layers, self.layers16)):
+            gemv(0, h, g.hidden, lw["ln1"], l16["qkv"], lw["qkv_b"], row, qkv)
+            kp, vp = self._kv_ptrs[layer]
+            _lib.call("bgtq_append_kv_rope", g.kv_heads, kp, vp, C.c_void_p(qkv.data_ptr()), row, row, qw,
+                      qw + kvw, 1, 0, B, self.inv_freq.ctypes.data, sp)
+            q = qkv[:, :qw].reshape(B, g.kv_heads, g.gqa, g.head_dim).contiguous()
+            att = self.attn[layer].attend(q).reshape(B, g.hidden)
+            gemv(1, att, g.hidden, None, l16["o"], None, g.hidden, h)
+            gemv(2, h, g.hidden, lw["ln2"], l16["gate_up"], None, g.intermediate, act)
+            gemv(1, act, g.intermediate, None, l16["down"], None, g.hidden, h)
+        logits = torch.empty((B, g.vocab), device=self.dev, dtype=torch.float32)
+        gemv(0, h, g.hidden, self.final_norm, self.emb16, None, g.vocab, logits)
+        self.length += 1
+        return logits
 
     def prefill(self, tokens, chunk: int | None = None):
         """decoder.ts:82: the prompt in chunks; returns the last chunk's logits."""

@@ -1,9 +1,10 @@
 """Multi-rank plumbing of the batched decode workload: one process per GPU.
 
 The workload shards by sequence (every sequence's cache lives on one rank), so the data
-path has no collective.  What the ranks share is bookkeeping: which global sequences a
-rank owns, a barrier around timed regions, the maximum of the per-rank timings, and a
-gather of per-rank output checksums for verification.  The helpers take the
+path has no collective.  What the ranks share: which global sequences a rank owns (a
+contiguous share of one batch), a barrier around timed regions, the maximum of the
+per-rank timings, and, after the timed region, the gather of every rank's attention
+outputs to rank 0 with exact per-rank checksums that prove the gathered copy.  The helpers take the
 ``torch.distributed`` module and the device of the collective tensors, so the same code
 runs over NCCL on GPUs and over gloo on CPU (the tests).
 """
@@ -67,6 +68,49 @@ def gather_checksums(tensors, dist, device):
     out = [torch.zeros_like(s) for _ in range(dist.get_world_size())]
     dist.all_gather(out, s)
     return [float(o) for o in out]
+
+
+def bit_checksum(x) -> int:
+    """Order-independent exact checksum of a tensor's bits: the sum of its 32-bit words as
+    int64 (integer addition, so every device and reduction order gives the same value)."""
+    import torch
+    t = x.contiguous().view(-1)
+    words = t.view(torch.int32) if t.element_size() == 4 else t.view(torch.int16)
+    return int(words.to(torch.int64).sum())
+
+
+def gather_to_root(x, counts, dist, device, dim: int = 0):
+    """Gather every rank's ``x`` to rank 0 along ``dim``: rank r holds ``counts[r]`` entries
+    of that dimension (a contiguous share of the batch, ``split_range``).  Returns the
+    concatenation in rank order on rank 0 and None elsewhere; a single process returns
+    ``x`` itself.  Shares are padded to the largest count so one collective carries them."""
+    import torch
+    if dist is None:
+        return x
+    world, rank = dist.get_world_size(), dist.get_rank()
+    if len(counts) != world or x.shape[dim] != counts[rank]:
+        raise ValueError("counts must give every rank's share of the gathered dimension")
+    width = max(counts)
+    shape = list(x.shape)
+    shape[dim] = width
+    padded = torch.zeros(shape, dtype=x.dtype, device=device)
+    padded.narrow(dim, 0, counts[rank]).copy_(x)
+    parts = [torch.empty_like(padded) for _ in range(world)] if rank == 0 else None
+    dist.gather(padded, gather_list=parts, dst=0)
+    if rank != 0:
+        return None
+    return torch.cat([p.narrow(dim, 0, c) for p, c in zip(parts, counts)], dim=dim)
+
+
+def gather_ints(values, dist, device):
+    """Every rank's list of Python ints (equal lengths), in rank order, on every rank."""
+    import torch
+    t = torch.tensor([int(v) for v in values], dtype=torch.int64, device=device)
+    if dist is None:
+        return [[int(v) for v in t.cpu()]]
+    out = [torch.zeros_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(out, t)
+    return [[int(v) for v in o.cpu()] for o in out]
 
 
 def barrier(dist, synchronize=None):

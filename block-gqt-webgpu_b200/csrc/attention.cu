@@ -109,6 +109,8 @@ uint32_t attention_tile_tokens(uint32_t d) {
     }
 }
 
+uint32_t attention_qm(KKind kk, uint32_t rows) { return pick_entry(kk, 0, 64, rows).qm; }
+
 cudaError_t preload_attention_kernels(KKind kk) {
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, attn::qrot_kernel);

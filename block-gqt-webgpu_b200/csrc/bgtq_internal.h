@@ -206,6 +206,8 @@ cudaError_t launch_prefill(const PrefillArgs &a, uint32_t max_cent, int umma, cu
 cudaError_t launch_prefill_tc(const PrefillArgs &a, uint32_t max_cent, cudaStream_t s);
 cudaError_t launch_probs(const float *logits, const float *lse, float *probs, uint64_t rows, uint32_t tokens,
                          uint32_t stride, cudaStream_t s);
+// Query rows per CTA tile (the QM template) the decode-attention kernels use for `rows` rows.
+uint32_t attention_qm(KKind kk, uint32_t rows);
 // Loads the code of every generic decode-attention kernel for keys of kind kk (and the
 // query rotation) on the current device, so that later launches load nothing.
 cudaError_t preload_attention_kernels(KKind kk);

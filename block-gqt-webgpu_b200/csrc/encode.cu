@@ -17,6 +17,8 @@
 // every fused multiply-add above is an explicit fmaf.
 #include <cuda_fp16.h>
 
+#include <cstdlib>
+
 #include "bgtq_internal.h"
 
 namespace bgtq {
@@ -245,6 +247,274 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(const __grid_constant_
     // ---- publish the new lengths ----
     if (blockIdx.x == 0 && h.lengths) {
         for (uint32_t s = tid; s < a.seq_count; s += kThreads)
+            h.lengths[a.seq_first + s] = (a.row0 ? a.row0[s] : a.row0_scalar) + count;
+    }
+}
+
+// Packed FP32 FMA (two lanes, each rounded to nearest like fmaf) in PTX.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+// ---- bulk encode, head dims up to 64: tiles of keys, every phase over the whole tile ----
+//
+// A persistent CTA of KT = 32 * KPL threads stages one head's tables once and walks tiles of
+// KT keys.  Per tile, in shared memory, the work the oracle does key by key in the same
+// operation order:
+//   1. input rows staged as FP16 words (coalesced), gathered through the permutation into
+//      X[i][k] (FP32, key-minor: lanes over keys read consecutive words);
+//   2. thread k: each group's sum of squares (sequential FMAs, ascending dims), its norm,
+//      and the division of the group's elements by it;
+//   3. the block-diagonal rotation as a register-blocked product: one warp per output dim
+//      pair (j, j + 1) of a group, each lane KPL keys, one packed FMA (fma.rn.f32x2) per two
+//      keys and dimension - each y_j still one sequential FMA chain over its group in
+//      ascending i, so every value is the oracle's bit for bit.  The dim pairs are dealt to
+//      the warps longest-group-first (each pair costs its group's size);
+//   4. thread k: per dimension the LUT bin and code, per group the sequential sum of the
+//      codebook values' squares and the FP16 corrected scale, the packed row bytes;
+//   5. rows and scales written with coalesced word stores.
+template <int D, int KPL>
+struct TileGeo {
+    static constexpr int KT = 32 * KPL;       // keys per tile = threads per CTA
+    static constexpr int W = KT / 32;         // warps
+    static constexpr int SW = D / 2 + 1;      // staged input words per key (odd: conflict-free gathers)
+};
+
+template <int D, int KPL>
+size_t encode_tile_smem(uint32_t cent_alloc, uint32_t lut_bytes, uint32_t row_stride, uint32_t scale_stride) {
+    using G = TileGeo<D, KPL>;
+    const size_t ow = (row_stride / 4) | 1u, sw = scale_stride / 2 + 1;
+    size_t b = 8ull * D * D;                                   // rdup
+    b += 16ull * D;                                            // per-dimension constants
+    b += 4ull * ((cent_alloc + 3) & ~3u);                      // codebooks
+    b += 4ull * D * G::KT * 2;                                 // X and Y
+    b += 4ull * kMaxGroups * G::KT;                            // group norms
+    b += 4ull * G::KT * sw;                                    // scale rows
+    b += 8ull * G::KT * 3;                                     // row address table
+    b += lut_bytes + D + (D / 2) * G::W + 16;                  // code LUT, permutation, schedule
+    (void)ow;
+    return (b + 15) & ~(size_t)15;
+}
+
+template <int D, int KPL>
+__global__ void __launch_bounds__(32 * KPL) encode_tile_kernel(const __grid_constant__ EncodeArgs a, uint32_t d,
+                                                               uint32_t cent_alloc, uint32_t lut_bytes,
+                                                               uint32_t total) {
+    using G = TileGeo<D, KPL>;
+    constexpr int KT = G::KT, SW = G::SW, W = G::W;
+    const EncodeHead &h = a.head[blockIdx.y];
+    const uint32_t row_words = h.row_stride / 4, ow = row_words | 1u;
+    const uint32_t sc_words = h.scale_stride / 2, sw = sc_words + 1;
+    const uint32_t ng = h.ng, ns = h.ns, count = a.count;
+
+    extern __shared__ __align__(16) unsigned char smem[];
+    float2 *rdup = reinterpret_cast<float2 *>(smem);                       // [D][D]: (R[j][i], R[j][i]) at i*D + j
+    float4 *jc = reinterpret_cast<float4 *>(rdup + D * D);                 // [D]: off, inv, lut base, cent base
+    float *cent_s = reinterpret_cast<float *>(jc + D);                     // [cent_alloc]
+    float *X = cent_s + ((cent_alloc + 3) & ~3u);                          // [D][KT]
+    float *Y = X + D * KT;                                                 // [D][KT]
+    float *nrm = Y + D * KT;                                               // [kMaxGroups][KT]
+    uint32_t *sc_s = reinterpret_cast<uint32_t *>(nrm + kMaxGroups * KT);  // [KT][sw]
+    uint64_t *rsrc_s = reinterpret_cast<uint64_t *>(sc_s + KT * sw);       // [KT]
+    uint64_t *rdst_s = rsrc_s + KT, *rsc_s = rdst_s + KT;                  // [KT] each
+    uint8_t *lut_s = reinterpret_cast<uint8_t *>(rsc_s + KT);              // [lut_bytes]
+    uint8_t *perm_s = lut_s + lut_bytes;                                   // [D]
+    uint8_t *sched_s = perm_s + D;                                         // [W][D/2] dim pairs per warp
+    __shared__ uint32_t sched_n[W];
+    uint32_t *stage_s = reinterpret_cast<uint32_t *>(Y);                   // [KT][SW], before Y is written
+    uint32_t *out_s = reinterpret_cast<uint32_t *>(X);                     // [KT][ow], after X is consumed
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // ---- the head's tables, once per CTA ----
+    for (uint32_t e = tid; e < (uint32_t)(D * D); e += KT) {
+        const uint32_t i = e / D, j = e % D;
+        const float r = (i < d && j < d) ? h.t.rot[j * d + i] : 0.0f;
+        rdup[e] = make_float2(r, r);
+    }
+    for (uint32_t j = tid; j < (uint32_t)D; j += KT) {
+        const bool live = j < d;
+        jc[j] = make_float4(live ? h.t.off[j] : 0.0f, live ? h.t.inv[j] : 0.0f,
+                            __uint_as_float(live ? (uint32_t)h.t.cbidx[j] * 256u : 0u),
+                            __uint_as_float(live ? (uint32_t)h.t.cb_base[j] : 0u));
+        perm_s[j] = live ? h.t.perm[j] : (uint8_t)j;
+    }
+    for (uint32_t e = tid; e < cent_alloc; e += KT) cent_s[e] = e < h.n_cent ? h.t.cent[e] : 0.0f;
+    for (uint32_t e = tid; e < lut_bytes; e += KT) lut_s[e] = e < h.ncb * 256u ? h.t.lut[e] : 0;
+    if (tid == 0) {
+        // longest-processing-time deal of the dim pairs to the warps; a pair costs its group size
+        uint32_t load[W];
+        for (int w = 0; w < W; ++w) load[w] = 0, sched_n[w] = 0;
+        bool taken[D / 2];
+        for (int p = 0; p < D / 2; ++p) taken[p] = 2u * p >= d;
+        for (uint32_t n = 0; n < d / 2; ++n) {
+            int best = -1;
+            uint32_t best_cost = 0;
+            for (int p = 0; p < D / 2; ++p) {
+                if (taken[p]) continue;
+                const uint32_t g = h.t.group_of[2 * p];
+                const uint32_t c = h.group_off[g + 1] - h.group_off[g];
+                if (best < 0 || c > best_cost) best = p, best_cost = c;
+            }
+            int wmin = 0;
+            for (int w = 1; w < W; ++w)
+                if (load[w] < load[wmin]) wmin = w;
+            taken[best] = true;
+            sched_s[wmin * (D / 2) + sched_n[wmin]++] = (uint8_t)best;
+            load[wmin] += best_cost;
+        }
+    }
+    const bool vec16 = !a.src_f32 && d == (uint32_t)D &&
+                       (((uintptr_t)a.src | ((a.seq_stride | a.row_stride | h.src_head_offset) * 2u)) & 15u) == 0;
+    const uint32_t rw_magic = row_words > 1 ? (uint32_t)((0x100000000ull + row_words - 1) / row_words) : 0u;
+    const uint32_t sw_magic = sc_words > 1 ? (uint32_t)((0x100000000ull + sc_words - 1) / sc_words) : 0u;
+    __syncthreads();
+
+    const uint32_t n_tiles = (total + KT - 1) / KT;
+    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const uint32_t first = tile * KT;
+        const uint32_t nrows = min((uint32_t)KT, total - first);
+        // ---- 0. per-key source and destination offsets ----
+        if ((uint32_t)tid < nrows) {
+            const uint32_t q = first + tid, s = q / count, rr = q % count;
+            const uint64_t dseq = a.seq_first + s, dst_row = (a.row0 ? a.row0[s] : a.row0_scalar) + rr;
+            rsrc_s[tid] = (uint64_t)s * a.seq_stride + (uint64_t)rr * a.row_stride + h.src_head_offset;
+            rdst_s[tid] = dseq * h.k_seq_stride + dst_row * h.row_stride;
+            rsc_s[tid] = dseq * h.s_seq_stride + dst_row * h.scale_stride;
+        }
+        __syncthreads();
+        // ---- 1. input rows as FP16 words (coalesced), then X[i][k] through the permutation ----
+        if (vec16) {
+            for (uint32_t w = tid; w < nrows * (uint32_t)(D / 8); w += KT) {
+                const uint32_t r = w / (D / 8), c = w % (D / 8);
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.src) + rsrc_s[r] + 8u * c));
+                uint32_t *dst = stage_s + r * SW + 4u * c;
+                dst[0] = v.x;
+                dst[1] = v.y;
+                dst[2] = v.z;
+                dst[3] = v.w;
+            }
+        } else {
+            for (uint32_t w = tid; w < nrows * (uint32_t)(D / 2); w += KT) {
+                const uint32_t r = w / (D / 2), c = w % (D / 2);
+                uint32_t word = 0;
+                if (2u * c < d) {
+                    const uint64_t e = rsrc_s[r] + 2u * c;
+                    if (a.src_f32) {
+                        const float *f = static_cast<const float *>(a.src) + e;
+                        word = (uint32_t)__half_as_ushort(__float2half_rn(f[0])) |
+                               ((uint32_t)__half_as_ushort(__float2half_rn(f[1])) << 16);
+                    } else {
+                        const uint16_t *p16 = static_cast<const uint16_t *>(a.src) + e;
+                        word = (uint32_t)p16[0] | ((uint32_t)p16[1] << 16);
+                    }
+                }
+                stage_s[r * SW + c] = word;
+            }
+        }
+        __syncthreads();
+        {
+            const uint16_t *st = reinterpret_cast<const uint16_t *>(stage_s + tid * SW);
+#pragma unroll 8
+            for (int i = 0; i < D; ++i) X[i * KT + tid] = __half2float(__ushort_as_half(st[perm_s[i]]));
+        }
+        __syncthreads();
+        // ---- 2. group norms and normalisation (thread = key) ----
+        for (uint32_t g = 0; g < ng; ++g) {
+            const uint32_t lo = h.group_off[g], hi = h.group_off[g + 1];
+            float acc = 0.0f;
+            for (uint32_t i = lo; i < hi; ++i) {
+                const float x = X[i * KT + tid];
+                acc = fmaf(x, x, acc);
+            }
+            const float n = sqrtf(acc + 1e-30f);
+            nrm[g * KT + tid] = n;
+            const float dv = n > 1e-10f ? n : 1.0f;
+#pragma unroll 4
+            for (uint32_t i = lo; i < hi; ++i) X[i * KT + tid] = X[i * KT + tid] / dv;
+        }
+        __syncthreads();
+        // ---- 3. rotation: warp = output dim pair, lane = KPL keys ----
+        {
+            const uint32_t npairs = sched_n[warp];
+            for (uint32_t t = 0; t < npairs; ++t) {
+                const uint32_t j0 = 2u * sched_s[warp * (D / 2) + t];
+                const uint32_t g = h.t.group_of[j0];
+                const uint32_t lo = h.group_off[g], hi = h.group_off[g + 1];
+                float2 y0[KPL / 2], y1[KPL / 2];
+#pragma unroll
+                for (int c = 0; c < KPL / 2; ++c) y0[c] = y1[c] = make_float2(0.0f, 0.0f);
+#pragma unroll 2
+                for (uint32_t i = lo; i < hi; ++i) {
+                    const float4 r = *reinterpret_cast<const float4 *>(rdup + i * D + j0);
+                    const float2 r0 = make_float2(r.x, r.y), r1 = make_float2(r.z, r.w);
+#pragma unroll
+                    for (int c = 0; c < KPL / 4; ++c) {
+                        const float4 x = *reinterpret_cast<const float4 *>(X + i * KT + c * 128 + 4 * lane);
+                        y0[2 * c] = ffma2(make_float2(x.x, x.y), r0, y0[2 * c]);
+                        y0[2 * c + 1] = ffma2(make_float2(x.z, x.w), r0, y0[2 * c + 1]);
+                        y1[2 * c] = ffma2(make_float2(x.x, x.y), r1, y1[2 * c]);
+                        y1[2 * c + 1] = ffma2(make_float2(x.z, x.w), r1, y1[2 * c + 1]);
+                    }
+                }
+#pragma unroll
+                for (int c = 0; c < KPL / 4; ++c) {
+                    *reinterpret_cast<float4 *>(Y + j0 * KT + c * 128 + 4 * lane) =
+                        make_float4(y0[2 * c].x, y0[2 * c].y, y0[2 * c + 1].x, y0[2 * c + 1].y);
+                    *reinterpret_cast<float4 *>(Y + (j0 + 1) * KT + c * 128 + 4 * lane) =
+                        make_float4(y1[2 * c].x, y1[2 * c].y, y1[2 * c + 1].x, y1[2 * c + 1].y);
+                }
+            }
+        }
+        __syncthreads();
+        // ---- 4. codes, corrected scales, packed row (thread = key) ----
+        {
+            uint32_t *orow = out_s + tid * ow;
+            for (uint32_t w = 0; w < ow; ++w) orow[w] = 0;
+            uint8_t *ob = reinterpret_cast<uint8_t *>(orow);
+            uint16_t *srow = reinterpret_cast<uint16_t *>(sc_s + tid * sw);
+            for (uint32_t w = 0; w < sw; ++w) sc_s[tid * sw + w] = 0;
+            for (uint32_t g = 0; g < ng; ++g) {
+                const uint32_t lo = h.group_off[g], hi = h.group_off[g + 1];
+                float cl = 0.0f;
+                uint32_t pend = 0;
+#pragma unroll 2
+                for (uint32_t j = lo; j < hi; ++j) {
+                    const float4 c4 = jc[j];
+                    float t = (Y[j * KT + tid] - c4.x) * c4.y;
+                    t = fminf(fmaxf(t, 0.0f), 255.0f);
+                    const uint32_t code = lut_s[__float_as_uint(c4.z) + (uint32_t)t];
+                    const float cv = cent_s[__float_as_uint(c4.w) + code];
+                    cl = fmaf(cv, cv, cl);
+                    if (j < ns) {
+                        if (j & 1u) ob[j >> 1] = (uint8_t)(pend | (code << 4));
+                        else pend = code;
+                    } else {
+                        ob[(ns >> 1) + (j - ns)] = (uint8_t)code;
+                    }
+                }
+                srow[g] = __half_as_ushort(__float2half_rn(nrm[g * KT + tid] / fmaxf(sqrtf(cl), 1e-10f)));
+            }
+        }
+        __syncthreads();
+        // ---- 5. rows and scales out (coalesced words) ----
+        for (uint32_t w = tid; w < nrows * row_words; w += KT) {
+            const uint32_t r = div_small(w, row_words, rw_magic), c = w - r * row_words;
+            reinterpret_cast<uint32_t *>(h.packed + rdst_s[r])[c] = out_s[r * ow + c];
+        }
+        for (uint32_t w = tid; w < nrows * sc_words; w += KT) {
+            const uint32_t r = div_small(w, sc_words, sw_magic), c = w - r * sc_words;
+            reinterpret_cast<uint32_t *>(h.scales + rsc_s[r])[c] = sc_s[r * sw + c];
+        }
+        __syncthreads();
+    }
+    if (blockIdx.x == 0 && h.lengths) {
+        for (uint32_t s = tid; s < a.seq_count; s += KT)
             h.lengths[a.seq_first + s] = (a.row0 ? a.row0[s] : a.row0_scalar) + count;
     }
 }
@@ -596,6 +866,52 @@ cudaError_t run_encode(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uin
     return cudaGetLastError();
 }
 
+template <int D, int KPL>
+cudaError_t run_encode_tile(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uint32_t max_ncb, cudaStream_t s) {
+    using G = TileGeo<D, KPL>;
+    uint32_t row_stride = 0, scale_stride = 0;
+    for (uint32_t h = 0; h < a.heads; ++h) {
+        row_stride = row_stride > a.head[h].row_stride ? row_stride : a.head[h].row_stride;
+        scale_stride = scale_stride > a.head[h].scale_stride ? scale_stride : a.head[h].scale_stride;
+    }
+    const uint32_t lut_bytes = (max_ncb * 256u + 15u) & ~15u;
+    const size_t smem = encode_tile_smem<D, KPL>(cent_alloc, lut_bytes, row_stride, scale_stride);
+    int dev = 0, sms = 0, max_optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (smem > (size_t)max_optin) return cudaErrorInvalidConfiguration;
+    cudaError_t e =
+        cudaFuncSetAttribute(encode_tile_kernel<D, KPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, encode_tile_kernel<D, KPL>, G::KT, smem);
+    if (per_sm < 1) per_sm = 1;
+    const uint32_t total = a.count * a.seq_count;
+    const uint32_t tiles = (total + G::KT - 1) / G::KT;
+    uint32_t grid_x = (uint32_t)(sms * per_sm) / (a.heads ? a.heads : 1);
+    if (grid_x < 1) grid_x = 1;
+    if (grid_x > tiles) grid_x = tiles;
+    encode_tile_kernel<D, KPL><<<dim3(grid_x, a.heads), G::KT, smem, s>>>(a, d, cent_alloc, lut_bytes, total);
+    return cudaGetLastError();
+}
+
+// Keys per lane of the tiled bulk encoder (tiles of 32 x KPL keys): 4 by default, 8 when
+// BGTQ_ENCODE_KPL=8 is set (a tuning knob; both give the same bytes).
+int encode_kpl() {
+    static int kpl = [] {
+        const char *e = getenv("BGTQ_ENCODE_KPL");
+        return (e && atoi(e) == 8) ? 8 : 4;
+    }();
+    return kpl;
+}
+
+template <int D>
+cudaError_t run_encode_tiled(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uint32_t max_ncb, cudaStream_t s) {
+    return encode_kpl() == 8 ? run_encode_tile<D, 8>(a, d, cent_alloc, max_ncb, s)
+                             : run_encode_tile<D, 4>(a, d, cent_alloc, max_ncb, s);
+}
+
 }  // namespace
 
 cudaError_t launch_kv_rope_append(const KvRopeArgs &a, uint32_t d, cudaStream_t s) {
@@ -618,9 +934,9 @@ cudaError_t launch_encode(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, 
         encode_warp_kernel<<<dim3(blocks, a.heads), kThreads, stage, s>>>(a, d, total, stage);
         return cudaGetLastError();
     }
-    if (d <= 16) return run_encode<16>(a, d, cent_alloc, max_ncb, s);
-    if (d <= 32) return run_encode<32>(a, d, cent_alloc, max_ncb, s);
-    if (d <= 64) return run_encode<64>(a, d, cent_alloc, max_ncb, s);
+    if (d <= 16) return run_encode_tiled<16>(a, d, cent_alloc, max_ncb, s);
+    if (d <= 32) return run_encode_tiled<32>(a, d, cent_alloc, max_ncb, s);
+    if (d <= 64) return run_encode_tiled<64>(a, d, cent_alloc, max_ncb, s);
     return run_encode<128>(a, d, cent_alloc, max_ncb, s);
 }
 

@@ -21,6 +21,12 @@
 // a graph, or by bgtq_layout_jit_wait.  Anything that fails
 // (no compiler, no sources, a compile or load error) leaves the generic kernel in use.
 // BGTQ_LAYOUT_JIT=0 in the environment or bgtq_set_layout_jit(0) turns it off.
+//
+// Prebuilt kernels: bgtq_layout_jit_prebuild compiles a key's kernel ahead of time (the build
+// does this for the structures of the benchmarked tables) into bgtq/aot/ next to the library,
+// under a name made from the key and the kernel sources' contents.  A launch whose key has a
+// prebuilt cubin there loads it at once instead of compiling, so a host without the toolkit
+// still runs the specialised kernel; a cubin of other sources never matches a name.
 #include <dlfcn.h>
 #include <spawn.h>
 #include <sys/wait.h>
@@ -177,6 +183,10 @@ std::string key_string(const JitKey &k) {
     return s;
 }
 
+// Changes whenever kernel_source below changes what it generates (it is part of the names of
+// prebuilt cubins).
+std::string kernel_source_marker() { return "bgtq_attn_jit/v1/"; }
+
 std::string kernel_source(const JitKey &k) {
     uint32_t cls[kMaxHeads] = {}, first[kMaxHeads] = {};
     const uint32_t n = layout_classes(k, cls, first);
@@ -263,6 +273,59 @@ bool nvcc_cubin(const std::string &src, const std::string &src_dir, std::vector<
     rmdir(dir.c_str());
     return ok;
 }
+
+// ---- prebuilt (ahead-of-time) kernels ----
+uint64_t fnv1a(const char *p, size_t n, uint64_t h = 1469598103934665603ull) {
+    for (size_t i = 0; i < n; ++i) h = (h ^ (unsigned char)p[i]) * 1099511628211ull;
+    return h;
+}
+
+bool read_file(const std::string &path, std::string &out) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f) return false;
+    std::stringstream ss;
+    ss << f.rdbuf();
+    out = ss.str();
+    return true;
+}
+
+// The kernel sources every layout-specialised kernel is built from, hashed: prebuilt cubins
+// are named with it, so only cubins of the current sources are found.  0 if unreadable.
+uint64_t sources_digest() {
+    static uint64_t digest = [] {
+        const std::string dir = source_dir();
+        if (dir.empty()) return (uint64_t)0;
+        uint64_t h = 1469598103934665603ull;
+        for (const char *f : {"attention_impl.cuh", "bgtq_internal.h"}) {
+            std::string text;
+            if (!read_file(dir + "/" + f, text)) return (uint64_t)0;
+            h = fnv1a(text.data(), text.size(), h);
+        }
+        return h;
+    }();
+    return digest;
+}
+
+// bgtq/aot/ beside this library.
+std::string aot_dir() {
+    Dl_info info{};
+    if (!dladdr(reinterpret_cast<void *>(&jit_set_enabled), &info) || !info.dli_fname) return "";
+    std::string p(info.dli_fname);
+    const size_t slash = p.find_last_of('/');
+    return (slash == std::string::npos ? std::string(".") : p.substr(0, slash)) + "/aot";
+}
+
+// File name of a key's prebuilt cubin ("" when the sources cannot be read).
+std::string aot_name(const std::string &ks) {
+    const uint64_t d = sources_digest();
+    if (!d) return "";
+    const std::string src = kernel_source_marker() + ks;
+    char buf[40];
+    std::snprintf(buf, sizeof buf, "attn_%016llx.cubin", (unsigned long long)fnv1a(src.data(), src.size(), d));
+    return buf;
+}
+
+std::atomic<uint32_t> g_prebuilt{0};  // keys served by a prebuilt cubin
 
 bool load(Entry &e) {
     if (cudaLibraryLoadData(&e.lib, e.cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0) != cudaSuccess) {
@@ -376,7 +439,12 @@ const void *jit_attention_kernel(const JitKey &key, cudaStream_t stream, bool *h
     if (it == g_cache.end()) {
         if (g_cache.size() >= kMaxEntries) return nullptr;
         it = g_cache.emplace(ks, Entry{}).first;
-        if (!multi_layout(key)) {
+        std::string pre;
+        const std::string name = aot_name(ks);
+        if (!name.empty() && read_file(aot_dir() + "/" + name, pre) && !pre.empty()) {
+            finish(it->second, std::vector<char>(pre.begin(), pre.end()));
+            g_prebuilt.fetch_add(1);
+        } else if (!multi_layout(key)) {
             finish(it->second, compile(key));
         } else {
             g_queue.push_back(Job{key, ks});
@@ -425,6 +493,73 @@ bgtq_status bgtq_layout_jit_wait(uint32_t timeout_ms) {
     const bool idle = bgtq::g_cv.wait_for(l, std::chrono::milliseconds(timeout_ms), [] { return bgtq::g_busy == 0; });
     for (auto &kv : bgtq::g_cache) bgtq::load_compiled(kv.second);
     return idle ? BGTQ_OK : BGTQ_ETIMEOUT;
+}
+
+bgtq_status bgtq_layout_jit_prebuilt(uint32_t *n) {
+    if (!n) return BGTQ_EINVAL;
+    *n = bgtq::g_prebuilt.load();
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_layout_jit_prebuild(const char *dir, uint32_t heads, const uint32_t *const *configs,
+                                     const size_t *n_configs, const float *const *tables, const size_t *n_tables,
+                                     uint32_t rows, int v_f32, char *name_out, size_t name_capacity) {
+    using namespace bgtq;
+    if (!dir || !configs || !n_configs || !tables || !n_tables || heads < 1 || heads > (uint32_t)kMaxHeads ||
+        rows < 1 || rows > (uint32_t)kMaxRows) {
+        set_last_error("Invalid prebuild request");
+        return BGTQ_EINVAL;
+    }
+    JitKey key{};
+    uint32_t dim = 0;
+    for (uint32_t h = 0; h < heads; ++h) {
+        Layout L;
+        std::string err;
+        const bgtq_status st = parse_layout(configs[h], n_configs[h], tables[h], n_tables[h], L, err);
+        if (st != BGTQ_OK) {
+            set_last_error(err);
+            return st;
+        }
+        if (h && L.d != dim) {
+            set_last_error("Invalid prebuild request: heads of different dims");
+            return BGTQ_EINVAL;
+        }
+        dim = L.d;
+        key.head[h].ns = L.ns;
+        key.head[h].ng = L.ng;
+        for (uint32_t g = 0; g <= L.ng && g <= (uint32_t)kMaxGroups; ++g) key.head[h].group_off[g] = L.group_off[g];
+    }
+    key.D = dim <= 16 ? 16u : dim <= 32 ? 32u : dim <= 64 ? 64u : 128u;
+    key.QM = attention_qm(KKind::Packed, rows);
+    key.vf32 = v_f32 ? 1u : 0u;
+    key.heads = heads;
+    const std::string name = aot_name(key_string(key));
+    if (name.empty()) {
+        set_last_error("kernel sources not found next to the library");
+        return BGTQ_ELAYOUT;
+    }
+    if (name_out && name_capacity) std::snprintf(name_out, name_capacity, "%s", name.c_str());
+    const std::string path = std::string(dir) + "/" + name, tmp = path + ".tmp";
+    if (exists(path)) return BGTQ_OK;  // built by an earlier run from the same sources
+    std::vector<char> cubin = compile(key);
+    if (cubin.empty()) {
+        set_last_error("layout-specialised kernel did not compile (is nvcc installed?)");
+        return BGTQ_ECUDA;
+    }
+    mkdir(dir, 0755);
+    {
+        std::ofstream f(tmp, std::ios::binary);
+        f.write(cubin.data(), (std::streamsize)cubin.size());
+        if (!f) {
+            set_last_error("cannot write " + tmp);
+            return BGTQ_EINVAL;
+        }
+    }
+    if (std::rename(tmp.c_str(), path.c_str()) != 0) {
+        set_last_error("cannot write " + path);
+        return BGTQ_EINVAL;
+    }
+    return BGTQ_OK;
 }
 
 bgtq_status bgtq_layout_jit_counts(uint32_t *compiled, uint32_t *loaded, uint32_t *failed) {

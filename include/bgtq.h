@@ -142,6 +142,20 @@ bgtq_status bgtq_layout_jit_counts(uint32_t *compiled, uint32_t *loaded, uint32_
  * had finished is loaded). */
 bgtq_status bgtq_layout_jit_wait(uint32_t timeout_ms);
 
+/* Ahead-of-time layout-specialised kernel: compiles the decode-attention kernel for `heads`
+ * packed-key heads with these flattened tables (config/table as for bgtq_tables_create),
+ * `rows` query rows per head and FP16 (v_f32 = 0) or FP32 values with the toolkit's nvcc
+ * (host only, no GPU needed) and stores the cubin in `dir` under a name made from the heads'
+ * group structures and the kernel sources (written to name_out if given; an existing file of
+ * that name is kept).  Launches look in bgtq/aot/ beside the library first, so a process on
+ * a host without the toolkit still gets the specialised kernel for prebuilt structures.  No
+ * counterpart in the reference. */
+bgtq_status bgtq_layout_jit_prebuild(const char *dir, uint32_t heads, const uint32_t *const *configs,
+                                     const size_t *n_configs, const float *const *tables, const size_t *n_tables,
+                                     uint32_t rows, int v_f32, char *name_out, size_t name_capacity);
+/* Keys whose kernel this process took from a prebuilt cubin. */
+bgtq_status bgtq_layout_jit_prebuilt(uint32_t *n);
+
 /* Fixture files of the reference's tests (tests/oracles/fixture.py:13-49): a JSON manifest
  * (metadata + array descriptors dtype f32/u32/u8/f16/u16, shape, offset, nbytes) beside a
  * little-endian payload checked by length and SHA-256.  Read errors are BGTQ_ELAYOUT with
@@ -349,6 +363,21 @@ bgtq_status bgtq_attention_last_launches(const bgtq_attention *a, uint32_t *laun
 bgtq_status bgtq_attend_static(uint32_t heads, bgtq_keys *const *keys, bgtq_values *const *values, const float *q,
                                const uint32_t *positions, int causal, uint32_t rows, uint32_t seq_first,
                                uint32_t seq_count, float *out, void *stream);
+
+/* ---- model decode kernels -------------------------------------------------------- */
+
+/* Fused decode-step GEMVs of the model path (the matmul / RMSNorm / SiLU-gate shaders of
+ * src/model/kernels.wgsl:11-54 as src/model/decoder.ts:31-81 chains them), for `batch` <= 8
+ * activation rows x[b] (FP32, row stride x_stride floats, in % 8 == 0) and FP16 weights w
+ * [rows][in] (16-byte aligned), FP32 arithmetic:
+ *   mode 0: y[b][r]  = w[r] . rmsnorm(x[b]) + bias[r]      (bias nullable; Q/K/V, lm_head)
+ *   mode 1: y[b][r] += w[r] . x[b]                          (residual add; o_proj, down_proj)
+ *   mode 2: y[b][r]  = silu(w[r] . n) * (w[out + r] . n)    (n = rmsnorm(x[b]); gate rows then up rows)
+ * rmsnorm(v) = v * rsqrt(mean(v^2) + eps) * norm_w.  r < out; y has row stride y_stride
+ * floats and must not overlap x.  Stream-ordered. */
+bgtq_status bgtq_model_gemv(int mode, const float *x, uint32_t batch, uint64_t x_stride, uint32_t in,
+                            const float *norm_w, float eps, const uint16_t *w, const float *bias, uint32_t out,
+                            float *y, uint64_t y_stride, void *stream);
 
 /* Device status word written by kernels (0 = fine); reading it synchronises. */
 bgtq_status bgtq_device_status(int device, uint32_t *status_out);

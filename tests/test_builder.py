@@ -12,6 +12,10 @@ Pins, all bit-exact:
 * all 90 heads of the SmolLM2 calibration (tests/golden/smollm2_calibration.npz: widths,
   pair order, row padding, scale stride and the SHA-256 of the reference's config / table):
   tables exact from the widths alone, configs exact given the pair order.
+* all 48 heads of the Qwen2.5-0.5B-geometry calibration (tests/golden/qwen_calibration.npz,
+  made by tests/golden/make_qwen_calibration.py with the reference's calibration procedure
+  and table code on the seeded random-init model): config and table exact from the widths
+  alone (the builder's own pair order).
 * the Haar rotation against NumPy's own generator + QR (the reference's
   _random_rotation_dense_torch, vendor/blockgtq/block_gtq_pipeline.py:81-92), and the
   builder's pair order against torch.argsort.
@@ -95,6 +99,17 @@ def test_tables_match_full_smollm2_calibration():
         cfg, tab = bgtq.build_tables(w, pair_order=z["pair_order"][i].astype(np.int64), **kw)
         assert _sha(cfg.astype(np.uint32)) == z["config_sha256"][i], i
         assert _sha(tab.astype(np.float32)) == z["table_sha256"][i], i
+
+
+def test_tables_match_qwen_calibration():
+    z = np.load(GOLDEN / "qwen_calibration.npz")
+    assert z["widths"].shape == (48, 32) and int(z["rotation_threshold"]) == 2
+    for i in range(48):
+        cfg, tab = bgtq.build_tables(z["widths"][i].astype(np.int64), rotation_threshold=2,
+                                     norm_stride=int(z["norm_stride"][i]))
+        assert _sha(cfg.astype(np.uint32)) == z["config_sha256"][i], i
+        assert _sha(tab.astype(np.float32)) == z["table_sha256"][i], i
+        assert np.array_equal(cfg[cfg[6]:cfg[6] + 64:2], z["pair_order"][i]), i
 
 
 def test_pair_order_is_torch_argsort():

@@ -131,6 +131,39 @@ def test_device_fp16_and_fp32_model_path_sources(cuda):
         np.testing.assert_array_equal(keys2.read()[0], packed)
 
 
+def test_bulk_fp32_strided_and_ragged_multi_sequence(cuda):
+    """The tiled bulk encoder (launches of more than 4096 keys) on the sources the prefill
+    path gives it - FP32 rows of a strided activation (rounded to FP16 first) - and on
+    several sequences whose appends start at different rows; bytes equal the oracle's."""
+    import torch
+    z = load_config("config4")
+    p, cfg, tab = params_tables(z)
+    rng = np.random.default_rng(23)
+    rows, kvh = 5000, 2
+    act = (synthetic.profiled(rng, rows * kvh, 64) * 3).reshape(rows, kvh, 64)
+    dev = torch.from_numpy(act).to(cuda)
+    for head in range(kvh):
+        keys = PackedKeys((cfg, tab), rows)
+        keys.append(dev[:, head, :])                       # one 5000-key FP32 strided launch
+        packed, norms = keys.read()
+        rp, rs = oracle.encode_f32(cfg, tab, act.reshape(-1), kvh * 64, head * 64, rows)
+        np.testing.assert_array_equal(packed, rp)
+        np.testing.assert_array_equal(norms, rs)
+    S = 3
+    keys = PackedKeys((cfg, tab), 3000, sequences=S)
+    lead = _edge_keys(rng, 7, 64)
+    keys.append(lead, seq_first=1)                         # sequence 1 starts 7 rows further on
+    batch = _edge_keys(rng, S * 2000, 64).reshape(S, 2000, 64)
+    keys.append(torch.from_numpy(batch.view(np.float16)).to(cuda), seq_first=0)   # 6000 keys, one launch
+    for s in range(S):
+        rows_s = batch[s] if s != 1 else np.concatenate([lead, batch[1]])
+        ref = oracle.encode(cfg, tab, rows_s, threads=4)
+        packed, norms = keys.read(s)
+        np.testing.assert_array_equal(packed, ref["packed"])
+        np.testing.assert_array_equal(norms, ref["scales"])
+    assert device_status(0) == 0
+
+
 def test_multi_sequence_ragged_appends(cuda):
     z = load_config("config4")
     p, cfg, tab = params_tables(z)

@@ -201,3 +201,29 @@ def test_wait_loads_and_graph_records_specialised_kernel(cuda):
     assert bgtq.layout_jit_wait(0.0)                  # nothing queued: returns at once
     del graph
     assert device_status(0) == 0
+
+
+def test_prebuilt_kernel_serves_the_config4_heads(cuda):
+    """The build compiles the specialised kernel of the benchmarked heads ahead of time
+    (bgtq/aot/): a launch over three config-4 heads with three query rows takes it from
+    there - no compiler needed at run time - and gives the generic kernel's bytes."""
+    import ctypes as C
+    import torch
+    from bgtq import _lib
+    aot = _lib.LIB_PATH.parent / "aot"
+    assert aot.is_dir() and any(aot.glob("*.cubin")), "build() writes the prebuilt kernels"
+    S, T, H, R = 4, 900, 3, 3
+    keys, vals, d, gen = _stores(cuda, "config4", S, T, H, "f16", seed=31)
+    att = GroupedAttention(keys, vals, R)
+    q = torch.randn((S, H, R, d), device=cuda, generator=gen)
+    bgtq.set_layout_jit(True)
+    spec = att.attend(q).clone()
+    n = C.c_uint32()
+    _lib.call("bgtq_layout_jit_prebuilt", C.byref(n))
+    assert n.value >= 1
+    bgtq.set_layout_jit(False)
+    generic = att.attend(q).clone()
+    bgtq.set_layout_jit(True)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(spec.cpu().numpy(), generic.cpu().numpy())
+    assert device_status(0) == 0

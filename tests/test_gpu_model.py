@@ -7,8 +7,12 @@ oracle's reconstruction of the packed cache the Decoder wrote, its values the FP
 projections, and its attention is oracle.attention in double precision.  Both run the same
 torch GEMMs on the same device, so the only difference is the attention kernels: logits
 must agree to 1e-4 abs + 1e-3 rel through a prefill chunk and decode steps, for a
-SmolLM2-like (GQA 3, no bias) and a Qwen-like (GQA 3 x 2 KV heads, QKV bias) geometry.
+SmolLM2-like (GQA 3, no bias) and a Qwen-like (GQA 3 x 2 KV heads, QKV bias) geometry;
+and, at the benchmarked context, through a 4096-token prefix prefilled in 1024-token chunks
+followed by decode steps replayed from the recorded CUDA graph.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -18,6 +22,7 @@ from bgtq.model import Decoder, ModelGeometry, random_weights
 from conftest import GOLDEN
 
 pytestmark = pytest.mark.gpu
+THREADS = os.cpu_count() or 8
 GEOMS = {
     "smollm2-like": ModelGeometry("smollm2", 2, 192, 256, 3, 1, 1e5, 1e-5, 500, False),
     "qwen-like": ModelGeometry("qwen2", 2, 384, 512, 6, 2, 1e6, 1e-6, 700, True),
@@ -65,10 +70,10 @@ def _reference_forward(dec, w, g, tokens, start, tables):
                 ref_v[b][hd] = vh if ref_v[b][hd] is None else np.concatenate([ref_v[b][hd], vh])
                 cfg, tab = tables[layer * g.kv_heads + hd]
                 packed, scales = dec.keys[layer][hd].read(b, 0, start + n)
-                kh = oracle.reconstruct(cfg, tab, packed, scales, threads=8)
+                kh = oracle.reconstruct(cfg, tab, packed, scales, threads=THREADS)
                 rows = qn[b, :, hd * g.gqa:(hd + 1) * g.gqa].reshape(n * g.gqa, 64)
                 ps = np.repeat(np.arange(start, start + n, dtype=np.uint32), g.gqa)
-                _, _, o = oracle.attention(rows, kh, ref_v[b][hd], ps, True, threads=8)
+                _, _, o = oracle.attention(rows, kh, ref_v[b][hd], ps, True, threads=THREADS)
                 out[b, :, hd * g.gqa:(hd + 1) * g.gqa] = o.reshape(n, g.gqa, 64)
         att = torch.from_numpy(out).to(h.device).reshape(B, n, g.hidden)
         h = h + lin(att, p + "self_attn.o_proj.weight")
@@ -103,6 +108,39 @@ def test_decoder_matches_reference_decoder(cuda, name):
         np.testing.assert_allclose(got.cpu().numpy(), ref.cpu().numpy(), atol=1e-4, rtol=1e-3)
         start += 1
     assert dec.length == prompt + steps
+    assert device_status(0) == 0
+    dec.destroy()
+
+
+@pytest.mark.parametrize("name", sorted(GEOMS))
+def test_graph_decode_after_4096_prefix_matches_reference(cuda, name):
+    """The benchmarked decode path at its context: a 4096-token prefix prefilled in four
+    1024-token chunks (tensor-core prefill), one eager decode step that records the CUDA
+    graph, then two replayed steps - each step's logits against the restated decoder with
+    oracle attention over the same 4096+ positions."""
+    import torch
+    g = GEOMS[name]
+    tables = _tables(g)
+    w = random_weights(g, seed=9, device=cuda, std=0.08)
+    prefix, chunk = 4096, 1024
+    dec = Decoder(w, g, prefix + 8, tables, batch=1)
+    dec._ref_v = {}
+    rng = np.random.default_rng(12)
+    toks = torch.from_numpy(rng.integers(0, g.vocab, (1, prefix))).to(cuda)
+    got = dec.prefill(toks, chunk=chunk)
+    for a in range(0, prefix, chunk):
+        ref = _reference_forward(dec, w, g, toks[:, a:a + chunk], a, tables)
+    np.testing.assert_allclose(got.cpu().numpy(), ref.cpu().numpy(), atol=1e-4, rtol=1e-3)
+    steps = [torch.from_numpy(rng.integers(0, g.vocab, (1, 1))).to(cuda) for _ in range(3)]
+    got = dec.capture_decode(steps[0])                       # eager step, then the graph is recorded
+    ref = _reference_forward(dec, w, g, steps[0], prefix, tables)
+    np.testing.assert_allclose(got.cpu().numpy(), ref.cpu().numpy(), atol=1e-4, rtol=1e-3)
+    for i, t in enumerate(steps[1:], start=1):
+        got = dec.decode_graph(t).clone()
+        dec._sync_lengths()                                  # the reference reads the replayed cache rows
+        ref = _reference_forward(dec, w, g, t, prefix + i, tables)
+        np.testing.assert_allclose(got.cpu().numpy(), ref.cpu().numpy(), atol=1e-4, rtol=1e-3)
+    assert dec.length == prefix + 3
     assert device_status(0) == 0
     dec.destroy()
 

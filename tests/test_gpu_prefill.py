@@ -3,8 +3,11 @@ oracle on the GPU's own codes, at the north-star tolerance (1e-5 abs + 1e-4 rel)
 
 Follows the model path's chunked prefill (src/model/decoder.ts:30-81): all query heads of
 every KV head (SmolLM2 GQA 3, Qwen GQA 7), whole-prefix and mid-sequence chunks, ragged
-sequence lengths, different calibrations per KV head.
+sequence lengths, different calibrations per KV head; and config 5's own size (8192
+positions, 128 key tiles, the Qwen calibration's tables) on both tensor-core kernels.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -64,6 +67,49 @@ def test_prefill_matches_oracle(cuda, heads, G, kernel):
     _check(att, keys, kv, q, 0, heads, G)
     q2 = synthetic.profiled(rng, S * 97 * heads * G, 64).reshape(S, 97, heads * G, 64)
     _check(att, keys, kv, q2, 333, heads, G)
+    assert device_status(0) == 0
+
+
+@pytest.mark.parametrize("kernel", ["umma", "mma"])
+def test_prefill_at_config5_size_matches_oracle(cuda, kernel):
+    """One sequence and one layer of config 5 at its benchmarked length: 8192 positions
+    (128 key tiles of accumulation) over 2 KV heads x 7 query heads with the Qwen
+    calibration's tables (a one-group and a three-group head).  Sampled query rows - the
+    first tiles, the middle, and the last 64 positions - against the oracle."""
+    import torch
+    zq = np.load(GOLDEN / "qwen_calibration.npz")
+    from bgtq import build_tables
+    picks = [0, int(np.argmax(zq["norm_stride"]))]
+    rng = np.random.default_rng(55)
+    T, H, G = 8192, 2, 7
+    keys, vals, kv = [], [], []
+    for h, j in enumerate(picks):
+        cfg, tab = build_tables(zq["widths"][j].astype(np.int64), rotation_threshold=2,
+                                norm_stride=int(zq["norm_stride"][j]))
+        k = PackedKeys((cfg, tab), T)
+        v = Values(64, T, "f16")
+        kb = (rng.standard_normal((T, 64)) * 1.5).astype(np.float16)
+        vb = (rng.standard_normal((T, 64)) * 1.5).astype(np.float16)
+        k.append(kb.view(np.uint16))
+        v.append(vb.view(np.uint16))
+        keys.append(k)
+        vals.append(v)
+        kv.append((cfg, tab, vb.astype(np.float32)))
+    att = GroupedAttention(keys, vals, G)
+    att.set_prefill_kernel(kernel)
+    q = (rng.standard_normal((1, T, H * G, 64)) * 1.5).astype(np.float32)
+    out = att.prefill(torch.from_numpy(q).to(cuda)).cpu().numpy()
+    sample = np.unique(np.concatenate([[0, 1, 63, 64, 65, 127, 128, 2047, 4095, 4096, 6000],
+                                       np.arange(T - 64, T)])).astype(np.uint32)
+    threads = os.cpu_count() or 8
+    for h in range(H):
+        cfg, tab, vf = kv[h]
+        kh = oracle.reconstruct(cfg, tab, *keys[h].read(0), threads=threads)
+        rows = q[0, sample][:, h * G:(h + 1) * G].reshape(-1, 64)
+        pos = np.repeat(sample, G)
+        _, _, ref = oracle.attention(rows, kh, vf, pos, True, threads=threads)
+        got = out[0, sample][:, h * G:(h + 1) * G].reshape(-1, 64)
+        np.testing.assert_allclose(got, ref, atol=ATOL, rtol=RTOL)
     assert device_status(0) == 0
 
 

@@ -1,7 +1,8 @@
 """Multi-rank host logic on CPU: two gloo ranks run the sequence-sharded decode
 bookkeeping that bench.py runs over NCCL (sequence ownership, max-over-ranks timing,
-gathered output checksums), and a rank that dies is reported to its peer as an error
-instead of a hang.
+gathered output checksums, one batch split over the ranks with its outputs gathered to
+rank 0 and proven by exact per-rank checksums), and a rank that dies is reported to its
+peer as an error instead of a hang.
 """
 import multiprocessing as mp
 import os
@@ -13,6 +14,7 @@ import pytest
 from bgtq import sharding
 
 D, T, R = 16, 40, 3
+TOTAL = 7        # one batch split over two ranks: 4 + 3 sequences
 
 
 def _free_port():
@@ -41,8 +43,19 @@ def _rank_main(rank, world, port, per_rank, mode, out_dir):
         outs = [torch.from_numpy(_sequence_output(s)) for s in sharding.sequence_range(per_rank, rank)]
         timing = sharding.max_over_ranks([0.25 * (rank + 1), -float(rank)], dist, "cpu")
         sums = sharding.gather_checksums(outs, dist, "cpu")
+        # one batch of TOTAL sequences split over the ranks, outputs gathered to rank 0
+        mine = sharding.split_range(TOTAL, world, rank)
+        share = torch.stack([torch.from_numpy(_sequence_output(s)).float() for s in mine])
+        counts = [len(sharding.split_range(TOTAL, world, r)) for r in range(world)]
+        gathered = sharding.gather_to_root(share, counts, dist, "cpu")
+        bits = sharding.gather_ints([sharding.bit_checksum(share)], dist, "cpu")
         sharding.barrier(dist)
         np.save(os.path.join(out_dir, f"rank{rank}.npy"), np.array(timing + sums))
+        if rank == 0:
+            np.save(os.path.join(out_dir, "gathered.npy"), gathered.numpy())
+            np.save(os.path.join(out_dir, "bits.npy"), np.array([b[0] for b in bits] +
+                                                                [sharding.bit_checksum(gathered[:counts[0]]),
+                                                                 sharding.bit_checksum(gathered[counts[0]:])]))
     except Exception as e:  # the peer's death surfaces here
         with open(os.path.join(out_dir, f"rank{rank}.err"), "w") as f:
             f.write(type(e).__name__ + ": " + str(e)[:200])
@@ -96,6 +109,12 @@ def test_two_gloo_ranks_max_timing_and_checksums(tmp_path):
         got = np.load(tmp_path / f"rank{r}.npy")
         np.testing.assert_allclose(got[:2], [0.5, 0.0])          # max over ranks, element-wise
         np.testing.assert_allclose(got[2:], expect, rtol=1e-12)  # rank-ordered checksums
+    # the split batch gathered to rank 0 equals the single-process outputs, bit for bit
+    gathered = np.load(tmp_path / "gathered.npy")
+    single = np.stack([_sequence_output(s).astype(np.float32) for s in range(TOTAL)])
+    assert np.array_equal(gathered, single)
+    bits = np.load(tmp_path / "bits.npy")
+    assert bits[0] == bits[2] and bits[1] == bits[3]                # per-rank checksums prove the copy
 
 
 def test_dead_rank_is_reported_not_waited_for(tmp_path):
