@@ -25,9 +25,10 @@ Metric: decoded tokens/s (whole job).
   fp16k_attention / prefill_config5_layer / config1  (N = 1) the FP16-K baseline attention
          at config-4 geometry, one config-5 prefill layer on the tensor cores, and the
          config-1 parity case's latency
-  cpu_baseline  (N = 1, rank 0, after all GPU work) the CPU oracle port on sampled
-         (layer, sequence, KV head) pairs of the real cache, which it also checks: the
-         prefix encode bit-exact and the GPU's attention outputs within 1e-5 / 1e-4
+  cpu_baseline  (N = 1, rank 0, after all GPU work) the reference's CPU path restated
+         (vectorised PyTorch, oracle/torch_port.py, or the C oracle, the faster) on sampled
+         (layer, sequence, KV head) pairs of the real cache, which the C oracle also checks:
+         the prefix encode bit-exact and the GPU's attention outputs within 1e-5 / 1e-4
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   torchrun --nproc-per-node N bench.py --gpus N ...
@@ -200,21 +201,59 @@ def _oracle():
     return oracle
 
 
-def cpu_pair_rate(oracle, cfg, tab, pairs, threads, budget_s, min_passes=1):
-    """Time the reference's CPU decode work per (sequence, KV head) pair - encode the new
-    key, reconstruct the pair's whole cache, attention for its GQA query rows - over the
-    sampled pairs until the budget is spent; returns (seconds per pair, pairs timed)."""
+def pair_runner(kind, threads):
+    """The reference's per-decode-step CPU work for one (sequence, KV head) pair - encode the
+    new key, reconstruct the pair's whole cache from its packed rows, attention for its GQA
+    query rows - in one of the two CPU restatements of the reference's path: "torch" (the
+    vectorised PyTorch form the reference's own CPU code has, oracle/torch_port.py) or "c"
+    (the C oracle, oracle/bgtq_oracle.c)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    if kind == "torch":
+        import torch
+        import torch_port
+        torch.set_num_threads(threads)
+        tbs = {}
+
+        def run(pr):
+            key = id(pr["cfg"])
+            if key not in tbs:
+                tbs[key] = torch_port.Tables(pr["cfg"], pr["tab"])
+            tb = tbs[key]
+            torch_port.encode(tb, pr["knew"])
+            kh = torch_port.reconstruct(tb, pr["packed"], pr["scales"])
+            torch_port.attention(pr["q"], kh, pr["v"])
+        return run
+    import oracle
+
+    def run(pr):
+        oracle.encode(pr["cfg"], pr["tab"], pr["knew"], threads=1)
+        kh = oracle.reconstruct(pr["cfg"], pr["tab"], pr["packed"], pr["scales"], threads=threads)
+        oracle.attention(pr["q"], kh, pr["v"], threads=threads)
+    return run
+
+
+def cpu_pair_rate(run, pairs, budget_s, min_passes=1):
+    """Run `run` over the sampled pairs until the budget is spent (at least min_passes
+    passes); returns (seconds per pair, pairs run)."""
     done, t0 = 0, time.perf_counter()
     while True:
         for pr in pairs:
-            c, t = pr.get("cfg", cfg), pr.get("tab", tab)
-            oracle.encode(c, t, pr["knew"], threads=1)
-            kh = oracle.reconstruct(c, t, pr["packed"], pr["scales"], threads=threads)
-            oracle.attention(pr["q"], kh, pr["v"], threads=threads)
+            run(pr)
             done += 1
         if done >= min_passes * len(pairs) and time.perf_counter() - t0 > budget_s:
             break
     return (time.perf_counter() - t0) / done, done
+
+
+def fastest_port(pairs, threads, budget_s):
+    """Both CPU restatements timed on the same pairs; the faster is the baseline."""
+    times = {}
+    for kind in ("torch", "c"):
+        run = pair_runner(kind, threads)
+        run(pairs[0])                                   # warm-up (tables, thread pools)
+        times[kind] = cpu_pair_rate(run, pairs, budget_s)
+    kind = min(times, key=lambda k: times[k][0])
+    return kind, times
 
 
 def synthetic_pairs(oracle, cfg, tab, context, n, seed=123):
@@ -226,19 +265,32 @@ def synthetic_pairs(oracle, cfg, tab, context, n, seed=123):
     k = synthetic.profiled(rng, context, HEAD_DIM).astype(np.float16).view(np.uint16)
     enc = oracle.encode(cfg, tab, k, threads=os.cpu_count() or 1)
     for _ in range(n):
-        out.append({"knew": k[:1], "packed": enc["packed"], "scales": enc["scales"],
+        out.append({"cfg": cfg, "tab": tab, "knew": k[:1], "packed": enc["packed"], "scales": enc["scales"],
                     "q": synthetic.profiled(rng, GQA, HEAD_DIM),
                     "v": rng.standard_normal((context, HEAD_DIM)).astype(np.float32)})
     return out
 
 
+def reference_timing_here():
+    """The reference's own Python path against the C port on config 1, measured in the build
+    container by oracle/time_reference_cpu.py (the reference checkout is not on this host)."""
+    f = ROOT / "oracle" / "reference_cpu_timing.json"
+    if not f.exists():
+        return None
+    r = json.loads(f.read_text())
+    return {"workload": r["workload"], "host": r["host"],
+            "reference_python_step_us": {t: round(v["step_us"]) for t, v in r["reference_python"].items()},
+            "port_c_step_us": {t: round(v["step_us"]) for t, v in r["port_c"].items()}}
+
+
 def cpu_baseline_and_check(samples, layers, budget_s):
-    """The cpu_baseline leg of the decode bench (N = 1, rank 0, after all GPU work): the
-    oracle on the sampled pairs of the real cache.  Checks first (untimed): the oracle's
-    encode of each pair's 32768-token prefix equals the packed rows and FP16 scales read
-    back from the GPU bit for bit, and the GPU's attention outputs of the last timed step
-    are within 1e-5 abs + 1e-4 rel of the oracle's on the GPU's own codes.  Then times the
-    per-decode-step CPU work on those pairs with all host threads and with one."""
+    """The cpu_baseline leg of the decode bench (N = 1, rank 0, after all GPU work) on
+    sampled pairs of the real cache.  Checks first (untimed, the C oracle): its encode of
+    each pair's 32768-token prefix equals the packed rows and FP16 scales read back from the
+    GPU bit for bit, and the GPU's attention outputs of the last timed step are within 1e-5
+    abs + 1e-4 rel of the oracle's on the GPU's own codes.  Then times the per-decode-step
+    CPU work on those pairs with all host threads in both CPU restatements (the faster is
+    the baseline) and with one thread."""
     oracle = _oracle()
     threads = os.cpu_count() or 1
     enc_ok, worst = True, 0.0
@@ -250,27 +302,34 @@ def cpu_baseline_and_check(samples, layers, budget_s):
         _, _, o = oracle.attention(pr["q"], kh, pr["v"], threads=threads)
         err = np.abs(pr["out"] - o) / (ATOL + RTOL * np.abs(o))
         worst = max(worst, float(err.max()))
-    per_pair, done = cpu_pair_rate(oracle, None, None, samples, threads, budget_s)
-    per_pair_1, done_1 = cpu_pair_rate(oracle, None, None, samples[:4], 1, min(4.0, budget_s / 3))
+    kind, times = fastest_port(samples, threads, budget_s / 2)
+    per_pair = times[kind][0]
+    per_pair_1, _ = cpu_pair_rate(pair_runner(kind, 1), samples[:4], min(4.0, budget_s / 4))
+    if kind == "torch":
+        import torch
+        torch.set_num_threads(threads)
     ctx = len(samples[0]["v"])
     return ({"value": 1.0 / (per_pair * layers * KV_HEADS), "unit": "tokens/s", "cores": threads, "kind": "port",
-             "single_thread_value": 1.0 / (per_pair_1 * layers * KV_HEADS),
-             "sample": f"{len(samples)} (layer, sequence, KV head) pairs of the real cache at context {ctx}, timed "
-                       f"{done} times on {threads} threads ({per_pair * 1e3:.2f} ms per pair) and {done_1} times on "
-                       f"1 thread ({per_pair_1 * 1e3:.1f} ms): encode the new key + reconstruct the pair's keys + "
-                       f"attention for its {GQA} query rows; tokens/s = 1 / (time per pair x {layers} layers x "
-                       f"{KV_HEADS} KV heads), the same rate for any batch",
-             "run_after_gpu_work": True},
+             "single_thread_value": 1.0 / (per_pair_1 * layers * KV_HEADS), "port": kind,
+             "ms_per_pair": {k: v[0] * 1e3 for k, v in times.items()},
+             "sample": f"{len(samples)} (layer, sequence, KV head) pairs of the real cache at context {ctx}: encode "
+                       f"the new key + reconstruct the pair's keys + attention for its {GQA} query rows, in the "
+                       f"vectorised PyTorch restatement of the reference's CPU path and in the C oracle on {threads} "
+                       f"threads (the faster, {kind}: {per_pair * 1e3:.2f} ms per pair; 1 thread: "
+                       f"{per_pair_1 * 1e3:.1f} ms); tokens/s = 1 / (time per pair x {layers} layers x {KV_HEADS} KV "
+                       "heads), the same rate for any batch",
+             "run_after_gpu_work": True, "reference_python_config1": reference_timing_here()},
             {"pairs": len(samples), "prefix_encode_bit_exact": enc_ok,
              "attention_worst_fraction_of_tolerance": worst, "attention_within_tolerance": worst <= 1.0})
 
 
 def run_reference(args, rank, world):
-    """The reference arm: the CPU implementation of this path (the oracle port, all host
-    threads) on the decode workload's config.  A step is a bounded sample: the per-decode-
-    step CPU work (encode the new key, reconstruct, attention) of `pairs` synthetic
-    (sequence, KV head) pairs at the full context; ms_per_step is that sample's measured
-    time and value the tokens/s it implies (1 / (time per pair x layers x KV heads))."""
+    """The reference arm: the CPU implementation of this path on the decode workload's config,
+    with all host threads - the vectorised PyTorch restatement of the reference's CPU code or
+    the C oracle, whichever is faster here.  A step is a bounded sample: the per-decode-step
+    CPU work (encode the new key, reconstruct, attention) of `pairs` synthetic (sequence, KV
+    head) pairs at the full context; ms_per_step is that sample's measured time and value the
+    tokens/s it implies (1 / (time per pair x layers x KV heads))."""
     if rank != 0:
         return
     import bgtq  # noqa: F401  (tables only)
@@ -278,22 +337,27 @@ def run_reference(args, rank, world):
     p, cfg, tab = tables()
     threads = os.cpu_count() or 1
     pairs = synthetic_pairs(oracle, cfg, tab, args.context, 8)
-    per_pair, _ = cpu_pair_rate(oracle, cfg, tab, pairs, threads, 0.0)
+    kind, times = fastest_port(pairs, threads, 0.0)
+    run = pair_runner(kind, threads)
+    per_pair = times[kind][0]
     per_step_pairs = max(8, int(1.0 / per_pair) // 8 * 8)            # about one second per step
     step_pairs = (pairs * (per_step_pairs // len(pairs) + 1))[:per_step_pairs]
     for _ in range(args.warmup):
-        cpu_pair_rate(oracle, cfg, tab, step_pairs, threads, 0.0)
-    times = []
+        cpu_pair_rate(run, step_pairs, 0.0)
+    times_s = []
     for _ in range(max(1, args.steps)):
         t0 = time.perf_counter()
-        cpu_pair_rate(oracle, cfg, tab, step_pairs, threads, 0.0)
-        times.append(time.perf_counter() - t0)
-    step_s = float(np.sum(times)) / len(times)
+        cpu_pair_rate(run, step_pairs, 0.0)
+        times_s.append(time.perf_counter() - t0)
+    step_s = float(np.sum(times_s)) / len(times_s)
     value = per_step_pairs / step_s / (args.layers * KV_HEADS)
-    cb = {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+    cb = {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "port": kind,
+          "ms_per_pair": {k: v[0] * 1e3 for k, v in times.items()},
           "sample": f"each step: {per_step_pairs} synthetic (sequence, KV head) pairs at context {args.context} "
-                    f"(encode the new key + reconstruct + attention for {GQA} query rows), {step_s * 1e3:.0f} ms; "
-                    f"tokens/s = pairs / time / ({args.layers} layers x {KV_HEADS} KV heads)"}
+                    f"(encode the new key + reconstruct + attention for {GQA} query rows) in the {kind} restatement "
+                    f"of the reference's CPU path, {step_s * 1e3:.0f} ms; tokens/s = pairs / time / "
+                    f"({args.layers} layers x {KV_HEADS} KV heads)",
+          "reference_python_config1": reference_timing_here()}
     print(json.dumps({"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
                       "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
                       "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",

@@ -223,6 +223,14 @@ class Values(_Store):
         self._handle = h
         self.dim, self.capacity, self.sequences, self.device, self.dtype = int(dim), int(capacity), int(sequences), device, dtype
 
+    def read(self, seq: int = 0, row0: int = 0, count: int | None = None):
+        """Rows [row0, row0 + count) of sequence seq as the store holds them: float16 for FP16
+        stores, float32 for FP32 stores, [count, dim] (bgtq_values_read)."""
+        count = self.lengths(seq) - row0 if count is None else count
+        out = np.zeros((count, self.dim), np.float16 if self.dtype == "f16" else np.float32)
+        _lib.call("bgtq_values_read", self._handle, seq, row0, count, out.ctypes.data)
+        return out
+
     def append(self, values, seq_first: int = 0, stream=None) -> None:
         ptr, dt, host, seqs, count, rs, ss, keep, ts = as_source(values, self.dim)
         _lib.call("bgtq_values_append", self._handle, C.c_void_p(ptr), dt, host, count, rs, seq_first, seqs, ss,

@@ -733,6 +733,33 @@ bgtq_status bgtq_values_append(bgtq_values *v, const void *src, bgtq_dtype dtype
     return BGTQ_OK;
 }
 
+bgtq_status bgtq_values_read(const bgtq_values *v, uint32_t seq, uint32_t row0, uint32_t count, void *out) {
+    if (!v || !out || seq >= v->sequences || (uint64_t)row0 + count > v->cap_alloc)
+        return fail(BGTQ_EINVAL, "invalid range");
+    if (!count) return BGTQ_OK;
+    DeviceGuard g(v->device);
+    CK(cudaDeviceSynchronize(), "V read");
+    const size_t es = v->dtype == BGTQ_F32 ? 4 : 2, row = (size_t)v->D * es;
+    std::vector<unsigned char> raw((size_t)count * row);
+    CK(cudaMemcpy(raw.data(), static_cast<const unsigned char *>(v->data) + ((uint64_t)seq * v->cap_alloc + row0) * row,
+                  raw.size(), cudaMemcpyDeviceToHost),
+       "V read");
+    const bool swz = values_swizzled(v->dtype == BGTQ_F32, v->D);
+    unsigned char *o = static_cast<unsigned char *>(out);
+    for (uint32_t r = 0; r < count; ++r) {
+        const uint32_t t = row0 + r;
+        for (uint32_t e = 0; e < v->dim; ++e) {
+            uint32_t de = e;
+            if (swz) {
+                const uint32_t c = e >> 3;
+                de = (((c & ~7u) | ((c ^ t) & 7u)) << 3) | (e & 7u);
+            }
+            std::memcpy(o + ((size_t)r * v->dim + e) * es, raw.data() + (size_t)r * row + (size_t)de * es, es);
+        }
+    }
+    return BGTQ_OK;
+}
+
 bgtq_status bgtq_values_length(const bgtq_values *v, uint32_t seq, uint32_t *out) {
     if (!v || !out || seq >= v->sequences) return fail(BGTQ_EINVAL, "invalid argument");
     *out = v->lengths[seq];

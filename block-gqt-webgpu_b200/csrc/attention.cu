@@ -210,15 +210,25 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
     a.tokens_per_split = tps;
     if (splits_out) *splits_out = splits;
     dim3 grid(splits, a.heads, a.seq_count);
-    attn::qrot_kernel<<<dim3(a.heads, a.seq_count), 128, 0, s>>>(a, d, D, e.qp, kk == KKind::Packed ? 1 : 0);
-    cudaError_t err = cudaGetLastError();
+    cudaError_t err = launch_pdl(attn::qrot_kernel, dim3(a.heads, a.seq_count), dim3(128), 0, s, a, d, D, e.qp,
+                                 kk == KKind::Packed ? 1 : 0);
     if (err != cudaSuccess) return err;
     if (jk) {
         uint32_t dd = d;
         Plan plc = pl;
         void *args[] = {&a, &plc, &dd};
         if (head_major) grid = dim3(splits, a.seq_count, a.heads);
-        return cudaLaunchKernel(jk, grid, dim3(attn::kThreads), args, pl.total, s);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(attn::kThreads);
+        cfg.dynamicSmemBytes = pl.total;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelExC(&cfg, jk, args);
     }
     return e.run(a, pl, d, grid, s);
 }

@@ -479,6 +479,7 @@ struct MinBlocks {
 template <int D, int QM, KKind KK, bool VF32, class LP>
 __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uint32_t d, uint32_t split, uint32_t hd,
                                           uint32_t s) {
+    pdl_wait();
     constexpr int TPL = Geo<D>::TPL, TT = Geo<D>::TT, QP = QPad<QM>::QP;
     constexpr bool MMA = UseMma<D, VF32>::value;
     constexpr int VSZ = VF32 ? 4 : 2, VEC = 16 / VSZ, LPT = D / VEC, TPS = 32 / LPT;
@@ -981,10 +982,18 @@ __device__ __forceinline__ float rope_elem(const float *q, uint32_t j, uint32_t 
 static __global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant__ AttnArgs a, uint32_t d, uint32_t D,
                                                    uint32_t QP, int packed) {
     __shared__ float qraw[kMaxRows * kMaxDim];
+    __shared__ __align__(16) float rot_s[64 * 64];   // the head's rotation, head dims up to 64
+    pdl_wait();
+    pdl_trigger();
     const uint32_t hd = blockIdx.x, s = blockIdx.y, R = a.rows;
     const AttnHead &h = a.head[hd];
     const float *qg = a.q + ((uint64_t)s * a.heads + hd) * (uint64_t)R * d;
     const uint32_t len = a.lengths[a.seq_first + s];
+    // the rotation rows are read by every output: one coalesced copy into shared memory
+    // instead of a chain of dependent L2 reads per output
+    const bool staged = packed && d <= 64;
+    if (staged)
+        for (uint32_t idx = threadIdx.x; idx < d * d; idx += blockDim.x) rot_s[idx] = h.rot[idx];
     for (uint32_t idx = threadIdx.x; idx < R * d; idx += blockDim.x) {
         const uint32_t r = idx / d, i = idx % d;
         // a query sits at its position (default: the last appended row)
@@ -1000,7 +1009,7 @@ static __global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant_
         if (r < R && j < d) {
             if (packed) {
                 const uint32_t g = h.group_of[j], lo = h.group_off[g], hi = h.group_off[g + 1];
-                const float *rj = h.rot + (uint64_t)j * d;
+                const float *rj = (staged ? rot_s : h.rot) + (uint64_t)j * d;
                 for (uint32_t i = lo; i < hi; ++i) v = fmaf(rj[i], qraw[r * d + i], v);
             } else {
                 v = qraw[r * d + j];
@@ -1024,8 +1033,7 @@ cudaError_t run(const AttnArgs &a, const Plan &pl, uint32_t d, dim3 grid, cudaSt
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = (int)pl.total;
     }
-    kern<<<grid, kThreads, pl.total, s>>>(a, pl, d);
-    return cudaGetLastError();
+    return launch_pdl(kern, grid, dim3(kThreads), pl.total, s, a, pl, d);
 }
 
 // Resident CTAs per SM for a plan; remembered per (device, shared-memory size), so launches

@@ -34,6 +34,17 @@ constexpr int kMaxHeads = 8;      // KV heads bound to one attention object / on
 constexpr int kMaxRows = 8;       // query rows per KV head
 constexpr uint32_t kTileRows = 64; // capacity is padded to a multiple of this
 
+// Programmatic dependent launch.  Kernels of the decode chain (model GEMVs, K/V append,
+// query rotation, attention) are launched with programmatic stream serialisation, so the
+// next kernel's launch overlaps the end of the one before it; each of them waits for its
+// predecessor's completion (griddepcontrol.wait) as its first statement, before it reads or
+// writes any memory, and the short ones allow their own successor to launch early
+// (griddepcontrol.launch_dependents).  Launched without the attribute, both are no-ops.
+#if defined(__CUDACC__) || defined(__CUDACC_RTC__)
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+#endif
+
 // Device status word bits (bgtq_device_status).
 constexpr uint32_t kStatusWaitTimeout = 1u;   // an mbarrier wait hit its iteration bound
 constexpr uint32_t kStatusBadLength = 2u;     // a kernel saw a length beyond capacity
@@ -233,6 +244,23 @@ void jit_set_enabled(int on);
 // promises no allocation at attention time: loading a specialised kernel allocates).
 void jit_suppress_on_thread(int on);
 
+// Launch `kern` with programmatic stream serialisation (see pdl_wait).
+#ifdef __CUDACC__
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<Args &&>(args)...);
+}
+#endif
 uint32_t *device_status_word(int device);  // lazily allocated per device
 uint32_t *device_status_word_if_present(int device);  // never allocates; null if absent
 void set_last_error(const std::string &message);     // message of bgtq_last_error()

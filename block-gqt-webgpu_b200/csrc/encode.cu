@@ -264,108 +264,137 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
 
 // ---- bulk encode, head dims up to 64: tiles of keys, every phase over the whole tile ----
 //
-// A persistent CTA of KT = 32 * KPL threads stages one head's tables once and walks tiles of
-// KT keys.  Per tile, in shared memory, the work the oracle does key by key in the same
-// operation order:
+// A persistent CTA of 256 threads stages one head's tables once and walks tiles of KT = 128
+// keys.  Per tile, in shared memory, the work the oracle does key by key, in its operation
+// order:
 //   1. input rows staged as FP16 words (coalesced), gathered through the permutation into
 //      X[i][k] (FP32, key-minor: lanes over keys read consecutive words);
-//   2. thread k: each group's sum of squares (sequential FMAs, ascending dims), its norm,
-//      and the division of the group's elements by it;
+//   2. one thread per (key, group): the group's sum of squares (sequential FMAs, ascending
+//      dims), its norm, and the division of the group's elements by it;
 //   3. the block-diagonal rotation as a register-blocked product: one warp per output dim
-//      pair (j, j + 1) of a group, each lane KPL keys, one packed FMA (fma.rn.f32x2) per two
-//      keys and dimension - each y_j still one sequential FMA chain over its group in
-//      ascending i, so every value is the oracle's bit for bit.  The dim pairs are dealt to
-//      the warps longest-group-first (each pair costs its group's size);
-//   4. thread k: per dimension the LUT bin and code, per group the sequential sum of the
-//      codebook values' squares and the FP16 corrected scale, the packed row bytes;
+//      pair (j, j + 1) of a group, each lane 4 keys, one packed FMA (fma.rn.f32x2) per two
+//      keys and dimension - every y_j still one sequential FMA chain over its group in
+//      ascending i, so each value is the oracle's bit for bit - and straight on to the LUT
+//      bin and the code, stored as bytes (the FP32 outputs never leave registers).  The dim
+//      pairs are dealt to the warps longest-group-first (a pair costs its group's size);
+//   4. one thread per (key, group): the codebook values' squares summed in ascending dims,
+//      the FP16 corrected scale, and the group's packed row bytes;
 //   5. rows and scales written with coalesced word stores.
-template <int D, int KPL>
-struct TileGeo {
-    static constexpr int KT = 32 * KPL;       // keys per tile = threads per CTA
-    static constexpr int W = KT / 32;         // warps
-    static constexpr int SW = D / 2 + 1;      // staged input words per key (odd: conflict-free gathers)
+// The rotation blocks are kept duplicated ((R[j][i], R[j][i]) float pairs, the operand
+// layout of the packed FMA) and compact (only the blocks on the diagonal).
+constexpr int kTileKeys = 128, kTileThreads = 256, kTileWarps = kTileThreads / 32;
+
+template <int D>
+struct TileSmem {
+    uint32_t rdup, jc, cent, x, nrm, uni, codes, out, sc, rows, lut, perm, task, total;
 };
 
-template <int D, int KPL>
-size_t encode_tile_smem(uint32_t cent_alloc, uint32_t lut_bytes, uint32_t row_stride, uint32_t scale_stride) {
-    using G = TileGeo<D, KPL>;
-    const size_t ow = (row_stride / 4) | 1u, sw = scale_stride / 2 + 1;
-    size_t b = 8ull * D * D;                                   // rdup
-    b += 16ull * D;                                            // per-dimension constants
-    b += 4ull * ((cent_alloc + 3) & ~3u);                      // codebooks
-    b += 4ull * D * G::KT * 2;                                 // X and Y
-    b += 4ull * kMaxGroups * G::KT;                            // group norms
-    b += 4ull * G::KT * sw;                                    // scale rows
-    b += 8ull * G::KT * 3;                                     // row address table
-    b += lut_bytes + D + (D / 2) * G::W + 16;                  // code LUT, permutation, schedule
-    (void)ow;
-    return (b + 15) & ~(size_t)15;
+template <int D>
+__host__ __device__ TileSmem<D> tile_smem(uint32_t rdup_pairs, uint32_t cent_alloc, uint32_t lut_bytes, uint32_t row_stride,
+                      uint32_t scale_stride) {
+    auto a16 = [](uint32_t x) { return (x + 15u) & ~15u; };
+    const uint32_t ow = (row_stride / 4) | 1u, sw = scale_stride / 2 + 1;
+    TileSmem<D> t{};
+    uint32_t o = 0;
+    t.rdup = o; o += a16(8u * rdup_pairs);
+    t.jc = o; o += 16u * D;
+    t.cent = o; o += a16(4u * cent_alloc);
+    t.x = o; o += 4u * D * kTileKeys;
+    t.nrm = o; o += 4u * kMaxGroups * kTileKeys;
+    // the staged FP16 input (phase 1) shares its space with the codes, rows and scales
+    // (phases 3-5)
+    const uint32_t stage = 4u * kTileKeys * (D / 2 + 1);
+    const uint32_t codes = a16(D * kTileKeys), out = a16(4u * kTileKeys * ow), sc = a16(4u * kTileKeys * sw);
+    t.uni = o;
+    t.codes = o; t.out = o + codes; t.sc = o + codes + out;
+    o += a16(stage > codes + out + sc ? stage : codes + out + sc);
+    t.rows = o; o += 8u * 3u * kTileKeys;
+    t.lut = o; o += a16(lut_bytes);
+    t.perm = o; o += a16(D);
+    t.task = o; o += 8u * (D / 2) * kTileWarps;
+    t.total = a16(o);
+    return t;
 }
 
-template <int D, int KPL>
-__global__ void __launch_bounds__(32 * KPL) encode_tile_kernel(const __grid_constant__ EncodeArgs a, uint32_t d,
-                                                               uint32_t cent_alloc, uint32_t lut_bytes,
-                                                               uint32_t total) {
-    using G = TileGeo<D, KPL>;
-    constexpr int KT = G::KT, SW = G::SW, W = G::W;
+template <int D>
+__global__ void __launch_bounds__(kTileThreads, 2) encode_tile_kernel(const __grid_constant__ EncodeArgs a, uint32_t d,
+                                                                      uint32_t cent_alloc, uint32_t lut_bytes,
+                                                                      uint32_t rdup_pairs, uint32_t total) {
+    constexpr int KT = kTileKeys, W = kTileWarps, SW = D / 2 + 1;
     const EncodeHead &h = a.head[blockIdx.y];
     const uint32_t row_words = h.row_stride / 4, ow = row_words | 1u;
     const uint32_t sc_words = h.scale_stride / 2, sw = sc_words + 1;
     const uint32_t ng = h.ng, ns = h.ns, count = a.count;
+    const TileSmem<D> L = tile_smem<D>(rdup_pairs, cent_alloc, lut_bytes, h.row_stride, h.scale_stride);
 
     extern __shared__ __align__(16) unsigned char smem[];
-    float2 *rdup = reinterpret_cast<float2 *>(smem);                       // [D][D]: (R[j][i], R[j][i]) at i*D + j
-    float4 *jc = reinterpret_cast<float4 *>(rdup + D * D);                 // [D]: off, inv, lut base, cent base
-    float *cent_s = reinterpret_cast<float *>(jc + D);                     // [cent_alloc]
-    float *X = cent_s + ((cent_alloc + 3) & ~3u);                          // [D][KT]
-    float *Y = X + D * KT;                                                 // [D][KT]
-    float *nrm = Y + D * KT;                                               // [kMaxGroups][KT]
-    uint32_t *sc_s = reinterpret_cast<uint32_t *>(nrm + kMaxGroups * KT);  // [KT][sw]
-    uint64_t *rsrc_s = reinterpret_cast<uint64_t *>(sc_s + KT * sw);       // [KT]
-    uint64_t *rdst_s = rsrc_s + KT, *rsc_s = rdst_s + KT;                  // [KT] each
-    uint8_t *lut_s = reinterpret_cast<uint8_t *>(rsc_s + KT);              // [lut_bytes]
-    uint8_t *perm_s = lut_s + lut_bytes;                                   // [D]
-    uint8_t *sched_s = perm_s + D;                                         // [W][D/2] dim pairs per warp
-    __shared__ uint32_t sched_n[W];
-    uint32_t *stage_s = reinterpret_cast<uint32_t *>(Y);                   // [KT][SW], before Y is written
-    uint32_t *out_s = reinterpret_cast<uint32_t *>(X);                     // [KT][ow], after X is consumed
+    float2 *rdup = reinterpret_cast<float2 *>(smem + L.rdup);      // diagonal blocks, (R[j][i], R[j][i])
+    float4 *jc = reinterpret_cast<float4 *>(smem + L.jc);          // [D]: off, inv, lut base, cent base
+    float *cent_s = reinterpret_cast<float *>(smem + L.cent);
+    float *X = reinterpret_cast<float *>(smem + L.x);              // [D][KT]
+    float *nrm = reinterpret_cast<float *>(smem + L.nrm);          // [kMaxGroups][KT]
+    uint32_t *stage_s = reinterpret_cast<uint32_t *>(smem + L.uni);  // [KT][SW] (phase 1 only)
+    uint8_t *codes = smem + L.codes;                               // [D][KT]
+    uint32_t *out_s = reinterpret_cast<uint32_t *>(smem + L.out);  // [KT][ow]
+    uint32_t *sc_s = reinterpret_cast<uint32_t *>(smem + L.sc);    // [KT][sw]
+    uint64_t *rsrc_s = reinterpret_cast<uint64_t *>(smem + L.rows), *rdst_s = rsrc_s + KT, *rsc_s = rdst_s + KT;
+    uint8_t *lut_s = smem + L.lut;
+    uint8_t *perm_s = smem + L.perm;
+    uint2 *task_s = reinterpret_cast<uint2 *>(smem + L.task);      // [W][D/2]
+    __shared__ uint32_t task_n[W];
+    __shared__ uint2 pair_s[D / 2];   // per dim pair: j0 | group start << 8 | group end << 16, block base
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // ---- the head's tables, once per CTA ----
-    for (uint32_t e = tid; e < (uint32_t)(D * D); e += KT) {
-        const uint32_t i = e / D, j = e % D;
-        const float r = (i < d && j < d) ? h.t.rot[j * d + i] : 0.0f;
-        rdup[e] = make_float2(r, r);
+    for (uint32_t g = 0; g < ng; ++g) {
+        const uint32_t lo = h.group_off[g], n = h.group_off[g + 1] - lo;
+        uint32_t base = 0;
+        for (uint32_t q = 0; q < g; ++q) base += (h.group_off[q + 1] - h.group_off[q]) * (h.group_off[q + 1] - h.group_off[q]);
+        for (uint32_t e = tid; e < n * n; e += kTileThreads) {
+            const uint32_t i = e / n, j = e % n;   // block element (i, j): R[lo + j][lo + i]
+            const float r = h.t.rot[(lo + j) * d + lo + i];
+            rdup[base + e] = make_float2(r, r);
+        }
     }
-    for (uint32_t j = tid; j < (uint32_t)D; j += KT) {
+    for (uint32_t j = tid; j < (uint32_t)D; j += kTileThreads) {
         const bool live = j < d;
         jc[j] = make_float4(live ? h.t.off[j] : 0.0f, live ? h.t.inv[j] : 0.0f,
                             __uint_as_float(live ? (uint32_t)h.t.cbidx[j] * 256u : 0u),
                             __uint_as_float(live ? (uint32_t)h.t.cb_base[j] : 0u));
         perm_s[j] = live ? h.t.perm[j] : (uint8_t)j;
     }
-    for (uint32_t e = tid; e < cent_alloc; e += KT) cent_s[e] = e < h.n_cent ? h.t.cent[e] : 0.0f;
-    for (uint32_t e = tid; e < lut_bytes; e += KT) lut_s[e] = e < h.ncb * 256u ? h.t.lut[e] : 0;
+    for (uint32_t e = tid; e < cent_alloc; e += kTileThreads) cent_s[e] = e < h.n_cent ? h.t.cent[e] : 0.0f;
+    for (uint32_t e = tid; e < lut_bytes; e += kTileThreads) lut_s[e] = e < h.ncb * 256u ? h.t.lut[e] : 0;
+    for (uint32_t p = tid; p < (uint32_t)D / 2; p += kTileThreads) {
+        uint2 w = make_uint2(0u, 0u);
+        if (2u * p < d) {
+            const uint32_t g = h.t.group_of[2 * p], lo = h.group_off[g], hi = h.group_off[g + 1];
+            uint32_t base = 0;
+            for (uint32_t q = 0; q < g; ++q)
+                base += (h.group_off[q + 1] - h.group_off[q]) * (h.group_off[q + 1] - h.group_off[q]);
+            w = make_uint2(2u * p | lo << 8 | hi << 16, base);
+        }
+        pair_s[p] = w;
+    }
+    __syncthreads();
     if (tid == 0) {
         // longest-processing-time deal of the dim pairs to the warps; a pair costs its group size
         uint32_t load[W];
-        for (int w = 0; w < W; ++w) load[w] = 0, sched_n[w] = 0;
-        bool taken[D / 2];
-        for (int p = 0; p < D / 2; ++p) taken[p] = 2u * p >= d;
+        for (int w = 0; w < W; ++w) load[w] = 0, task_n[w] = 0;
+        uint64_t taken = 0;
         for (uint32_t n = 0; n < d / 2; ++n) {
             int best = -1;
             uint32_t best_cost = 0;
             for (int p = 0; p < D / 2; ++p) {
-                if (taken[p]) continue;
-                const uint32_t g = h.t.group_of[2 * p];
-                const uint32_t c = h.group_off[g + 1] - h.group_off[g];
+                if (((taken >> p) & 1u) || 2u * p >= d) continue;
+                const uint32_t w = pair_s[p].x, c = (w >> 16) - ((w >> 8) & 0xffu);
                 if (best < 0 || c > best_cost) best = p, best_cost = c;
             }
             int wmin = 0;
             for (int w = 1; w < W; ++w)
                 if (load[w] < load[wmin]) wmin = w;
-            taken[best] = true;
-            sched_s[wmin * (D / 2) + sched_n[wmin]++] = (uint8_t)best;
+            taken |= 1ull << best;
+            task_s[wmin * (D / 2) + task_n[wmin]++] = pair_s[best];
             load[wmin] += best_cost;
         }
     }
@@ -390,7 +419,7 @@ __global__ void __launch_bounds__(32 * KPL) encode_tile_kernel(const __grid_cons
         __syncthreads();
         // ---- 1. input rows as FP16 words (coalesced), then X[i][k] through the permutation ----
         if (vec16) {
-            for (uint32_t w = tid; w < nrows * (uint32_t)(D / 8); w += KT) {
+            for (uint32_t w = tid; w < nrows * (uint32_t)(D / 8); w += kTileThreads) {
                 const uint32_t r = w / (D / 8), c = w % (D / 8);
                 const uint4 v = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(a.src) + rsrc_s[r] + 8u * c));
                 uint32_t *dst = stage_s + r * SW + 4u * c;
@@ -400,7 +429,7 @@ __global__ void __launch_bounds__(32 * KPL) encode_tile_kernel(const __grid_cons
                 dst[3] = v.w;
             }
         } else {
-            for (uint32_t w = tid; w < nrows * (uint32_t)(D / 2); w += KT) {
+            for (uint32_t w = tid; w < nrows * (uint32_t)(D / 2); w += kTileThreads) {
                 const uint32_t r = w / (D / 2), c = w % (D / 2);
                 uint32_t word = 0;
                 if (2u * c < d) {
@@ -419,102 +448,112 @@ __global__ void __launch_bounds__(32 * KPL) encode_tile_kernel(const __grid_cons
         }
         __syncthreads();
         {
-            const uint16_t *st = reinterpret_cast<const uint16_t *>(stage_s + tid * SW);
+            // thread = key (lanes over keys: conflict-free, SW odd) x a quarter of the dims
+            const uint32_t k = tid % KT, i0 = tid / KT;
+            const __half *st = reinterpret_cast<const __half *>(stage_s + k * SW);
 #pragma unroll 8
-            for (int i = 0; i < D; ++i) X[i * KT + tid] = __half2float(__ushort_as_half(st[perm_s[i]]));
+            for (uint32_t i = i0; i < (uint32_t)D; i += kTileThreads / KT) X[i * KT + k] = __half2float(st[perm_s[i]]);
         }
         __syncthreads();
-        // ---- 2. group norms and normalisation (thread = key) ----
-        for (uint32_t g = 0; g < ng; ++g) {
+        // ---- 2. group norms and normalisation, one thread per (key, group) ----
+        for (uint32_t t = tid; t < KT * ng; t += kTileThreads) {
+            const uint32_t k = t % KT, g = t / KT;
             const uint32_t lo = h.group_off[g], hi = h.group_off[g + 1];
             float acc = 0.0f;
+            const float *xk = X + k;
+#pragma unroll 4
             for (uint32_t i = lo; i < hi; ++i) {
-                const float x = X[i * KT + tid];
+                const float x = xk[i * KT];
                 acc = fmaf(x, x, acc);
             }
             const float n = sqrtf(acc + 1e-30f);
-            nrm[g * KT + tid] = n;
+            nrm[g * KT + k] = n;
             const float dv = n > 1e-10f ? n : 1.0f;
 #pragma unroll 4
-            for (uint32_t i = lo; i < hi; ++i) X[i * KT + tid] = X[i * KT + tid] / dv;
+            for (uint32_t i = lo; i < hi; ++i) X[i * KT + k] = X[i * KT + k] / dv;
         }
         __syncthreads();
-        // ---- 3. rotation: warp = output dim pair, lane = KPL keys ----
+        // ---- 3. rotation + codes: warp = output dim pair, lane = 4 keys ----
         {
-            const uint32_t npairs = sched_n[warp];
-            for (uint32_t t = 0; t < npairs; ++t) {
-                const uint32_t j0 = 2u * sched_s[warp * (D / 2) + t];
-                const uint32_t g = h.t.group_of[j0];
-                const uint32_t lo = h.group_off[g], hi = h.group_off[g + 1];
-                float2 y0[KPL / 2], y1[KPL / 2];
-#pragma unroll
-                for (int c = 0; c < KPL / 2; ++c) y0[c] = y1[c] = make_float2(0.0f, 0.0f);
-#pragma unroll 2
-                for (uint32_t i = lo; i < hi; ++i) {
-                    const float4 r = *reinterpret_cast<const float4 *>(rdup + i * D + j0);
+            const uint32_t ntask = task_n[warp];
+            for (uint32_t t = 0; t < ntask; ++t) {
+                const uint2 task = task_s[warp * (D / 2) + t];
+                const uint32_t j0 = task.x & 0xffu, lo = (task.x >> 8) & 0xffu, hi = task.x >> 16, n = hi - lo;
+                const float4 *rb = reinterpret_cast<const float4 *>(rdup + task.y + (j0 - lo));
+                const float4 *xp = reinterpret_cast<const float4 *>(X + lo * KT + 4 * lane);
+                const uint32_t rstep = n / 2;   // float4 per block row
+                float2 y0a = make_float2(0.0f, 0.0f), y0b = y0a, y1a = y0a, y1b = y0a;
+#pragma unroll 4
+                for (uint32_t i = 0; i < n; ++i) {
+                    const float4 r = rb[i * rstep];
+                    const float4 x = xp[i * (KT / 4)];
                     const float2 r0 = make_float2(r.x, r.y), r1 = make_float2(r.z, r.w);
-#pragma unroll
-                    for (int c = 0; c < KPL / 4; ++c) {
-                        const float4 x = *reinterpret_cast<const float4 *>(X + i * KT + c * 128 + 4 * lane);
-                        y0[2 * c] = ffma2(make_float2(x.x, x.y), r0, y0[2 * c]);
-                        y0[2 * c + 1] = ffma2(make_float2(x.z, x.w), r0, y0[2 * c + 1]);
-                        y1[2 * c] = ffma2(make_float2(x.x, x.y), r1, y1[2 * c]);
-                        y1[2 * c + 1] = ffma2(make_float2(x.z, x.w), r1, y1[2 * c + 1]);
-                    }
+                    const float2 xa = make_float2(x.x, x.y), xb = make_float2(x.z, x.w);
+                    y0a = ffma2(xa, r0, y0a);
+                    y0b = ffma2(xb, r0, y0b);
+                    y1a = ffma2(xa, r1, y1a);
+                    y1b = ffma2(xb, r1, y1b);
                 }
+                const float y0[4] = {y0a.x, y0a.y, y0b.x, y0b.y}, y1[4] = {y1a.x, y1a.y, y1b.x, y1b.y};
 #pragma unroll
-                for (int c = 0; c < KPL / 4; ++c) {
-                    *reinterpret_cast<float4 *>(Y + j0 * KT + c * 128 + 4 * lane) =
-                        make_float4(y0[2 * c].x, y0[2 * c].y, y0[2 * c + 1].x, y0[2 * c + 1].y);
-                    *reinterpret_cast<float4 *>(Y + (j0 + 1) * KT + c * 128 + 4 * lane) =
-                        make_float4(y1[2 * c].x, y1[2 * c].y, y1[2 * c + 1].x, y1[2 * c + 1].y);
+                for (int q = 0; q < 2; ++q) {
+                    const uint32_t j = j0 + q;
+                    const float4 c4 = jc[j];
+                    uint32_t word = 0;
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        float tv = ((q ? y1[kk] : y0[kk]) - c4.x) * c4.y;
+                        tv = fminf(fmaxf(tv, 0.0f), 255.0f);
+                        word |= (uint32_t)lut_s[__float_as_uint(c4.z) + (uint32_t)tv] << (8 * kk);
+                    }
+                    reinterpret_cast<uint32_t *>(codes + j * KT)[lane] = word;
                 }
             }
         }
         __syncthreads();
-        // ---- 4. codes, corrected scales, packed row (thread = key) ----
-        {
-            uint32_t *orow = out_s + tid * ow;
-            for (uint32_t w = 0; w < ow; ++w) orow[w] = 0;
-            uint8_t *ob = reinterpret_cast<uint8_t *>(orow);
-            uint16_t *srow = reinterpret_cast<uint16_t *>(sc_s + tid * sw);
-            for (uint32_t w = 0; w < sw; ++w) sc_s[tid * sw + w] = 0;
-            for (uint32_t g = 0; g < ng; ++g) {
-                const uint32_t lo = h.group_off[g], hi = h.group_off[g + 1];
-                float cl = 0.0f;
-                uint32_t pend = 0;
-#pragma unroll 2
-                for (uint32_t j = lo; j < hi; ++j) {
-                    const float4 c4 = jc[j];
-                    float t = (Y[j * KT + tid] - c4.x) * c4.y;
-                    t = fminf(fmaxf(t, 0.0f), 255.0f);
-                    const uint32_t code = lut_s[__float_as_uint(c4.z) + (uint32_t)t];
-                    const float cv = cent_s[__float_as_uint(c4.w) + code];
-                    cl = fmaf(cv, cv, cl);
-                    if (j < ns) {
-                        if (j & 1u) ob[j >> 1] = (uint8_t)(pend | (code << 4));
-                        else pend = code;
-                    } else {
-                        ob[(ns >> 1) + (j - ns)] = (uint8_t)code;
-                    }
+        // ---- 4. corrected scales and packed bytes, one thread per (key, group) ----
+        for (uint32_t t = tid; t < KT * ng; t += kTileThreads) {
+            const uint32_t k = t % KT, g = t / KT;
+            const uint32_t lo = h.group_off[g], hi = h.group_off[g + 1];
+            uint8_t *ob = reinterpret_cast<uint8_t *>(out_s + k * ow);
+            float cl = 0.0f;
+#pragma unroll 4
+            for (uint32_t j = lo; j < hi; j += 2) {
+                const uint32_t c0 = codes[j * KT + k], c1 = codes[(j + 1) * KT + k];
+                const float v0 = cent_s[__float_as_uint(jc[j].w) + c0], v1 = cent_s[__float_as_uint(jc[j + 1].w) + c1];
+                cl = fmaf(v0, v0, cl);
+                cl = fmaf(v1, v1, cl);
+                if (j < ns) {
+                    ob[j >> 1] = (uint8_t)(c0 | (c1 << 4));
+                } else {
+                    ob[(ns >> 1) + (j - ns)] = (uint8_t)c0;
+                    ob[(ns >> 1) + (j - ns) + 1] = (uint8_t)c1;
                 }
-                srow[g] = __half_as_ushort(__float2half_rn(nrm[g * KT + tid] / fmaxf(sqrtf(cl), 1e-10f)));
             }
+            reinterpret_cast<uint16_t *>(sc_s + k * sw)[g] =
+                __half_as_ushort(__float2half_rn(nrm[g * KT + k] / fmaxf(sqrtf(cl), 1e-10f)));
+        }
+        // row padding and unused scale slots are zero
+        for (uint32_t k = tid; k < KT; k += kTileThreads) {
+            uint8_t *ob = reinterpret_cast<uint8_t *>(out_s + k * ow);
+            for (uint32_t b = ns / 2 + (d - ns); b < row_words * 4; ++b) ob[b] = 0;
+            uint16_t *sr = reinterpret_cast<uint16_t *>(sc_s + k * sw);
+            for (uint32_t g = ng; g < sc_words * 2; ++g) sr[g] = 0;
         }
         __syncthreads();
         // ---- 5. rows and scales out (coalesced words) ----
-        for (uint32_t w = tid; w < nrows * row_words; w += KT) {
+        for (uint32_t w = tid; w < nrows * row_words; w += kTileThreads) {
             const uint32_t r = div_small(w, row_words, rw_magic), c = w - r * row_words;
             reinterpret_cast<uint32_t *>(h.packed + rdst_s[r])[c] = out_s[r * ow + c];
         }
-        for (uint32_t w = tid; w < nrows * sc_words; w += KT) {
+        for (uint32_t w = tid; w < nrows * sc_words; w += kTileThreads) {
             const uint32_t r = div_small(w, sc_words, sw_magic), c = w - r * sc_words;
             reinterpret_cast<uint32_t *>(h.scales + rsc_s[r])[c] = sc_s[r * sw + c];
         }
         __syncthreads();
     }
     if (blockIdx.x == 0 && h.lengths) {
-        for (uint32_t s = tid; s < a.seq_count; s += KT)
+        for (uint32_t s = tid; s < a.seq_count; s += kTileThreads)
             h.lengths[a.seq_first + s] = (a.row0 ? a.row0[s] : a.row0_scalar) + count;
     }
 }
@@ -732,6 +771,8 @@ __device__ __forceinline__ float src_elem(const void *p, uint64_t i, uint32_t f1
 __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_constant__ KvRopeArgs a, uint32_t d,
                                                                   uint32_t total, uint32_t stage_bytes) {
     constexpr int W = kThreads / 32;
+    pdl_wait();
+    pdl_trigger();
     const uint32_t hd = blockIdx.y;
     __shared__ WarpKey wks[W];
     __shared__ float kr[W][kMaxDim];
@@ -866,50 +907,37 @@ cudaError_t run_encode(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uin
     return cudaGetLastError();
 }
 
-template <int D, int KPL>
+template <int D>
 cudaError_t run_encode_tile(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uint32_t max_ncb, cudaStream_t s) {
-    using G = TileGeo<D, KPL>;
-    uint32_t row_stride = 0, scale_stride = 0;
+    uint32_t row_stride = 0, scale_stride = 0, rdup_pairs = 0;
     for (uint32_t h = 0; h < a.heads; ++h) {
-        row_stride = row_stride > a.head[h].row_stride ? row_stride : a.head[h].row_stride;
-        scale_stride = scale_stride > a.head[h].scale_stride ? scale_stride : a.head[h].scale_stride;
+        const EncodeHead &e = a.head[h];
+        row_stride = row_stride > e.row_stride ? row_stride : e.row_stride;
+        scale_stride = scale_stride > e.scale_stride ? scale_stride : e.scale_stride;
+        uint32_t pairs = 0;
+        for (uint32_t g = 0; g < e.ng; ++g) pairs += (e.group_off[g + 1] - e.group_off[g]) * (e.group_off[g + 1] - e.group_off[g]);
+        rdup_pairs = rdup_pairs > pairs ? rdup_pairs : pairs;
     }
     const uint32_t lut_bytes = (max_ncb * 256u + 15u) & ~15u;
-    const size_t smem = encode_tile_smem<D, KPL>(cent_alloc, lut_bytes, row_stride, scale_stride);
+    const uint32_t smem = tile_smem<D>(rdup_pairs, cent_alloc, lut_bytes, row_stride, scale_stride).total;
     int dev = 0, sms = 0, max_optin = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    if (smem > (size_t)max_optin) return cudaErrorInvalidConfiguration;
-    cudaError_t e =
-        cudaFuncSetAttribute(encode_tile_kernel<D, KPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem > (uint32_t)max_optin) return cudaErrorInvalidConfiguration;
+    cudaError_t e = cudaFuncSetAttribute(encode_tile_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, encode_tile_kernel<D, KPL>, G::KT, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, encode_tile_kernel<D>, kTileThreads, smem);
     if (per_sm < 1) per_sm = 1;
     const uint32_t total = a.count * a.seq_count;
-    const uint32_t tiles = (total + G::KT - 1) / G::KT;
+    const uint32_t tiles = (total + kTileKeys - 1) / kTileKeys;
     uint32_t grid_x = (uint32_t)(sms * per_sm) / (a.heads ? a.heads : 1);
     if (grid_x < 1) grid_x = 1;
     if (grid_x > tiles) grid_x = tiles;
-    encode_tile_kernel<D, KPL><<<dim3(grid_x, a.heads), G::KT, smem, s>>>(a, d, cent_alloc, lut_bytes, total);
+    encode_tile_kernel<D><<<dim3(grid_x, a.heads), kTileThreads, smem, s>>>(a, d, cent_alloc, lut_bytes, rdup_pairs,
+                                                                            total);
     return cudaGetLastError();
-}
-
-// Keys per lane of the tiled bulk encoder (tiles of 32 x KPL keys): 4 by default, 8 when
-// BGTQ_ENCODE_KPL=8 is set (a tuning knob; both give the same bytes).
-int encode_kpl() {
-    static int kpl = [] {
-        const char *e = getenv("BGTQ_ENCODE_KPL");
-        return (e && atoi(e) == 8) ? 8 : 4;
-    }();
-    return kpl;
-}
-
-template <int D>
-cudaError_t run_encode_tiled(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uint32_t max_ncb, cudaStream_t s) {
-    return encode_kpl() == 8 ? run_encode_tile<D, 8>(a, d, cent_alloc, max_ncb, s)
-                             : run_encode_tile<D, 4>(a, d, cent_alloc, max_ncb, s);
 }
 
 }  // namespace
@@ -919,8 +947,7 @@ cudaError_t launch_kv_rope_append(const KvRopeArgs &a, uint32_t d, cudaStream_t 
     if (!total) return cudaSuccess;
     const uint32_t blocks = (total + kThreads / 32 - 1) / (kThreads / 32);
     const uint32_t stage = encode_stage_bytes(a.head, a.heads);
-    kv_rope_append_kernel<<<dim3(blocks, a.heads), kThreads, stage, s>>>(a, d, total, stage);
-    return cudaGetLastError();
+    return launch_pdl(kv_rope_append_kernel, dim3(blocks, a.heads), dim3(kThreads), stage, s, a, d, total, stage);
 }
 
 cudaError_t launch_encode(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, uint32_t max_ncb, cudaStream_t s) {
@@ -934,9 +961,9 @@ cudaError_t launch_encode(const EncodeArgs &a, uint32_t d, uint32_t cent_alloc, 
         encode_warp_kernel<<<dim3(blocks, a.heads), kThreads, stage, s>>>(a, d, total, stage);
         return cudaGetLastError();
     }
-    if (d <= 16) return run_encode_tiled<16>(a, d, cent_alloc, max_ncb, s);
-    if (d <= 32) return run_encode_tiled<32>(a, d, cent_alloc, max_ncb, s);
-    if (d <= 64) return run_encode_tiled<64>(a, d, cent_alloc, max_ncb, s);
+    if (d <= 16) return run_encode_tile<16>(a, d, cent_alloc, max_ncb, s);
+    if (d <= 32) return run_encode_tile<32>(a, d, cent_alloc, max_ncb, s);
+    if (d <= 64) return run_encode_tile<64>(a, d, cent_alloc, max_ncb, s);
     return run_encode<128>(a, d, cent_alloc, max_ncb, s);
 }
 

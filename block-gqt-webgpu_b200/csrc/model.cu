@@ -50,6 +50,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const float *__restr
                                                             uint32_t out, float *y, uint64_t y_stride) {
     extern __shared__ __align__(16) float xs[];       // [B][in] activations (normalised for the NORM modes)
     __shared__ float red[kGemvWarps][B];
+    pdl_wait();
+    pdl_trigger();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // ---- the activation rows into shared memory (and their RMSNorm) ----
     for (uint32_t e = tid; e < (uint32_t)B * in; e += kGemvThreads) {
@@ -156,12 +158,12 @@ cudaError_t run_gemv(const float *x, uint64_t xs, uint32_t in, const float *nw, 
     }
     if (out >= 16384u) {
         const uint32_t per = kGemvWarps * 4;
-        gemv_kernel<MODE, B, 4><<<(out + per - 1) / per, kGemvThreads, smem, s>>>(x, xs, in, nw, eps, w, bias, out, y, ys);
-    } else {
-        const uint32_t per = kGemvWarps;
-        gemv_kernel<MODE, B, 1><<<(out + per - 1) / per, kGemvThreads, smem, s>>>(x, xs, in, nw, eps, w, bias, out, y, ys);
+        return launch_pdl(gemv_kernel<MODE, B, 4>, dim3((out + per - 1) / per), dim3(kGemvThreads), smem, s, x, xs, in,
+                          nw, eps, w, bias, out, y, ys);
     }
-    return cudaGetLastError();
+    const uint32_t per = kGemvWarps;
+    return launch_pdl(gemv_kernel<MODE, B, 1>, dim3((out + per - 1) / per), dim3(kGemvThreads), smem, s, x, xs, in, nw,
+                      eps, w, bias, out, y, ys);
 }
 
 template <int MODE>

@@ -272,6 +272,10 @@ bgtq_status bgtq_values_append(bgtq_values *v, const void *src, bgtq_dtype dtype
                                uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
                                void *stream);
 bgtq_status bgtq_values_length(const bgtq_values *v, uint32_t seq, uint32_t *length_out);
+/* Copy rows [row0, row0+count) of sequence `seq` to host memory as the store holds them:
+ * FP16 bits or FP32, `dim` elements per row, in dimension order (the device layout's chunk
+ * swizzle undone).  Synchronous (inspection / tests only).  No counterpart in the reference. */
+bgtq_status bgtq_values_read(const bgtq_values *v, uint32_t seq, uint32_t row0, uint32_t count, void *out);
 /* As bgtq_keys_reset, for a value store. */
 bgtq_status bgtq_values_reset(bgtq_values *v, void *stream);
 

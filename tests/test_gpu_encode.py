@@ -324,3 +324,22 @@ def test_append_kv_host_sources(cuda):
         append_kv(hk, hv, np.zeros((B, 1, H, d), np.float16), bad)
     assert hk[0].lengths(0) == 4 and hv[1].lengths(3) == 4
     assert device_status(0) == 0
+
+
+@pytest.mark.parametrize("dtype,dim", [("f16", 64), ("f16", 128), ("f16", 48), ("f32", 64)])
+def test_values_read_round_trip(cuda, dtype, dim):
+    """bgtq_values_read returns the rows as appended (FP16 rows of 64 / 128 halves are stored
+    chunk-swizzled on the device; the read undoes it)."""
+    from bgtq import Values
+    rng = np.random.default_rng(dim)
+    S, n = 3, 77
+    v = Values(dim, 200, dtype, sequences=S)
+    rows = rng.standard_normal((S, n, dim)).astype(np.float16 if dtype == "f16" else np.float32)
+    v.append(rows)
+    v.append(rows[:, :5], seq_first=0)
+    for s in range(S):
+        got = v.read(s)
+        assert got.shape == (n + 5, dim)
+        np.testing.assert_array_equal(got[:n], rows[s])
+        np.testing.assert_array_equal(got[n:], rows[s, :5])
+    np.testing.assert_array_equal(v.read(1, 10, 3), rows[1, 10:13])

@@ -61,19 +61,22 @@ def _reference_forward(dec, w, g, tokens, start, tables):
         bias = (lambda nm: p + f"self_attn.{nm}.bias") if g.qkv_bias else (lambda nm: None)
         q = rope(lin(x, p + "self_attn.q_proj.weight", bias("q_proj")).view(B, n, g.q_heads, 64))
         v = lin(x, p + "self_attn.v_proj.weight", bias("v_proj")).view(B, n, g.kv_heads, 64)
-        ref_v = dec._ref_v.setdefault(layer, [[None] * g.kv_heads for _ in range(B)])
         out = np.zeros((B, n, g.q_heads, 64), np.float32)
         qn = q.cpu().numpy()
         for b in range(B):
             for hd in range(g.kv_heads):
-                vh = v[b, :, hd].half().float().cpu().numpy()
-                ref_v[b][hd] = vh if ref_v[b][hd] is None else np.concatenate([ref_v[b][hd], vh])
+                # the Decoder's own FP16 V rows (as its own K codes below): the restated
+                # projection agrees with them to FP32 rounding, but one FP16 rounding step
+                # apart in a few elements, which the comparison is not about
+                vh = dec.values[layer][hd].read(b, 0, start + n).astype(np.float32)
+                mine = v[b, :, hd].half().float().cpu().numpy()
+                assert np.abs(vh[start:] - mine).max() <= 2.0 ** -10 * max(1.0, float(np.abs(mine).max()))
                 cfg, tab = tables[layer * g.kv_heads + hd]
                 packed, scales = dec.keys[layer][hd].read(b, 0, start + n)
                 kh = oracle.reconstruct(cfg, tab, packed, scales, threads=THREADS)
                 rows = qn[b, :, hd * g.gqa:(hd + 1) * g.gqa].reshape(n * g.gqa, 64)
                 ps = np.repeat(np.arange(start, start + n, dtype=np.uint32), g.gqa)
-                _, _, o = oracle.attention(rows, kh, ref_v[b][hd], ps, True, threads=THREADS)
+                _, _, o = oracle.attention(rows, kh, vh, ps, True, threads=THREADS)
                 out[b, :, hd * g.gqa:(hd + 1) * g.gqa] = o.reshape(n, g.gqa, 64)
         att = torch.from_numpy(out).to(h.device).reshape(B, n, g.hidden)
         h = h + lin(att, p + "self_attn.o_proj.weight")
@@ -92,7 +95,6 @@ def test_decoder_matches_reference_decoder(cuda, name):
     w = random_weights(g, seed=3, device=cuda, std=0.08)
     B, prompt, steps = 2, 150, 3
     dec = Decoder(w, g, 256, tables, batch=B)
-    dec._ref_v = {}
     rng = np.random.default_rng(1)
     toks = torch.from_numpy(rng.integers(0, g.vocab, (B, prompt))).to(cuda)
     got = dec.prefill(toks, chunk=100)       # two chunks: 100 + 50 positions
@@ -124,7 +126,6 @@ def test_graph_decode_after_4096_prefix_matches_reference(cuda, name):
     w = random_weights(g, seed=9, device=cuda, std=0.08)
     prefix, chunk = 4096, 1024
     dec = Decoder(w, g, prefix + 8, tables, batch=1)
-    dec._ref_v = {}
     rng = np.random.default_rng(12)
     toks = torch.from_numpy(rng.integers(0, g.vocab, (1, prefix))).to(cuda)
     got = dec.prefill(toks, chunk=chunk)

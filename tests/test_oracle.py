@@ -132,3 +132,34 @@ def test_pack_roundtrip_random():
         codes = np.concatenate([rng.integers(0, 16, (9, ns)), rng.integers(0, 256, (9, d - ns))], axis=1).astype(np.uint8)
         rb = ns // 2 + d - ns + 5
         np.testing.assert_array_equal(oracle.unpack(oracle.pack(codes, ns, rb), d, ns), codes)
+
+
+@pytest.mark.parametrize("name", ["config1", "config4"])
+def test_torch_port_agrees_with_c_oracle(name):
+    """The vectorised PyTorch restatement of the reference's CPU path (oracle/torch_port.py,
+    the timed CPU baseline on the GPU box) against the C oracle: codes equal except at LUT
+    bin edges, FP16 scales within one unit, and attention over the same packed keys within
+    the attention tolerance."""
+    import torch_port
+    from bgtq import synthetic
+    z = load_config(name)
+    p, cfg, tab = params_tables(z)
+    tb = torch_port.Tables(cfg, tab)
+    k, q, v = synthetic.decode_workload(7, 2048, p.dim, queries=3)
+    kb = k.view(np.uint16)
+    codes, scales = torch_port.encode(tb, kb)
+    ref = oracle.encode(cfg, tab, kb, threads=4)
+    ref_codes = oracle.unpack(ref["packed"][:, :p.row_bytes], p.dim, p.nibble_dims)
+    assert (codes.numpy() == ref_codes).mean() > 0.999
+    d16 = np.abs(scales.numpy().view(np.uint16).astype(int)[:, :p.groups] -
+                 ref["scales"][:, :p.groups].astype(int))
+    assert d16.max() <= 1
+    kh = torch_port.reconstruct(tb, ref["packed"][:, :p.row_bytes], ref["scales"])
+    np.testing.assert_allclose(kh.numpy(), oracle.reconstruct(cfg, tab, ref["packed"], ref["scales"]),
+                               atol=1e-5, rtol=1e-5)
+    pos = np.array([0, 1000, 2047])
+    _, _, out = torch_port.attention(q, kh, v.astype(np.float32), pos, True)
+    _, _, out_c = oracle.attention(q, oracle.reconstruct(cfg, tab, ref["packed"], ref["scales"]),
+                                   v.astype(np.float32), pos.astype(np.uint32), True)
+    np.testing.assert_allclose(out.numpy(), out_c, atol=1e-5, rtol=1e-4)
+    assert np.array_equal(torch_port.pack(tb, codes.numpy()), oracle.pack(codes.numpy(), p.nibble_dims, p.row_bytes))
