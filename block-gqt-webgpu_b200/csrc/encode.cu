@@ -316,6 +316,50 @@ __host__ __device__ TileSmem<D> tile_smem(uint32_t rdup_pairs, uint32_t cent_all
     return t;
 }
 
+// Output dims j0 .. j0 + NJ - 1 (NJ = 2 or 4, one group [lo, hi)) of the lane's 4 keys: each y
+// one sequential FMA chain over the group in ascending i (packed: two keys per instruction),
+// then straight to the LUT bin and code; codes stored as one word per dim (4 keys).
+template <int NJ>
+__device__ __forceinline__ void rotate_codes(const float2 *rdup, const float *X, const float4 *jc,
+                                             const uint8_t *lut_s, uint8_t *codes, uint32_t base, uint32_t j0,
+                                             uint32_t lo, uint32_t hi, int lane) {
+    constexpr int KT = kTileKeys;
+    const uint32_t n = hi - lo, rstep = n / 2;                  // float4 per block row
+    const float4 *rb = reinterpret_cast<const float4 *>(rdup + base + (j0 - lo));
+    const float4 *xp = reinterpret_cast<const float4 *>(X + lo * KT + 4 * lane);
+    float2 ya[NJ], yb[NJ];                                      // keys (0, 1) and (2, 3) of dim j0 + q
+#pragma unroll
+    for (int q = 0; q < NJ; ++q) ya[q] = yb[q] = make_float2(0.0f, 0.0f);
+#pragma unroll 4
+    for (uint32_t i = 0; i < n; ++i) {
+        const float4 x = xp[i * (KT / 4)];
+        const float2 xa = make_float2(x.x, x.y), xb = make_float2(x.z, x.w);
+#pragma unroll
+        for (int q2 = 0; q2 < NJ / 2; ++q2) {
+            const float4 r = rb[i * rstep + q2];
+            const float2 r0 = make_float2(r.x, r.y), r1 = make_float2(r.z, r.w);
+            ya[2 * q2] = ffma2(xa, r0, ya[2 * q2]);
+            yb[2 * q2] = ffma2(xb, r0, yb[2 * q2]);
+            ya[2 * q2 + 1] = ffma2(xa, r1, ya[2 * q2 + 1]);
+            yb[2 * q2 + 1] = ffma2(xb, r1, yb[2 * q2 + 1]);
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < NJ; ++q) {
+        const uint32_t j = j0 + q;
+        const float4 c4 = jc[j];
+        const float y[4] = {ya[q].x, ya[q].y, yb[q].x, yb[q].y};
+        uint32_t word = 0;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            float tv = (y[kk] - c4.x) * c4.y;
+            tv = fminf(fmaxf(tv, 0.0f), 255.0f);
+            word |= (uint32_t)lut_s[__float_as_uint(c4.z) + (uint32_t)tv] << (8 * kk);
+        }
+        reinterpret_cast<uint32_t *>(codes + j * KT)[lane] = word;
+    }
+}
+
 template <int D>
 __global__ void __launch_bounds__(kTileThreads, 2) encode_tile_kernel(const __grid_constant__ EncodeArgs a, uint32_t d,
                                                                       uint32_t cent_alloc, uint32_t lut_bytes,
@@ -365,31 +409,39 @@ __global__ void __launch_bounds__(kTileThreads, 2) encode_tile_kernel(const __gr
     }
     for (uint32_t e = tid; e < cent_alloc; e += kTileThreads) cent_s[e] = e < h.n_cent ? h.t.cent[e] : 0.0f;
     for (uint32_t e = tid; e < lut_bytes; e += kTileThreads) lut_s[e] = e < h.ncb * 256u ? h.t.lut[e] : 0;
+    // tasks: each group's dims in fours from its start, a last pair where the size leaves two;
+    // word j0 | group start << 8 | group end << 16 | four dims << 24 | valid << 25, and the
+    // group's rotation block offset; kept at the slot of the task's first dim pair
+    constexpr uint32_t kQuad = 1u << 24, kValid = 1u << 25;
     for (uint32_t p = tid; p < (uint32_t)D / 2; p += kTileThreads) {
         uint2 w = make_uint2(0u, 0u);
-        if (2u * p < d) {
-            const uint32_t g = h.t.group_of[2 * p], lo = h.group_off[g], hi = h.group_off[g + 1];
+        const uint32_t j0 = 2u * p;
+        if (j0 < d) {
+            const uint32_t g = h.t.group_of[j0], lo = h.group_off[g], hi = h.group_off[g + 1];
             uint32_t base = 0;
             for (uint32_t q = 0; q < g; ++q)
                 base += (h.group_off[q + 1] - h.group_off[q]) * (h.group_off[q + 1] - h.group_off[q]);
-            w = make_uint2(2u * p | lo << 8 | hi << 16, base);
+            if ((j0 - lo) % 4 == 0) w = make_uint2(j0 | lo << 8 | hi << 16 | (j0 + 4 <= hi ? kQuad : 0u) | kValid, base);
         }
         pair_s[p] = w;
     }
     __syncthreads();
     if (tid == 0) {
-        // longest-processing-time deal of the dim pairs to the warps; a pair costs its group size
+        // longest-processing-time deal of the tasks to the warps; a task costs its group size
+        // times its dim pairs
         uint32_t load[W];
         for (int w = 0; w < W; ++w) load[w] = 0, task_n[w] = 0;
         uint64_t taken = 0;
-        for (uint32_t n = 0; n < d / 2; ++n) {
+        for (;;) {
             int best = -1;
             uint32_t best_cost = 0;
             for (int p = 0; p < D / 2; ++p) {
-                if (((taken >> p) & 1u) || 2u * p >= d) continue;
-                const uint32_t w = pair_s[p].x, c = (w >> 16) - ((w >> 8) & 0xffu);
-                if (best < 0 || c > best_cost) best = p, best_cost = c;
+                const uint32_t w = pair_s[p].x;
+                if (((taken >> p) & 1u) || !(w & kValid)) continue;
+                const uint32_t cost = (((w >> 16) & 0xffu) - ((w >> 8) & 0xffu)) * ((w & kQuad) ? 2u : 1u);
+                if (best < 0 || cost > best_cost) best = p, best_cost = cost;
             }
+            if (best < 0) break;
             int wmin = 0;
             for (int w = 1; w < W; ++w)
                 if (load[w] < load[wmin]) wmin = w;
@@ -473,41 +525,14 @@ __global__ void __launch_bounds__(kTileThreads, 2) encode_tile_kernel(const __gr
             for (uint32_t i = lo; i < hi; ++i) X[i * KT + k] = X[i * KT + k] / dv;
         }
         __syncthreads();
-        // ---- 3. rotation + codes: warp = output dim pair, lane = 4 keys ----
+        // ---- 3. rotation + codes: warp = 2 or 4 output dims of a group, lane = 4 keys ----
         {
             const uint32_t ntask = task_n[warp];
             for (uint32_t t = 0; t < ntask; ++t) {
                 const uint2 task = task_s[warp * (D / 2) + t];
-                const uint32_t j0 = task.x & 0xffu, lo = (task.x >> 8) & 0xffu, hi = task.x >> 16, n = hi - lo;
-                const float4 *rb = reinterpret_cast<const float4 *>(rdup + task.y + (j0 - lo));
-                const float4 *xp = reinterpret_cast<const float4 *>(X + lo * KT + 4 * lane);
-                const uint32_t rstep = n / 2;   // float4 per block row
-                float2 y0a = make_float2(0.0f, 0.0f), y0b = y0a, y1a = y0a, y1b = y0a;
-#pragma unroll 4
-                for (uint32_t i = 0; i < n; ++i) {
-                    const float4 r = rb[i * rstep];
-                    const float4 x = xp[i * (KT / 4)];
-                    const float2 r0 = make_float2(r.x, r.y), r1 = make_float2(r.z, r.w);
-                    const float2 xa = make_float2(x.x, x.y), xb = make_float2(x.z, x.w);
-                    y0a = ffma2(xa, r0, y0a);
-                    y0b = ffma2(xb, r0, y0b);
-                    y1a = ffma2(xa, r1, y1a);
-                    y1b = ffma2(xb, r1, y1b);
-                }
-                const float y0[4] = {y0a.x, y0a.y, y0b.x, y0b.y}, y1[4] = {y1a.x, y1a.y, y1b.x, y1b.y};
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    const uint32_t j = j0 + q;
-                    const float4 c4 = jc[j];
-                    uint32_t word = 0;
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        float tv = ((q ? y1[kk] : y0[kk]) - c4.x) * c4.y;
-                        tv = fminf(fmaxf(tv, 0.0f), 255.0f);
-                        word |= (uint32_t)lut_s[__float_as_uint(c4.z) + (uint32_t)tv] << (8 * kk);
-                    }
-                    reinterpret_cast<uint32_t *>(codes + j * KT)[lane] = word;
-                }
+                const uint32_t j0 = task.x & 0xffu, lo = (task.x >> 8) & 0xffu, hi = (task.x >> 16) & 0xffu;
+                if (task.x & (1u << 24)) rotate_codes<4>(rdup, X, jc, lut_s, codes, task.y, j0, lo, hi, lane);
+                else rotate_codes<2>(rdup, X, jc, lut_s, codes, task.y, j0, lo, hi, lane);
             }
         }
         __syncthreads();
