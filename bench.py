@@ -819,6 +819,11 @@ def run_model(args, rank, world, local_rank):
     def step():
         logits.append(dec.decode_graph(next(it)).clone())
 
+    def timed_step():
+        torch.cuda.nvtx.range_push("timed_step")   # marks the timed steps for profilers
+        step()
+        torch.cuda.nvtx.range_pop()
+
     def barrier():
         sharding.barrier(dist, torch.cuda.synchronize)
 
@@ -830,7 +835,7 @@ def run_model(args, rank, world, local_rank):
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(steps):
-        step()
+        timed_step()
     t1.record()
     barrier()
     clk = clocks.stop()

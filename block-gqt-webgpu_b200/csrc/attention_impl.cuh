@@ -479,7 +479,6 @@ struct MinBlocks {
 template <int D, int QM, KKind KK, bool VF32, class LP>
 __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uint32_t d, uint32_t split, uint32_t hd,
                                           uint32_t s) {
-    pdl_wait();
     constexpr int TPL = Geo<D>::TPL, TT = Geo<D>::TT, QP = QPad<QM>::QP;
     constexpr bool MMA = UseMma<D, VF32>::value;
     constexpr int VSZ = VF32 ? 4 : 2, VEC = 16 / VSZ, LPT = D / VEC, TPS = 32 / LPT;
@@ -493,13 +492,18 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     constexpr bool TMMA = MMA && QM <= 4;
 
     const AttnHead &h = a.head[hd];
+    const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+    extern __shared__ __align__(128) unsigned char smem[];
+    float *cent_s = reinterpret_cast<float *>(smem + pl.cent);
+    // the codebooks are the store's own tables: staged while the kernel before this one (the
+    // query rotation) finishes; lengths, query records and cache rows only after the wait
+    if constexpr (KK == KKind::Packed)
+        for (uint32_t i = tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < h.n_lookup ? h.lookup[i] : 0.0f;
+    pdl_wait();
     const uint32_t seq = a.seq_first + s;
     const uint32_t len = a.lengths[seq];
     const uint32_t R = a.rows;
-    const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
 
-    extern __shared__ __align__(128) unsigned char smem[];
-    float *cent_s = reinterpret_cast<float *>(smem + pl.cent);
     unsigned char *rec = smem + pl.qrec;
     float *qrec_s = reinterpret_cast<float *>(rec);
     // P rows of TT floats at a stride of TT + 8: the P.V operand loads of four rows fall in
@@ -532,7 +536,6 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     // ---- prologue: codebooks, query tables, barriers ----
     const float *qt = a.qt + ((uint64_t)s * a.heads + hd) * (uint64_t)(D * QP);
     if constexpr (KK == KKind::Packed) {
-        for (uint32_t i = tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < h.n_lookup ? h.lookup[i] : 0.0f;
         build_tables<D, QM, QP>(h, qt, rec, d, pl.cent, tid);
     } else {
         const float4 *src = reinterpret_cast<const float4 *>(qt);
@@ -983,17 +986,18 @@ static __global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant_
                                                    uint32_t QP, int packed) {
     __shared__ float qraw[kMaxRows * kMaxDim];
     __shared__ __align__(16) float rot_s[64 * 64];   // the head's rotation, head dims up to 64
-    pdl_wait();
-    pdl_trigger();
     const uint32_t hd = blockIdx.x, s = blockIdx.y, R = a.rows;
     const AttnHead &h = a.head[hd];
-    const float *qg = a.q + ((uint64_t)s * a.heads + hd) * (uint64_t)R * d;
-    const uint32_t len = a.lengths[a.seq_first + s];
     // the rotation rows are read by every output: one coalesced copy into shared memory
-    // instead of a chain of dependent L2 reads per output
+    // instead of a chain of dependent L2 reads per output.  They are the store's own tables,
+    // so the copy runs before the wait for the kernel ahead (programmatic launch)
     const bool staged = packed && d <= 64;
     if (staged)
         for (uint32_t idx = threadIdx.x; idx < d * d; idx += blockDim.x) rot_s[idx] = h.rot[idx];
+    pdl_wait();
+    pdl_trigger();
+    const float *qg = a.q + ((uint64_t)s * a.heads + hd) * (uint64_t)R * d;
+    const uint32_t len = a.lengths[a.seq_first + s];
     for (uint32_t idx = threadIdx.x; idx < R * d; idx += blockDim.x) {
         const uint32_t r = idx / d, i = idx % d;
         // a query sits at its position (default: the last appended row)

@@ -37,9 +37,11 @@ constexpr uint32_t kTileRows = 64; // capacity is padded to a multiple of this
 // Programmatic dependent launch.  Kernels of the decode chain (model GEMVs, K/V append,
 // query rotation, attention) are launched with programmatic stream serialisation, so the
 // next kernel's launch overlaps the end of the one before it; each of them waits for its
-// predecessor's completion (griddepcontrol.wait) as its first statement, before it reads or
-// writes any memory, and the short ones allow their own successor to launch early
-// (griddepcontrol.launch_dependents).  Launched without the attribute, both are no-ops.
+// predecessor's completion (griddepcontrol.wait) before it reads anything another kernel
+// writes and before it writes any memory - only constant data (weights, the stores' own
+// tables) is fetched ahead of the wait - and the short ones allow their own successor to
+// launch early (griddepcontrol.launch_dependents).  Launched without the attribute, both
+// are no-ops.
 #if defined(__CUDACC__) || defined(__CUDACC_RTC__)
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

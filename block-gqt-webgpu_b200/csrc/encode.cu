@@ -796,8 +796,6 @@ __device__ __forceinline__ float src_elem(const void *p, uint64_t i, uint32_t f1
 __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_constant__ KvRopeArgs a, uint32_t d,
                                                                   uint32_t total, uint32_t stage_bytes) {
     constexpr int W = kThreads / 32;
-    pdl_wait();
-    pdl_trigger();
     const uint32_t hd = blockIdx.y;
     __shared__ WarpKey wks[W];
     __shared__ float kr[W][kMaxDim];
@@ -805,7 +803,11 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
     __shared__ __align__(16) unsigned char hs_raw[sizeof(EncodeHead)];
     EncodeHead &hs = *reinterpret_cast<EncodeHead *>(hs_raw);
     __shared__ __align__(8) uint64_t stage_bar;
+    // the tables are the store's own (never written by other kernels): their copy starts
+    // while the kernel before this one finishes (programmatic launch)
     if (stage_bytes) stage_head_tables(a.head[hd], tab_s, hs, &stage_bar);
+    pdl_wait();
+    pdl_trigger();
     const bool staged = stage_bytes && staged_tables_ready(&stage_bar, a.status);
     const EncodeHead &h = staged ? hs : a.head[hd];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;

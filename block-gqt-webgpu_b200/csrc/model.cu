@@ -50,9 +50,29 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const float *__restr
                                                             uint32_t out, float *y, uint64_t y_stride) {
     extern __shared__ __align__(16) float xs[];       // [B][in] activations (normalised for the NORM modes)
     __shared__ float red[kGemvWarps][B];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t chunks = in / 8;
+    const uint32_t r0 = (blockIdx.x * kGemvWarps + warp) * RPW;
+    constexpr int NW = MODE == 2 ? 2 : 1;   // gate and up rows
+    // the weights do not depend on the kernel before this one: their first pass is loaded
+    // while that kernel finishes (programmatic launch), the activations after the wait
+    uint4 wv[RPW][NW][kChunks];
+    auto load_pass = [&](uint32_t base) {
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+            for (int u = 0; u < NW; ++u)
+#pragma unroll
+                for (int c = 0; c < kChunks; ++c) {
+                    const uint32_t row = r0 + r, ch = base + lane + 32u * c;
+                    wv[r][u][c] = row < out && ch < chunks
+                                      ? __ldg(reinterpret_cast<const uint4 *>(w + (uint64_t)(row + u * out) * in) + ch)
+                                      : make_uint4(0, 0, 0, 0);
+                }
+    };
+    load_pass(0);
     pdl_wait();
     pdl_trigger();
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // ---- the activation rows into shared memory (and their RMSNorm) ----
     for (uint32_t e = tid; e < (uint32_t)B * in; e += kGemvThreads) {
         const uint32_t b = e / in, i = e - b * in;
@@ -83,10 +103,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const float *__restr
             for (uint32_t i = tid; i < in; i += kGemvThreads) xs[b * in + i] = xs[b * in + i] * ss[b] * norm_w[i];
         __syncthreads();
     }
-    // ---- rows: each pass has CH weight chunks per lane and row in flight, then the dots ----
-    const uint32_t chunks = in / 8;
-    const uint32_t r0 = (blockIdx.x * kGemvWarps + warp) * RPW;
-    constexpr int NW = MODE == 2 ? 2 : 1;   // gate and up rows
+    // ---- rows: each pass has kChunks weight chunks per lane and row in flight, then the dots ----
     float acc[RPW][NW][B];
 #pragma unroll
     for (int r = 0; r < RPW; ++r)
@@ -95,18 +112,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const float *__restr
 #pragma unroll
             for (int b = 0; b < B; ++b) acc[r][u][b] = 0.0f;
     for (uint32_t base = 0; base < chunks; base += 32u * kChunks) {
-        uint4 wv[RPW][NW][kChunks];
-#pragma unroll
-        for (int r = 0; r < RPW; ++r)
-#pragma unroll
-            for (int u = 0; u < NW; ++u)
-#pragma unroll
-                for (int c = 0; c < kChunks; ++c) {
-                    const uint32_t row = r0 + r, ch = base + lane + 32u * c;
-                    wv[r][u][c] = row < out && ch < chunks
-                                      ? __ldg(reinterpret_cast<const uint4 *>(w + (uint64_t)(row + u * out) * in) + ch)
-                                      : make_uint4(0, 0, 0, 0);
-                }
+        if (base) load_pass(base);
 #pragma unroll
         for (int c = 0; c < kChunks; ++c) {
             const uint32_t ch = base + lane + 32u * c;
