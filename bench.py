@@ -75,6 +75,7 @@ def parse():
     ap.add_argument("--no-weak", action="store_true", help="N > 1: skip the per-GPU-256 weak-scaling run")
     ap.add_argument("--no-extras", action="store_true", help="N = 1: skip the FP16-K / prefill / config-1 keys")
     ap.add_argument("--clocks-dir", type=Path, default=None, help="keep the nvidia-smi samples here")
+    ap.add_argument("--splits", type=int, default=0, help="decode: force the split-KV factor (0: the planner's)")
     ap.add_argument("--tables", choices=["config4", "calibration"], default="config4",
                     help="decode: config-4 tables for every head (the headline), or the 90 heads of the "
                          "reference's SmolLM2 calibration (30 layers x 3 KV heads)")
@@ -432,6 +433,8 @@ def run_ours(args, rank, world, local_rank):
         keys.append(lk)
         values.append(lv)
         atts.append(bgtq.GroupedAttention(lk, lv, R))
+        if args.splits:
+            atts[-1].set_splits(args.splits)
     setup_s = time.perf_counter() - t_setup
     q = [torch.randn((BA, H, R, d), device=dev, generator=gen) for _ in range(L)]
     knew = [profiled_keys(BA, H) for _ in range(L)]                 # [BA, H, d] new token keys

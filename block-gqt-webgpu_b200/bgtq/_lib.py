@@ -70,6 +70,8 @@ SIGNATURES = {
     "bgtq_layout_jit_prebuild": (I32, [C.c_char_p, U32, P, P, P, P, U32, C.c_int, P, C.c_size_t]),
     "bgtq_layout_jit_prebuilt": (I32, [P]),
     "bgtq_values_read": (I32, [P, U32, U32, U32, P]),
+    "bgtq_values_info": (I32, [P, P, P, P, P]),
+    "bgtq_keys_layout": (I32, [P, P]),
     "bgtq_model_gemv": (I32, [C.c_int, P, U32, C.c_uint64, U32, P, C.c_float, P, P, U32, P, C.c_uint64, P]),
     "bgtq_layout_jit_wait": (I32, [U32]),
     "bgtq_fixture_read": (I32, [C.c_char_p, P]),

@@ -584,6 +584,23 @@ bgtq_status bgtq_keys_info(const bgtq_keys *k, bgtq_keys_kind *kind, uint32_t *d
     return BGTQ_OK;
 }
 
+bgtq_status bgtq_keys_layout(const bgtq_keys *k, bgtq_layout_info *info) {
+    if (!k || !info) return fail(BGTQ_EINVAL, "null argument");
+    if (k->kind == BGTQ_KEYS_FP16) return fail(BGTQ_EINVAL, "FP16 keys have no Block-GTQ layout");
+    const Layout &L = k->L;
+    info->dim = L.d;
+    info->groups = L.ng;
+    info->row_bytes = L.row_bytes;
+    info->norm_stride = L.norm_stride;
+    info->nibble_dims = L.ns;
+    info->max_centroids = L.maxc;
+    info->logical_row_bytes = L.logical_rb;
+    info->device_row_stride = L.dev_row_stride;
+    info->device_scale_stride = L.dev_scale_stride;
+    info->codebooks = L.ncb;
+    return BGTQ_OK;
+}
+
 bgtq_status bgtq_keys_read(const bgtq_keys *k, uint32_t seq, uint32_t row0, uint32_t count, uint8_t *packed_out,
                            uint16_t *scales_out) {
     if (!k || seq >= k->sequences || (uint64_t)row0 + count > k->cap_alloc) return fail(BGTQ_EINVAL, "invalid range");
@@ -730,6 +747,16 @@ bgtq_status bgtq_values_append(bgtq_values *v, const void *src, bgtq_dtype dtype
         if (e != cudaSuccess) return cuda_fail(e, "V append");
     }
     for (uint32_t i = 0; i < seq_count; ++i) v->lengths[seq_first + i] += count;
+    return BGTQ_OK;
+}
+
+bgtq_status bgtq_values_info(const bgtq_values *v, bgtq_dtype *dtype, uint32_t *dim, uint32_t *capacity,
+                             uint32_t *sequences) {
+    if (!v) return fail(BGTQ_EINVAL, "null argument");
+    if (dtype) *dtype = v->dtype;
+    if (dim) *dim = v->dim;
+    if (capacity) *capacity = v->capacity;
+    if (sequences) *sequences = v->sequences;
     return BGTQ_OK;
 }
 

@@ -500,6 +500,9 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     if constexpr (KK == KKind::Packed)
         for (uint32_t i = tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < h.n_lookup ? h.lookup[i] : 0.0f;
     pdl_wait();
+    // the kernel after this one may launch once every CTA of this grid has started: it then
+    // takes only the slots this grid's last wave frees, fetches its constant tables and waits
+    pdl_trigger();
     const uint32_t seq = a.seq_first + s;
     const uint32_t len = a.lengths[seq];
     const uint32_t R = a.rows;

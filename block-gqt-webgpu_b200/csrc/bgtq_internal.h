@@ -39,9 +39,10 @@ constexpr uint32_t kTileRows = 64; // capacity is padded to a multiple of this
 // next kernel's launch overlaps the end of the one before it; each of them waits for its
 // predecessor's completion (griddepcontrol.wait) before it reads anything another kernel
 // writes and before it writes any memory - only constant data (weights, the stores' own
-// tables) is fetched ahead of the wait - and the short ones allow their own successor to
-// launch early (griddepcontrol.launch_dependents).  Launched without the attribute, both
-// are no-ops.
+// tables) is fetched ahead of the wait - and each allows its own successor to launch as
+// soon as all of its CTAs have started (griddepcontrol.launch_dependents), so a successor
+// only ever takes the slots the last wave frees.  Launched without the attribute, both are
+// no-ops.
 #if defined(__CUDACC__) || defined(__CUDACC_RTC__)
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

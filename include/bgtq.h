@@ -247,6 +247,9 @@ bgtq_status bgtq_keys_reset(bgtq_keys *k, void *stream);
 bgtq_status bgtq_keys_info(const bgtq_keys *k, bgtq_keys_kind *kind, uint32_t *dim, uint32_t *capacity,
                            uint32_t *sequences);
 
+/* The Block-GTQ layout of a packed / compressed key store (its tables' shape and strides). */
+bgtq_status bgtq_keys_layout(const bgtq_keys *k, bgtq_layout_info *info_out);
+
 /* Copy rows [row0, row0+count) of sequence `seq` to host memory in the reference's
  * strides: packed rows of config rowBytes bytes, scales of config normStride FP16 bits
  * (zero padded), as the reference's packed/norms GPU buffers hold them.  FP16 stores
@@ -272,6 +275,8 @@ bgtq_status bgtq_values_append(bgtq_values *v, const void *src, bgtq_dtype dtype
                                uint64_t row_stride, uint32_t seq_first, uint32_t seq_count, uint64_t seq_stride,
                                void *stream);
 bgtq_status bgtq_values_length(const bgtq_values *v, uint32_t seq, uint32_t *length_out);
+bgtq_status bgtq_values_info(const bgtq_values *v, bgtq_dtype *dtype, uint32_t *dim, uint32_t *capacity,
+                             uint32_t *sequences);
 /* Copy rows [row0, row0+count) of sequence `seq` to host memory as the store holds them:
  * FP16 bits or FP32, `dim` elements per row, in dimension order (the device layout's chunk
  * swizzle undone).  Synchronous (inspection / tests only).  No counterpart in the reference. */
