@@ -497,8 +497,27 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     float *cent_s = reinterpret_cast<float *>(smem + pl.cent);
     // the codebooks are the store's own tables: staged while the kernel before this one (the
     // query rotation) finishes; lengths, query records and cache rows only after the wait
-    if constexpr (KK == KKind::Packed)
-        for (uint32_t i = tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < h.n_lookup ? h.lookup[i] : 0.0f;
+    if constexpr (KK == KKind::Packed) {
+        // 16-byte loads, four in flight per thread (the table is 16-byte aligned in its blob):
+        // a few KB per CTA that a scalar loop would fetch one L2 round trip at a time
+        const uint32_t n4 = pl.cent_alloc / 4u, nl = h.n_lookup;
+        const float4 *src = reinterpret_cast<const float4 *>(h.lookup);
+        float4 *dst = reinterpret_cast<float4 *>(cent_s);
+#pragma unroll 4
+        for (uint32_t q = tid; q < n4; q += kThreads) {
+            float4 v;
+            if (4u * q + 3u < nl) {
+                v = __ldg(src + q);
+            } else {
+                v.x = 4u * q < nl ? h.lookup[4u * q] : 0.0f;
+                v.y = 4u * q + 1u < nl ? h.lookup[4u * q + 1u] : 0.0f;
+                v.z = 4u * q + 2u < nl ? h.lookup[4u * q + 2u] : 0.0f;
+                v.w = 0.0f;
+            }
+            dst[q] = v;
+        }
+        for (uint32_t i = 4u * n4 + tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < nl ? h.lookup[i] : 0.0f;
+    }
     pdl_wait();
     // the kernel after this one may launch once every CTA of this grid has started: it then
     // takes only the slots this grid's last wave frees, fetches its constant tables and waits
@@ -995,8 +1014,14 @@ static __global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant_
     // instead of a chain of dependent L2 reads per output.  They are the store's own tables,
     // so the copy runs before the wait for the kernel ahead (programmatic launch)
     const bool staged = packed && d <= 64;
-    if (staged)
-        for (uint32_t idx = threadIdx.x; idx < d * d; idx += blockDim.x) rot_s[idx] = h.rot[idx];
+    if (staged) {
+        // 16-byte loads, eight in flight per thread (d * d is a multiple of 4; the rotation
+        // is 16-byte aligned in the table blob)
+        const float4 *src = reinterpret_cast<const float4 *>(h.rot);
+        float4 *dst = reinterpret_cast<float4 *>(rot_s);
+#pragma unroll 8
+        for (uint32_t idx = threadIdx.x; idx < d * d / 4; idx += blockDim.x) dst[idx] = __ldg(src + idx);
+    }
     pdl_wait();
     pdl_trigger();
     const float *qg = a.q + ((uint64_t)s * a.heads + hd) * (uint64_t)R * d;

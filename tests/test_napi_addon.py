@@ -33,6 +33,13 @@ class JsRangeError(JsError):
     pass
 
 
+class JsValue:
+    """A value the addon returned (a napi_value of the stand-in runtime)."""
+
+    def __init__(self, ptr):
+        self.ptr = ptr
+
+
 class Addon:
     """The addon's exports behind the stand-in runtime."""
 
@@ -51,12 +58,14 @@ class Addon:
             f = getattr(self.h, name)
             f.restype, f.argtypes = res, args
         self.env = self.h.fake_env()
-        self.exports = self.h.fake_module(self.env)
+        self.exports = JsValue(self.h.fake_module(self.env))
         self.keep = []
 
     def arg(self, x):
         """A JS value for x; typed arrays view the NumPy buffer (no copy), so results written
         into an output array show up in the caller's array."""
+        if isinstance(x, JsValue):
+            return x.ptr
         if x is None:
             return self.h.fake_null()
         if isinstance(x, bool):
@@ -71,30 +80,30 @@ class Addon:
             vals = (C.c_void_p * len(x))(*[self.arg(e) for e in x])
             self.keep.append(vals)
             return self.h.fake_array(vals, len(x))
-        return x  # a handle returned by an earlier call
+        raise TypeError(f"no JavaScript value for {type(x)}")
 
     def __call__(self, name, *args):
         argv = (C.c_void_p * max(1, len(args)))(*[self.arg(a) for a in args])
-        r = self.h.fake_call(self.env, self.exports, name.encode(), argv, len(args))
+        r = self.h.fake_call(self.env, self.exports.ptr, name.encode(), argv, len(args))
         msg = C.create_string_buffer(1024)
         kind = self.h.fake_exception(self.env, msg, 1024)
         if kind:
             raise (JsRangeError if kind == 2 else JsError)(msg.value.decode())
-        return r
+        return JsValue(r)
 
     def typed(self, v):
         data, n = C.c_void_p(), C.c_size_t()
-        t = self.h.fake_typed_info(v, C.byref(data), C.byref(n))
+        t = self.h.fake_typed_info(v.ptr, C.byref(data), C.byref(n))
         assert t >= 0, "not a typed array"
         dt = NP_OF[t]
         return np.ctypeslib.as_array(C.cast(data, C.POINTER(np.ctypeslib.as_ctypes_type(dt))), (n.value,)).copy() \
             if n.value else np.zeros(0, dt)
 
     def get(self, obj, name):
-        return self.h.fake_get(obj, name.encode())
+        return JsValue(self.h.fake_get(obj.ptr, name.encode()))
 
     def number(self, v):
-        return self.h.fake_get_number(v)
+        return self.h.fake_get_number(v.ptr)
 
 
 @pytest.fixture(scope="module")
@@ -114,7 +123,7 @@ def test_addon_exports_every_function(addon):
     for name in ("validateLayout", "allocateBits", "buildTables", "packedKeysCreate", "fp16KeysCreate",
                  "valuesCreate", "keysAppend", "valuesAppend", "keysLength", "valuesLength", "keysRead",
                  "attentionCreate", "attend", "attendPrefill", "destroy", "deviceStatus"):
-        assert addon.h.fake_kind(addon.get(addon.exports, name)) == 8, name   # a function
+        assert addon.h.fake_kind(addon.get(addon.exports, name).ptr) == 8, name   # a function
 
 
 @pytest.mark.parametrize("name", ["config1", "config4"])
