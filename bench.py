@@ -76,6 +76,8 @@ def parse():
     ap.add_argument("--no-extras", action="store_true", help="N = 1: skip the FP16-K / prefill / config-1 keys")
     ap.add_argument("--clocks-dir", type=Path, default=None, help="keep the nvidia-smi samples here")
     ap.add_argument("--splits", type=int, default=0, help="decode: force the split-KV factor (0: the planner's)")
+    ap.add_argument("--schedule", choices=["auto", "split", "stream_k"], default="auto",
+                    help="decode attention schedule (auto: stream-K when estimated faster than split-KV)")
     ap.add_argument("--tables", choices=["config4", "calibration"], default="config4",
                     help="decode: config-4 tables for every head (the headline), or the 90 heads of the "
                          "reference's SmolLM2 calibration (30 layers x 3 KV heads)")
@@ -435,6 +437,7 @@ def run_ours(args, rank, world, local_rank):
         atts.append(bgtq.GroupedAttention(lk, lv, R))
         if args.splits:
             atts[-1].set_splits(args.splits)
+        atts[-1].set_schedule(args.schedule)
     setup_s = time.perf_counter() - t_setup
     q = [torch.randn((BA, H, R, d), device=dev, generator=gen) for _ in range(L)]
     knew = [profiled_keys(BA, H) for _ in range(L)]                 # [BA, H, d] new token keys
@@ -482,6 +485,7 @@ def run_ours(args, rank, world, local_rank):
     strong_out = torch.stack([o[:B] for o in outs])          # [L, B, H, R, d] of the last timed step
     rows_seen = T + warmup + steps
     splits = atts[0].last_splits
+    sk_ctas = atts[0].last_stream_k
 
     # ---- e2e through the C ABI with host buffers ----
     e2e = None
@@ -596,7 +600,8 @@ def run_ours(args, rank, world, local_rank):
                                                           else "attn_kernel<64,3,packed,f16>")
                                    + " per layer (CUDA events, rank 0)",
                          "algorithmic_bytes_per_launch": alg_bytes,
-                         "bytes_per_token_head": bpt, "mean_launch_ms": mean_launch_s * 1e3, "split_kv": splits},
+                         "bytes_per_token_head": bpt, "mean_launch_ms": mean_launch_s * 1e3,
+                         "split_kv": None if sk_ctas else splits, "stream_k_ctas": sk_ctas or None},
             "k_encode": {"value": enc_rate / 1e6, "unit": "Mkeys/s", "keys_per_launch": enc_keys,
                          "ms_per_launch": enc_ms_med, "hbm_frac": enc_rate * enc_bytes / 1e9 / hbm,
                          "fp32_tflops": enc_rate * enc_flops / 1e12,

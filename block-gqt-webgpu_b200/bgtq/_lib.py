@@ -101,6 +101,8 @@ SIGNATURES = {
     "bgtq_attend": (I32, [P, P, P, C.c_int, U32, U32, U32, P, P, P, C.c_int, P]),
     "bgtq_attention_last_splits": (I32, [P, C.POINTER(U32)]),
     "bgtq_attention_set_splits": (I32, [P, U32]),
+    "bgtq_attention_set_schedule": (I32, [P, I32]),
+    "bgtq_attention_last_stream_k": (I32, [P, C.POINTER(U32)]),
     "bgtq_attention_last_launches": (I32, [P, C.POINTER(U32)]),
     "bgtq_device_status": (I32, [C.c_int, C.POINTER(U32)]),
     "bgtq_attend_static": (I32, [U32, P, P, P, P, C.c_int, U32, U32, U32, P, P]),

@@ -109,6 +109,21 @@ class GroupedAttention:
     def set_splits(self, splits: int) -> None:
         _lib.call("bgtq_attention_set_splits", self._handle, int(splits))
 
+    def set_schedule(self, mode: str) -> None:
+        """'auto' (stream-K when estimated faster), 'split' (split-KV only) or 'stream_k'
+        (whenever the kernel allows)."""
+        modes = {"auto": 0, "split": 1, "stream_k": 2}
+        if mode not in modes:
+            raise ValueError(f"schedule must be one of {sorted(modes)}")
+        _lib.call("bgtq_attention_set_schedule", self._handle, modes[mode])
+
+    @property
+    def last_stream_k(self) -> int:
+        """CTAs of the last stream-K launch, 0 when the last launch used split-KV."""
+        n = C.c_uint32()
+        _lib.call("bgtq_attention_last_stream_k", self._handle, C.byref(n))
+        return n.value
+
     def destroy(self) -> None:
         if getattr(self, "_handle", None):
             _lib.lib().bgtq_attention_destroy(self._handle)

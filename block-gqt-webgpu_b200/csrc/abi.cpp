@@ -1025,9 +1025,9 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
     a.rows = rows;
     a.causal = causal ? 1u : 0u;
     a.logit_stride = max_len;
-    uint32_t splits = 1;
+    uint32_t splits = 1, sk = 0;
     cudaError_t e = launch_attention(a, kk, at->values[0]->dtype == BGTQ_F32, d, max_cent, plan_len, at->forced_splits,
-                                     at->max_splits, &splits, stream);
+                                     at->max_splits, at->schedule, &splits, &sk, stream);
     if (e != cudaSuccess) return cuda_fail(e, "attention launch");
     launches += 2;  // query rotation + attention
     if (probs) {
@@ -1036,6 +1036,7 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
         ++launches;
     }
     at->last_splits = splits;
+    at->last_sk_units = sk;
     at->last_launches = launches;
     if (host) {
         CK(cudaMemcpyAsync(out, dout, nq * 4, cudaMemcpyDeviceToHost, stream), "output download");
@@ -1120,6 +1121,16 @@ bgtq_status bgtq_attention_last_splits(const bgtq_attention *a, uint32_t *out) {
 bgtq_status bgtq_attention_set_splits(bgtq_attention *a, uint32_t splits) {
     if (!a || splits > 64) return fail(BGTQ_EINVAL, "invalid split count");
     a->forced_splits = splits;
+    return BGTQ_OK;
+}
+bgtq_status bgtq_attention_set_schedule(bgtq_attention *a, int mode) {
+    if (!a || mode < 0 || mode > 2) return fail(BGTQ_EINVAL, "invalid schedule");
+    a->schedule = mode;
+    return BGTQ_OK;
+}
+bgtq_status bgtq_attention_last_stream_k(const bgtq_attention *a, uint32_t *units_out) {
+    if (!a || !units_out) return fail(BGTQ_EINVAL, "null argument");
+    *units_out = a->last_sk_units;
     return BGTQ_OK;
 }
 bgtq_status bgtq_attention_plan_for_capacity(bgtq_attention *a, int on) {

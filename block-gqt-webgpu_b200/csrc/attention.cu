@@ -163,9 +163,37 @@ static void choose_splits(uint32_t pairs, uint32_t max_len, uint32_t chunk, uint
     *splits = std::max(1u, (max_len + t - 1) / t);
 }
 
+// Stream-K plan: `total` = pairs x nt CTA tiles (nt = tiles of one pair) over at most one
+// wave of CTAs, `per` tiles each.  A CTA pays the same fixed start-up as a split (tables,
+// first tile latency, merge) for each pair segment it runs.  Chosen when its critical path
+// undercuts the split-KV plan's by a margin, and when every pair's segments fit the partial
+// buffers (at most `cap` per pair), or whenever it is possible (`always`).
+static bool choose_stream_k(uint32_t pairs, uint32_t max_len, uint32_t chunk, uint32_t slots, uint32_t splits,
+                            uint32_t tps, uint32_t cap, bool always, uint32_t *units, uint32_t *per) {
+    const uint64_t nt = (max_len + chunk - 1) / chunk, total = (uint64_t)pairs * nt;
+    if (total < 2 || slots == 0) return false;
+    uint64_t k = (total + slots - 1) / slots;
+    while ((nt + k - 1) / k + 1 > cap) ++k;
+    if (always) {
+        *units = (uint32_t)((total + k - 1) / k);
+        *per = (uint32_t)k;
+        return true;
+    }
+    const uint64_t w = (total + k - 1) / k;
+    // segments per CTA: a range of k tiles meets at most ceil(k / nt) + 1 pairs
+    const uint64_t segs = std::min<uint64_t>((k + nt - 1) / nt + 1, k);
+    const uint64_t sk_cost = k * chunk + segs * chunk;
+    const uint64_t waves = ((uint64_t)pairs * splits + slots - 1) / slots;
+    const uint64_t kv_cost = waves * (tps + chunk);
+    if (sk_cost * 8 > kv_cost * 7) return false;  // within 12.5 %: keep split-KV
+    *units = (uint32_t)w;
+    *per = (uint32_t)k;
+    return true;
+}
+
 cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t d, uint32_t max_cent,
-                             uint32_t max_len, uint32_t forced_splits, uint32_t max_splits, uint32_t *splits_out,
-                             cudaStream_t s) {
+                             uint32_t max_len, uint32_t forced_splits, uint32_t max_splits, int schedule,
+                             uint32_t *splits_out, uint32_t *sk_out, cudaStream_t s) {
     AttnArgs a = a_in;
     const uint32_t D = dim_template(d);
     const Entry e = pick_entry(kk, v_f32, D, a.rows);
@@ -204,12 +232,28 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
     int per_sm = jk ? jit_occupancy(jk, dev, pl.total) : e.occ(pl);
     if (per_sm < 1) per_sm = 1;
     uint32_t splits = 1, tps = 0;
-    choose_splits(a.seq_count * a.heads, max_len, attn::kWarps * TT, (uint32_t)(sms * per_sm), forced_splits,
-                  std::max(1u, max_splits), &splits, &tps);
+    const uint32_t slots = (uint32_t)(sms * per_sm), chunk = attn::kWarps * TT, pairs = a.seq_count * a.heads;
+    choose_splits(pairs, max_len, chunk, slots, forced_splits, std::max(1u, max_splits), &splits, &tps);
     a.splits = splits;
     a.tokens_per_split = tps;
-    if (splits_out) *splits_out = splits;
+    a.sk_units = a.sk_tiles = a.sk_pair_tiles = 0;
     dim3 grid(splits, a.heads, a.seq_count);
+    // Stream-K for launches that split-KV fits poorly in whole waves: one wave of equal
+    // ranges of CTA tiles.  Only kernels that serve every head with one body (a head-major
+    // grid has one body per group structure).
+    if (!forced_splits && !head_major && max_len && schedule != 1) {
+        uint32_t units = 0, per = 0;
+        if (choose_stream_k(pairs, max_len, chunk, slots, splits, tps, std::max(1u, max_splits), schedule == 2, &units,
+                            &per)) {
+            a.sk_units = units;
+            a.sk_tiles = per;
+            a.sk_pair_tiles = (max_len + chunk - 1) / chunk;
+            grid = dim3(units, 1, 1);
+            splits = (a.sk_pair_tiles + per - 1) / per + 1;  // most segments of one pair
+        }
+    }
+    if (splits_out) *splits_out = splits;
+    if (sk_out) *sk_out = a.sk_units;
     cudaError_t err = launch_pdl(attn::qrot_kernel, dim3(a.heads, a.seq_count), dim3(128), 0, s, a, d, D, e.qp,
                                  kk == KKind::Packed ? 1 : 0);
     if (err != cudaSuccess) return err;

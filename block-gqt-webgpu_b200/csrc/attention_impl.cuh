@@ -476,9 +476,33 @@ struct MinBlocks {
     static constexpr int value = (KK == KKind::Packed && D <= 64 && QM <= 4) ? 3 : 1;
 };
 
+// The head's codebook lookup table into shared memory with 16-byte loads, four in flight
+// per thread (the table is 16-byte aligned in its blob), zero past its end: a few KB per CTA
+// that a scalar loop would fetch one L2 round trip at a time.
+__device__ __forceinline__ void stage_lookup(const AttnHead &h, const Plan &pl, float *cent_s, int tid) {
+    const uint32_t n4 = pl.cent_alloc / 4u, nl = h.n_lookup;
+    const float4 *src = reinterpret_cast<const float4 *>(h.lookup);
+    float4 *dst = reinterpret_cast<float4 *>(cent_s);
+#pragma unroll 4
+    for (uint32_t q = tid; q < n4; q += kThreads) {
+        float4 v;
+        if (4u * q + 3u < nl) {
+            v = __ldg(src + q);
+        } else {
+            v.x = 4u * q < nl ? h.lookup[4u * q] : 0.0f;
+            v.y = 4u * q + 1u < nl ? h.lookup[4u * q + 1u] : 0.0f;
+            v.z = 4u * q + 2u < nl ? h.lookup[4u * q + 2u] : 0.0f;
+            v.w = 0.0f;
+        }
+        dst[q] = v;
+    }
+    for (uint32_t i = 4u * n4 + tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < nl ? h.lookup[i] : 0.0f;
+}
+
 template <int D, int QM, KKind KK, bool VF32, class LP>
-__device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uint32_t d, uint32_t split, uint32_t hd,
-                                          uint32_t s) {
+__device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uint32_t d, uint32_t hd, uint32_t s,
+                                          uint32_t t_lo, uint32_t t_hi, uint32_t slot, uint32_t nslots,
+                                          uint32_t &phase, uint32_t &staged_hd) {
     constexpr int TPL = Geo<D>::TPL, TT = Geo<D>::TT, QP = QPad<QM>::QP;
     constexpr bool MMA = UseMma<D, VF32>::value;
     constexpr int VSZ = VF32 ? 4 : 2, VEC = 16 / VSZ, LPT = D / VEC, TPS = 32 / LPT;
@@ -494,34 +518,11 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     const AttnHead &h = a.head[hd];
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
     extern __shared__ __align__(128) unsigned char smem[];
-    float *cent_s = reinterpret_cast<float *>(smem + pl.cent);
-    // the codebooks are the store's own tables: staged while the kernel before this one (the
-    // query rotation) finishes; lengths, query records and cache rows only after the wait
-    if constexpr (KK == KKind::Packed) {
-        // 16-byte loads, four in flight per thread (the table is 16-byte aligned in its blob):
-        // a few KB per CTA that a scalar loop would fetch one L2 round trip at a time
-        const uint32_t n4 = pl.cent_alloc / 4u, nl = h.n_lookup;
-        const float4 *src = reinterpret_cast<const float4 *>(h.lookup);
-        float4 *dst = reinterpret_cast<float4 *>(cent_s);
-#pragma unroll 4
-        for (uint32_t q = tid; q < n4; q += kThreads) {
-            float4 v;
-            if (4u * q + 3u < nl) {
-                v = __ldg(src + q);
-            } else {
-                v.x = 4u * q < nl ? h.lookup[4u * q] : 0.0f;
-                v.y = 4u * q + 1u < nl ? h.lookup[4u * q + 1u] : 0.0f;
-                v.z = 4u * q + 2u < nl ? h.lookup[4u * q + 2u] : 0.0f;
-                v.w = 0.0f;
-            }
-            dst[q] = v;
-        }
-        for (uint32_t i = 4u * n4 + tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < nl ? h.lookup[i] : 0.0f;
+    if (KK == KKind::Packed && hd != staged_hd) {  // a later pair of another head
+        __syncthreads();
+        stage_lookup(h, pl, reinterpret_cast<float *>(smem + pl.cent), tid);
+        staged_hd = hd;
     }
-    pdl_wait();
-    // the kernel after this one may launch once every CTA of this grid has started: it then
-    // takes only the slots this grid's last wave frees, fetches its constant tables and waits
-    pdl_trigger();
     const uint32_t seq = a.seq_first + s;
     const uint32_t len = a.lengths[seq];
     const uint32_t R = a.rows;
@@ -552,38 +553,9 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
 #pragma unroll
     for (int r = 0; r < QM; ++r)
         if ((uint32_t)r < R) pmin = min(pmin, pos[r]);
-    const uint32_t t0 = split * a.tokens_per_split;
-    const uint32_t t1 = min(t0 + a.tokens_per_split, tend);
+    const uint32_t t0 = t_lo;
+    const uint32_t t1 = min(t_hi, tend);
 
-    // ---- prologue: codebooks, query tables, barriers ----
-    const float *qt = a.qt + ((uint64_t)s * a.heads + hd) * (uint64_t)(D * QP);
-    if constexpr (KK == KKind::Packed) {
-        build_tables<D, QM, QP>(h, qt, rec, d, pl.cent, tid);
-    } else {
-        const float4 *src = reinterpret_cast<const float4 *>(qt);
-        float4 *dst = reinterpret_cast<float4 *>(qrec_s);
-        for (uint32_t i = tid; i < (uint32_t)(D * QP / 4); i += kThreads) dst[i] = __ldg(src + i);
-    }
-    if (tid < kWarps * 4) mbar_init(smem_u32(smem + pl.bars) + tid * 8u, 1u);
-    fence_barrier_init();
-    __syncthreads();
-
-    // ---- per-warp flash-decoding over this split ----
-    float m[QM], l[QM];
-#pragma unroll
-    for (int r = 0; r < QM; ++r) { m[r] = -INFINITY; l[r] = 0.0f; }
-    constexpr int OS = TMMA ? (D / 16) * 4 : MMA ? NT * 4 : QM * VEC;  // output accumulators per lane
-    float O[OS];
-#pragma unroll
-    for (int i = 0; i < OS; ++i) O[i] = 0.0f;
-    float qreg[QM][KVEC];
-    if constexpr (KK != KKind::Packed) {
-        const int dl = (lane % LPTK) * KVEC;
-#pragma unroll
-        for (int r = 0; r < QM; ++r)
-#pragma unroll
-            for (int e = 0; e < KVEC; ++e) qreg[r][e] = qrec_s[(dl + e) * QP + r];
-    }
     const uint32_t ntok = t1 > t0 ? t1 - t0 : 0u;
     const uint32_t ntiles = (ntok + TT - 1) / TT;
     unsigned char *vbuf = smem + pl.stage + (size_t)w * pl.warp_bytes;
@@ -622,10 +594,40 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     };
 
     bool ok = true;
-    uint32_t phase = 0;  // bit st: parity of K buffer st; bit 2: parity of the V buffer
+    // phase (the caller's, carried across the pairs of one CTA): bit st = parity of K buffer
+    // st; bit 2 = parity of the V buffer.  The first tiles are requested before the query
+    // tables are built: the copies' latency overlaps the prologue.
     if ((uint32_t)w < ntiles) {
         issue_k(w, 0);
         issue_v(w);
+    }
+
+    // ---- prologue: codebooks, query tables, barriers ----
+    const float *qt = a.qt + ((uint64_t)s * a.heads + hd) * (uint64_t)(D * QP);
+    if constexpr (KK == KKind::Packed) {
+        build_tables<D, QM, QP>(h, qt, rec, d, pl.cent, tid);
+    } else {
+        const float4 *src = reinterpret_cast<const float4 *>(qt);
+        float4 *dst = reinterpret_cast<float4 *>(qrec_s);
+        for (uint32_t i = tid; i < (uint32_t)(D * QP / 4); i += kThreads) dst[i] = __ldg(src + i);
+    }
+    __syncthreads();
+
+    // ---- per-warp flash-decoding over this range ----
+    float m[QM], l[QM];
+#pragma unroll
+    for (int r = 0; r < QM; ++r) { m[r] = -INFINITY; l[r] = 0.0f; }
+    constexpr int OS = TMMA ? (D / 16) * 4 : MMA ? NT * 4 : QM * VEC;  // output accumulators per lane
+    float O[OS];
+#pragma unroll
+    for (int i = 0; i < OS; ++i) O[i] = 0.0f;
+    float qreg[QM][KVEC];
+    if constexpr (KK != KKind::Packed) {
+        const int dl = (lane % LPTK) * KVEC;
+#pragma unroll
+        for (int r = 0; r < QM; ++r)
+#pragma unroll
+            for (int e = 0; e < KVEC; ++e) qreg[r][e] = qrec_s[(dl + e) * QP + r];
     }
     int it = 0;
     for (uint32_t k = w; k < ntiles; k += kWarps, ++it) {
@@ -868,10 +870,12 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     }
     if (!ok) {
         // report the timeout, then give the copies still in flight a bounded chance to land
-        // before this shared memory is reused or released
+        // before this shared memory is reused or released (a drained barrier moves on a phase,
+        // as the next pair of a stream-K CTA expects)
         if (lane == 0) atomicOr(a.status, kStatusWaitTimeout);
         for (int b = 0; b < 3; ++b)
-            if (pending & (1u << b)) mbar_wait_bounded(bar0 + (b == 2 ? 16u : 8u * b), (phase >> b) & 1u);
+            if ((pending & (1u << b)) && mbar_wait_bounded(bar0 + (b == 2 ? 16u : 8u * b), (phase >> b) & 1u))
+                phase ^= 1u << b;
     }
 
     // ---- merge the warps of this CTA ----
@@ -943,21 +947,21 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
             L = fmaf(ml[ww * QP + r], f, L);
             Ov = fmaf(mO[(ww * QP + r) * D + dd], f, Ov);
         }
-        if (a.splits == 1) {
+        if (nslots == 1) {
             a.out[(obase + r) * d + dd] = Ov / L;
             if (dd == 0 && a.lse) a.lse[obase + r] = (M + log2f(L) - kPShift) * kLn2;
         } else {
-            float *pp = a.part + ((((uint64_t)split * a.seq_count + s) * a.heads + hd) * R + r) * (uint64_t)(d + 2);
+            float *pp = a.part + ((((uint64_t)slot * a.seq_count + s) * a.heads + hd) * R + r) * (uint64_t)(d + 2);
             pp[dd] = Ov;
             if (dd == 0) { pp[d] = M; pp[d + 1] = L; }
         }
     }
-    if (a.splits > 1) {
+    if (nslots > 1) {
         __threadfence();
         __syncthreads();
         if (tid == 0) {
             const uint32_t ticket = atomicAdd(&a.counters[s * a.heads + hd], 1u);
-            s_last = ticket == a.splits - 1 ? 1u : 0u;
+            s_last = ticket == nslots - 1 ? 1u : 0u;
         }
         __syncthreads();
         if (s_last) {
@@ -967,9 +971,9 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
                 const uint32_t r = idx / d, dd = idx % d;
                 const float *pp = a.part + (((uint64_t)s * a.heads + hd) * R + r) * (uint64_t)(d + 2);
                 float M = -INFINITY;
-                for (uint32_t sp = 0; sp < a.splits; ++sp) M = fmaxf(M, __ldcg(pp + sp * sstride + d));
+                for (uint32_t sp = 0; sp < nslots; ++sp) M = fmaxf(M, __ldcg(pp + sp * sstride + d));
                 float L = 0.0f, Ov = 0.0f;
-                for (uint32_t sp = 0; sp < a.splits; ++sp) {
+                for (uint32_t sp = 0; sp < nslots; ++sp) {
                     const float ms = __ldcg(pp + sp * sstride + d);
                     const float f = ms == -INFINITY ? 0.0f : ex2(ms - M);
                     L = fmaf(__ldcg(pp + sp * sstride + d + 1), f, L);
@@ -980,6 +984,56 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
             }
             if (tid == 0) a.counters[s * a.heads + hd] = 0u;
         }
+    }
+    __syncthreads();  // the merge scratch and tile buffers are free for the next pair
+}
+
+// One CTA of the decode attention.  Split-KV (a.sk_units == 0): the CTA owns split `split`
+// of the pair (sequence s, KV head hd).  Stream-K (a.sk_units CTAs): the pairs' token tiles
+// (a.sk_pair_tiles of kWarps * TT tokens per pair, pairs in head-major order) are dealt to
+// the CTAs as equal contiguous ranges of a.sk_tiles, so one wave of CTAs covers the whole
+// launch with the same work each; a range crossing pairs runs one segment per pair, and the
+// segments of a pair are merged like splits by the last to finish.
+template <int D, int QM, KKind KK, bool VF32, class LP>
+__device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uint32_t d, uint32_t split, uint32_t hd,
+                                          uint32_t s) {
+    constexpr int TT = Geo<D>::TT;
+    constexpr uint32_t CT = kWarps * TT;  // tokens per tile of the whole CTA
+    const int tid = threadIdx.x;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const uint32_t P = a.heads * a.seq_count, nt = a.sk_pair_tiles, K = a.sk_tiles;
+    const uint64_t g0 = (uint64_t)split * K, total = (uint64_t)P * nt;
+    if (a.sk_units && g0 < total) {
+        const uint32_t p0 = (uint32_t)(g0 / nt);
+        hd = p0 / a.seq_count;
+        s = p0 % a.seq_count;
+    }
+    // the codebooks are the store's own tables: staged while the kernel before this one (the
+    // query rotation) finishes; lengths, query records and cache rows only after the wait
+    if constexpr (KK == KKind::Packed) stage_lookup(a.head[hd], pl, reinterpret_cast<float *>(smem + pl.cent), tid);
+    pdl_wait();
+    // the kernel after this one may launch once every CTA of this grid has started: it then
+    // takes only the slots this grid's last wave frees, fetches its constant tables and waits
+    pdl_trigger();
+    if (tid < kWarps * 4) mbar_init(smem_u32(smem + pl.bars) + tid * 8u, 1u);
+    fence_barrier_init();
+    __syncthreads();
+    uint32_t phase = 0, staged_hd = hd;
+    if (!a.sk_units) {
+        attn_pair<D, QM, KK, VF32, LP>(a, pl, d, hd, s, split * a.tokens_per_split,
+                                       split * a.tokens_per_split + a.tokens_per_split, split, a.splits, phase,
+                                       staged_hd);
+        return;
+    }
+    const uint64_t g1 = g0 + K < total ? g0 + K : total;
+    for (uint64_t g = g0; g < g1;) {
+        const uint32_t p = (uint32_t)(g / nt);
+        const uint64_t pstart = (uint64_t)p * nt;
+        const uint32_t lo = (uint32_t)(g - pstart), hi = (uint32_t)((g1 < pstart + nt ? g1 : pstart + nt) - pstart);
+        const uint32_t first = (uint32_t)(pstart / K), last = (uint32_t)((pstart + nt - 1) / K);
+        attn_pair<D, QM, KK, VF32, LP>(a, pl, d, p / a.seq_count, p % a.seq_count, lo * CT, hi * CT, split - first,
+                                       last - first + 1, phase, staged_hd);
+        g = pstart + nt;
     }
 }
 

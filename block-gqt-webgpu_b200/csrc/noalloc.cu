@@ -152,8 +152,8 @@ extern "C" bgtq_status bgtq_attend_static(uint32_t heads, bgtq_keys *const *keys
     const uint32_t max_splits = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(64, kPartFloats / per_split));
     uint32_t splits = 1;
     jit_suppress_on_thread(1);  // generic kernel: loading a specialised one would allocate
-    e = launch_attention(a, KKind::Packed, values[0]->dtype == BGTQ_F32, d, max_cent, max_len, 0, max_splits, &splits,
-                         stream);
+    e = launch_attention(a, KKind::Packed, values[0]->dtype == BGTQ_F32, d, max_cent, max_len, 0, max_splits, 0, &splits,
+                         nullptr, stream);
     jit_suppress_on_thread(0);
     if (e != cudaSuccess) return fail(BGTQ_ECUDA, std::string("attention launch: ") + cudaGetErrorString(e));
     return BGTQ_OK;

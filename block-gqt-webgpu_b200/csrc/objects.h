@@ -69,7 +69,8 @@ struct bgtq_attention {
     float *lse = nullptr;
     float *qt = nullptr;
     bgtq::DevBuf q_dev, pos_dev, out_dev, logits_dev, probs_dev, prefill_qt;
-    uint32_t forced_splits = 0, last_splits = 0, last_launches = 0, max_splits = 64;
+    uint32_t forced_splits = 0, last_splits = 0, last_launches = 0, max_splits = 64, last_sk_units = 0;
+    int schedule = 0;  // 0 automatic, 1 split-KV only, 2 stream-K whenever the kernel allows
     uint32_t prefill_kernel = 0;  // 0: tcgen05 / TMEM kernel, 1: mma.sync kernel
     bgtq::DevBuf rope;            // RoPE table when queries arrive before RoPE (else empty)
     bool use_rope = false;

@@ -331,6 +331,14 @@ bgtq_status bgtq_attend_prefill(bgtq_attention *a, const float *q, uint32_t pos_
 bgtq_status bgtq_attention_last_splits(const bgtq_attention *a, uint32_t *splits_out);
 /* Force a split-KV factor (0 = automatic). */
 bgtq_status bgtq_attention_set_splits(bgtq_attention *a, uint32_t splits);
+/* Decode schedule: 0 automatic (stream-K when estimated faster than split-KV: launches whose
+ * split-KV grid fills its last wave poorly), 1 split-KV only, 2 stream-K whenever the kernel
+ * allows (tests).  Stream-K deals the pairs' key tiles to one wave of CTAs in equal ranges;
+ * a forced split count (set_splits) implies split-KV.  No counterpart in the reference,
+ * whose decode is one workgroup per (query head, position). */
+bgtq_status bgtq_attention_set_schedule(bgtq_attention *a, int mode);
+/* CTAs of the last bgtq_attend's stream-K launch, 0 when it used split-KV. */
+bgtq_status bgtq_attention_last_stream_k(const bgtq_attention *a, uint32_t *units_out);
 /* For launches recorded once (CUDA graph capture) and replayed while sequences grow: on != 0
  * makes bgtq_attend plan its split-KV factor for the keys' capacity instead of the current
  * lengths, so a replay covers every row appended since.  No counterpart in the reference. */

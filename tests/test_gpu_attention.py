@@ -177,6 +177,112 @@ def test_grouped_decode_ragged_batch(cuda, vdtype, rows):
     assert device_status(0) == 0
 
 
+@pytest.mark.parametrize("vdtype", ["f16", "f32"])
+@pytest.mark.parametrize("rows", [1, 3])
+def test_stream_k_decode_matches_oracle(cuda, vdtype, rows):
+    """Stream-K schedule (key tiles dealt to one wave of CTAs in equal ranges, ranges crossing
+    pairs; segments merged like splits): ragged lengths, one calibration for every head
+    (one kernel body), against the oracle and the split-KV schedule."""
+    zh = np.load(GOLDEN / "smollm2_heads.npz")
+    layouts = [(zh["h0_config"], zh["h0_table"])] * 3
+    rng = np.random.default_rng(40 + rows)
+    S, lengths = 6, [1, 77, 640, 1500, 3001, 4096]
+    stores = _grouped_case(rng, layouts, S, lengths, rows, vdtype, 4096)
+    att = GroupedAttention([s[0] for s in stores], [s[1] for s in stores], rows)
+    q = synthetic.profiled(rng, S * 3 * rows, 64).reshape(S, 3, rows, 64)
+    positions = np.array([[max(0, L - 1 - r * 5) for r in range(rows)] for L in lengths], np.uint32)
+    for causal in (False, True):
+        att.set_schedule("stream_k")
+        sk = att.attend(q, positions, causal)
+        assert att.last_stream_k > 0
+        att.set_schedule("split")
+        kv = att.attend(q, positions, causal)
+        assert att.last_stream_k == 0
+        for s in range(S):
+            for h, (keys, values, ks, vs, cfg, tab) in enumerate(stores):
+                kh = oracle.reconstruct(cfg, tab, *keys.read(s))
+                _, _, ref = oracle.attention(q[s, h], kh, vs[s], positions[s], causal)
+                np.testing.assert_allclose(sk[s, h], ref, atol=ATOL, rtol=RTOL)
+                np.testing.assert_allclose(kv[s, h], ref, atol=ATOL, rtol=RTOL)
+    # back to back: the per-pair tickets are reset by each launch's last segment
+    att.set_schedule("stream_k")
+    np.testing.assert_array_equal(att.attend(q), att.attend(q))
+    assert device_status(0) == 0
+
+
+def test_stream_k_fp16_keys_logits_and_sequence_window(cuda):
+    """Stream-K with dense FP16 keys: ragged lengths over every sequence, then raw logits
+    captured over every key of a window of equal-length sequences (seq_first > 0)."""
+    rng = np.random.default_rng(7)
+    S, lengths, rows = 5, [300, 1500, 1500, 1500, 77], 2
+    keys = [FP16Keys(64, 2048, sequences=S) for _ in range(2)]
+    values = [Values(64, 2048, "f16", sequences=S) for _ in range(2)]
+    kv = []
+    for k, v in zip(keys, values):
+        ks, vs = [], []
+        for s in range(S):
+            kk = (rng.standard_normal((lengths[s], 64)) * 0.5).astype(np.float16)
+            vv = rng.standard_normal((lengths[s], 64)).astype(np.float16)
+            k.append(kk.view(np.uint16), seq_first=s)
+            v.append(vv, seq_first=s)
+            ks.append(kk.astype(np.float32))
+            vs.append(vv.astype(np.float32))
+        kv.append((ks, vs))
+    att = GroupedAttention(keys, values, rows)
+    att.set_schedule("stream_k")
+    q = rng.standard_normal((S, 2, rows, 64)).astype(np.float32)
+    out = att.attend(q)
+    assert att.last_stream_k > 0
+    for s in range(S):
+        for h in range(2):
+            ks, vs = kv[h]
+            _, _, ref = oracle.attention(q[s, h], ks[s], vs[s])
+            np.testing.assert_allclose(out[s, h], ref, atol=ATOL, rtol=RTOL)
+    logits = np.zeros((3, 2, rows, 1500), np.float32)
+    out = att.attend(q[1:4], seq_first=1, seq_count=3, logits=logits)
+    assert att.last_stream_k > 0
+    for i, s in enumerate(range(1, 4)):
+        for h in range(2):
+            ks, vs = kv[h]
+            lg, _, ref = oracle.attention(q[s, h], ks[s], vs[s])
+            np.testing.assert_allclose(out[i, h], ref, atol=ATOL, rtol=RTOL)
+            np.testing.assert_allclose(logits[i, h], lg, atol=1e-4, rtol=1e-4)
+    assert device_status(0) == 0
+
+
+def test_stream_k_full_length_batch_and_schedule_switches(cuda):
+    """A 32-sequence batch of 8192-token sequences over three KV heads of one calibration (the
+    per-GPU share of config 4 at eight GPUs): stream-K, split-KV and the automatic schedule
+    agree; a forced split count implies split-KV."""
+    zh = np.load(GOLDEN / "smollm2_heads.npz")
+    cfg, tab = zh["h0_config"], zh["h0_table"]
+    rng = np.random.default_rng(3)
+    S, T = 32, 8192
+    keys = [PackedKeys((cfg, tab), T, sequences=S) for _ in range(3)]
+    values = [Values(64, T, "f16", sequences=S) for _ in range(3)]
+    k = synthetic.profiled(rng, T, 64).astype(np.float16).view(np.uint16)
+    v = rng.standard_normal((T, 64)).astype(np.float16)
+    for kk, vv in zip(keys, values):
+        for s in range(S):
+            kk.append(k, seq_first=s)
+            vv.append(v, seq_first=s)
+    att = GroupedAttention(keys, values, 3)
+    q = synthetic.profiled(rng, S * 9, 64).reshape(S, 3, 3, 64)
+    auto = att.attend(q)
+    att.set_schedule("stream_k")
+    sk = att.attend(q)
+    assert att.last_stream_k > 0
+    att.set_splits(4)
+    forced = att.attend(q)
+    assert att.last_stream_k == 0 and att.last_splits == 4
+    np.testing.assert_allclose(sk, auto, atol=ATOL, rtol=RTOL)
+    np.testing.assert_allclose(forced, auto, atol=ATOL, rtol=RTOL)
+    kh = oracle.reconstruct(cfg, tab, *keys[1].read(5))
+    _, _, ref = oracle.attention(q[5, 1], kh, v.astype(np.float32))
+    np.testing.assert_allclose(sk[5, 1], ref, atol=ATOL, rtol=RTOL)
+    assert device_status(0) == 0
+
+
 def test_device_io_matches_host_io(cuda):
     import torch
     zh = np.load(GOLDEN / "smollm2_heads.npz")
