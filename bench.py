@@ -76,6 +76,8 @@ def parse():
     ap.add_argument("--no-extras", action="store_true", help="N = 1: skip the FP16-K / prefill / config-1 keys")
     ap.add_argument("--clocks-dir", type=Path, default=None, help="keep the nvidia-smi samples here")
     ap.add_argument("--splits", type=int, default=0, help="decode: force the split-KV factor (0: the planner's)")
+    ap.add_argument("--model-path", choices=["step", "graph"], default="step",
+                    help="model decode: the persistent step kernel (default) or the CUDA graph of per-layer launches")
     ap.add_argument("--schedule", choices=["auto", "split", "stream_k"], default="auto",
                     help="decode attention schedule (auto: stream-K when estimated faster than split-KV)")
     ap.add_argument("--tables", choices=["config4", "calibration"], default="config4",
@@ -813,45 +815,57 @@ def run_model(args, rank, world, local_rank):
     g = SMOLLM2_135M if args.workload == "model-smollm2" else QWEN25_05B
     prefix, steps, warmup = 4096, args.steps, max(3, args.warmup)
     tables = calibration_tables(g.family, g.layers * g.kv_heads)
-    dec = Decoder(random_weights(g, seed=7 + rank, device=dev), g, prefix + warmup + steps + 4, tables, batch=1)
+    dec = Decoder(random_weights(g, seed=7 + rank, device=dev), g, prefix + 2 * (warmup + steps) + 8, tables, batch=1)
     rng = np.random.default_rng(rank)
     t_pre = time.perf_counter()
     dec.prefill(torch.from_numpy(rng.integers(0, g.vocab, (1, prefix))).to(dev), chunk=1024)
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t_pre
-    toks = [torch.from_numpy(rng.integers(0, g.vocab, (1, 1))).to(dev) for _ in range(warmup + steps + 1)]
+    toks = [torch.from_numpy(rng.integers(0, g.vocab, (1, 1))).to(dev) for _ in range(2 * (warmup + steps) + 1)]
     it = iter(toks)
     logits = []
-    dec.capture_decode(next(it))   # one eager decode step, then the step recorded as a CUDA graph
-
-    def step():
-        logits.append(dec.decode_graph(next(it)).clone())
-
-    def timed_step():
-        torch.cuda.nvtx.range_push("timed_step")   # marks the timed steps for profilers
-        step()
-        torch.cuda.nvtx.range_pop()
 
     def barrier():
         sharding.barrier(dist, torch.cuda.synchronize)
 
-    for _ in range(warmup):
-        step()
-    barrier()
-    clocks = Clocks(local_rank, args.clocks_dir)
-    clocks.start()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(steps):
-        timed_step()
-    t1.record()
-    barrier()
-    clk = clocks.stop()
-    (ms,) = sharding.max_over_ranks([t0.elapsed_time(t1) / steps], dist, dev)
+    def timed(step):
+        """W untimed, then K timed steps (CUDA events on the launching stream, max over ranks)."""
+        def timed_step():
+            torch.cuda.nvtx.range_push("timed_step")   # marks the timed steps for profilers
+            step()
+            torch.cuda.nvtx.range_pop()
+        for _ in range(warmup):
+            step()
+        barrier()
+        clocks = Clocks(local_rank, args.clocks_dir)
+        clocks.start()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(steps):
+            timed_step()
+        t1.record()
+        barrier()
+        clk = clocks.stop()
+        (ms,) = sharding.max_over_ranks([t0.elapsed_time(t1) / steps], dist, dev)
+        return ms, clk
+
+    # the persistent step: the whole model per token as one cooperative launch
+    use_step = dec.step_kernel and args.model_path == "step"
+    if use_step:
+        ms, clk = timed(lambda: logits.append(dec.forward(next(it), _check=False)))
+        ctas, smem, _ = dec.step_info()
+    # the same step as a CUDA graph of seven launches per layer
+    dec.capture_decode(next(it))
+    graph_ms, graph_clk = timed(lambda: logits.append(dec.decode_graph(next(it)).clone()))
+    if not use_step:
+        ms, clk = graph_ms, graph_clk
     finite = all(bool(torch.isfinite(x).all()) for x in logits)
     if rank == 0:
+        path = (f"one persistent cooperative launch per token ({ctas} CTAs, {smem} B shared memory each)"
+                if use_step else "CUDA graph of seven launches per layer")
         print(json.dumps({
-            "metric": f"{g.family} whole-model decode tokens/s (batch 1 per GPU, 4096-token prefix, CUDA graph)",
+            "metric": f"{g.family} whole-model decode tokens/s (batch 1 per GPU, 4096-token prefix)",
+            "decode_path": path, "graph_ms_per_step": graph_ms,
             "value": world * 1e3 / ms, "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (random-init FP16 weights N(0,0.02), uniform random token ids)",

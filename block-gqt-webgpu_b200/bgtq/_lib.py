@@ -54,6 +54,15 @@ class Allocation(C.Structure):
     _fields_ = [("name", C.c_char_p), ("role", C.c_char_p), ("bytes", C.c_uint64)]
 
 
+class DecoderDesc(C.Structure):
+    """bgtq_decoder_desc: per-layer arrays are pointers to arrays of device pointers."""
+    _fields_ = [(n, C.c_uint32) for n in ("layers", "batch", "hidden", "q_heads", "kv_heads", "head_dim",
+                                          "intermediate", "vocab")] + [
+        ("rms_eps", C.c_float)] + [(n, C.c_void_p) for n in (
+            "inv_freq", "ln1", "qkv_bias", "ln2", "w_qkv", "w_o", "w_gate_up", "w_down", "final_norm", "lm_head",
+            "embedding", "attention")] + [("ctas_per_sm", C.c_uint32)]
+
+
 # (name, restype, argtypes) for every exported symbol declared in include/bgtq.h
 P, U32, U64, I32, I64, SZ = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int32, C.c_int64, C.c_size_t
 SIGNATURES = {
@@ -73,6 +82,11 @@ SIGNATURES = {
     "bgtq_values_info": (I32, [P, P, P, P, P]),
     "bgtq_keys_layout": (I32, [P, P]),
     "bgtq_model_gemv": (I32, [C.c_int, P, U32, C.c_uint64, U32, P, C.c_float, P, P, U32, P, C.c_uint64, P]),
+    "bgtq_decoder_create": (I32, [C.POINTER(DecoderDesc), C.POINTER(P)]),
+    "bgtq_decoder_step": (I32, [P, P, P, P, P]),
+    "bgtq_decoder_info": (I32, [P, C.POINTER(U32), C.POINTER(U32), C.POINTER(U32)]),
+    "bgtq_decoder_trace": (I32, [P, C.c_int, P, U32, C.POINTER(U32)]),
+    "bgtq_decoder_destroy": (None, [P]),
     "bgtq_layout_jit_wait": (I32, [U32]),
     "bgtq_fixture_read": (I32, [C.c_char_p, P]),
     "bgtq_fixture_array_count": (I32, [P, P]),

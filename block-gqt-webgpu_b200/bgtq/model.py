@@ -97,6 +97,9 @@ class Decoder:
     fused: decode steps (one token per sequence, batch <= 8, FP16 weights, FP32 compute) run
     the library's fused weight-streaming kernels on the FP16 weights (bgtq_model_gemv):
     seven launches per layer instead of about a dozen torch / cuBLAS ones.
+    step: eager fused decode steps of up to 4 sequences run the whole model as one persistent
+    cooperative launch (bgtq_decoder_step) with grid barriers between the phases; a step
+    recorded into a CUDA graph (capture_decode) takes the seven-launch path.
 
     Per layer: RMSNorm, one fused Q/K/V GEMM, one library call that applies RoPE to the new
     keys, encodes them into the packed stores and appends the FP16 values
@@ -107,7 +110,7 @@ class Decoder:
     """
 
     def __init__(self, weights, geometry: ModelGeometry, capacity: int, tables, batch: int = 1,
-                 compute=None, device: int = 0, fused: bool = True):
+                 compute=None, device: int = 0, fused: bool = True, step: bool = True, step_ctas_per_sm: int = 0):
         import torch
         from . import _lib
         g = geometry
@@ -162,6 +165,10 @@ class Decoder:
             self.keys.append(ks)
             self.values.append(vs)
             self.attn.append(att)
+        # eager decode steps of up to 4 sequences run as one persistent launch (bgtq_decoder_step)
+        self.step_kernel = bool(step) and self.fused and batch <= 4
+        self._step = None
+        self._step_ctas_per_sm = int(step_ctas_per_sm)
         self._kv_ptrs = []
         import ctypes as C
         for layer in range(g.layers):
@@ -189,6 +196,10 @@ class Decoder:
                 raise ValueError("Invalid tokens/capacity")  # decoder.ts:33
         start = self.length
         st = torch.cuda.current_stream(self.dev).cuda_stream
+        # the persistent step is one cooperative launch; a stream being recorded into a CUDA
+        # graph takes the seven-launch path
+        if n == 1 and self.step_kernel and not torch.cuda.is_current_stream_capturing():
+            return self._decode_step(tokens, st)
         if n == 1 and self.fused:
             return self._decode_fused(tokens, st)
         qw, kvw = g.q_heads * g.head_dim, g.kv_heads * g.head_dim
@@ -215,6 +226,82 @@ class Decoder:
         last = self._norm(h[:, -1], self.final_norm)
         self.length += n
         return (last @ self.emb.t()).float()
+
+    def _step_handle(self):
+        """The persistent decode step (bgtq_decoder_create) over this decoder's FP16 weights,
+        FP32 norms / bias / embedding and per-layer stores, created on first use."""
+        if self._step is None:
+            import ctypes as C
+            from . import _lib
+            g, L = self.g, self.g.layers
+
+            def arr(ts):
+                return (C.c_void_p * L)(*[None if t is None else t.data_ptr() for t in ts])
+
+            keep = dict(ln1=arr([lw["ln1"] for lw in self.layers]), ln2=arr([lw["ln2"] for lw in self.layers]),
+                        bias=arr([lw["qkv_b"] for lw in self.layers]) if g.qkv_bias else None,
+                        qkv=arr([l16["qkv"] for l16 in self.layers16]), o=arr([l16["o"] for l16 in self.layers16]),
+                        gu=arr([l16["gate_up"] for l16 in self.layers16]),
+                        down=arr([l16["down"] for l16 in self.layers16]),
+                        att=(C.c_void_p * L)(*[a._handle.value for a in self.attn]))
+            ad = {k: (None if v is None else C.addressof(v)) for k, v in keep.items()}
+            desc = _lib.DecoderDesc(L, self.batch, g.hidden, g.q_heads, g.kv_heads, g.head_dim, g.intermediate,
+                                    g.vocab, g.rms_eps, self.inv_freq.ctypes.data, ad["ln1"], ad["bias"], ad["ln2"],
+                                    ad["qkv"], ad["o"], ad["gu"], ad["down"], self.final_norm.data_ptr(),
+                                    self.emb16.data_ptr(), self.emb.data_ptr(), ad["att"], self._step_ctas_per_sm)
+            h = C.c_void_p()
+            _lib.call("bgtq_decoder_create", C.byref(desc), C.byref(h))
+            self._step = h
+            import torch
+            self._step_h = torch.empty((self.batch, g.hidden), device=self.dev, dtype=torch.float32)
+        return self._step
+
+    def step_info(self):
+        """(CTAs, dynamic shared memory bytes, staged encode-table bytes) of the persistent
+        decode step."""
+        import ctypes as C
+        from . import _lib
+        n, smem, tab = C.c_uint32(), C.c_uint32(), C.c_uint32()
+        _lib.call("bgtq_decoder_info", self._step_handle(), C.byref(n), C.byref(smem), C.byref(tab))
+        return n.value, smem.value, tab.value
+
+    def step_trace(self, on: bool = True):
+        """Phase timing of the persistent step (bgtq_decoder_trace): switches recording on or
+        off and returns the last traced step's stamps (ns, CTA 0's global timer: start, the
+        end of each layer's five phases, the end of the lm_head) as a uint64 array."""
+        import ctypes as C
+        from . import _lib
+        n = C.c_uint32()
+        out = np.zeros(2 + 5 * self.g.layers, np.uint64)
+        _lib.call("bgtq_decoder_trace", self._step_handle(), int(bool(on)), out.ctypes.data, len(out), C.byref(n))
+        return out
+
+    def _decode_step(self, tokens, st):
+        """One token per sequence as one persistent launch (bgtq_decoder_step): the embedding
+        rows, every layer and the lm_head; the same arithmetic as _decode_fused."""
+        import ctypes as C
+        import torch
+        from . import _lib
+        handle = self._step_handle()
+        tok = tokens[:, 0].contiguous()
+        logits = torch.empty((self.batch, self.g.vocab), device=self.dev, dtype=torch.float32)
+        _lib.call("bgtq_decoder_step", handle, C.c_void_p(tok.data_ptr()), C.c_void_p(self._step_h.data_ptr()),
+                  C.c_void_p(logits.data_ptr()), C.c_void_p(st))
+        self.length += 1
+        return logits
+
+    def close(self):
+        """Releases the persistent step (the stores and weights go with the object)."""
+        from . import _lib
+        if getattr(self, "_step", None) is not None:
+            _lib.lib().bgtq_decoder_destroy(self._step)
+            self._step = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
     def _decode_fused(self, tokens, st):
         """One token per sequence through the fused decode kernels: per layer RMSNorm + Q/K/V
@@ -319,6 +406,7 @@ class Decoder:
             self._host_stale = False
 
     def destroy(self):
+        self.close()
         self._graph = None
         for a in self.attn:
             a.destroy()

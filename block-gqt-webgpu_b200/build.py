@@ -28,7 +28,7 @@ LIB = HERE / "bgtq" / "libbgtq.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr", "-I", str(SRC)]
-STRICT_FP = {"encode.cu", "rows.cu"}
+STRICT_FP = {"encode.cu", "rows.cu", "step.cu"}
 
 
 def sources():

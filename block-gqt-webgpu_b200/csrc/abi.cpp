@@ -207,24 +207,6 @@ bgtq_status check_append(uint32_t dim, uint32_t capacity, uint32_t sequences, co
     return BGTQ_OK;
 }
 
-void fill_encode_head(const bgtq_keys *k, EncodeHead &h) {
-    std::memset(&h, 0, sizeof(h));
-    h.t = k->dt;
-    h.packed = k->rows;
-    h.scales = k->scales;
-    h.k_seq_stride = (uint64_t)k->cap_alloc * k->row_stride;
-    h.s_seq_stride = (uint64_t)k->cap_alloc * k->scale_stride;
-    h.row_stride = k->row_stride;
-    h.scale_stride = k->scale_stride;
-    h.ns = k->L.ns;
-    h.ng = k->L.ng;
-    h.n_cent = (uint32_t)k->L.cent_compact.size();
-    h.ncb = k->L.ncb;
-    for (int i = 0; i < 4; ++i) h.bound_mask[i] = k->L.bound_mask[i];
-    for (int g = 0; g <= kMaxGroups; ++g) h.group_off[g] = k->L.group_off[g];
-    h.lengths = k->d_lengths;
-}
-
 }  // namespace
 
 extern "C" {
@@ -874,6 +856,24 @@ void bgtq_attention_destroy(bgtq_attention *a) {
 
 namespace bgtq {
 // Kernel arguments of one packed-key head with its value store.
+void fill_encode_head(const bgtq_keys *k, EncodeHead &h) {
+    std::memset(&h, 0, sizeof(h));
+    h.t = k->dt;
+    h.packed = k->rows;
+    h.scales = k->scales;
+    h.k_seq_stride = (uint64_t)k->cap_alloc * k->row_stride;
+    h.s_seq_stride = (uint64_t)k->cap_alloc * k->scale_stride;
+    h.row_stride = k->row_stride;
+    h.scale_stride = k->scale_stride;
+    h.ns = k->L.ns;
+    h.ng = k->L.ng;
+    h.n_cent = (uint32_t)k->L.cent_compact.size();
+    h.ncb = k->L.ncb;
+    for (int i = 0; i < 4; ++i) h.bound_mask[i] = k->L.bound_mask[i];
+    for (int g = 0; g <= kMaxGroups; ++g) h.group_off[g] = k->L.group_off[g];
+    h.lengths = k->d_lengths;
+}
+
 void fill_packed_head(AttnHead &ah, const bgtq_keys *k, const bgtq_values *v) {
     const size_t vsz = v->dtype == BGTQ_F32 ? 4 : 2;
     ah.v = v->data;

@@ -267,28 +267,36 @@ __device__ __forceinline__ void load_q(const float *p, float (&q)[QP]) {
 // lookups stay inside the table and its zero tail, so whatever code bytes they meet
 // contribute exactly 0).
 template <int D, int QM, int QP>
+// qt_generic: qt may be shared memory (plain loads; __ldg is for global memory only).
 __device__ __forceinline__ void build_tables(const AttnHead &h, const float *qt, unsigned char *rec, uint32_t d,
-                                             uint32_t cent_off, int tid) {
+                                             uint32_t cent_off, int tid, bool qt_generic = false) {
+    auto qload = [&](const float *p) { return qt_generic ? *p : __ldg(p); };
     using G = RecGeo<D, QM>;
     uint32_t *recs = reinterpret_cast<uint32_t *>(rec);
-    uint32_t base = 0;
-    for (uint32_t g = 0; g < h.ng; ++g) {
-        const uint32_t p0 = h.group_off[g] / 2, p1 = h.group_off[g + 1] / 2;
-        const uint32_t n = ((p1 - p0 + 3) / 4) * 4;
-        for (uint32_t i = tid; i < n; i += kThreads) {
-            uint32_t *rp = recs + (base + i) * G::RP;
-            const uint32_t pr = p0 + i, j0 = 2 * pr;
-            const bool live = pr < p1;
-            for (int r = 0; r < QM; ++r) {
-                rp[2 * r] = __float_as_uint(live ? __ldg(qt + j0 * QP + r) : 0.0f);
-                rp[2 * r + 1] = __float_as_uint(live ? __ldg(qt + (j0 + 1) * QP + r) : 0.0f);
-            }
-            const uint32_t ja = min(j0, d - 1u), jb = min(j0 + 1, d - 1u);
-            rp[2 * QM] = cent_off + 4u * __ldg(h.lookup_off + ja);
-            rp[2 * QM + 1] = cent_off + 4u * __ldg(h.lookup_off + jb);
-            for (int x = 2 * QM + 2; x < G::RP; ++x) rp[x] = 0u;
+    // records of all groups (each padded to a multiple of 4) flattened over the threads, so
+    // a thread's loads are independent of one another (one round trip, not one per group)
+    uint32_t total = 0;
+    for (uint32_t g = 0; g < h.ng; ++g) total += ((h.group_off[g + 1] / 2 - h.group_off[g] / 2 + 3) / 4) * 4;
+    for (uint32_t rix = tid; rix < total; rix += kThreads) {
+        uint32_t g = 0, base = 0, p0 = 0, p1 = 0;
+        for (;; ++g) {
+            p0 = h.group_off[g] / 2;
+            p1 = h.group_off[g + 1] / 2;
+            const uint32_t n = ((p1 - p0 + 3) / 4) * 4;
+            if (rix < base + n) break;
+            base += n;
         }
-        base += n;
+        uint32_t *rp = recs + rix * G::RP;
+        const uint32_t pr = p0 + (rix - base), j0 = 2 * pr;
+        const bool live = pr < p1;
+        for (int r = 0; r < QM; ++r) {
+            rp[2 * r] = __float_as_uint(live ? qload(qt + j0 * QP + r) : 0.0f);
+            rp[2 * r + 1] = __float_as_uint(live ? qload(qt + (j0 + 1) * QP + r) : 0.0f);
+        }
+        const uint32_t ja = min(j0, d - 1u), jb = min(j0 + 1, d - 1u);
+        rp[2 * QM] = cent_off + 4u * __ldg(h.lookup_off + ja);
+        rp[2 * QM + 1] = cent_off + 4u * __ldg(h.lookup_off + jb);
+        for (int x = 2 * QM + 2; x < G::RP; ++x) rp[x] = 0u;
     }
 }
 
@@ -502,7 +510,8 @@ __device__ __forceinline__ void stage_lookup(const AttnHead &h, const Plan &pl, 
 template <int D, int QM, KKind KK, bool VF32, class LP>
 __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uint32_t d, uint32_t hd, uint32_t s,
                                           uint32_t t_lo, uint32_t t_hi, uint32_t slot, uint32_t nslots,
-                                          uint32_t &phase, uint32_t &staged_hd) {
+                                          uint32_t &phase, uint32_t &staged_hd, const float *qt_src = nullptr,
+                                          bool defer_merge = false) {
     constexpr int TPL = Geo<D>::TPL, TT = Geo<D>::TT, QP = QPad<QM>::QP;
     constexpr bool MMA = UseMma<D, VF32>::value;
     constexpr int VSZ = VF32 ? 4 : 2, VEC = 16 / VSZ, LPT = D / VEC, TPS = 32 / LPT;
@@ -524,7 +533,7 @@ __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uin
         staged_hd = hd;
     }
     const uint32_t seq = a.seq_first + s;
-    const uint32_t len = a.lengths[seq];
+    const uint32_t len = __ldcg(a.lengths + seq);  // L2: a persistent caller's lengths change between phases
     const uint32_t R = a.rows;
 
     unsigned char *rec = smem + pl.qrec;
@@ -603,13 +612,14 @@ __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uin
     }
 
     // ---- prologue: codebooks, query tables, barriers ----
-    const float *qt = a.qt + ((uint64_t)s * a.heads + hd) * (uint64_t)(D * QP);
+    // the pair's query records: the query rotation's output, or the caller's copy (qt_src)
+    const float *qt = qt_src ? qt_src : a.qt + ((uint64_t)s * a.heads + hd) * (uint64_t)(D * QP);
     if constexpr (KK == KKind::Packed) {
-        build_tables<D, QM, QP>(h, qt, rec, d, pl.cent, tid);
+        build_tables<D, QM, QP>(h, qt, rec, d, pl.cent, tid, qt_src != nullptr);
     } else {
         const float4 *src = reinterpret_cast<const float4 *>(qt);
         float4 *dst = reinterpret_cast<float4 *>(qrec_s);
-        for (uint32_t i = tid; i < (uint32_t)(D * QP / 4); i += kThreads) dst[i] = __ldg(src + i);
+        for (uint32_t i = tid; i < (uint32_t)(D * QP / 4); i += kThreads) dst[i] = qt_src ? src[i] : __ldg(src + i);
     }
     __syncthreads();
 
@@ -956,7 +966,8 @@ __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uin
             if (dd == 0) { pp[d] = M; pp[d + 1] = L; }
         }
     }
-    if (nslots > 1) {
+    // defer_merge: the caller merges the partials itself after a grid-wide barrier
+    if (nslots > 1 && !defer_merge) {
         __threadfence();
         __syncthreads();
         if (tid == 0) {
@@ -967,18 +978,49 @@ __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uin
         if (s_last) {
             __threadfence();
             const uint64_t sstride = (uint64_t)a.seq_count * a.heads * R * (d + 2);
+            const float *pbase = a.part + ((uint64_t)s * a.heads + hd) * R * (uint64_t)(d + 2);
+            // every slot's (maximum, sum) of every row in one round of independent loads, the
+            // per-row maximum, weights and sum from shared memory, then the weighted outputs
+            // eight slots of loads at a time: the same arithmetic in the same order as a
+            // per-element pass over the slots, without one L2 round trip per slot
+            float *ms = reinterpret_cast<float *>(smem + pl.stage);  // [nslots][QP] maxima, then weights
+            float *ls = ms + nslots * QP;                             // [nslots][QP] sums
+            float *rs = ls + nslots * QP;                             // [QP] (maximum, sum) per row
+            for (uint32_t idx = tid; idx < rows_live * nslots; idx += kThreads) {
+                const uint32_t r = idx / nslots, sp = idx % nslots;
+                const float *pp = pbase + (uint64_t)r * (d + 2) + sp * sstride;
+                ms[sp * QP + r] = __ldcg(pp + d);
+                ls[sp * QP + r] = __ldcg(pp + d + 1);
+            }
+            __syncthreads();
+            if ((uint32_t)tid < rows_live) {
+                const uint32_t r = tid;
+                float M = -INFINITY;
+                for (uint32_t sp = 0; sp < nslots; ++sp) M = fmaxf(M, ms[sp * QP + r]);
+                float L = 0.0f;
+                for (uint32_t sp = 0; sp < nslots; ++sp) {
+                    const float m = ms[sp * QP + r];
+                    const float f = m == -INFINITY ? 0.0f : ex2(m - M);
+                    L = fmaf(ls[sp * QP + r], f, L);
+                    ms[sp * QP + r] = f;
+                }
+                rs[2 * r] = M;
+                rs[2 * r + 1] = L;
+            }
+            __syncthreads();
             for (uint32_t idx = tid; idx < rows_live * d; idx += kThreads) {
                 const uint32_t r = idx / d, dd = idx % d;
-                const float *pp = a.part + (((uint64_t)s * a.heads + hd) * R + r) * (uint64_t)(d + 2);
-                float M = -INFINITY;
-                for (uint32_t sp = 0; sp < nslots; ++sp) M = fmaxf(M, __ldcg(pp + sp * sstride + d));
-                float L = 0.0f, Ov = 0.0f;
-                for (uint32_t sp = 0; sp < nslots; ++sp) {
-                    const float ms = __ldcg(pp + sp * sstride + d);
-                    const float f = ms == -INFINITY ? 0.0f : ex2(ms - M);
-                    L = fmaf(__ldcg(pp + sp * sstride + d + 1), f, L);
-                    Ov = fmaf(__ldcg(pp + sp * sstride + dd), f, Ov);
+                const float *pp = pbase + (uint64_t)r * (d + 2) + dd;
+                float Ov = 0.0f;
+                for (uint32_t sp0 = 0; sp0 < nslots; sp0 += 8) {
+                    float v[8];
+#pragma unroll
+                    for (uint32_t k = 0; k < 8; ++k) v[k] = sp0 + k < nslots ? __ldcg(pp + (sp0 + k) * sstride) : 0.0f;
+#pragma unroll
+                    for (uint32_t k = 0; k < 8; ++k)
+                        if (sp0 + k < nslots) Ov = fmaf(v[k], ms[(sp0 + k) * QP + r], Ov);
                 }
+                const float M = rs[2 * r], L = rs[2 * r + 1];
                 a.out[(obase + r) * d + dd] = Ov / L;
                 if (dd == 0 && a.lse) a.lse[obase + r] = (M + log2f(L) - kPShift) * kLn2;
             }

@@ -81,4 +81,6 @@ namespace bgtq {
 // Kernel arguments of one packed-key head with its value store (every attention entry
 // point over packed keys fills its heads through this one function).
 void fill_packed_head(AttnHead &ah, const bgtq_keys *k, const bgtq_values *v);
+// Encode arguments of one packed-key store (every K append fills its heads through this).
+void fill_encode_head(const bgtq_keys *k, EncodeHead &h);
 }  // namespace bgtq

@@ -396,6 +396,55 @@ bgtq_status bgtq_model_gemv(int mode, const float *x, uint32_t batch, uint64_t x
                             const float *norm_w, float eps, const uint16_t *w, const float *bias, uint32_t out,
                             float *y, uint64_t y_stride, void *stream);
 
+/* Persistent decode step of a decoder model (src/model/decoder.ts:31-81 decode: per layer
+ * RMSNorm + Q/K/V (+ bias), RoPE + K encode + V append, compressed-K GQA attention, o_proj +
+ * residual, RMSNorm + gate/up + SiLU, down_proj + residual; final RMSNorm + lm_head) as ONE
+ * cooperative launch with grid-wide barriers between the phases, replacing the seven
+ * launches per layer of bgtq_model_gemv / bgtq_append_kv_rope / bgtq_attend.  Same
+ * arithmetic as those entry points (the K encode bit for bit).  No counterpart in the
+ * reference, whose decoder dispatches one compute pass per shader. */
+typedef struct bgtq_decoder bgtq_decoder;
+typedef struct {
+    uint32_t layers, batch, hidden, q_heads, kv_heads, head_dim, intermediate, vocab;
+    float rms_eps;
+    const float *inv_freq;               /* host [head_dim / 2]: split-half RoPE table of Q and K */
+    const float *const *ln1;             /* [layers] device RMSNorm weights [hidden] */
+    const float *const *qkv_bias;        /* [layers] device [(q_heads + 2 kv_heads) head_dim], or null */
+    const float *const *ln2;             /* [layers] device [hidden] */
+    const uint16_t *const *w_qkv;        /* [layers] FP16 [(q_heads + 2 kv_heads) head_dim][hidden] */
+    const uint16_t *const *w_o;          /* [layers] FP16 [hidden][q_heads head_dim] */
+    const uint16_t *const *w_gate_up;    /* [layers] FP16 [2 intermediate][hidden]: gate rows, up rows */
+    const uint16_t *const *w_down;       /* [layers] FP16 [hidden][intermediate] */
+    const float *final_norm;             /* device [hidden] */
+    const uint16_t *lm_head;             /* FP16 [vocab][hidden] */
+    const float *embedding;              /* FP32 [vocab][hidden] for token-id steps, or null */
+    bgtq_attention *const *attention;    /* [layers]: kv_heads packed-key stores + FP16 value stores */
+    uint32_t ctas_per_sm;                /* resident CTAs per SM (0: one; at most as many as fit) */
+} bgtq_decoder_desc;
+/* Requires head_dim 64, gqa = q_heads / kv_heads in 1..8, kv_heads <= 8, batch 1..4,
+ * hidden, intermediate and q_heads head_dim multiples of 8, 16-byte aligned weights, and
+ * attention objects of kv_heads heads, >= gqa query rows and >= batch sequences.  The step
+ * covers sequences 0 .. batch-1.  Errors: BGTQ_EINVAL (shape), BGTQ_ECUDA. */
+bgtq_status bgtq_decoder_create(const bgtq_decoder_desc *desc, bgtq_decoder **out);
+/* One token per sequence.  tokens: device int64 [batch] token ids (needs the embedding), or
+ * null when h already holds the embedded rows.  h: device FP32 [batch][hidden], the residual
+ * stream (overwritten); logits: device FP32 [batch][vocab].  Every layer's stores must hold
+ * the same length per sequence, below their capacity.  Stream-ordered; moves the stores'
+ * lengths on by one.  A barrier wait that runs out sets the device status word
+ * (bgtq_device_status) and every later step of the object ends at its first barrier.
+ * Errors: BGTQ_EINVAL, BGTQ_EBUSY (lengths), BGTQ_ECAPACITY, BGTQ_ECUDA. */
+bgtq_status bgtq_decoder_step(bgtq_decoder *dec, const int64_t *tokens, float *h, float *logits, void *stream);
+/* Phase timing: on != 0 makes later steps record CTA 0's global-timer stamps (ns) at the
+ * start, after each of the 5 phases of every layer (Q/K/V; append and attention; o_proj;
+ * gate/up; down) and at the end (2 + 5 layers stamps).
+ * out (nullable, cap entries): the last traced step's stamps, copied synchronously before
+ * the switch takes effect; *n_out = the stamp count. */
+bgtq_status bgtq_decoder_trace(bgtq_decoder *dec, int on, uint64_t *out, uint32_t cap, uint32_t *n_out);
+/* CTAs of the cooperative launch, its dynamic shared memory per CTA, and the bytes of encode
+ * tables the append CTAs stage in shared memory (0: read from global memory).  Nullable. */
+bgtq_status bgtq_decoder_info(const bgtq_decoder *dec, uint32_t *ctas, uint32_t *smem_bytes, uint32_t *table_bytes);
+void bgtq_decoder_destroy(bgtq_decoder *dec);
+
 /* Device status word written by kernels (0 = fine); reading it synchronises. */
 bgtq_status bgtq_device_status(int device, uint32_t *status_out);
 
