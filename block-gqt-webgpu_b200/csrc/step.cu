@@ -525,30 +525,14 @@ __device__ void attention_phase(const Args &A, const AttnArgs &a, const Tasks &t
             query_records<QM>(A, a, hd, s, A.len_new[s] - 1u, a.head[hd].rot, qraw_s, qt_s);
             q_pair = p;
         }
+        // a range holding the row this step appends waits (bounded, inside the body, after its
+        // query tables) for the sequence's appends: this head's row, and head 0's, whose
+        // lengths the body reads
         const uint32_t last = A.len_new[s] - 1u;
-        if (i * T <= last && last < (i + 1) * T) {
-            // the range holds the row this step appends: wait (bounded) for the sequence's
-            // appends - this head's row, and head 0's, whose lengths the body reads
-            if (tid < 2u) {
-                const uint32_t h2 = tid == 0 ? hd : 0u;
-                uint32_t it = 0, ok = 1;
-                while (ld_acquire(flags + s * A.kv_heads + h2) != A.step_id) {
-                    if (++it > kSpinLimit) {
-                        ok = 0;
-                        break;
-                    }
-                    if (it > 64u) __nanosleep(32);
-                }
-                if (!ok) {
-                    atomicOr(A.status, kStatusWaitTimeout);
-                    atomicExch(A.bar + 2, 1u);
-                }
-            }
-            __syncthreads();
-            fence_proxy_global();  // the new row, stored by generic stores, is read by bulk copies
-        }
-        attn::attn_pair<D, QM, KKind::Packed, false, attn::RuntimeGroups>(a, A.pl, A.d, hd, s, i * T, (i + 1) * T, i,
-                                                                           tk.nt, phase, staged_hd, qt_s, true);
+        const bool holds_new = i * T <= last && last < (i + 1) * T;
+        attn::attn_pair<D, QM, KKind::Packed, false, attn::RuntimeGroups>(
+            a, A.pl, A.d, hd, s, i * T, (i + 1) * T, i, tk.nt, phase, staged_hd, qt_s, true,
+            holds_new ? flags + s * A.kv_heads : nullptr, A.step_id);
     }
     // every copy has landed (each pair ends with its waits and a CTA barrier): the region
     // goes back to the GEMV phases
