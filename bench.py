@@ -816,13 +816,13 @@ def run_model(args, rank, world, local_rank):
     g = SMOLLM2_135M if args.workload == "model-smollm2" else QWEN25_05B
     prefix, steps, warmup = 4096, args.steps, max(3, args.warmup)
     tables = calibration_tables(g.family, g.layers * g.kv_heads)
-    dec = Decoder(random_weights(g, seed=7 + rank, device=dev), g, prefix + 2 * (warmup + steps) + 8, tables, batch=1)
+    dec = Decoder(random_weights(g, seed=7 + rank, device=dev), g, prefix + 2 * (warmup + steps) + 16, tables, batch=1)
     rng = np.random.default_rng(rank)
     t_pre = time.perf_counter()
     dec.prefill(torch.from_numpy(rng.integers(0, g.vocab, (1, prefix))).to(dev), chunk=1024)
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t_pre
-    toks = [torch.from_numpy(rng.integers(0, g.vocab, (1, 1))).to(dev) for _ in range(2 * (warmup + steps) + 1)]
+    toks = [torch.from_numpy(rng.integers(0, g.vocab, (1, 1))).to(dev) for _ in range(2 * (warmup + steps) + 4)]
     it = iter(toks)
     logits = []
 
@@ -855,6 +855,18 @@ def run_model(args, rank, world, local_rank):
     if dec.step_kernel and args.model_path in ("step", "best"):
         step_ms, step_clk = timed(lambda: logits.append(dec.forward(next(it), _check=False)))
         ctas, smem, _ = dec.step_info()
+        # phase breakdown of one more step (CTA 0's global-timer stamps at the end of each
+        # phase): medians over the layers, outside the timed region
+        dec.step_trace(True)
+        logits.append(dec.forward(next(it), _check=False))
+        torch.cuda.synchronize()
+        st = dec.step_trace(False).astype(np.int64)
+        d_us = np.diff(st) / 1e3
+        phases = d_us[:-1].reshape(g.layers, 5)
+        step_phases = {"qkv": float(np.median(phases[:, 0])), "append_and_attention": float(np.median(phases[:, 1])),
+                       "merge_and_o_proj": float(np.median(phases[:, 2])), "gate_up": float(np.median(phases[:, 3])),
+                       "down": float(np.median(phases[:, 4])), "lm_head": float(d_us[-1]),
+                       "total": float((st[-1] - st[0]) / 1e3), "unit": "us (median over layers; one traced step)"}
     # the same step as a CUDA graph of seven launches per layer
     graph_ms = None
     if args.model_path in ("graph", "best") or step_ms is None:
@@ -870,6 +882,7 @@ def run_model(args, rank, world, local_rank):
         print(json.dumps({
             "metric": f"{g.family} whole-model decode tokens/s (batch 1 per GPU, 4096-token prefix)",
             "decode_path": path, "persistent_step_ms_per_step": step_ms, "graph_ms_per_step": graph_ms,
+            "persistent_step_phases": step_phases if step_ms is not None else None,
             "value": world * 1e3 / ms, "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (random-init FP16 weights N(0,0.02), uniform random token ids)",
