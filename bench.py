@@ -484,7 +484,9 @@ def run_ours(args, rank, world, local_rank):
     clk = clocks.stop()
     elapsed = t_start.elapsed_time(t_end) / 1e3
     launch_ms = [a.elapsed_time(b) for evs in attn_ms for a, b in evs]
-    launches = steps * L * 3  # per layer: fused K/V append (bumps the lengths too) + query rotation + attention
+    # per layer: the fused K/V append (bumps the lengths too) + the attention's launches (the
+    # query rotation, unless the attention CTAs rotate their own queries, and the attention)
+    launches = steps * L * (1 + atts[0].last_launches)
     strong_out = torch.stack([o[:B] for o in outs])          # [L, B, H, R, d] of the last timed step
     rows_seen = T + warmup + steps
     splits = atts[0].last_splits

@@ -1025,11 +1025,11 @@ bgtq_status bgtq_attend(bgtq_attention *at, const float *q, const uint32_t *posi
     a.rows = rows;
     a.causal = causal ? 1u : 0u;
     a.logit_stride = max_len;
-    uint32_t splits = 1, sk = 0;
+    uint32_t splits = 1, sk = 0, attn_launches = 2;
     cudaError_t e = launch_attention(a, kk, at->values[0]->dtype == BGTQ_F32, d, max_cent, plan_len, at->forced_splits,
-                                     at->max_splits, at->schedule, &splits, &sk, stream);
+                                     at->max_splits, at->schedule, &splits, &sk, stream, &attn_launches);
     if (e != cudaSuccess) return cuda_fail(e, "attention launch");
-    launches += 2;  // query rotation + attention
+    launches += attn_launches;  // query rotation (unless fused) + attention
     if (probs) {
         e = launch_probs(dlogits, at->lse, dprobs, (uint64_t)seq_count * H * rows, max_len, max_len, stream);
         if (e != cudaSuccess) return cuda_fail(e, "probabilities launch");

@@ -193,7 +193,7 @@ static bool choose_stream_k(uint32_t pairs, uint32_t max_len, uint32_t chunk, ui
 
 cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t d, uint32_t max_cent,
                              uint32_t max_len, uint32_t forced_splits, uint32_t max_splits, int schedule,
-                             uint32_t *splits_out, uint32_t *sk_out, cudaStream_t s) {
+                             uint32_t *splits_out, uint32_t *sk_out, cudaStream_t s, uint32_t *launches_out) {
     AttnArgs a = a_in;
     const uint32_t D = dim_template(d);
     const Entry e = pick_entry(kk, v_f32, D, a.rows);
@@ -254,9 +254,22 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
     }
     if (splits_out) *splits_out = splits;
     if (sk_out) *sk_out = a.sk_units;
-    cudaError_t err = launch_pdl(attn::qrot_kernel, dim3(a.heads, a.seq_count), dim3(128), 0, s, a, d, D, e.qp,
-                                 kk == KKind::Packed ? 1 : 0);
-    if (err != cudaSuccess) return err;
+    // one partial wave of split-KV CTAs over packed keys: each CTA rotates its pair's queries
+    // itself (the rotation staged in its tile buffers, the records in its P buffers), which
+    // takes a launch off the critical path of small batches; larger launches rotate once per
+    // pair in a launch of their own
+    const uint32_t stage_bytes = attn::kWarps * pl.warp_bytes, pbuf_bytes = pl.bars - pl.pbuf;
+    a.fuse_q = kk == KKind::Packed && d <= 64u && !a.sk_units && (uint64_t)pairs * splits <= slots &&
+                       stage_bytes >= 4u * (d * d + a.rows * d) && pbuf_bytes >= 4u * D * e.qp
+                   ? 1u
+                   : 0u;
+    if (launches_out) *launches_out = a.fuse_q ? 1u : 2u;
+    cudaError_t err = cudaSuccess;
+    if (!a.fuse_q) {
+        err = launch_pdl(attn::qrot_kernel, dim3(a.heads, a.seq_count), dim3(128), 0, s, a, d, D, e.qp,
+                         kk == KKind::Packed ? 1 : 0);
+        if (err != cudaSuccess) return err;
+    }
     if (jk) {
         uint32_t dd = d;
         Plan plc = pl;

@@ -1056,6 +1056,50 @@ __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uin
     __syncthreads();  // the merge scratch and tile buffers are free for the next pair
 }
 
+// Element j of query row q after split-half RoPE at position pos (src/model/kernels.wgsl:
+// 49-54) with the table inv[d/2], rounded like separate multiplies and adds; without a
+// table the element itself.
+__device__ __forceinline__ float rope_elem(const float *q, uint32_t j, uint32_t d, uint32_t pos, const float *inv) {
+    if (!inv) return q[j];
+    const uint32_t pairs = d / 2, p = j < pairs ? j : j - pairs;
+    const float ang = __fmul_rn((float)pos, inv[p]);
+    const float c = cosf(ang), sn = sinf(ang), x = q[p], y = q[p + pairs];
+    return j < pairs ? __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn)) : __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+}
+
+// The CTA's own query records for (sequence s, KV head hd), with the query rotation
+// kernel's arithmetic (qrot_kernel, below): for launches of one partial wave, where a
+// separate rotation launch on the critical path costs more than every CTA rotating its
+// pair's few query rows.  rot_s: the head's rotation already in shared memory (head dims
+// up to 64); qraw: R * d floats of scratch; qt: [D][QP] output, shared memory.
+template <int D, int QP>
+__device__ __forceinline__ void own_query_records(const AttnArgs &a, uint32_t d, uint32_t hd, uint32_t s,
+                                                  const float *rot_s, float *qraw, float *qt) {
+    const AttnHead &h = a.head[hd];
+    const uint32_t R = a.rows, tid = threadIdx.x;
+    const float *qg = a.q + ((uint64_t)s * a.heads + hd) * (uint64_t)R * d;
+    const uint32_t len = __ldcg(a.lengths + a.seq_first + s);
+    for (uint32_t idx = tid; idx < R * d; idx += kThreads) {
+        const uint32_t r = idx / d, i = idx % d;
+        const uint32_t pos = a.positions ? a.positions[s * R + r] : (len ? len - 1 : 0);
+        qraw[idx] = rope_elem(qg + r * d, h.perm[i], d, pos, a.rope);
+    }
+    __syncthreads();
+    const float qscale = kLog2e / sqrtf((float)d);
+    for (uint32_t idx = tid; idx < (uint32_t)(D * QP); idx += kThreads) {
+        const uint32_t j = idx / QP, r = idx % QP;
+        float v = 0.0f;
+        if (r < R && j < d) {
+            const uint32_t g = h.group_of[j], lo = h.group_off[g], hi = h.group_off[g + 1];
+            const float *rj = rot_s + (uint64_t)j * d;
+            for (uint32_t i = lo; i < hi; ++i) v = fmaf(rj[i], qraw[r * d + i], v);
+            v *= qscale;
+        }
+        qt[idx] = v;
+    }
+    __syncthreads();
+}
+
 // One CTA of the decode attention.  Split-KV (a.sk_units == 0): the CTA owns split `split`
 // of the pair (sequence s, KV head hd).  Stream-K (a.sk_units CTAs): the pairs' token tiles
 // (a.sk_pair_tiles of kWarps * TT tokens per pair, pairs in head-major order) are dealt to
@@ -1079,6 +1123,17 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     // the codebooks are the store's own tables: staged while the kernel before this one (the
     // query rotation) finishes; lengths, query records and cache rows only after the wait
     if constexpr (KK == KKind::Packed) stage_lookup(a.head[hd], pl, reinterpret_cast<float *>(smem + pl.cent), tid);
+    // a.fuse_q: this CTA rotates its pair's queries itself (no rotation launch before it);
+    // the rotation, a table of the store, comes into the tile buffers before the wait
+    constexpr int QP = QPad<QM>::QP;
+    const bool fq = KK == KKind::Packed && a.fuse_q && !a.sk_units;
+    float *rot_s = reinterpret_cast<float *>(smem + pl.stage);
+    if (fq) {
+        const float4 *src = reinterpret_cast<const float4 *>(a.head[hd].rot);
+        float4 *dst = reinterpret_cast<float4 *>(rot_s);
+#pragma unroll 8
+        for (uint32_t idx = tid; idx < d * d / 4; idx += kThreads) dst[idx] = __ldg(src + idx);
+    }
     pdl_wait();
     // the kernel after this one may launch once every CTA of this grid has started: it then
     // takes only the slots this grid's last wave frees, fetches its constant tables and waits
@@ -1088,9 +1143,13 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     __syncthreads();
     uint32_t phase = 0, staged_hd = hd;
     if (!a.sk_units) {
+        // fused rotation: query records into the P buffers (free until the tile loop), raw
+        // query rows after the rotation in the tile buffers (free until the first copies)
+        float *qt_s = reinterpret_cast<float *>(smem + pl.pbuf);
+        if (fq) own_query_records<D, QP>(a, d, hd, s, rot_s, rot_s + d * d, qt_s);
         attn_pair<D, QM, KK, VF32, LP>(a, pl, d, hd, s, split * a.tokens_per_split,
                                        split * a.tokens_per_split + a.tokens_per_split, split, a.splits, phase,
-                                       staged_hd);
+                                       staged_hd, fq ? qt_s : nullptr);
         return;
     }
     const uint64_t g1 = g0 + K < total ? g0 + K : total;
@@ -1109,17 +1168,6 @@ template <int D, int QM, KKind KK, bool VF32>
 __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value)
     attn_kernel(const __grid_constant__ AttnArgs a, const Plan pl, uint32_t d) {
     attn_body<D, QM, KK, VF32, RuntimeGroups>(a, pl, d, blockIdx.x, blockIdx.y, blockIdx.z);
-}
-
-// Element j of query row q after split-half RoPE at position pos (src/model/kernels.wgsl:
-// 49-54) with the table inv[d/2], rounded like separate multiplies and adds; without a
-// table the element itself.
-__device__ __forceinline__ float rope_elem(const float *q, uint32_t j, uint32_t d, uint32_t pos, const float *inv) {
-    if (!inv) return q[j];
-    const uint32_t pairs = d / 2, p = j < pairs ? j : j - pairs;
-    const float ang = __fmul_rn((float)pos, inv[p]);
-    const float c = cosf(ang), sn = sinf(ang), x = q[p], y = q[p + pairs];
-    return j < pairs ? __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn)) : __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
 }
 
 // Query records for one (sequence, KV head): qt[j][r] = sum_{i in group(j)} R[j][i] *

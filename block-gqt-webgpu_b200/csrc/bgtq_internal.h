@@ -174,6 +174,7 @@ struct AttnArgs {
     // stream-K (sk_units != 0 CTAs): each pair spans sk_pair_tiles tiles of kWarps warp tiles,
     // dealt to the CTAs sk_tiles at a time in head-major pair order; splits is then unused
     uint32_t sk_units, sk_tiles, sk_pair_tiles;
+    uint32_t fuse_q;  // split-KV CTAs rotate their pair's queries themselves (no rotation launch)
 };
 
 // Prefill: n query positions per sequence, all gqa query heads of each KV head.
@@ -215,10 +216,11 @@ cudaError_t launch_reconstruct(const ReconArgs &a, uint32_t n_cent, cudaStream_t
 // Attention over a.seq_count sequences x a.heads KV heads; picks the split-KV factor
 // (forced_splits = 0: automatic) and writes it to *splits_out, or a stream-K schedule
 // (schedule 0: when it is estimated faster; 1: never; 2: whenever the kernel allows) and
-// writes its CTA count to *sk_out (0 for split-KV).
+// writes its CTA count to *sk_out (0 for split-KV); *launches_out: kernels launched (the
+// query rotation runs inside the attention CTAs of a launch of one partial wave).
 cudaError_t launch_attention(const AttnArgs &a, KKind kk, int v_f32, uint32_t d, uint32_t max_cent,
                              uint32_t max_len, uint32_t forced_splits, uint32_t max_splits, int schedule,
-                             uint32_t *splits_out, uint32_t *sk_out, cudaStream_t s);
+                             uint32_t *splits_out, uint32_t *sk_out, cudaStream_t s, uint32_t *launches_out = nullptr);
 // Causal prefill attention (packed keys, FP16 values, head dim <= 64): the query rotation,
 // then the tcgen05/TMEM kernel (umma != 0) or the mma.sync kernel.
 cudaError_t launch_prefill(const PrefillArgs &a, uint32_t max_cent, int umma, cudaStream_t s);

@@ -293,6 +293,7 @@ def test_device_io_matches_host_io(cuda):
     att = GroupedAttention([s[0] for s in stores], [s[1] for s in stores], 3)
     q = synthetic.profiled(rng, S * 9, 64).reshape(S, 3, 3, 64)
     host = att.attend(q)
+    assert att.last_launches == 1   # one partial wave: every CTA rotates its own queries
     dev = att.attend(torch.from_numpy(q).to(cuda))
     torch.cuda.synchronize()
     np.testing.assert_array_equal(dev.cpu().numpy(), host)
