@@ -335,11 +335,10 @@ __global__ void __launch_bounds__(NTH, 2) prefill_tc_kernel(const __grid_constan
         // ---- this half row's scores, mask, online softmax, P halves ----
         float sv[32];
         {
+            // the two high x high parts in one round trip, then the cross terms (added in the
+            // same order as before: hh0 + hh1, then + x)
             float t[32];
-            tmem_ld32(tmem + tlane + kColHH0 + c0, t);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) sv[i] = t[i];
+            tmem_ld32(tmem + tlane + kColHH0 + c0, sv);
             tmem_ld32(tmem + tlane + kColHH1 + c0, t);
             tmem_wait_ld();
 #pragma unroll
