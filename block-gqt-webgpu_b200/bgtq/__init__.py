@@ -18,10 +18,11 @@ __all__ = ["BGTQError", "DeviceError", "LayoutError", "RangeError", "StateError"
            "layout_jit_counts", "layout_jit_wait"]
 
 
-def set_layout_jit(on: bool) -> None:
-    """Use (default) or bypass the layout-specialised decode attention kernels (bgtq_set_layout_jit)."""
+def set_layout_jit(on) -> None:
+    """Layout-specialised decode attention kernels (bgtq_set_layout_jit): True = every launch,
+    False = never, "auto" (the default) = launches of more than one wave of CTAs."""
     from . import _lib
-    _lib.call("bgtq_set_layout_jit", 1 if on else 0)
+    _lib.call("bgtq_set_layout_jit", 2 if on == "auto" else 1 if on else 0)
 
 
 def layout_jit_stats() -> tuple[int, int]:

@@ -371,7 +371,14 @@ class Decoder:
         from . import _lib, layout_jit_wait
         for a in self.attn:
             _lib.call("bgtq_attention_plan_for_capacity", a._handle, 1)
-        out = self.forward(token)                      # eager step: warms every kernel up
+        # the eager step runs the launches the graph will record (not the persistent step), so
+        # every kernel they use - the layout-specialised attention kernels above all - is
+        # loaded before the capture
+        step, self.step_kernel = self.step_kernel, False
+        try:
+            out = self.forward(token)                  # eager step: warms every kernel up
+        finally:
+            self.step_kernel = step
         torch.cuda.synchronize(self.dev)
         layout_jit_wait(jit_wait_s)
         self._tok = torch.as_tensor(token, device=self.dev).reshape(self.batch, 1).long().clone()

@@ -210,10 +210,24 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
     const Plan pl =
         attn::make_plan(kk, v_f32, D, e.qp, TT, row_stride, scale_stride, max_cent, (uint32_t)optin - 64u, 2, e.qm);
     if (pl.total > (uint32_t)optin) return cudaErrorInvalidConfiguration;
-    // packed keys: the kernel specialised for the heads' group structures, once available
+    // packed keys: the kernel specialised for the heads' group structures, once available.
+    // Automatic mode keeps launches of one partial wave of the generic kernel on the generic
+    // kernel: they are latency-bound, the specialised kernel's fewer instructions do not
+    // shorten them, and its larger unrolled bodies (one per layer and head structure) start
+    // every launch with cold instruction caches (the SmolLM2 decode step took 1.67 ms with
+    // the specialised kernels against 1.28 ms with the generic one)
+    const uint32_t chunk = attn::kWarps * TT, pairs = a.seq_count * a.heads;
+    bool try_jit = kk == KKind::Packed && jit_mode() != 0;
+    if (try_jit && jit_mode() == 2 && !forced_splits) {
+        const int g_per_sm = std::max(1, e.occ(pl));
+        const uint32_t g_slots = (uint32_t)(sms * g_per_sm);
+        uint32_t sp = 1, tp = 0;
+        choose_splits(pairs, max_len, chunk, g_slots, 0, std::max(1u, max_splits), &sp, &tp);
+        if ((uint64_t)pairs * sp <= g_slots) try_jit = false;
+    }
     const void *jk = nullptr;
     bool head_major = false;
-    if (kk == KKind::Packed) {
+    if (try_jit) {
         JitKey key{};
         key.D = D;
         key.QM = e.qm;
@@ -232,7 +246,7 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
     int per_sm = jk ? jit_occupancy(jk, dev, pl.total) : e.occ(pl);
     if (per_sm < 1) per_sm = 1;
     uint32_t splits = 1, tps = 0;
-    const uint32_t slots = (uint32_t)(sms * per_sm), chunk = attn::kWarps * TT, pairs = a.seq_count * a.heads;
+    const uint32_t slots = (uint32_t)(sms * per_sm);
     choose_splits(pairs, max_len, chunk, slots, forced_splits, std::max(1u, max_splits), &splits, &tps);
     a.splits = splits;
     a.tokens_per_split = tps;

@@ -249,7 +249,8 @@ struct JitKey {
     JitLayout head[kMaxHeads];
 };
 const void *jit_attention_kernel(const JitKey &key, cudaStream_t stream, bool *head_major);
-void jit_set_enabled(int on);
+void jit_set_enabled(int on);  // 0 off, 1 every launch, 2 automatic
+int jit_mode();
 // The calling thread's launches keep the generic kernel while on != 0 (an entry point that
 // promises no allocation at attention time: loading a specialised kernel allocates).
 void jit_suppress_on_thread(int on);

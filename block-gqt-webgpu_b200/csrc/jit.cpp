@@ -409,19 +409,23 @@ void load_compiled(Entry &e) {
     std::vector<char>().swap(e.cubin);
 }
 
-bool enabled() {
+// 0 off, 1 every launch, 2 automatic (the default; BGTQ_LAYOUT_JIT=0 / 1 in the environment
+// selects off / every launch)
+int mode() {
     int v = g_enabled.load();
     if (v < 0) {
         const char *e = std::getenv("BGTQ_LAYOUT_JIT");
-        v = (e && e[0] == '0') ? 0 : 1;
+        v = e && e[0] == '0' ? 0 : e && e[0] == '1' ? 1 : 2;
         g_enabled.store(v);
     }
-    return v != 0;
+    return v;
 }
+bool enabled() { return mode() != 0; }
 
 }  // namespace
 
-void jit_set_enabled(int on) { g_enabled.store(on ? 1 : 0); }
+void jit_set_enabled(int on) { g_enabled.store(on < 0 || on > 2 ? 2 : on); }
+int jit_mode() { return mode(); }
 
 namespace {
 thread_local int t_suppressed = 0;

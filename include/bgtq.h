@@ -128,7 +128,9 @@ bgtq_status bgtq_optimal_centroids(uint32_t bits, uint32_t n, float *out);
  * process; identical results, fewer instructions).  Heads sharing one structure compile on the
  * first launch; heads with several compile on a background thread while the generic kernel
  * runs, and a later launch outside a graph capture loads the result.  on = 0 keeps the
- * generic kernel (also BGTQ_LAYOUT_JIT=0 in the environment).  No counterpart in the
+ * generic kernel (also BGTQ_LAYOUT_JIT=0 in the environment), 1 specialises every launch
+ * (BGTQ_LAYOUT_JIT=1), 2 (the default) every launch of more than one wave of CTAs: launches of
+ * one partial wave are latency-bound and stay on the generic kernel.  No counterpart in the
  * reference. */
 bgtq_status bgtq_set_layout_jit(int on);
 /* Specialised kernels loaded / keys that failed to build (and use the generic kernel). */

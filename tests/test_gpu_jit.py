@@ -17,6 +17,15 @@ from conftest import GOLDEN, load_config
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _default_jit_mode():
+    """Every test switches the specialised kernels on for every launch (its sizes are one wave
+    of CTAs, which the automatic mode leaves on the generic kernel); the default comes back
+    afterwards."""
+    yield
+    bgtq.set_layout_jit("auto")
+
+
 def _stores(cuda, name, S, T, H, vdtype, seed):
     import torch
     z = load_config(name)
