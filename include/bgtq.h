@@ -434,6 +434,8 @@ bgtq_status bgtq_decoder_create(const bgtq_decoder_desc *desc, bgtq_decoder **ou
  * the same length per sequence, below their capacity.  Stream-ordered; moves the stores'
  * lengths on by one.  A barrier wait that runs out sets the device status word
  * (bgtq_device_status) and every later step of the object ends at its first barrier.
+ * Steps of one decoder share its barrier words and scratch: issue them in order on one
+ * stream, and destroy the decoder only after its last step has finished on the GPU.
  * Errors: BGTQ_EINVAL, BGTQ_EBUSY (lengths), BGTQ_ECAPACITY, BGTQ_ECUDA. */
 bgtq_status bgtq_decoder_step(bgtq_decoder *dec, const int64_t *tokens, float *h, float *logits, void *stream);
 /* Phase timing: on != 0 makes later steps record CTA 0's global-timer stamps (ns) at the

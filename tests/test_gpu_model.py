@@ -283,3 +283,37 @@ def test_persistent_step_matches_launch_path(cuda, name, batch):
     assert device_status(0) == 0
     step.destroy()
     ref.destroy()
+
+
+def test_persistent_step_rejects_bad_requests(cuda):
+    """bgtq_decoder_create refuses geometries the step kernel does not serve (head dim other
+    than 64, more than 4 sequences), and bgtq_decoder_step refuses stores whose lengths
+    differ between layers; a refused step changes no length."""
+    import ctypes as C
+    import torch
+    from bgtq import _lib
+    g = GEOMS["smollm2-like"]
+    dec = Decoder(random_weights(g, seed=2, device=cuda), g, 64, _tables(g), batch=1)
+    handle = dec._step_handle()
+    assert handle is not None
+    base = C.c_void_p()
+    desc = _lib.DecoderDesc(g.layers, 1, g.hidden, g.q_heads, g.kv_heads, 32, g.intermediate, g.vocab, g.rms_eps,
+                            dec.inv_freq.ctypes.data, None, None, None, None, None, None, None, None, None, None, None,
+                            0)
+    with pytest.raises(_lib.RangeError):
+        _lib.call("bgtq_decoder_create", C.byref(desc), C.byref(base))
+    desc.head_dim, desc.batch = 64, 5
+    with pytest.raises(_lib.RangeError):
+        _lib.call("bgtq_decoder_create", C.byref(desc), C.byref(base))
+    # layer 1's stores one row ahead of layer 0's: the step refuses before launching
+    k = torch.zeros((1, 64), dtype=torch.float16, device=cuda)
+    for ks, vs in zip(dec.keys[1:], dec.values[1:]):
+        for kk, vv in zip(ks, vs):
+            kk.append(k)
+            vv.append(k)
+    t = torch.zeros((1, 1), dtype=torch.int64, device=cuda)
+    with pytest.raises(_lib.StateError):
+        dec.forward(t, _check=False)
+    assert dec.keys[0][0].lengths(0) == 0 and dec.keys[1][0].lengths(0) == 1
+    assert device_status(0) == 0
+    dec.destroy()
