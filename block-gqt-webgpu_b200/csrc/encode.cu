@@ -522,8 +522,20 @@ __global__ void __launch_bounds__(kTileThreads, 2) encode_tile_kernel(const __gr
             const float n = sqrtf(acc + 1e-30f);
             nrm[g * KT + k] = n;
             const float dv = n > 1e-10f ? n : 1.0f;
+            if (!isinf(dv)) {
+                // the IEEE quotient from one reciprocal per group (Markstein, IBM J. Res. Dev.
+                // 34(1), 1990): with y = RN(1/dv) and q0 = RN(x y) within an ulp of x / dv,
+                // the residual x - dv q0 is exact in one FMA and RN(q0 + r y) = RN(x / dv)
+                // (no overflow or underflow here: |x| <= dv and x is FP16)
+                const float y = __frcp_rn(dv);
 #pragma unroll 4
-            for (uint32_t i = lo; i < hi; ++i) X[i * KT + k] = X[i * KT + k] / dv;
+                for (uint32_t i = lo; i < hi; ++i) {
+                    const float x = X[i * KT + k], q0 = __fmul_rn(x, y);
+                    X[i * KT + k] = __fmaf_rn(__fmaf_rn(-dv, q0, x), y, q0);
+                }
+            } else {
+                for (uint32_t i = lo; i < hi; ++i) X[i * KT + k] = X[i * KT + k] / dv;
+            }
         }
         __syncthreads();
         // ---- 3. rotation + codes: warp = 2 or 4 output dims of a group, lane = 4 keys ----
