@@ -511,8 +511,7 @@ template <int D, int QM, KKind KK, bool VF32, class LP>
 __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uint32_t d, uint32_t hd, uint32_t s,
                                           uint32_t t_lo, uint32_t t_hi, uint32_t slot, uint32_t nslots,
                                           uint32_t &phase, uint32_t &staged_hd, const float *qt_src = nullptr,
-                                          bool defer_merge = false, const uint32_t *wait_flags = nullptr,
-                                          uint32_t wait_value = 0) {
+                                          bool defer_merge = false) {
     constexpr int TPL = Geo<D>::TPL, TT = Geo<D>::TT, QP = QPad<QM>::QP;
     constexpr bool MMA = UseMma<D, VF32>::value;
     constexpr int VSZ = VF32 ? 4 : 2, VEC = 16 / VSZ, LPT = D / VEC, TPS = 32 / LPT;
@@ -545,28 +544,6 @@ __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uin
             for (uint32_t i = tid; i < (uint32_t)(D * QP / 4); i += kThreads) dst[i] = qt_src ? src[i] : __ldg(src + i);
         }
     };
-    // wait_flags (a persistent caller whose range holds a row other CTAs are still storing):
-    // the query tables first, then a bounded wait until wait_flags[hd] and wait_flags[0] (the
-    // stores of this head and of the head whose lengths are read) hold wait_value, then the
-    // lengths, the range and the tile copies
-    if (wait_flags) {
-        query_tables();
-        if (tid < 2) {
-            const uint32_t *f = wait_flags + (tid == 0 ? hd : 0u);
-            uint32_t it = 0, v = 0;
-            for (;;) {
-                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-                if (v == wait_value) break;
-                if (++it > (1u << 22)) {
-                    atomicOr(a.status, kStatusWaitTimeout);
-                    break;
-                }
-                if (it > 64u) __nanosleep(32);
-            }
-        }
-        __syncthreads();
-        asm volatile("fence.proxy.async.global;" ::: "memory");  // stored by generic stores, read by bulk copies
-    }
     const uint32_t seq = a.seq_first + s;
     const uint32_t len = __ldcg(a.lengths + seq);  // L2: a persistent caller's lengths change between phases
     const uint32_t R = a.rows;
@@ -645,8 +622,8 @@ __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uin
         issue_v(w);
     }
 
-    // ---- prologue: query tables (unless built before a wait) ----
-    if (!wait_flags) query_tables();
+    // ---- prologue: query tables ----
+    query_tables();
     __syncthreads();
 
     // ---- per-warp flash-decoding over this range ----

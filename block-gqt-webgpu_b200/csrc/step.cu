@@ -7,16 +7,18 @@
 //   1. RMSNorm + Q/K/V projection (+ bias)            GEMV over the residual stream h
 //   2. K/V append: split-half RoPE on K at the token's row, Block-GTQ encode into the packed
 //      store (bit for bit the append kernels' arithmetic: this file is compiled with
-//      -fmad=false like encode.cu), V to the FP16 store, lengths moved on; meanwhile other
-//      CTAs rotate each (sequence, KV head)'s queries into the code domain (RoPE at the new
-//      row, block rotation: the query rotation kernel's arithmetic) and every CTA stages
-//      the codebooks of its first attention task
-//   3. attention: tasks of (KV head, sequence, key range); each runs the decode-attention
-//      body over its range and leaves a partial; the last task of a pair merges (the
-//      split-KV merge of the attention kernel)
-//   4. o_proj + residual add into h
-//   5. RMSNorm + gate/up + SiLU gating
-//   6. down_proj + residual add into h
+//      -fmad=false like encode.cu), V to the FP16 store, lengths moved on; the appending
+//      warp then scores its new key against the pair's query rows itself (the key
+//      reconstructed from its codes and scales) and leaves the new row's partial.  In the
+//      same phase the other CTAs rotate each (sequence, KV head)'s queries into the code
+//      domain (RoPE at the new row, block rotation: the query rotation kernel's arithmetic)
+//      and run the attention tasks: (KV head, sequence, range of the keys stored before this
+//      step), each the decode-attention body over its range leaving a partial.  No task
+//      reads a row this phase writes, so none waits for the append.
+//   3. every CTA merges the pairs' partials (the attention kernel's split-KV merge), then
+//      o_proj + residual add into h
+//   4. RMSNorm + gate/up + SiLU gating
+//   5. down_proj + residual add into h
 // then the final RMSNorm + lm_head.  The stand-alone path runs the same work as seven
 // launches per layer; a decode step of a small model is a chain of microsecond kernels, and
 // here each kernel boundary becomes a grid barrier (one atomic per CTA and a poll of one L2
@@ -86,8 +88,6 @@ struct Args {
     uint32_t *status;
     uint32_t len_new[kMaxRows];  // per sequence: its length once this step's token is appended
     unsigned long long *trace;   // optional: global-timer stamps of CTA 0 at each phase end
-    uint32_t *flags;             // [layers][B][kv_heads]: step_id once the pair's new K/V row is stored
-    uint32_t step_id;            // this launch's number (from 1; the flags only ever hold past ones)
 };
 
 // CTA 0's global-timer stamp k (the phase breakdown of bgtq_decoder_trace).
@@ -107,9 +107,6 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t *p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
-}
-__device__ __forceinline__ void st_release(uint32_t *p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 // An mbarrier's shared memory is repurposed (the phases share regions) or initialised again
 // (once per layer) only after it is invalidated.
@@ -455,6 +452,64 @@ __device__ void append_one(const Args &A, const KvRopeArgs &a, const EncodeHead 
     fence_proxy_global();  // the rows are read next by bulk copies (async proxy)
 }
 
+// The attention partial of the row append_one just stored (sequence b, KV head hd, row pos),
+// written by the same warp into partial slot `slot`: the key reconstructed from the warp's
+// codebook values and FP16 scales (src/reference/production_math.py:27-31: per group
+// s_g R^T c, in the permuted order), each of the pair's query rows RoPE'd at pos, their dot
+// product in log2 units (the query records' log2(e) / sqrt(d)); then, as the attention body
+// leaves a range of one key: maximum = the logit, sum = 2^kPShift, output = 2^kPShift * V.
+// kr (the warp's RoPE scratch) holds the reconstructed key.
+template <bool kStaged>
+__device__ void new_row_partial(const Args &A, const KvRopeArgs &kv, const AttnArgs &a, const EncodeHead &h,
+                                uint32_t hd, uint32_t b, uint32_t pos, uint32_t slot, const WarpKey &wk, float *kr,
+                                int lane) {
+    const uint32_t d = A.d, pairs = d / 2, R = a.rows;
+    for (uint32_t i = lane; i < d; i += 32) {
+        const uint32_t g = h.t.group_of[i], lo = h.group_off[g], hi = h.group_off[g + 1];
+        float x = 0.0f;
+#pragma unroll 8
+        for (uint32_t j = lo; j < hi; ++j) x = fmaf(table_load<kStaged>(h.t.rot + (uint64_t)j * d + i), wk.cv[j], x);
+        kr[i] = __fmul_rn(x, __half2float(__ushort_as_half(wk.srow[g])));
+    }
+    __syncwarp();
+    // this lane's two permuted dims: their query elements' RoPE angle, the same for every row
+    const float *qg = A.qkv + (uint64_t)b * A.qkv_row + (uint64_t)hd * R * d;
+    float c[2], sn[2], kv_i[2];
+    uint32_t pj[2];
+    bool first[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const uint32_t i = lane + 32u * u;
+        const bool live = i < d;
+        const uint32_t j = live ? h.t.perm[i] : 0u;
+        pj[u] = j < pairs ? j : j - pairs;
+        first[u] = j < pairs;
+        const float ang = a.rope ? __fmul_rn((float)pos, a.rope[pj[u]]) : 0.0f;
+        c[u] = a.rope ? cosf(ang) : 1.0f;
+        sn[u] = a.rope ? sinf(ang) : 0.0f;
+        kv_i[u] = live ? kr[i] : 0.0f;
+    }
+    const float qscale = attn::kLog2e / sqrtf((float)d), one = (float)(1u << (int)attn::kPShift);
+    const float *vs = static_cast<const float *>(kv.v_src) + (uint64_t)b * kv.seq_stride + (uint64_t)hd * d;
+    for (uint32_t r = 0; r < R; ++r) {
+        float dot = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const float x = ldcg(qg + r * d + pj[u]), y = ldcg(qg + r * d + pj[u] + pairs);
+            const float q = first[u] ? __fsub_rn(__fmul_rn(x, c[u]), __fmul_rn(y, sn[u]))
+                                     : __fadd_rn(__fmul_rn(y, c[u]), __fmul_rn(x, sn[u]));
+            dot = fmaf(q, kv_i[u], dot);
+        }
+        const float lg = __fmul_rn(warp_sum(dot), qscale);
+        float *pp = a.part + ((((uint64_t)slot * a.seq_count + b) * a.heads + hd) * R + r) * (uint64_t)(d + 2);
+        for (uint32_t e = lane; e < d; e += 32) pp[e] = __fmul_rn(one, __half2float(__float2half_rn(ldcg(vs + e))));
+        if (lane == 0) {
+            pp[d] = lg;
+            pp[d + 1] = one;
+        }
+    }
+}
+
 // Query records of (sequence s, KV head hd) into shared memory qt [D][QP] (qrot_kernel's
 // arithmetic): the gqa query rows of the head, split-half RoPE at row pos, permuted and
 // rotated into the code domain, scaled to log2 units; zero past the rows.  rot: the head's
@@ -489,16 +544,17 @@ __device__ void query_records(const Args &A, const AttnArgs &a, uint32_t hd, uin
     __syncthreads();
 }
 
-// Attention tasks: nt key ranges of task_tokens per pair, pairs in head-major order; task t
+// Attention tasks: nt ranges of task_tokens per pair over the keys stored before this step
+// (partial slots 0 .. nt-1; slot nt is the new row's), pairs in head-major order; task t
 // runs on CTA (t + n_app) mod grid, so the K/V append CTAs take tasks last.
 struct Tasks {
     uint32_t nt, total, first;  // ranges per pair, tasks, this CTA's first task (>= total: none)
 };
 __device__ __forceinline__ Tasks tasks(const Args &A, uint32_t n_app) {
-    uint32_t lmax = 1;
+    uint32_t lmax = 2;
     for (uint32_t b = 0; b < A.batch; ++b) lmax = max(lmax, A.len_new[b]);
     Tasks t;
-    t.nt = (lmax + A.task_tokens - 1) / A.task_tokens;
+    t.nt = (lmax - 1u + A.task_tokens - 1) / A.task_tokens;
     t.total = A.kv_heads * A.batch * t.nt;
     t.first = (blockIdx.x + gridDim.x - n_app % gridDim.x) % gridDim.x;
     return t;
@@ -509,7 +565,7 @@ __device__ __forceinline__ Tasks tasks(const Args &A, uint32_t n_app) {
 // rotation.  staged_hd: the head whose codebooks the CTA staged already.
 template <int QM>
 __device__ void attention_phase(const Args &A, const AttnArgs &a, const Tasks &tk, float *qraw_s, float *qt_s,
-                                bool qt_ready, uint32_t staged_hd, const uint32_t *flags) {
+                                bool qt_ready, uint32_t staged_hd) {
     extern __shared__ __align__(128) unsigned char smem[];
     const uint32_t B = A.batch, T = A.task_tokens, tid = threadIdx.x;
     if (tk.first >= tk.total) return;
@@ -525,14 +581,12 @@ __device__ void attention_phase(const Args &A, const AttnArgs &a, const Tasks &t
             query_records<QM>(A, a, hd, s, A.len_new[s] - 1u, a.head[hd].rot, qraw_s, qt_s);
             q_pair = p;
         }
-        // a range holding the row this step appends waits (bounded, inside the body, after its
-        // query tables) for the sequence's appends: this head's row, and head 0's, whose
-        // lengths the body reads
-        const uint32_t last = A.len_new[s] - 1u;
-        const bool holds_new = i * T <= last && last < (i + 1) * T;
+        // the range ends before the row this step appends (the body bounds it by the stored
+        // length too, which the append may or may not have moved on yet: either way the end
+        // is the same)
         attn::attn_pair<D, QM, KKind::Packed, false, attn::RuntimeGroups>(
-            a, A.pl, A.d, hd, s, i * T, (i + 1) * T, i, tk.nt, phase, staged_hd, qt_s, true,
-            holds_new ? flags + s * A.kv_heads : nullptr, A.step_id);
+            a, A.pl, A.d, hd, s, i * T, min((i + 1) * T, A.len_new[s] - 1u), i, tk.nt + 1, phase, staged_hd, qt_s,
+            true);
     }
     // every copy has landed (each pair ends with its waits and a CTA barrier): the region
     // goes back to the GEMV phases
@@ -627,11 +681,14 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             const uint32_t b = (blockIdx.x / H) * kWarps + warp;
             if (b < B) {
                 const uint32_t pos = A.len_new[b] - 1u;
-                if (staged) append_one<true>(A, kv, hs, app_hd, b, pos, wks[warp], kr[warp], lane);
-                else append_one<false>(A, kv, kv.head[app_hd], app_hd, b, pos, wks[warp], kr[warp], lane);
-                __syncwarp();
-                // the rows and lengths the warp stored are published with the pair's flag
-                if (lane == 0) st_release(A.flags + (l * B + b) * H + app_hd, A.step_id);
+                if (staged) {
+                    append_one<true>(A, kv, hs, app_hd, b, pos, wks[warp], kr[warp], lane);
+                    new_row_partial<true>(A, kv, att, hs, app_hd, b, pos, tk.nt, wks[warp], kr[warp], lane);
+                } else {
+                    append_one<false>(A, kv, kv.head[app_hd], app_hd, b, pos, wks[warp], kr[warp], lane);
+                    new_row_partial<false>(A, kv, att, kv.head[app_hd], app_hd, b, pos, tk.nt, wks[warp], kr[warp],
+                                           lane);
+                }
             }
             if (staging) {
                 staged_tables_drain(&stage_bar, staged);
@@ -649,20 +706,21 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             qt_ready = true;
         }
         if (has_task) attn::stage_lookup(att.head[first_hd], A.pl, reinterpret_cast<float *>(smem + A.pl.cent), tid);
-        // ---- attention, in the same phase: a task whose key range holds the new row waits
-        //      for its pair's append (a flag); the others read rows no append touches.  The
-        //      next layer's Q/K/V weights are requested into L2 meanwhile ----
+        // ---- attention over the keys stored before this step, in the same phase (no range
+        //      reads a row the appends write).  The next layer's Q/K/V weights are requested
+        //      into L2 meanwhile ----
         if (l + 1 < A.n_layers) prefetch_l2(A.layers[l + 1].w_qkv, qkv_bytes);
         else prefetch_l2(A.lm_head, (uint64_t)A.vocab * A.hidden * 2u);
-        attention_phase<QM>(A, att, tk, qraw_s, qt_s, qt_ready, first_hd, A.flags + l * B * H);
+        attention_phase<QM>(A, att, tk, qraw_s, qt_s, qt_ready, first_hd);
         Pass<1, 1, kChunks> po;
         po.preload(L.w_o, A.q_heads * d, A.hidden);
         if (!grid_barrier(A.bar, A.bar_base + (unsigned long long)(++nb) * gridDim.x, A.status)) return;
         stamp(A, 2 + 5 * l);
         // ---- 4. o_proj + residual ----
-        const Merge mg{&att, tk.nt, A.off_part ? reinterpret_cast<float *>(smem + A.off_part) : nullptr, &mrg_bar};
+        const Merge mg{&att, tk.nt + 1, A.off_part ? reinterpret_cast<float *>(smem + A.off_part) : nullptr,
+                       &mrg_bar};
         gemv<1, BT, 1, kChunks>(A, A.att, A.q_heads * d, nullptr, A.q_heads * d, nullptr, L.w_o, nullptr, A.hidden,
-                                A.h, A.hidden, xs, po, tk.nt > 1 ? &mg : nullptr);
+                                A.h, A.hidden, xs, po, &mg);
         Pass<2, 2, kChunks> pg;
         pg.preload(L.w_gu, A.hidden, A.inter);
         if (!grid_barrier(A.bar, A.bar_base + (unsigned long long)(++nb) * gridDim.x, A.status)) return;
@@ -702,8 +760,7 @@ struct bgtq_decoder {
     const void *kernel = nullptr;
     uint32_t ctas = 0, smem = 0, qkv_row = 0, gqa = 0;
     bgtq::step::Args args{};      // everything but the per-step fields
-    bgtq::DevBuf layers, scratch, bar, rope, trace, flags;
-    uint32_t step_count = 0;  // launches so far: the next step's id is step_count + 1 (never 0)
+    bgtq::DevBuf layers, scratch, bar, rope, trace;
     unsigned long long bar_epoch = 0;  // the device arrival counter after the last step
     bool tracing = false;
 };
@@ -783,12 +840,11 @@ bgtq_status bgtq_decoder_create(const bgtq_decoder_desc *dp, bgtq_decoder **out)
     // scratch: Q/K/V rows, attention output, gate/up activations; RoPE table; barrier words
     const size_t n_qkv = (size_t)B * qkv_row, n_att = (size_t)B * att_w, n_act = (size_t)B * d.intermediate;
     if (!ck(dec->scratch.ensure(4 * (n_qkv + n_att + n_act))) || !ck(dec->rope.ensure(4 * (hd_dim / 2))) ||
-        !ck(dec->bar.ensure(16)) || !ck(dec->layers.ensure(sizeof(Layer) * L)) ||
-        !ck(dec->flags.ensure(4u * L * B * d.kv_heads)))
+        !ck(dec->bar.ensure(16)) || !ck(dec->layers.ensure(sizeof(Layer) * L)))
         return bail(BGTQ_ECUDA, "decoder: device allocation");
     float *qkv = static_cast<float *>(dec->scratch.p), *attn_out = qkv + n_qkv, *act = attn_out + n_att;
     if (!ck(cudaMemcpy(dec->rope.p, d.inv_freq, 4 * (hd_dim / 2), cudaMemcpyHostToDevice)) ||
-        !ck(cudaMemset(dec->bar.p, 0, 16)) || !ck(cudaMemset(dec->flags.p, 0, 4u * L * B * d.kv_heads)))
+        !ck(cudaMemset(dec->bar.p, 0, 16)))
         return bail(BGTQ_ECUDA, "decoder: upload");
     // per-layer arguments
     std::vector<Layer> hl(L);
@@ -862,10 +918,12 @@ bgtq_status bgtq_decoder_create(const bgtq_decoder_desc *dp, bgtq_decoder **out)
     const uint32_t BT = B == 1 ? 1u : 4u;
     const uint32_t max_in = std::max(std::max(d.hidden, att_w), d.intermediate);
     // GEMV activations, and in the o_proj phase the split-merge weights after them
-    // attention tasks of whole CTA tiles, few enough per pair for the partial buffers
+    // attention tasks of whole CTA tiles, few enough per pair that their partials and the new
+    // row's fit the partial buffers
+    if (max_splits < 2) return bail(BGTQ_EINVAL, "decoder: the attention objects need room for two partials");
     const uint32_t chunk = attn::kWarps * TT, tiles = (cap + chunk - 1) / chunk;
-    const uint32_t task_tokens = chunk * ((tiles + max_splits - 1) / max_splits);
-    const uint32_t max_nt = (cap + task_tokens - 1) / task_tokens;
+    const uint32_t task_tokens = chunk * ((tiles + max_splits - 2) / (max_splits - 1));
+    const uint32_t max_nt = (cap + task_tokens - 1) / task_tokens + 1;  // partial slots per pair
     // region U: the attention plan, or the GEMV activations with (o_proj phase) the merge
     // weights and a copy of the partials after them
     const uint32_t off_part = attn::align128(4u * (BT * max_in + BT * d.q_heads * (2 * max_nt + 2)));
@@ -949,8 +1007,6 @@ bgtq_status bgtq_decoder_step(bgtq_decoder *dec, const int64_t *tokens, float *h
     A.logits = logits;
     A.trace = dec->tracing ? static_cast<unsigned long long *>(dec->trace.p) : nullptr;
     A.bar_base = dec->bar_epoch;
-    A.flags = static_cast<uint32_t *>(dec->flags.p);
-    A.step_id = dec->step_count + 1u == 0u ? 1u : dec->step_count + 1u;
     Guard g(dec->device);
     if (!g.ok) return dfail(BGTQ_ECUDA, "cannot select device");
     void *params[] = {&A};
@@ -958,7 +1014,6 @@ bgtq_status bgtq_decoder_step(bgtq_decoder *dec, const int64_t *tokens, float *h
                                                       dec->smem, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return dfail(BGTQ_ECUDA, std::string("decoder step launch: ") + cudaGetErrorString(e));
     dec->bar_epoch += (unsigned long long)step::kBarriersPerLayer * dec->desc.layers * dec->ctas;
-    dec->step_count = A.step_id;
     for (bgtq_attention *at : dec->att)
         for (uint32_t hh = 0; hh < H; ++hh)
             for (uint32_t s = 0; s < B; ++s) {
@@ -1000,7 +1055,6 @@ void bgtq_decoder_destroy(bgtq_decoder *dec) {
         dec->bar.release();
         dec->rope.release();
         dec->trace.release();
-        dec->flags.release();
     }
     delete dec;
 }
