@@ -268,8 +268,10 @@ __device__ __forceinline__ void load_q(const float *p, float (&q)[QP]) {
 // contribute exactly 0).
 template <int D, int QM, int QP>
 // qt_generic: qt may be shared memory (plain loads; __ldg is for global memory only).
+// lko_s: the head's lookup offsets in shared memory, or null (read from the table blob).
 __device__ __forceinline__ void build_tables(const AttnHead &h, const float *qt, unsigned char *rec, uint32_t d,
-                                             uint32_t cent_off, int tid, bool qt_generic = false) {
+                                             uint32_t cent_off, int tid, bool qt_generic = false,
+                                             const uint16_t *lko_s = nullptr) {
     auto qload = [&](const float *p) { return qt_generic ? *p : __ldg(p); };
     using G = RecGeo<D, QM>;
     uint32_t *recs = reinterpret_cast<uint32_t *>(rec);
@@ -294,8 +296,8 @@ __device__ __forceinline__ void build_tables(const AttnHead &h, const float *qt,
             rp[2 * r + 1] = __float_as_uint(live ? qload(qt + (j0 + 1) * QP + r) : 0.0f);
         }
         const uint32_t ja = min(j0, d - 1u), jb = min(j0 + 1, d - 1u);
-        rp[2 * QM] = cent_off + 4u * __ldg(h.lookup_off + ja);
-        rp[2 * QM + 1] = cent_off + 4u * __ldg(h.lookup_off + jb);
+        rp[2 * QM] = cent_off + 4u * (lko_s ? lko_s[ja] : __ldg(h.lookup_off + ja));
+        rp[2 * QM + 1] = cent_off + 4u * (lko_s ? lko_s[jb] : __ldg(h.lookup_off + jb));
         for (int x = 2 * QM + 2; x < G::RP; ++x) rp[x] = 0u;
     }
 }
@@ -507,11 +509,22 @@ __device__ __forceinline__ void stage_lookup(const AttnHead &h, const Plan &pl, 
     for (uint32_t i = 4u * n4 + tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < nl ? h.lookup[i] : 0.0f;
 }
 
-template <int D, int QM, KKind KK, bool VF32, class LP>
+// A caller's work between the first tile copies and the query tables (NoPrologue: none).
+struct NoPrologue {
+    __device__ __forceinline__ void operator()() const {}
+};
+
+// One (sequence s, KV head hd) key range [t_lo, t_hi) into partial slot `slot` of nslots.
+// A persistent caller may pass: len_known, the sequence's key length when it knows it (0:
+// read the device length), lko_s, the head's lookup offsets in shared memory, and pro, work
+// of its own that runs once this range's first tile copies are in flight and before the
+// query tables are built (its query records, say), ending with a CTA barrier.
+template <int D, int QM, KKind KK, bool VF32, class LP, class Pro = NoPrologue>
 __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uint32_t d, uint32_t hd, uint32_t s,
                                           uint32_t t_lo, uint32_t t_hi, uint32_t slot, uint32_t nslots,
                                           uint32_t &phase, uint32_t &staged_hd, const float *qt_src = nullptr,
-                                          bool defer_merge = false) {
+                                          bool defer_merge = false, uint32_t len_known = 0u,
+                                          const uint16_t *lko_s = nullptr, const Pro &pro = Pro{}) {
     constexpr int TPL = Geo<D>::TPL, TT = Geo<D>::TT, QP = QPad<QM>::QP;
     constexpr bool MMA = UseMma<D, VF32>::value;
     constexpr int VSZ = VF32 ? 4 : 2, VEC = 16 / VSZ, LPT = D / VEC, TPS = 32 / LPT;
@@ -527,17 +540,12 @@ __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uin
     const AttnHead &h = a.head[hd];
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
     extern __shared__ __align__(128) unsigned char smem[];
-    if (KK == KKind::Packed && hd != staged_hd) {  // a later pair of another head
-        __syncthreads();
-        stage_lookup(h, pl, reinterpret_cast<float *>(smem + pl.cent), tid);
-        staged_hd = hd;
-    }
     unsigned char *rec = smem + pl.qrec;
     // the pair's query records: the query rotation's output, or the caller's copy (qt_src)
     const float *qt = qt_src ? qt_src : a.qt + ((uint64_t)s * a.heads + hd) * (uint64_t)(D * QP);
     auto query_tables = [&]() {
         if constexpr (KK == KKind::Packed) {
-            build_tables<D, QM, QP>(h, qt, rec, d, pl.cent, tid, qt_src != nullptr);
+            build_tables<D, QM, QP>(h, qt, rec, d, pl.cent, tid, qt_src != nullptr, lko_s);
         } else {
             const float4 *src = reinterpret_cast<const float4 *>(qt);
             float4 *dst = reinterpret_cast<float4 *>(rec);
@@ -545,7 +553,8 @@ __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uin
         }
     };
     const uint32_t seq = a.seq_first + s;
-    const uint32_t len = __ldcg(a.lengths + seq);  // L2: a persistent caller's lengths change between phases
+    // L2: a persistent caller's lengths change between phases
+    const uint32_t len = len_known ? len_known : __ldcg(a.lengths + seq);
     const uint32_t R = a.rows;
 
     float *qrec_s = reinterpret_cast<float *>(rec);
@@ -621,6 +630,12 @@ __device__ __forceinline__ void attn_pair(const AttnArgs &a, const Plan &pl, uin
         issue_k(w, 0);
         issue_v(w);
     }
+    if (KK == KKind::Packed && hd != staged_hd) {  // a later pair of another head
+        __syncthreads();
+        stage_lookup(h, pl, reinterpret_cast<float *>(smem + pl.cent), tid);
+        staged_hd = hd;
+    }
+    pro();
 
     // ---- prologue: query tables ----
     query_tables();

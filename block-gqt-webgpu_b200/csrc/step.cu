@@ -155,9 +155,10 @@ __device__ __forceinline__ bool grid_barrier(uint32_t *bar, unsigned long long t
 }
 
 // Asks L2 for this CTA's share of `bytes` (a multiple of 16) at p (16-byte aligned): one bulk
-// prefetch per CTA, so a matrix the next phase streams is on chip when it starts.
-__device__ __forceinline__ void prefetch_l2(const void *p, uint64_t bytes) {
-    if (threadIdx.x != 0 || !p || !bytes) return;
+// prefetch per CTA (issued by thread `issuer`), so a matrix the next phase streams is on chip
+// when it starts.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint64_t bytes, uint32_t issuer = 0) {
+    if (threadIdx.x != issuer || !p || !bytes) return;
     const uint64_t per = ((bytes + gridDim.x - 1) / gridDim.x + 15u) & ~15ull;
     const uint64_t b0 = (uint64_t)blockIdx.x * per;
     if (b0 >= bytes) return;
@@ -412,37 +413,42 @@ __device__ __forceinline__ void gemv(const Args &A, const float *x, uint32_t x_s
 
 // K/V append of sequence b, KV head hd at row pos (kv_rope_append_kernel's arithmetic for
 // one token, FP32 sources): RoPE'd K rounded to FP16, encoded into the packed store; V to
-// the FP16 store; then the head's key and value lengths moved to pos + 1.  One warp.
+// the FP16 store; then the head's key and value lengths moved to pos + 1.  One warp; d = 64
+// (lane p holds dim pair p), cs: the row's RoPE angles.  vv returns the lane's V elements
+// (lane, lane + 32) as read from the source.
 template <bool kStaged>
 __device__ void append_one(const Args &A, const KvRopeArgs &a, const EncodeHead &h, uint32_t hd, uint32_t b,
-                           uint32_t pos, WarpKey &wk, float *kr, int lane) {
+                           uint32_t pos, const float2 *cs, WarpKey &wk, float *kr, int lane, float (&vv)[2]) {
     const uint32_t d = A.d, pairs = d / 2, seq = a.seq_first + b;
+    vv[0] = vv[1] = 0.0f;
     if (pos >= a.capacity) {  // the host checked the capacity: refuse, report
         if (lane == 0) atomicOr(A.status, kStatusBadLength);
         return;
     }
     const uint64_t at = (uint64_t)b * a.seq_stride + (uint64_t)hd * d;
     const float *ks = static_cast<const float *>(a.k_src), *vs = static_cast<const float *>(a.v_src);
-    for (uint32_t p = lane; p < pairs; p += 32) {
-        const float ang = __fmul_rn((float)pos, a.inv_freq[p]);
-        const float c = cosf(ang), sn = sinf(ang);
-        const float x = ldcg(ks + at + p), y = ldcg(ks + at + p + pairs);
-        kr[p] = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
-        kr[p + pairs] = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+    // the row's K pair and V elements of this lane in one round trip
+    const float x = ldcg(ks + at + lane), y = ldcg(ks + at + lane + pairs);
+    vv[0] = ldcg(vs + at + lane);
+    vv[1] = ldcg(vs + at + lane + 32u);
+    {
+        const float c = cs[lane].x, sn = cs[lane].y;
+        kr[lane] = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
+        kr[lane + pairs] = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
     }
     __syncwarp();
     for (uint32_t i = lane; i < d; i += 32) wk.xs[i] = __half2float(__float2half_rn(kr[h.t.perm[i]]));
     warp_encode<kStaged>(h, d, wk, seq, pos, lane);
     __half *vrow = reinterpret_cast<__half *>(a.v[hd]) + (uint64_t)seq * a.v_seq_stride[hd] + (uint64_t)pos * a.vD;
-#pragma unroll 4
-    for (uint32_t e = lane; e < a.vD; e += 32) {
-        const float x = e < d ? ldcg(vs + at + e) : 0.0f;
+#pragma unroll
+    for (uint32_t u = 0; u < 2; ++u) {
+        const uint32_t e = lane + 32u * u;
         uint32_t de = e;
         if (a.v_swizzle) {
             const uint32_t c = e >> 3;
             de = (((c & ~7u) | ((c ^ pos) & 7u)) << 3) | (e & 7u);
         }
-        vrow[de] = __float2half_rn(x);
+        vrow[de] = __float2half_rn(vv[u]);
     }
     __syncwarp();
     if (lane == 0) {
@@ -452,18 +458,37 @@ __device__ void append_one(const Args &A, const KvRopeArgs &a, const EncodeHead 
     fence_proxy_global();  // the rows are read next by bulk copies (async proxy)
 }
 
-// The attention partial of the row append_one just stored (sequence b, KV head hd, row pos),
-// written by the same warp into partial slot `slot`: the key reconstructed from the warp's
-// codebook values and FP16 scales (src/reference/production_math.py:27-31: per group
-// s_g R^T c, in the permuted order), each of the pair's query rows RoPE'd at pos, their dot
-// product in log2 units (the query records' log2(e) / sqrt(d)); then, as the attention body
-// leaves a range of one key: maximum = the logit, sum = 2^kPShift, output = 2^kPShift * V.
-// kr (the warp's RoPE scratch) holds the reconstructed key.
-template <bool kStaged>
-__device__ void new_row_partial(const Args &A, const KvRopeArgs &kv, const AttnArgs &a, const EncodeHead &h,
-                                uint32_t hd, uint32_t b, uint32_t pos, uint32_t slot, const WarpKey &wk, float *kr,
+// The attention partial of the row append_one just stored (sequence b, KV head hd), written
+// by the same warp into partial slot `slot`: the key reconstructed from the warp's codebook
+// values and FP16 scales (src/reference/production_math.py:27-31: per group s_g R^T c, in
+// the permuted order), each of the pair's query rows RoPE'd at the row (cs: its angles),
+// their dot product in log2 units (the query records' log2(e) / sqrt(d)); then, as the
+// attention body leaves a range of one key: maximum = the logit, sum = 2^kPShift, output =
+// 2^kPShift * V, V the FP16 row (vv: the lane's source elements).  kr (the warp's RoPE
+// scratch) holds the reconstructed key.  The query elements of every row are loaded in one
+// batch.  d = 64; QM bounds the rows.
+template <bool kStaged, int QM>
+__device__ void new_row_partial(const Args &A, const AttnArgs &a, const EncodeHead &h, uint32_t hd, uint32_t b,
+                                uint32_t slot, const float2 *cs, const float (&vv)[2], const WarpKey &wk, float *kr,
                                 int lane) {
     const uint32_t d = A.d, pairs = d / 2, R = a.rows;
+    const float *qg = A.qkv + (uint64_t)b * A.qkv_row + (uint64_t)hd * R * d;
+    uint32_t pj[2];
+    bool first[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const uint32_t j = h.t.perm[lane + 32u * u];
+        pj[u] = j < pairs ? j : j - pairs;
+        first[u] = j < pairs;
+    }
+    float qx[QM][2], qy[QM][2];
+#pragma unroll
+    for (uint32_t r = 0; r < (uint32_t)QM; ++r)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            qx[r][u] = r < R ? ldcg(qg + r * d + pj[u]) : 0.0f;
+            qy[r][u] = r < R ? ldcg(qg + r * d + pj[u] + pairs) : 0.0f;
+        }
     for (uint32_t i = lane; i < d; i += 32) {
         const uint32_t g = h.t.group_of[i], lo = h.group_off[g], hi = h.group_off[g + 1];
         float x = 0.0f;
@@ -472,37 +497,31 @@ __device__ void new_row_partial(const Args &A, const KvRopeArgs &kv, const AttnA
         kr[i] = __fmul_rn(x, __half2float(__ushort_as_half(wk.srow[g])));
     }
     __syncwarp();
-    // this lane's two permuted dims: their query elements' RoPE angle, the same for every row
-    const float *qg = A.qkv + (uint64_t)b * A.qkv_row + (uint64_t)hd * R * d;
-    float c[2], sn[2], kv_i[2];
-    uint32_t pj[2];
-    bool first[2];
+    float kv_i[2];
+    float2 cu[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-        const uint32_t i = lane + 32u * u;
-        const bool live = i < d;
-        const uint32_t j = live ? h.t.perm[i] : 0u;
-        pj[u] = j < pairs ? j : j - pairs;
-        first[u] = j < pairs;
-        const float ang = a.rope ? __fmul_rn((float)pos, a.rope[pj[u]]) : 0.0f;
-        c[u] = a.rope ? cosf(ang) : 1.0f;
-        sn[u] = a.rope ? sinf(ang) : 0.0f;
-        kv_i[u] = live ? kr[i] : 0.0f;
+        kv_i[u] = kr[lane + 32u * u];
+        cu[u] = cs[pj[u]];
     }
     const float qscale = attn::kLog2e / sqrtf((float)d), one = (float)(1u << (int)attn::kPShift);
-    const float *vs = static_cast<const float *>(kv.v_src) + (uint64_t)b * kv.seq_stride + (uint64_t)hd * d;
-    for (uint32_t r = 0; r < R; ++r) {
+    const float o0 = __fmul_rn(one, __half2float(__float2half_rn(vv[0])));
+    const float o1 = __fmul_rn(one, __half2float(__float2half_rn(vv[1])));
+#pragma unroll
+    for (uint32_t r = 0; r < (uint32_t)QM; ++r) {
+        if (r >= R) break;
         float dot = 0.0f;
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-            const float x = ldcg(qg + r * d + pj[u]), y = ldcg(qg + r * d + pj[u] + pairs);
-            const float q = first[u] ? __fsub_rn(__fmul_rn(x, c[u]), __fmul_rn(y, sn[u]))
-                                     : __fadd_rn(__fmul_rn(y, c[u]), __fmul_rn(x, sn[u]));
+            const float x = qx[r][u], y = qy[r][u], c = cu[u].x, sn = cu[u].y;
+            const float q = first[u] ? __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn))
+                                     : __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
             dot = fmaf(q, kv_i[u], dot);
         }
         const float lg = __fmul_rn(warp_sum(dot), qscale);
         float *pp = a.part + ((((uint64_t)slot * a.seq_count + b) * a.heads + hd) * R + r) * (uint64_t)(d + 2);
-        for (uint32_t e = lane; e < d; e += 32) pp[e] = __fmul_rn(one, __half2float(__float2half_rn(ldcg(vs + e))));
+        pp[lane] = o0;
+        pp[lane + 32] = o1;
         if (lane == 0) {
             pp[d] = lg;
             pp[d + 1] = one;
@@ -510,31 +529,57 @@ __device__ void new_row_partial(const Args &A, const KvRopeArgs &kv, const AttnA
     }
 }
 
+// Split-half RoPE of element j of a raw row q (d = 2 * pairs) with the angle's cosine and
+// sine cs[j mod pairs]: attn::rope_elem's arithmetic, the angle computed once per launch.
+__device__ __forceinline__ float rope_cs(const float *q, uint32_t j, uint32_t pairs, const float2 *cs) {
+    const uint32_t p = j < pairs ? j : j - pairs;
+    const float c = cs[p].x, sn = cs[p].y, x = q[p], y = q[p + pairs];
+    return j < pairs ? __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn)) : __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
+}
+
 // Query records of (sequence s, KV head hd) into shared memory qt [D][QP] (qrot_kernel's
-// arithmetic): the gqa query rows of the head, split-half RoPE at row pos, permuted and
-// rotated into the code domain, scaled to log2 units; zero past the rows.  rot: the head's
-// rotation (shared memory when staged, else the table in global memory).  One CTA; qraw
-// (kMaxRows * D floats) is its scratch.  Ends with a CTA barrier.
+// arithmetic): the gqa query rows of the head, split-half RoPE at the sequence's new row
+// (cs: that row's angles), permuted and rotated into the code domain, scaled to log2 units;
+// zero past the rows.  rot, perm, grp: the head's rotation, permutation and group of each
+// dim (shared-memory copies, or the tables in global memory); the permutation and group
+// entries a thread needs are fetched together with the query rows, so the chain holds one
+// round trip.  One CTA; qraw (kMaxRows * D floats) is its scratch.  Ends with a CTA barrier.
 template <int QM>
-__device__ void query_records(const Args &A, const AttnArgs &a, uint32_t hd, uint32_t s, uint32_t pos,
-                              const float *rot, float *qraw, float *qt) {
+__device__ void query_records(const Args &A, const AttnArgs &a, uint32_t hd, uint32_t s, const float2 *cs,
+                              const float *rot, const uint8_t *perm, const uint8_t *grp, float *qraw, float *qt) {
     constexpr uint32_t QP = attn::QPad<QM>::QP;
+    constexpr uint32_t kE2 = (kMaxRows * D + kThreads - 1) / kThreads, kE3 = (D * QP + kThreads - 1) / kThreads;
     const AttnHead &h = a.head[hd];
     const uint32_t R = a.rows, d = A.d, tid = threadIdx.x;
     const float *qg = A.qkv + (uint64_t)s * A.qkv_row + (uint64_t)hd * R * d;
+    uint32_t pm[kE2], gq[kE3];
+#pragma unroll
+    for (uint32_t u = 0; u < kE2; ++u) {
+        const uint32_t idx = tid + u * kThreads;
+        pm[u] = idx < R * d ? perm[idx % d] : 0u;
+    }
+#pragma unroll
+    for (uint32_t u = 0; u < kE3; ++u) {
+        const uint32_t j = (tid + u * kThreads) / QP;
+        gq[u] = j < d ? grp[j] : 0u;
+    }
     for (uint32_t idx = tid; idx < R * d; idx += kThreads) qt[idx] = ldcg(qg + idx);  // raw rows, then RoPE
     __syncthreads();
-    for (uint32_t idx = tid; idx < R * d; idx += kThreads) {
-        const uint32_t r = idx / d, i = idx % d;
-        qraw[idx] = attn::rope_elem(qt + r * d, h.perm[i], d, pos, a.rope);
+#pragma unroll
+    for (uint32_t u = 0; u < kE2; ++u) {
+        const uint32_t idx = tid + u * kThreads;
+        if (idx < R * d) qraw[idx] = rope_cs(qt + (idx / d) * d, pm[u], d / 2, cs);
     }
     __syncthreads();
     const float qscale = attn::kLog2e / sqrtf((float)d);
-    for (uint32_t idx = tid; idx < D * QP; idx += kThreads) {
+#pragma unroll
+    for (uint32_t u = 0; u < kE3; ++u) {
+        const uint32_t idx = tid + u * kThreads;
+        if (idx >= D * QP) break;
         const uint32_t j = idx / QP, r = idx % QP;
         float v = 0.0f;
         if (r < R && j < d) {
-            const uint32_t g = h.group_of[j], lo = h.group_off[g], hi = h.group_off[g + 1];
+            const uint32_t g = gq[u], lo = h.group_off[g], hi = h.group_off[g + 1];
             const float *rj = rot + (uint64_t)j * d;
             for (uint32_t i = lo; i < hi; ++i) v = fmaf(rj[i], qraw[r * d + i], v);
             v *= qscale;
@@ -542,6 +587,41 @@ __device__ void query_records(const Args &A, const AttnArgs &a, uint32_t hd, uin
         qt[idx] = v;
     }
     __syncthreads();
+}
+
+// The head's codebooks in the decode-attention lookup layout (attn::stage_lookup's copy), in
+// two halves around other work: fetch issues the leading kLookupRegs float4 per thread into
+// registers, store writes them (and the rest, fetched then) into shared memory.
+constexpr uint32_t kLookupRegs = 6;
+struct LookupFetch {
+    float4 v[kLookupRegs];
+};
+__device__ __forceinline__ void lookup_fetch(const AttnHead &h, const attn::Plan &pl, LookupFetch &f, int tid) {
+    const uint32_t n4 = pl.cent_alloc / 4u, nl = h.n_lookup;
+    const float4 *src = reinterpret_cast<const float4 *>(h.lookup);
+#pragma unroll
+    for (uint32_t u = 0; u < kLookupRegs; ++u) {
+        const uint32_t q = tid + u * kThreads;
+        f.v[u] = q < n4 && 4u * q + 3u < nl ? __ldg(src + q) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+}
+__device__ __forceinline__ float4 lookup_tail(const AttnHead &h, uint32_t q, uint32_t nl) {
+    return make_float4(4u * q < nl ? h.lookup[4u * q] : 0.0f, 4u * q + 1u < nl ? h.lookup[4u * q + 1u] : 0.0f,
+                       4u * q + 2u < nl ? h.lookup[4u * q + 2u] : 0.0f, 0.0f);
+}
+__device__ __forceinline__ void lookup_store(const AttnHead &h, const attn::Plan &pl, const LookupFetch &f,
+                                             float *cent_s, int tid) {
+    const uint32_t n4 = pl.cent_alloc / 4u, nl = h.n_lookup;
+    const float4 *src = reinterpret_cast<const float4 *>(h.lookup);
+    float4 *dst = reinterpret_cast<float4 *>(cent_s);
+#pragma unroll
+    for (uint32_t u = 0; u < kLookupRegs; ++u) {
+        const uint32_t q = tid + u * kThreads;
+        if (q < n4) dst[q] = 4u * q + 3u < nl ? f.v[u] : lookup_tail(h, q, nl);
+    }
+    for (uint32_t q = tid + kLookupRegs * kThreads; q < n4; q += kThreads)
+        dst[q] = 4u * q + 3u < nl ? __ldg(src + q) : lookup_tail(h, q, nl);
+    for (uint32_t i = 4u * n4 + tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < nl ? h.lookup[i] : 0.0f;
 }
 
 // Attention tasks: nt ranges of task_tokens per pair over the keys stored before this step
@@ -560,33 +640,51 @@ __device__ __forceinline__ Tasks tasks(const Args &A, uint32_t n_app) {
     return t;
 }
 
-// The attention phase of one layer.  The CTA's first pair has its query records in qt_s
-// already when qt_ready; later pairs (more tasks than CTAs) compute theirs from the global
-// rotation.  staged_hd: the head whose codebooks the CTA staged already.
+// Shared-memory copies of the head tables of a CTA's first attention pair, made during the
+// Q/K/V phase: rotation [d][d], permutation, group of each dim, lookup offsets (rot null:
+// none, every pair reads the tables in global memory).
+struct HeadCopy {
+    const float *rot;
+    const uint8_t *perm, *grp;
+    const uint16_t *lko;
+    uint32_t hd;
+};
+
+// The attention phase of one layer: the CTA's tasks, each attn::attn_pair over its range.  A
+// task that starts a pair builds the pair's query records (and stages a new head's
+// codebooks) as the body's prologue, after the range's first tile copies are issued, so the
+// copies land meanwhile.  cs: the new rows' RoPE angles, [batch][d / 2].
 template <int QM>
-__device__ void attention_phase(const Args &A, const AttnArgs &a, const Tasks &tk, float *qraw_s, float *qt_s,
-                                bool qt_ready, uint32_t staged_hd) {
+__device__ void attention_phase(const Args &A, const AttnArgs &a, const Tasks &tk, const float2 *cs, float *qraw_s,
+                                float *qt_s, const HeadCopy &hc) {
     extern __shared__ __align__(128) unsigned char smem[];
     const uint32_t B = A.batch, T = A.task_tokens, tid = threadIdx.x;
     if (tk.first >= tk.total) return;
-    fence_proxy_global();  // K/V rows written by other CTAs' generic stores, read by bulk copies
     // the body's mbarriers (their shared memory held GEMV activations in between)
     if (tid < kWarps * 4) attn::mbar_init(attn::smem_u32(smem + A.pl.bars) + tid * 8u, 1u);
     attn::fence_barrier_init();
     __syncthreads();
-    uint32_t phase = 0, q_pair = qt_ready ? tk.first / tk.nt : ~0u;
+    float *cent_s = reinterpret_cast<float *>(smem + A.pl.cent);
+    uint32_t phase = 0, q_pair = ~0u, staged_hd = ~0u;
     for (uint32_t t = tk.first; t < tk.total; t += gridDim.x) {
         const uint32_t p = t / tk.nt, i = t % tk.nt, hd = p / B, s = p % B;
-        if (p != q_pair) {
-            query_records<QM>(A, a, hd, s, A.len_new[s] - 1u, a.head[hd].rot, qraw_s, qt_s);
-            q_pair = p;
-        }
-        // the range ends before the row this step appends (the body bounds it by the stored
-        // length too, which the append may or may not have moved on yet: either way the end
-        // is the same)
+        const AttnHead &h = a.head[hd];
+        const bool fresh = p != q_pair, restage = hd != staged_hd, own = hc.rot && hd == hc.hd;
+        auto prologue = [&]() {
+            if (!fresh) return;
+            LookupFetch lf;
+            if (restage) lookup_fetch(h, A.pl, lf, (int)tid);
+            query_records<QM>(A, a, hd, s, cs + s * (D / 2), own ? hc.rot : h.rot, own ? hc.perm : h.perm,
+                              own ? hc.grp : h.group_of, qraw_s, qt_s);
+            if (restage) lookup_store(h, A.pl, lf, cent_s, (int)tid);
+        };
+        staged_hd = hd;  // a new head's codebooks are staged by the prologue
+        q_pair = p;
+        // the range ends before the row this step appends, and its length is known: the
+        // keys stored before this step
         attn::attn_pair<D, QM, KKind::Packed, false, attn::RuntimeGroups>(
             a, A.pl, A.d, hd, s, i * T, min((i + 1) * T, A.len_new[s] - 1u), i, tk.nt + 1, phase, staged_hd, qt_s,
-            true);
+            true, A.len_new[s] - 1u, own ? hc.lko : nullptr, prologue);
     }
     // every copy has landed (each pair ends with its waits and a CTA barrier): the region
     // goes back to the GEMV phases
@@ -611,17 +709,25 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
     float *xs = reinterpret_cast<float *>(smem);  // GEMV activations (the attention plan's region)
     unsigned char *enc_s = smem + A.off_e;
     float *rot_s = reinterpret_cast<float *>(smem + A.off_r);
+    const uint8_t *tab_s = smem + A.off_r + 4u * D * D;  // permutation, group of each dim, lookup offsets
     float *qraw_s = reinterpret_cast<float *>(smem + A.off_q), *qt_s = qraw_s + kQrawFloats;
+    // cosine and sine of every sequence's new-row RoPE angles (the same in every layer)
+    __shared__ float2 cs_s[kMaxRows * (D / 2)];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t B = A.batch, H = A.kv_heads, d = A.d;
+    for (uint32_t idx = tid; idx < B * (D / 2); idx += kThreads) {
+        const uint32_t b = idx / (D / 2), p = idx % (D / 2);
+        const float ang = __fmul_rn((float)(A.len_new[b] - 1u), A.layers[0].kv.inv_freq[p]);
+        cs_s[idx] = make_float2(cosf(ang), sinf(ang));
+    }
     const uint32_t n_app = H * ((B + kWarps - 1) / kWarps);  // CTAs of the K/V append: a warp per key
     const bool app_cta = blockIdx.x < n_app;
     const uint32_t app_hd = blockIdx.x % H;
     const Tasks tk = tasks(A, n_app);
     const bool has_task = tk.first < tk.total;
-    const uint32_t first_p = has_task ? tk.first / tk.nt : 0u, first_hd = first_p / B, first_s = first_p % B;
-    // CTAs with an attention task and no append rotate their first pair's queries before the
-    // attention phase, from a rotation copied into shared memory during the Q/K/V phase
+    const uint32_t first_p = has_task ? tk.first / tk.nt : 0u, first_hd = first_p / B;
+    // CTAs with an attention task and no append copy their first pair's head tables into
+    // shared memory during the Q/K/V phase
     const bool early_q = has_task && !app_cta;
     const uint32_t rot_bytes = d * d * 4u, rbar = attn::smem_u32(&rot_bar), abar = attn::smem_u32(&args_bar);
     const uint32_t args_bytes = (has_task ? kAttBytes : 0u) + (app_cta ? kKvBytes : 0u);
@@ -647,11 +753,17 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             if (app_cta) attn::bulk_g2s(attn::smem_u32(kv_raw), &L.kv, kKvBytes, abar);
         }
         if (early_q && tid == 0) {
+            // rotation, permutation, group of each dim and lookup offsets of the first pair's
+            // head (16-byte aligned in the table blob; d = 64, so whole 16-byte units)
+            const AttnHead &fh = L.att.head[first_hd];
             attn::mbar_init(rbar, 1u);
             attn::fence_barrier_init();
             attn::fence_proxy_async();
-            attn::mbar_expect_tx(rbar, rot_bytes);
-            attn::bulk_g2s(attn::smem_u32(rot_s), L.att.head[first_hd].rot, rot_bytes, rbar);
+            attn::mbar_expect_tx(rbar, rot_bytes + 4u * d);
+            attn::bulk_g2s(attn::smem_u32(rot_s), fh.rot, rot_bytes, rbar);
+            attn::bulk_g2s(attn::smem_u32(tab_s), fh.perm, d, rbar);
+            attn::bulk_g2s(attn::smem_u32(tab_s + d), fh.group_of, d, rbar);
+            attn::bulk_g2s(attn::smem_u32(tab_s + 2 * d), fh.lookup_off, 2 * d, rbar);
         }
         gemv<0, BT, 2, kChunks>(A, A.h, A.hidden, l == 0 ? A.tokens : nullptr, A.hidden, L.ln1, L.w_qkv, L.qkv_b,
                                 A.qkv_row, A.qkv, A.qkv_row, xs, pq);
@@ -662,10 +774,10 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             return;
         }
         stamp(A, 1 + 5 * l);
-        // ---- 2. K/V append | query records | codebooks of the first attention task ----
-        prefetch_l2(L.w_o, (uint64_t)A.hidden * A.q_heads * d * 2u);
-        prefetch_l2(L.w_gu, (uint64_t)2u * A.inter * A.hidden * 2u);
-        prefetch_l2(L.w_down, (uint64_t)A.hidden * A.inter * 2u);
+        // ---- 2. K/V append | attention tasks ----
+        prefetch_l2(L.w_o, (uint64_t)A.hidden * A.q_heads * d * 2u, 32);
+        prefetch_l2(L.w_gu, (uint64_t)2u * A.inter * A.hidden * 2u, 64);
+        prefetch_l2(L.w_down, (uint64_t)A.hidden * A.inter * 2u, 96);
         bool args_landed = false;
         if (args_bytes) {
             args_landed = __syncthreads_and(attn::mbar_wait_bounded(abar, 0u));
@@ -681,12 +793,14 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             const uint32_t b = (blockIdx.x / H) * kWarps + warp;
             if (b < B) {
                 const uint32_t pos = A.len_new[b] - 1u;
+                const float2 *csb = cs_s + b * (D / 2);
+                float vv[2];
                 if (staged) {
-                    append_one<true>(A, kv, hs, app_hd, b, pos, wks[warp], kr[warp], lane);
-                    new_row_partial<true>(A, kv, att, hs, app_hd, b, pos, tk.nt, wks[warp], kr[warp], lane);
+                    append_one<true>(A, kv, hs, app_hd, b, pos, csb, wks[warp], kr[warp], lane, vv);
+                    new_row_partial<true, QM>(A, att, hs, app_hd, b, tk.nt, csb, vv, wks[warp], kr[warp], lane);
                 } else {
-                    append_one<false>(A, kv, kv.head[app_hd], app_hd, b, pos, wks[warp], kr[warp], lane);
-                    new_row_partial<false>(A, kv, att, kv.head[app_hd], app_hd, b, pos, tk.nt, wks[warp], kr[warp],
+                    append_one<false>(A, kv, kv.head[app_hd], app_hd, b, pos, csb, wks[warp], kr[warp], lane, vv);
+                    new_row_partial<false, QM>(A, att, kv.head[app_hd], app_hd, b, tk.nt, csb, vv, wks[warp], kr[warp],
                                            lane);
                 }
             }
@@ -696,22 +810,19 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
                 if (tid == 0) mbar_inval(smem_addr(&stage_bar));  // initialised again next layer
             }
         }
-        bool qt_ready = false;
+        HeadCopy hc{};
         if (early_q) {
             const bool landed = __syncthreads_and(attn::mbar_wait_bounded(rbar, 0u));
             if (!landed && tid == 0) atomicOr(A.status, kStatusWaitTimeout);
-            query_records<QM>(A, att, first_hd, first_s, A.len_new[first_s] - 1u,
-                              landed ? rot_s : att.head[first_hd].rot, qraw_s, qt_s);
+            if (landed) hc = HeadCopy{rot_s, tab_s, tab_s + d, reinterpret_cast<const uint16_t *>(tab_s + 2 * d), first_hd};
             if (landed && tid == 0) mbar_inval(rbar);  // initialised again next layer
-            qt_ready = true;
         }
-        if (has_task) attn::stage_lookup(att.head[first_hd], A.pl, reinterpret_cast<float *>(smem + A.pl.cent), tid);
         // ---- attention over the keys stored before this step, in the same phase (no range
         //      reads a row the appends write).  The next layer's Q/K/V weights are requested
         //      into L2 meanwhile ----
         if (l + 1 < A.n_layers) prefetch_l2(A.layers[l + 1].w_qkv, qkv_bytes);
         else prefetch_l2(A.lm_head, (uint64_t)A.vocab * A.hidden * 2u);
-        attention_phase<QM>(A, att, tk, qraw_s, qt_s, qt_ready, first_hd);
+        attention_phase<QM>(A, att, tk, cs_s, qraw_s, qt_s, hc);
         Pass<1, 1, kChunks> po;
         po.preload(L.w_o, A.q_heads * d, A.hidden);
         if (!grid_barrier(A.bar, A.bar_base + (unsigned long long)(++nb) * gridDim.x, A.status)) return;
@@ -866,6 +977,7 @@ bgtq_status bgtq_decoder_create(const bgtq_decoder_desc *dp, bgtq_decoder **out)
         for (uint32_t h = 0; h < d.kv_heads; ++h) {
             bgtq_keys *k = at->keys[h];
             bgtq_values *v = at->values[h];
+            if (v->D != hd_dim) return bail(BGTQ_EINVAL, "decoder: value rows must have the head dim");
             fill_encode_head(k, kv.head[h]);
             kv.v[h] = v->data;
             kv.v_lengths[h] = v->d_lengths;
@@ -930,7 +1042,7 @@ bgtq_status bgtq_decoder_create(const bgtq_decoder_desc *dp, bgtq_decoder **out)
     const uint32_t part_bytes = attn::align16(4u * max_nt * B * d.q_heads * (hd_dim + 2));
     const bool part_copy = off_part + part_bytes <= 128u * 1024u;
     const uint32_t region_u = attn::align128(std::max(pl.total, part_copy ? off_part + part_bytes : off_part));
-    const uint32_t off_e = region_u, off_r = attn::align128(off_e + enc_stage), off_q = off_r + 4u * hd_dim * hd_dim;
+    const uint32_t off_e = region_u, off_r = attn::align128(off_e + enc_stage), off_q = off_r + 4u * hd_dim * hd_dim + 4u * hd_dim;
     const uint32_t smem = off_q + 4u * (step::kQrawFloats + step::kQtFloats);
     const void *kern = pick_kernel(gqa, B);
     cudaFuncAttributes fa{};
