@@ -83,6 +83,7 @@ struct Args {
     uint32_t enc_stage;      // bytes of staged encode tables (0: read from global memory)
     uint32_t off_e, off_r, off_q;  // dynamic shared memory: encode tables, rotation, query scratch
     uint32_t off_part;             // the attention partials' copy in the GEMV region (0: read through L2)
+    uint32_t off_lk;               // the first attention pair's codebooks (lookup layout, 1024-aligned)
     uint32_t *bar;           // grid barrier: 64-bit arrival counter, abort word
     unsigned long long bar_base;  // the arrival counter at launch
     uint32_t *status;
@@ -154,13 +155,18 @@ __device__ __forceinline__ bool grid_barrier(uint32_t *bar, unsigned long long t
     return s_ok != 0;
 }
 
-// Asks L2 for this CTA's share of `bytes` (a multiple of 16) at p (16-byte aligned): one bulk
-// prefetch per CTA (issued by thread `issuer`), so a matrix the next phase streams is on chip
-// when it starts.
-__device__ __forceinline__ void prefetch_l2(const void *p, uint64_t bytes, uint32_t issuer = 0) {
+// Asks L2 for share `part` of `parts` of `bytes` (a multiple of 16) at p (16-byte aligned):
+// bulk prefetches issued by thread `issuer`, so a matrix a later phase streams is on chip when
+// it starts.  By default every CTA takes its share.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint64_t bytes, uint32_t issuer = 0,
+                                            uint32_t part = ~0u, uint32_t parts = 0) {
     if (threadIdx.x != issuer || !p || !bytes) return;
-    const uint64_t per = ((bytes + gridDim.x - 1) / gridDim.x + 15u) & ~15ull;
-    const uint64_t b0 = (uint64_t)blockIdx.x * per;
+    if (!parts) {
+        part = blockIdx.x;
+        parts = gridDim.x;
+    }
+    const uint64_t per = ((bytes + parts - 1) / parts + 15u) & ~15ull;
+    const uint64_t b0 = (uint64_t)part * per;
     if (b0 >= bytes) return;
     uint64_t n = bytes - b0 < per ? bytes - b0 : per;
     const unsigned char *q = static_cast<const unsigned char *>(p) + b0;
@@ -589,40 +595,6 @@ __device__ void query_records(const Args &A, const AttnArgs &a, uint32_t hd, uin
     __syncthreads();
 }
 
-// The head's codebooks in the decode-attention lookup layout (attn::stage_lookup's copy), in
-// two halves around other work: fetch issues the leading kLookupRegs float4 per thread into
-// registers, store writes them (and the rest, fetched then) into shared memory.
-constexpr uint32_t kLookupRegs = 6;
-struct LookupFetch {
-    float4 v[kLookupRegs];
-};
-__device__ __forceinline__ void lookup_fetch(const AttnHead &h, const attn::Plan &pl, LookupFetch &f, int tid) {
-    const uint32_t n4 = pl.cent_alloc / 4u, nl = h.n_lookup;
-    const float4 *src = reinterpret_cast<const float4 *>(h.lookup);
-#pragma unroll
-    for (uint32_t u = 0; u < kLookupRegs; ++u) {
-        const uint32_t q = tid + u * kThreads;
-        f.v[u] = q < n4 && 4u * q + 3u < nl ? __ldg(src + q) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    }
-}
-__device__ __forceinline__ float4 lookup_tail(const AttnHead &h, uint32_t q, uint32_t nl) {
-    return make_float4(4u * q < nl ? h.lookup[4u * q] : 0.0f, 4u * q + 1u < nl ? h.lookup[4u * q + 1u] : 0.0f,
-                       4u * q + 2u < nl ? h.lookup[4u * q + 2u] : 0.0f, 0.0f);
-}
-__device__ __forceinline__ void lookup_store(const AttnHead &h, const attn::Plan &pl, const LookupFetch &f,
-                                             float *cent_s, int tid) {
-    const uint32_t n4 = pl.cent_alloc / 4u, nl = h.n_lookup;
-    const float4 *src = reinterpret_cast<const float4 *>(h.lookup);
-    float4 *dst = reinterpret_cast<float4 *>(cent_s);
-#pragma unroll
-    for (uint32_t u = 0; u < kLookupRegs; ++u) {
-        const uint32_t q = tid + u * kThreads;
-        if (q < n4) dst[q] = 4u * q + 3u < nl ? f.v[u] : lookup_tail(h, q, nl);
-    }
-    for (uint32_t q = tid + kLookupRegs * kThreads; q < n4; q += kThreads)
-        dst[q] = 4u * q + 3u < nl ? __ldg(src + q) : lookup_tail(h, q, nl);
-    for (uint32_t i = 4u * n4 + tid; i < pl.cent_alloc; i += kThreads) cent_s[i] = i < nl ? h.lookup[i] : 0.0f;
-}
 
 // Attention tasks: nt ranges of task_tokens per pair over the keys stored before this step
 // (partial slots 0 .. nt-1; slot nt is the new row's), pairs in head-major order; task t
@@ -653,7 +625,9 @@ struct HeadCopy {
 // The attention phase of one layer: the CTA's tasks, each attn::attn_pair over its range.  A
 // task that starts a pair builds the pair's query records (and stages a new head's
 // codebooks) as the body's prologue, after the range's first tile copies are issued, so the
-// copies land meanwhile.  cs: the new rows' RoPE angles, [batch][d / 2].
+// copies land meanwhile.  The head of hc (the CTA's first pair) has its codebooks in their
+// own region (A.off_lk, copied during the Q/K/V phase); other heads are staged into the
+// plan's.  cs: the new rows' RoPE angles, [batch][d / 2].
 template <int QM>
 __device__ void attention_phase(const Args &A, const AttnArgs &a, const Tasks &tk, const float2 *cs, float *qraw_s,
                                 float *qt_s, const HeadCopy &hc) {
@@ -665,26 +639,27 @@ __device__ void attention_phase(const Args &A, const AttnArgs &a, const Tasks &t
     attn::fence_barrier_init();
     __syncthreads();
     float *cent_s = reinterpret_cast<float *>(smem + A.pl.cent);
+    attn::Plan pl_own = A.pl;
+    pl_own.cent = A.off_lk;
     uint32_t phase = 0, q_pair = ~0u, staged_hd = ~0u;
     for (uint32_t t = tk.first; t < tk.total; t += gridDim.x) {
         const uint32_t p = t / tk.nt, i = t % tk.nt, hd = p / B, s = p % B;
         const AttnHead &h = a.head[hd];
-        const bool fresh = p != q_pair, restage = hd != staged_hd, own = hc.rot && hd == hc.hd;
+        const bool own = hc.rot && hd == hc.hd, fresh = p != q_pair, restage = !own && hd != staged_hd;
         auto prologue = [&]() {
-            if (!fresh) return;
-            LookupFetch lf;
-            if (restage) lookup_fetch(h, A.pl, lf, (int)tid);
-            query_records<QM>(A, a, hd, s, cs + s * (D / 2), own ? hc.rot : h.rot, own ? hc.perm : h.perm,
-                              own ? hc.grp : h.group_of, qraw_s, qt_s);
-            if (restage) lookup_store(h, A.pl, lf, cent_s, (int)tid);
+            if (restage) attn::stage_lookup(h, A.pl, cent_s, (int)tid);
+            if (fresh)
+                query_records<QM>(A, a, hd, s, cs + s * (D / 2), own ? hc.rot : h.rot, own ? hc.perm : h.perm,
+                                  own ? hc.grp : h.group_of, qraw_s, qt_s);
         };
-        staged_hd = hd;  // a new head's codebooks are staged by the prologue
+        if (!own) staged_hd = hd;
         q_pair = p;
+        uint32_t body_hd = hd;  // codebooks in place: the body stages none
         // the range ends before the row this step appends, and its length is known: the
         // keys stored before this step
         attn::attn_pair<D, QM, KKind::Packed, false, attn::RuntimeGroups>(
-            a, A.pl, A.d, hd, s, i * T, min((i + 1) * T, A.len_new[s] - 1u), i, tk.nt + 1, phase, staged_hd, qt_s,
-            true, A.len_new[s] - 1u, own ? hc.lko : nullptr, prologue);
+            a, own ? pl_own : A.pl, A.d, hd, s, i * T, min((i + 1) * T, A.len_new[s] - 1u), i, tk.nt + 1, phase,
+            body_hd, qt_s, true, A.len_new[s] - 1u, own ? hc.lko : nullptr, prologue);
     }
     // every copy has landed (each pair ends with its waits and a CTA barrier): the region
     // goes back to the GEMV phases
@@ -759,11 +734,19 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             attn::mbar_init(rbar, 1u);
             attn::fence_barrier_init();
             attn::fence_proxy_async();
-            attn::mbar_expect_tx(rbar, rot_bytes + 4u * d);
+            const uint32_t lk_bytes = attn::align16(4u * fh.n_lookup);  // the blob pads with zeros
+            attn::mbar_expect_tx(rbar, rot_bytes + 4u * d + lk_bytes);
             attn::bulk_g2s(attn::smem_u32(rot_s), fh.rot, rot_bytes, rbar);
+            attn::bulk_g2s(attn::smem_u32(smem + A.off_lk), fh.lookup, lk_bytes, rbar);
             attn::bulk_g2s(attn::smem_u32(tab_s), fh.perm, d, rbar);
             attn::bulk_g2s(attn::smem_u32(tab_s + d), fh.group_of, d, rbar);
             attn::bulk_g2s(attn::smem_u32(tab_s + 2 * d), fh.lookup_off, 2 * d, rbar);
+        }
+        if (early_q) {
+            // the zero tail after the copied codebooks (lookups of padding records land there)
+            const uint32_t n0 = attn::align16(4u * L.att.head[first_hd].n_lookup) / 4u;
+            float *lk = reinterpret_cast<float *>(smem + A.off_lk);
+            for (uint32_t i = n0 + tid; i < min(n0 + 256u, A.pl.cent_alloc); i += kThreads) lk[i] = 0.0f;
         }
         gemv<0, BT, 2, kChunks>(A, A.h, A.hidden, l == 0 ? A.tokens : nullptr, A.hidden, L.ln1, L.w_qkv, L.qkv_b,
                                 A.qkv_row, A.qkv, A.qkv_row, xs, pq);
@@ -774,10 +757,20 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             return;
         }
         stamp(A, 1 + 5 * l);
-        // ---- 2. K/V append | attention tasks ----
-        prefetch_l2(L.w_o, (uint64_t)A.hidden * A.q_heads * d * 2u, 32);
-        prefetch_l2(L.w_gu, (uint64_t)2u * A.inter * A.hidden * 2u, 64);
-        prefetch_l2(L.w_down, (uint64_t)A.hidden * A.inter * 2u, 96);
+        // ---- 2. K/V append | attention tasks.  The later phases' matrices are requested into
+        //      L2 by the CTAs with neither (every CTA its share when few are idle) ----
+        {
+            const uint32_t busy = n_app + tk.total, n_idle = busy < gridDim.x ? gridDim.x - busy : 0u;
+            const bool by_idle = n_idle >= 16u;
+            if (!by_idle || blockIdx.x >= busy) {
+                const uint32_t part = by_idle ? blockIdx.x - busy : ~0u, parts = by_idle ? n_idle : 0u;
+                prefetch_l2(L.w_o, (uint64_t)A.hidden * A.q_heads * d * 2u, 0, part, parts);
+                prefetch_l2(L.w_gu, (uint64_t)2u * A.inter * A.hidden * 2u, 32, part, parts);
+                prefetch_l2(L.w_down, (uint64_t)A.hidden * A.inter * 2u, 64, part, parts);
+                if (l + 1 < A.n_layers) prefetch_l2(A.layers[l + 1].w_qkv, qkv_bytes, 96, part, parts);
+                else prefetch_l2(A.lm_head, (uint64_t)A.vocab * A.hidden * 2u, 96, part, parts);
+            }
+        }
         bool args_landed = false;
         if (args_bytes) {
             args_landed = __syncthreads_and(attn::mbar_wait_bounded(abar, 0u));
@@ -818,10 +811,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
             if (landed && tid == 0) mbar_inval(rbar);  // initialised again next layer
         }
         // ---- attention over the keys stored before this step, in the same phase (no range
-        //      reads a row the appends write).  The next layer's Q/K/V weights are requested
-        //      into L2 meanwhile ----
-        if (l + 1 < A.n_layers) prefetch_l2(A.layers[l + 1].w_qkv, qkv_bytes);
-        else prefetch_l2(A.lm_head, (uint64_t)A.vocab * A.hidden * 2u);
+        //      reads a row the appends write) ----
         attention_phase<QM>(A, att, tk, cs_s, qraw_s, qt_s, hc);
         Pass<1, 1, kChunks> po;
         po.preload(L.w_o, A.q_heads * d, A.hidden);
@@ -1043,7 +1033,8 @@ bgtq_status bgtq_decoder_create(const bgtq_decoder_desc *dp, bgtq_decoder **out)
     const bool part_copy = off_part + part_bytes <= 128u * 1024u;
     const uint32_t region_u = attn::align128(std::max(pl.total, part_copy ? off_part + part_bytes : off_part));
     const uint32_t off_e = region_u, off_r = attn::align128(off_e + enc_stage), off_q = off_r + 4u * hd_dim * hd_dim + 4u * hd_dim;
-    const uint32_t smem = off_q + 4u * (step::kQrawFloats + step::kQtFloats);
+    const uint32_t off_lk = (off_q + 4u * (step::kQrawFloats + step::kQtFloats) + 1023u) & ~1023u;
+    const uint32_t smem = off_lk + 4u * pl.cent_alloc;
     const void *kern = pick_kernel(gqa, B);
     cudaFuncAttributes fa{};
     if (!ck(cudaFuncGetAttributes(&fa, kern))) return bail(BGTQ_ECUDA, "decoder: kernel attributes");
@@ -1090,6 +1081,7 @@ bgtq_status bgtq_decoder_create(const bgtq_decoder_desc *dp, bgtq_decoder **out)
     A.off_e = off_e;
     A.off_r = off_r;
     A.off_part = part_copy ? off_part : 0u;
+    A.off_lk = off_lk;
     A.off_q = off_q;
     A.bar = static_cast<uint32_t *>(dec->bar.p);
     A.status = status;
