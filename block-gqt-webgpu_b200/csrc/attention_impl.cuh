@@ -1063,18 +1063,23 @@ __device__ __forceinline__ float rope_elem(const float *q, uint32_t j, uint32_t 
 // kernel's arithmetic (qrot_kernel, below): for launches of one partial wave, where a
 // separate rotation launch on the critical path costs more than every CTA rotating its
 // pair's few query rows.  rot_s: the head's rotation already in shared memory (head dims
-// up to 64); qraw: R * d floats of scratch; qt: [D][QP] output, shared memory.
+// up to 64); pg_s: its permutation [D] then group of each dim [D], in shared memory too; qraw:
+// R * d floats of scratch; qt: [D][QP] output, shared memory, which first holds the raw query
+// rows (read in the same round trip as the length).  Returns the sequence's key length.
 template <int D, int QP>
-__device__ __forceinline__ void own_query_records(const AttnArgs &a, uint32_t d, uint32_t hd, uint32_t s,
-                                                  const float *rot_s, float *qraw, float *qt) {
+__device__ __forceinline__ uint32_t own_query_records(const AttnArgs &a, uint32_t d, uint32_t hd, uint32_t s,
+                                                      const float *rot_s, const uint8_t *pg_s, float *qraw,
+                                                      float *qt) {
     const AttnHead &h = a.head[hd];
     const uint32_t R = a.rows, tid = threadIdx.x;
     const float *qg = a.q + ((uint64_t)s * a.heads + hd) * (uint64_t)R * d;
     const uint32_t len = __ldcg(a.lengths + a.seq_first + s);
+    for (uint32_t idx = tid; idx < R * d; idx += kThreads) qt[idx] = __ldcg(qg + idx);
+    __syncthreads();
     for (uint32_t idx = tid; idx < R * d; idx += kThreads) {
         const uint32_t r = idx / d, i = idx % d;
         const uint32_t pos = a.positions ? a.positions[s * R + r] : (len ? len - 1 : 0);
-        qraw[idx] = rope_elem(qg + r * d, h.perm[i], d, pos, a.rope);
+        qraw[idx] = rope_elem(qt + r * d, pg_s[i], d, pos, a.rope);
     }
     __syncthreads();
     const float qscale = kLog2e / sqrtf((float)d);
@@ -1082,7 +1087,7 @@ __device__ __forceinline__ void own_query_records(const AttnArgs &a, uint32_t d,
         const uint32_t j = idx / QP, r = idx % QP;
         float v = 0.0f;
         if (r < R && j < d) {
-            const uint32_t g = h.group_of[j], lo = h.group_off[g], hi = h.group_off[g + 1];
+            const uint32_t g = pg_s[D + j], lo = h.group_off[g], hi = h.group_off[g + 1];
             const float *rj = rot_s + (uint64_t)j * d;
             for (uint32_t i = lo; i < hi; ++i) v = fmaf(rj[i], qraw[r * d + i], v);
             v *= qscale;
@@ -1090,6 +1095,7 @@ __device__ __forceinline__ void own_query_records(const AttnArgs &a, uint32_t d,
         qt[idx] = v;
     }
     __syncthreads();
+    return len;
 }
 
 // One CTA of the decode attention.  Split-KV (a.sk_units == 0): the CTA owns split `split`
@@ -1120,11 +1126,23 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     constexpr int QP = QPad<QM>::QP;
     const bool fq = KK == KKind::Packed && a.fuse_q && !a.sk_units;
     float *rot_s = reinterpret_cast<float *>(smem + pl.stage);
+    // with it the permutation and group of each dim (after the raw query scratch), and the
+    // lookup offsets after the query records in the P buffers (the query tables read them
+    // once the first tile copies have taken over the tile buffers)
+    uint8_t *pg_s = reinterpret_cast<uint8_t *>(rot_s + d * d + kMaxRows * D);
+    float *qt_s = reinterpret_cast<float *>(smem + pl.pbuf);
+    uint16_t *lko_s = reinterpret_cast<uint16_t *>(qt_s + D * QP);
     if (fq) {
-        const float4 *src = reinterpret_cast<const float4 *>(a.head[hd].rot);
+        const AttnHead &fh = a.head[hd];
+        const float4 *src = reinterpret_cast<const float4 *>(fh.rot);
         float4 *dst = reinterpret_cast<float4 *>(rot_s);
 #pragma unroll 8
         for (uint32_t idx = tid; idx < d * d / 4; idx += kThreads) dst[idx] = __ldg(src + idx);
+        for (uint32_t i = tid; i < d; i += kThreads) {
+            pg_s[i] = fh.perm[i];
+            pg_s[D + i] = fh.group_of[i];
+            lko_s[i] = fh.lookup_off[i];
+        }
     }
     pdl_wait();
     // the kernel after this one may launch once every CTA of this grid has started: it then
@@ -1135,13 +1153,12 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     __syncthreads();
     uint32_t phase = 0, staged_hd = hd;
     if (!a.sk_units) {
-        // fused rotation: query records into the P buffers (free until the tile loop), raw
+        // fused rotation: query records into the P buffers (free until the tile loop), rotated
         // query rows after the rotation in the tile buffers (free until the first copies)
-        float *qt_s = reinterpret_cast<float *>(smem + pl.pbuf);
-        if (fq) own_query_records<D, QP>(a, d, hd, s, rot_s, rot_s + d * d, qt_s);
+        const uint32_t len = fq ? own_query_records<D, QP>(a, d, hd, s, rot_s, pg_s, rot_s + d * d, qt_s) : 0u;
         attn_pair<D, QM, KK, VF32, LP>(a, pl, d, hd, s, split * a.tokens_per_split,
                                        split * a.tokens_per_split + a.tokens_per_split, split, a.splits, phase,
-                                       staged_hd, fq ? qt_s : nullptr);
+                                       staged_hd, fq ? qt_s : nullptr, false, len, fq ? lko_s : nullptr);
         return;
     }
     const uint64_t g1 = g0 + K < total ? g0 + K : total;
