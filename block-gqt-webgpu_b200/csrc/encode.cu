@@ -673,31 +673,45 @@ __global__ void __launch_bounds__(kThreads) kv_rope_append_kernel(const __grid_c
     const uint32_t pairs = d / 2;
     for (uint32_t q = blockIdx.x * W + w; q < total; q += gridDim.x * W) {
         const uint32_t s = q / a.count, rr = q % a.count, seq = a.seq_first + s;
+        const uint64_t at = (uint64_t)s * a.seq_stride + (uint64_t)rr * a.row_stride + (uint64_t)hd * d;
+        // the lane's K and V source elements (lane + 32 u), fetched in the same round trip as
+        // the row position
+        float kx[kMaxDim / 32], vx[kMaxDim / 32];
+#pragma unroll
+        for (uint32_t u = 0; u < (uint32_t)kMaxDim / 32; ++u) {
+            const uint32_t e = lane + 32u * u;
+            kx[u] = e < d ? src_elem(a.k_src, at + e, a.k_f16) : 0.0f;
+            vx[u] = e < d ? src_elem(a.v_src, at + e, a.v_f16) : 0.0f;
+        }
         const uint32_t pos = a.start[seq] + rr;
         if (pos >= a.capacity) {  // replayed past the capacity the host checked: refuse, report
             if (lane == 0) atomicOr(a.status, kStatusBadLength);
             continue;
         }
-        const uint64_t at = (uint64_t)s * a.seq_stride + (uint64_t)rr * a.row_stride + (uint64_t)hd * d;
+#pragma unroll
+        for (uint32_t u = 0; u < (uint32_t)kMaxDim / 32; ++u)
+            if (lane + 32u * u < d) kr[w][lane + 32u * u] = kx[u];
+        __syncwarp();
         if (a.rope) {
             for (uint32_t p = lane; p < pairs; p += 32) {
                 const float ang = __fmul_rn((float)pos, a.inv_freq[p]);
                 const float c = cosf(ang), sn = sinf(ang);
-                const float x = src_elem(a.k_src, at + p, a.k_f16), y = src_elem(a.k_src, at + p + pairs, a.k_f16);
+                const float x = kr[w][p], y = kr[w][p + pairs];
                 kr[w][p] = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, sn));
                 kr[w][p + pairs] = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, sn));
             }
-        } else {
-            for (uint32_t i = lane; i < d; i += 32) kr[w][i] = src_elem(a.k_src, at + i, a.k_f16);
+            __syncwarp();
         }
-        __syncwarp();
         for (uint32_t i = lane; i < d; i += 32) wk.xs[i] = __half2float(__float2half_rn(kr[w][h.t.perm[i]]));
         if (staged) warp_encode<true>(h, d, wk, seq, pos, lane);
         else warp_encode<false>(h, d, wk, seq, pos, lane);
         // V row: FP32 -> FP16, chunk-swizzled for head dims 64 / 128
         __half *vrow = reinterpret_cast<__half *>(a.v[hd]) + (uint64_t)seq * a.v_seq_stride[hd] + (uint64_t)pos * a.vD;
-        for (uint32_t e = lane; e < a.vD; e += 32) {
-            const float x = e < d ? src_elem(a.v_src, at + e, a.v_f16) : 0.0f;
+#pragma unroll
+        for (uint32_t u = 0; u < (uint32_t)kMaxDim / 32; ++u) {
+            const uint32_t e = lane + 32u * u;
+            if (e >= a.vD) break;
+            const float x = vx[u];  // zero past the head dim
             uint32_t de = e;
             if (a.v_swizzle) {
                 const uint32_t c = e >> 3;
