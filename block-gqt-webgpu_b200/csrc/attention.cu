@@ -269,12 +269,14 @@ cudaError_t launch_attention(const AttnArgs &a_in, KKind kk, int v_f32, uint32_t
     if (splits_out) *splits_out = splits;
     if (sk_out) *sk_out = a.sk_units;
     // one partial wave of split-KV CTAs over packed keys: each CTA rotates its pair's queries
-    // itself (the rotation staged in its tile buffers, the records in its P buffers), which
-    // takes a launch off the critical path of small batches; larger launches rotate once per
-    // pair in a launch of their own
+    // itself (the rotation, transposed in rows of D + 1 floats, the raw query rows and the
+    // permutation and group tables staged in its tile buffers; the records and lookup offsets
+    // in its P buffers), which takes a launch off the critical path of small batches; larger
+    // launches rotate once per pair in a launch of their own
     const uint32_t stage_bytes = attn::kWarps * pl.warp_bytes, pbuf_bytes = pl.bars - pl.pbuf;
     a.fuse_q = kk == KKind::Packed && d <= 64u && !a.sk_units && (uint64_t)pairs * splits <= slots &&
-                       stage_bytes >= 4u * (d * d + a.rows * d) && pbuf_bytes >= 4u * D * e.qp
+                       stage_bytes >= 4u * (D * (D + 1) + kMaxRows * D) + 2u * D &&
+                       pbuf_bytes >= 4u * D * e.qp + 2u * D
                    ? 1u
                    : 0u;
     if (launches_out) *launches_out = a.fuse_q ? 1u : 2u;

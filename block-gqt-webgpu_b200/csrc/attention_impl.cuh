@@ -1063,12 +1063,15 @@ __device__ __forceinline__ float rope_elem(const float *q, uint32_t j, uint32_t 
 // kernel's arithmetic (qrot_kernel, below): for launches of one partial wave, where a
 // separate rotation launch on the critical path costs more than every CTA rotating its
 // pair's few query rows.  rot_s: the head's rotation already in shared memory (head dims
-// up to 64); pg_s: its permutation [D] then group of each dim [D], in shared memory too; qraw:
-// R * d floats of scratch; qt: [D][QP] output, shared memory, which first holds the raw query
-// rows (read in the same round trip as the length).  Returns the sequence's key length.
+// up to 64), transposed: R[j][i] at rot_t[i * (D + 1) + j], so lanes over consecutive j
+// read 32 banks (the padded row stride; rows 64 floats apart would share one); pg_s: its
+// permutation [D] then group of each dim [D], in shared memory too; qraw: R * d floats of
+// scratch; qt: [D][QP] output, shared memory, which first holds the raw query rows (read in
+// the same round trip as the length).  Every output is one ascending FMA chain over its
+// group, as in qrot_kernel.  Returns the sequence's key length.
 template <int D, int QP>
 __device__ __forceinline__ uint32_t own_query_records(const AttnArgs &a, uint32_t d, uint32_t hd, uint32_t s,
-                                                      const float *rot_s, const uint8_t *pg_s, float *qraw,
+                                                      const float *rot_t, const uint8_t *pg_s, float *qraw,
                                                       float *qt) {
     const AttnHead &h = a.head[hd];
     const uint32_t R = a.rows, tid = threadIdx.x;
@@ -1084,15 +1087,14 @@ __device__ __forceinline__ uint32_t own_query_records(const AttnArgs &a, uint32_
     __syncthreads();
     const float qscale = kLog2e / sqrtf((float)d);
     for (uint32_t idx = tid; idx < (uint32_t)(D * QP); idx += kThreads) {
-        const uint32_t j = idx / QP, r = idx % QP;
+        const uint32_t j = idx % D, r = idx / D;
         float v = 0.0f;
         if (r < R && j < d) {
             const uint32_t g = pg_s[D + j], lo = h.group_off[g], hi = h.group_off[g + 1];
-            const float *rj = rot_s + (uint64_t)j * d;
-            for (uint32_t i = lo; i < hi; ++i) v = fmaf(rj[i], qraw[r * d + i], v);
+            for (uint32_t i = lo; i < hi; ++i) v = fmaf(rot_t[i * (D + 1) + j], qraw[r * d + i], v);
             v *= qscale;
         }
-        qt[idx] = v;
+        qt[j * QP + r] = v;
     }
     __syncthreads();
     return len;
@@ -1125,19 +1127,18 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     // the rotation, a table of the store, comes into the tile buffers before the wait
     constexpr int QP = QPad<QM>::QP;
     const bool fq = KK == KKind::Packed && a.fuse_q && !a.sk_units;
-    float *rot_s = reinterpret_cast<float *>(smem + pl.stage);
+    float *rot_s = reinterpret_cast<float *>(smem + pl.stage);  // transposed, rows of D + 1 floats
     // with it the permutation and group of each dim (after the raw query scratch), and the
     // lookup offsets after the query records in the P buffers (the query tables read them
     // once the first tile copies have taken over the tile buffers)
-    uint8_t *pg_s = reinterpret_cast<uint8_t *>(rot_s + d * d + kMaxRows * D);
+    float *qraw_s = rot_s + D * (D + 1);
+    uint8_t *pg_s = reinterpret_cast<uint8_t *>(qraw_s + kMaxRows * D);
     float *qt_s = reinterpret_cast<float *>(smem + pl.pbuf);
     uint16_t *lko_s = reinterpret_cast<uint16_t *>(qt_s + D * QP);
     if (fq) {
         const AttnHead &fh = a.head[hd];
-        const float4 *src = reinterpret_cast<const float4 *>(fh.rot);
-        float4 *dst = reinterpret_cast<float4 *>(rot_s);
 #pragma unroll 8
-        for (uint32_t idx = tid; idx < d * d / 4; idx += kThreads) dst[idx] = __ldg(src + idx);
+        for (uint32_t e = tid; e < d * d; e += kThreads) rot_s[(e % d) * (D + 1) + e / d] = __ldg(fh.rot + e);
         for (uint32_t i = tid; i < d; i += kThreads) {
             pg_s[i] = fh.perm[i];
             pg_s[D + i] = fh.group_of[i];
@@ -1155,7 +1156,7 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a, const Plan &pl, uin
     if (!a.sk_units) {
         // fused rotation: query records into the P buffers (free until the tile loop), rotated
         // query rows after the rotation in the tile buffers (free until the first copies)
-        const uint32_t len = fq ? own_query_records<D, QP>(a, d, hd, s, rot_s, pg_s, rot_s + d * d, qt_s) : 0u;
+        const uint32_t len = fq ? own_query_records<D, QP>(a, d, hd, s, rot_s, pg_s, qraw_s, qt_s) : 0u;
         attn_pair<D, QM, KK, VF32, LP>(a, pl, d, hd, s, split * a.tokens_per_split,
                                        split * a.tokens_per_split + a.tokens_per_split, split, a.splits, phase,
                                        staged_hd, fq ? qt_s : nullptr, false, len, fq ? lko_s : nullptr);
