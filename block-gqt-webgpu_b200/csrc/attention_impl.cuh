@@ -1186,31 +1186,40 @@ __global__ void __launch_bounds__(kThreads, MinBlocks<D, QM, KK>::value)
 // (head, sequence), computed once instead of once per split.
 static __global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant__ AttnArgs a, uint32_t d, uint32_t D,
                                                    uint32_t QP, int packed) {
-    __shared__ float qraw[kMaxRows * kMaxDim];
-    __shared__ __align__(16) float rot_s[64 * 64];   // the head's rotation, head dims up to 64
-    const uint32_t hd = blockIdx.x, s = blockIdx.y, R = a.rows;
+    constexpr uint32_t RS = 64 + 1;      // row stride of the transposed rotation (padded)
+    __shared__ float qin[kMaxRows * kMaxDim];         // the raw query rows
+    __shared__ float qraw[kMaxRows * (kMaxDim + 1)];  // RoPE'd and permuted, rows of d + 1
+    __shared__ float rot_s[64 * RS];   // the head's rotation transposed, head dims up to 64
+    __shared__ uint8_t pg_s[2 * 64];   // its permutation, then the group of each dim
+    const uint32_t hd = blockIdx.x, s = blockIdx.y, R = a.rows, RQ = d + 1;
     const AttnHead &h = a.head[hd];
-    // the rotation rows are read by every output: one coalesced copy into shared memory
-    // instead of a chain of dependent L2 reads per output.  They are the store's own tables,
-    // so the copy runs before the wait for the kernel ahead (programmatic launch)
+    // the rotation is read by every output: one copy into shared memory instead of a chain of
+    // dependent L2 reads per output, transposed (R[j][i] at rot_s[i * RS + j]) so that the
+    // outputs of one warp (consecutive j) read consecutive banks, where rows 64 floats apart
+    // would share one; with it the permutation and groups.  They are the store's own tables,
+    // so the copies run before the wait for the kernel ahead (programmatic launch)
     const bool staged = packed && d <= 64;
     if (staged) {
-        // 16-byte loads, eight in flight per thread (d * d is a multiple of 4; the rotation
-        // is 16-byte aligned in the table blob)
-        const float4 *src = reinterpret_cast<const float4 *>(h.rot);
-        float4 *dst = reinterpret_cast<float4 *>(rot_s);
 #pragma unroll 8
-        for (uint32_t idx = threadIdx.x; idx < d * d / 4; idx += blockDim.x) dst[idx] = __ldg(src + idx);
+        for (uint32_t e = threadIdx.x; e < d * d; e += blockDim.x) rot_s[(e % d) * RS + e / d] = __ldg(h.rot + e);
+        for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) {
+            pg_s[i] = h.perm[i];
+            pg_s[64 + i] = h.group_of[i];
+        }
     }
     pdl_wait();
     pdl_trigger();
     const float *qg = a.q + ((uint64_t)s * a.heads + hd) * (uint64_t)R * d;
+    // the raw rows in the same round trip as the length (no load waits on the permutation)
     const uint32_t len = a.lengths[a.seq_first + s];
+    for (uint32_t idx = threadIdx.x; idx < R * d; idx += blockDim.x) qin[idx] = __ldcg(qg + idx);
+    __syncthreads();
     for (uint32_t idx = threadIdx.x; idx < R * d; idx += blockDim.x) {
         const uint32_t r = idx / d, i = idx % d;
         // a query sits at its position (default: the last appended row)
         const uint32_t pos = a.positions ? a.positions[s * R + r] : (len ? len - 1 : 0);
-        qraw[idx] = rope_elem(qg + r * d, packed ? h.perm[i] : i, d, pos, a.rope);
+        const uint32_t src = packed ? (staged ? pg_s[i] : h.perm[i]) : i;
+        qraw[r * RQ + i] = rope_elem(qin + r * d, src, d, pos, a.rope);
     }
     __syncthreads();
     const float qscale = kLog2e / sqrtf((float)d);  // scores in log2 units
@@ -1219,12 +1228,17 @@ static __global__ void __launch_bounds__(128) qrot_kernel(const __grid_constant_
         const uint32_t j = idx / QP, r = idx % QP;
         float v = 0.0f;
         if (r < R && j < d) {
+            const float *qr = qraw + r * RQ;
             if (packed) {
-                const uint32_t g = h.group_of[j], lo = h.group_off[g], hi = h.group_off[g + 1];
-                const float *rj = (staged ? rot_s : h.rot) + (uint64_t)j * d;
-                for (uint32_t i = lo; i < hi; ++i) v = fmaf(rj[i], qraw[r * d + i], v);
+                const uint32_t g = staged ? pg_s[64 + j] : h.group_of[j], lo = h.group_off[g], hi = h.group_off[g + 1];
+                if (staged) {
+                    for (uint32_t i = lo; i < hi; ++i) v = fmaf(rot_s[i * RS + j], qr[i], v);
+                } else {
+                    const float *rj = h.rot + (uint64_t)j * d;
+                    for (uint32_t i = lo; i < hi; ++i) v = fmaf(rj[i], qr[i], v);
+                }
             } else {
-                v = qraw[r * d + j];
+                v = qr[j];
             }
             v *= qscale;
         }
