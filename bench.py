@@ -1,4 +1,4 @@
-"""Benchmark: batched compressed-K GQA decode on B200.
+"""Benchmark: batched compressed-K GQA decode on B200 (the headline configuration, config 4).
 
 Workload: SmolLM2-135M attention geometry - 30 layers, 3 KV heads, 9 query heads (GQA 3),
 head_dim 64 - one batch of 256 sequences x 32768 cached tokens, Block-GTQ packed K

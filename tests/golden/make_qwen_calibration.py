@@ -1,4 +1,4 @@
-"""Frozen Block-GTQ tables for the Qwen2.5-0.5B geometry (BASELINE configs 3 and 5).
+"""Frozen Block-GTQ tables for the Qwen2.5-0.5B geometry (benchmark configs 3 and 5).
 
 The reference's Qwen calibration is not part of its checkout (``models/qwen2.5-0.5b/`` is
 git-ignored there), so this script runs the reference's calibration procedure
